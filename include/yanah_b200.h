@@ -1,0 +1,194 @@
+/*
+ * yanah_b200: C ABI of the B200 (sm_100a) sparse-MoE decode path.
+ *
+ * The reference engine (moe_prefetch) runs this path as MLX operations
+ * called from Python (moe_prefetch/mlx_backend.py). Each entry point below
+ * replaces one of those operation groups; the comment on each names the
+ * reference call site (path:line inside the reference project).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only. Every pointer marked "device" is CUDA
+ *    device memory of the current device; "host" pointers are host memory.
+ *  - bf16 and fp16 values travel as uint16_t bit patterns.
+ *  - Quantised matrices use MLX's affine format: `weight` is (rows,
+ *    cols*bits/32) uint32 words, code k of a row sits in word k/(32/bits) at
+ *    bit offset bits*(k%(32/bits)); `scales`/`biases` are (rows, cols/group)
+ *    fp16; w[r][k] = scale*q + bias.
+ *  - Expert records follow the repacked on-disk order gate/up/down x
+ *    weight/scales/biases (moe_prefetch/repack.py:27-29), one record per slot.
+ *  - Functions return 0 on success or a negative YN_E* code; nothing on the
+ *    compute path allocates memory: callers pass a workspace sized by
+ *    yn_workspace_bytes and cleared once with yn_workspace_init.
+ *  - `stream` is a cudaStream_t passed as void*.
+ */
+#ifndef YANAH_B200_H
+#define YANAH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- errors */
+#define YN_OK 0
+#define YN_E_INVALID (-1)      /* bad argument (shape, alignment, null pointer) */
+#define YN_E_UNSUPPORTED (-2)  /* shape/bit-width outside what the kernels implement */
+#define YN_E_CUDA (-3)         /* a CUDA runtime call failed (see yn_last_error) */
+#define YN_E_DEVICE (-4)       /* a kernel reported an error in the workspace error word */
+
+/* Text of the last error raised on this thread. */
+const char* yn_last_error(void);
+
+/* ------------------------------------------------------------ data types */
+
+/* One MLX-affine quantised matrix (device pointers). */
+typedef struct yn_qmat {
+  const void* weight;   /* (rows, cols*bits/32) uint32 */
+  const void* scales;   /* (rows, cols/group_size) fp16 */
+  const void* biases;   /* (rows, cols/group_size) fp16 */
+  int32_t rows, cols, bits, group_size;
+} yn_qmat;
+
+/* Model dimensions of one MoE layer (moe_prefetch/layout.py:28-40). */
+typedef struct yn_dims {
+  int32_t hidden;        /* H */
+  int32_t n_experts;     /* E */
+  int32_t top_k;         /* k */
+  int32_t moe_inter;     /* I, routed expert intermediate size */
+  int32_t shared_inter;  /* I_sh, shared expert intermediate size (0: none) */
+  int32_t norm_topk;     /* 1: renormalise the top-k weights (norm_topk_prob) */
+  float rms_eps;         /* RMSNorm epsilon */
+} yn_dims;
+
+/* Record geometry of one routed expert (moe_prefetch/repack.py:32-63). */
+typedef struct yn_record {
+  int32_t bits, group_size;
+  int64_t piece_offset[9];  /* byte offset of each piece inside a record */
+  int64_t record_bytes;
+} yn_record;
+
+/* Dense (resident) weights of one layer plus its routed-expert storage. */
+typedef struct yn_layer {
+  const void* post_norm;       /* (H) bf16 post_attention_layernorm weight */
+  yn_qmat router;              /* (E, H) mlp.gate */
+  const float* router_bias;    /* (E) fp32 logit offset added before softmax, or NULL */
+  yn_qmat shared_gate;         /* (I_sh, H) shared_expert.gate_proj */
+  yn_qmat shared_up;           /* (I_sh, H) shared_expert.up_proj */
+  yn_qmat shared_down;         /* (H, I_sh) shared_expert.down_proj */
+  yn_qmat shared_expert_gate;  /* (1, H) shared_expert_gate */
+  const void* expert_base;     /* device base of the slot arena */
+  int64_t slot_stride;         /* bytes between consecutive slots */
+  int32_t n_slots;             /* slots addressable from expert_base */
+  const int32_t* expert_slot;  /* (E) device table expert id -> slot, or NULL for slot = id */
+  yn_record record;            /* routed expert record geometry */
+} yn_layer;
+
+/* ------------------------------------------------------------- workspace */
+
+/* Bytes of workspace for one model shape. One workspace serves every call
+ * (any row count T <= YN_MAX_ROWS, up to YN_MAX_TARGETS lookahead routers)
+ * but calls that share a workspace must not run concurrently. */
+#define YN_MAX_ROWS 8
+#define YN_MAX_TARGETS 2
+size_t yn_workspace_bytes(const yn_dims* dims);
+/* Zero the workspace counters and error word (once, after allocation). */
+int yn_workspace_init(void* ws, size_t ws_bytes, const yn_dims* dims, void* stream);
+/* Read and clear the device error word (synchronises the stream). */
+int yn_workspace_error(void* ws, const yn_dims* dims, void* stream, int32_t* code_out);
+
+/* Device pointers to the named outputs inside a workspace (for readback).
+ * Row t of a (T, ...) array starts at row t regardless of T. */
+typedef struct yn_ws_view {
+  void* x;         /* (T, H) bf16: post-attention RMSNorm output */
+  float* logits;   /* (T, E) router logits (bf16 values held in fp32) */
+  int32_t* ids;    /* (T, k) routed expert ids, descending probability */
+  float* weights;  /* (T, k) routing weights (bf16 values held in fp32) */
+  float* flogits;  /* (n_targets, T, E) lookahead router logits (bf16 values in fp32) */
+  float* fprobs;   /* (n_targets, E) lookahead probabilities, max over rows */
+  void* act;       /* (T, k, I) bf16 SwiGLU activations of the routed experts */
+  void* act_sh;    /* (T, I_sh) bf16 SwiGLU activations of the shared expert */
+  float* sgate;    /* (T) sigmoid(shared_expert_gate(x)), bf16 values */
+  void* y;         /* (T*k, H) bf16 routed down outputs, row t*k + j */
+  void* y_shared;  /* (T, H) bf16 sigmoid(gate) * shared down output */
+  int32_t* error;  /* device error word */
+} yn_ws_view;
+int yn_workspace_view(void* ws, const yn_dims* dims, yn_ws_view* out);
+
+/* --------------------------------------------------------------- kernels */
+
+/* mx.dequantize (moe_prefetch/mlx_backend.py:272, quantize_2bit.py:158):
+ * out[r][k] = fp32 fmaf(scale, q, bias), written as fp32 (rows, cols). */
+int yn_dequantize(const yn_qmat* m, float* out, void* stream);
+
+/* QuantizedLinear forward for T rows (mlx_backend.py:305-306, `m.gate(x)`):
+ * y[t][r] = bf16(sum_k x[t][k] w[r][k]) in the canonical reduction order. */
+int yn_qlinear(const yn_qmat* m, const void* x, int32_t T, float* y, void* stream);
+
+/* Routing (mlx_backend.py:308-316): softmax(precise) -> top-k -> renormalise.
+ * logits (T,E) fp32 holding bf16 values. ids (T,k) int32 in descending
+ * probability (ties: lower id first); weights (T,k) bf16 values in fp32. */
+int yn_route(const float* logits, int32_t T, const yn_dims* dims, int32_t* ids, float* weights,
+             void* stream);
+
+/* The post-attention half of a decoder layer plus routing and lookahead
+ * (mlx_backend.py:302-306 `_post_attention` + :326-348 `route_and_forecast`):
+ * x = RMSNorm(h1); shared-expert activations and gate; router logits; top-k
+ * ids and weights; for each target layer t: softmax(router_t(RMSNorm_t(h1)))
+ * in fp32, max over rows. All outputs land in the workspace (yn_ws_view). */
+int yn_post_attention(const yn_dims* dims, const yn_layer* layer, const void* h1, int32_t T,
+                      const yn_layer* targets, int32_t n_targets, void* ws, void* stream);
+
+/* Routed-expert gate/up + SwiGLU for a subset of the k columns
+ * (mlx_backend.py:447-456 `_switch_glu` up to swiglu; :376-391 `moe_ready`
+ * starts the resident columns). ids: (T,k) device, or NULL to use the ids in
+ * the workspace. cols: host array of column indices (NULL = all k). */
+int yn_moe_up(const yn_dims* dims, const yn_layer* layer, const void* x, const int32_t* ids,
+              int32_t T, const int32_t* cols, int32_t n_cols, void* ws, void* stream);
+
+/* Down projections of every routed column and the shared expert, then the
+ * combine (mlx_backend.py:456-459 down, :409/:420 weighted sum, :438-440
+ * routed + shared, orchestrator.py:287 residual):
+ *   mode 0: out = sum_j w_j y_j
+ *   mode 1: out = sum_j w_j y_j + sigmoid(g) * shared(x)
+ *   mode 2: out = h_res + (sum_j w_j y_j + sigmoid(g) * shared(x))
+ * ids/weights: (T,k) device or NULL for the workspace's. out: (T,H) bf16. */
+int yn_moe_down(const yn_dims* dims, const yn_layer* layer, const int32_t* ids, const float* weights,
+                int32_t T, const void* h_res, int32_t mode, void* out, void* ws, void* stream);
+
+/* One whole pool-path MoE layer on device (orchestrator.py:226-300 with every
+ * expert resident): post_attention, routing, experts, combine, residual.
+ * h_in/h_out: (T,H) bf16 device (may not alias). */
+int yn_moe_layer(const yn_dims* dims, const yn_layer* layer, const void* h_in, int32_t T,
+                 const yn_layer* targets, int32_t n_targets, void* h_out, void* ws, void* stream);
+
+/* ---------------------------------------------------------- slot copies */
+
+/* Copy `n` expert records host -> slot arena (io_lanes.py:121-126
+ * read_record, which the reference runs as preadv into pool slots):
+ * record i goes from host_src[i] (pinned host memory recommended) to
+ * arena + slot[i]*slot_stride. One cudaMemcpyAsync per record on `stream`. */
+int yn_slot_copy(void* arena, int64_t slot_stride, const int32_t* slots, const void* const* host_src,
+                 int32_t n, int64_t record_bytes, void* stream);
+
+/* ------------------------------------------------------- synthetic data */
+
+/* Fill `n_words` uint32 words with the counter-based generator used for the
+ * seeded synthetic workloads: word i = hash(seed, stream_id, i). */
+int yn_synth_u32(void* dst, int64_t n_words, uint64_t seed, uint64_t stream_id, void* stream);
+/* Fill `n` fp16 values with approximately normal samples (Irwin-Hall, 4
+ * uniforms) of standard deviation `std` (absolute value if `absolute`). */
+int yn_synth_f16(void* dst, int64_t n, uint64_t seed, uint64_t stream_id, float std, int32_t absolute,
+                 void* stream);
+/* Same for bf16 outputs. */
+int yn_synth_bf16(void* dst, int64_t n, uint64_t seed, uint64_t stream_id, float std, float mean,
+                  void* stream);
+
+/* Library version string. */
+const char* yn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* YANAH_B200_H */

@@ -1,0 +1,168 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle.
+
+Bit-exact: synthetic generator, dequantisation, 8-bit QuantizedLinear,
+RMSNorm, routing ids and weights, lookahead probabilities, shared-expert
+activations and gate. Within REL_L2_TOL (1e-2 relative L2, the bf16 output
+tolerance): routed expert activations, expert outputs and layer outputs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import cpu
+from tests.gpu_helpers import (REL_L2_TOL, DeviceModel, bf16_dev, bf16_np, hidden_rows, rel_l2, small_config)
+from yanah_b200 import _lib
+from yanah_b200.device import DeviceQMat, stream_ptr
+from yanah_b200.formats import pack
+from yanah_b200.synthetic import qwen3_next_block, qwen3_next_stack
+
+pytestmark = pytest.mark.gpu
+
+
+def test_synth_bit_exact():
+    lib = _lib.lib()
+    n = 100_003
+    d = torch.empty(n * 4, dtype=torch.uint8, device="cuda")
+    _lib.check(lib.yn_synth_u32(d.data_ptr(), n, 7, 1234, stream_ptr()))
+    assert np.array_equal(d.cpu().numpy().view(np.uint32), cpu.synth_u32(n, 7, 1234))
+    _lib.check(lib.yn_synth_f16(d.data_ptr(), n, 7, 99, 0.02, 1, stream_ptr()))
+    assert np.array_equal(d[: 2 * n].cpu().numpy().view(np.uint16), cpu.synth_f16(n, 7, 99, 0.02, True))
+    _lib.check(lib.yn_synth_bf16(d.data_ptr(), n, 5, 3, 1.0, 0.0, stream_ptr()))
+    assert np.array_equal(d[: 2 * n].cpu().numpy().view(np.uint16), cpu.synth_bf16(n, 5, 3, 1.0))
+
+
+@pytest.mark.parametrize("bits,gs", [(2, 32), (2, 64), (4, 64), (4, 128), (8, 64)])
+def test_dequantize_bit_exact(bits, gs):
+    rng = np.random.default_rng(bits * 100 + gs)
+    rows, cols = 96, 512
+    codes = rng.integers(0, 2 ** bits, (rows, cols))
+    w = pack(codes, bits)
+    s = np.abs(rng.standard_normal((rows, cols // gs)) * 0.02).astype(np.float16)
+    b = (rng.standard_normal((rows, cols // gs)) * 0.01).astype(np.float16)
+    m = DeviceQMat(w, s, b, cols, bits, gs, "cuda")
+    out = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().yn_dequantize(C.byref(m.struct()), out.data_ptr(), stream_ptr()))
+    ref = cpu.dequantize(w, s, b, cols, bits, gs)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("H,T", [(2048, 1), (2048, 3), (1024, 2), (256, 1)])
+def test_qlinear8_bit_exact(H, T):
+    rng = np.random.default_rng(H + T)
+    rows, gs = 200, 64
+    w = rng.integers(0, 2 ** 32, (rows, H // 4), dtype=np.uint32)
+    s = np.abs(rng.standard_normal((rows, H // gs)) * 1e-3).astype(np.float16)
+    b = (-127.5 * s.astype(np.float32)).astype(np.float16)
+    x = cpu.synth_bf16(T * H, 1, 2, 1.0).reshape(T, H)
+    m = DeviceQMat(w, s, b, H, 8, gs, "cuda")
+    y = torch.empty((T, rows), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().yn_qlinear(C.byref(m.struct()), bf16_dev(x).data_ptr(), T, y.data_ptr(), stream_ptr()))
+    ref = cpu.qlinear(w, s, b, H, 8, gs, x)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("E,k", [(512, 10), (64, 4), (100, 8), (1024, 16)])
+def test_route_bit_exact_with_ties(E, k):
+    rng = np.random.default_rng(E)
+    T = 6
+    # bf16-valued logits on a coarse grid: many exact ties near the top-k boundary
+    lg = (np.round(rng.standard_normal((T, E)) * 4) / 4).astype(np.float32)
+    lg[2, :] = 0.0  # every expert tied
+    dims = _lib.Dims(2048, E, k, 512, 512, 1, 1e-6)
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    _lib.check(_lib.lib().yn_route(torch.from_numpy(lg).cuda().data_ptr(), T, C.byref(dims), ids.data_ptr(),
+                                   w.data_ptr(), stream_ptr()))
+    rids, rw = cpu.route(lg, k)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), rw.view(np.uint32))
+    assert list(rids[2]) == list(range(k))  # full tie: lowest ids win
+
+
+@pytest.mark.parametrize("T,targets", [(1, (1, 2)), (3, (1,)), (1, ())])
+def test_post_attention_bit_exact(T, targets):
+    cfg = small_config(bits=(4, 4, 2), hidden=2048, n_experts=512, top_k=10, inter=512, shared=512)
+    dm = DeviceModel(cfg)
+    o = cpu.OracleStack(cfg)
+    h = hidden_rows(cfg, T, stream=11)
+    dm.post_attention(0, bf16_dev(h), targets)
+    torch.cuda.synchronize()
+    assert dm.ws.check_error() == 0
+    got = dm.ws_out(T, len(targets))
+    ref = o.post_attention(0, h, targets)
+    assert np.array_equal(got["x"], ref["x"])
+    assert np.array_equal(got["logits"].view(np.uint32), ref["logits"].view(np.uint32))
+    assert np.array_equal(got["ids"], ref["ids"])
+    assert np.array_equal(got["w"].view(np.uint32), ref["w"].view(np.uint32))
+    assert np.array_equal(got["act_sh"], ref["act_sh"][:, : cfg.shared_inter])
+    assert np.array_equal(got["sgate"].view(np.uint32), ref["sgate"].view(np.uint32))
+    if targets:
+        assert np.array_equal(got["fprobs"].view(np.uint32), ref["fprobs"][: len(targets)].view(np.uint32))
+
+
+def _layer_case(cfg, T):
+    dm = DeviceModel(cfg)
+    o = cpu.OracleStack(cfg)
+    h = hidden_rows(cfg, T, stream=5)
+    hin = bf16_dev(h)
+    hout = torch.empty_like(hin)
+    dm.layer(0, hin, hout)
+    torch.cuda.synchronize()
+    assert dm.ws.check_error() == 0
+    got = dm.ws_out(T)
+    ref = o.layer(0, h)
+    assert np.array_equal(got["ids"], ref["ids"])
+    assert np.array_equal(got["w"].view(np.uint32), ref["w"].view(np.uint32))
+    for t in range(T):
+        for j in range(cfg.top_k):
+            assert rel_l2(got["act"][t, j], ref["act"][t, j]) < REL_L2_TOL
+            assert rel_l2(got["y"][t, j], ref["y"][t, j]) < REL_L2_TOL
+    if cfg.shared_inter:
+        assert rel_l2(got["ysh"], ref["ysh"]) < REL_L2_TOL
+    out = bf16_np(hout)
+    err = rel_l2(out, ref["out"])
+    assert err < REL_L2_TOL, err
+    return err
+
+
+def test_layer_qwen3_next_block_4bit():
+    _layer_case(qwen3_next_block(seed=1), T=1)
+
+
+def test_layer_qwen3_next_2bit_rows4():
+    cfg = qwen3_next_stack(seed=2)
+    cfg = small_config(bits=(2,), hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=2)
+    _layer_case(cfg, T=4)
+
+
+@pytest.mark.parametrize("bits,gs,T", [(4, 64, 1), (2, 32, 2), (2, 64, 1), (4, 128, 3)])
+def test_layer_small_shapes(bits, gs, T):
+    _layer_case(small_config(bits=(bits,), gs=gs), T=T)
+
+
+def test_layer_no_shared_expert():
+    _layer_case(small_config(bits=(4,), shared=0), T=2)
+
+
+def test_stack_teacher_forced_routing():
+    """Four layers (4,2,2,4-bit): at every layer the device routing equals the
+    oracle's on the device's own layer input, and outputs stay within tolerance."""
+    cfg = small_config(bits=(4, 2, 2, 4), hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=9)
+    dm = DeviceModel(cfg)
+    o = cpu.OracleStack(cfg)
+    h = bf16_dev(hidden_rows(cfg, 1, stream=1))
+    for l in range(cfg.n_layers):
+        hout = torch.empty_like(h)
+        dm.layer(l, h, hout)
+        torch.cuda.synchronize()
+        got = dm.ws_out(1)
+        ref = o.layer(l, bf16_np(h))
+        assert np.array_equal(got["ids"], ref["ids"]), l
+        assert rel_l2(bf16_np(hout), ref["out"]) < REL_L2_TOL, l
+        h = hout
+    assert dm.ws.check_error() == 0

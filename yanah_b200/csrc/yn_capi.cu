@@ -1,0 +1,516 @@
+// extern "C" entry points of libyanah_b200.so (declared in include/yanah_b200.h).
+//
+// Host-side responsibilities: validate shapes and alignment, choose tile
+// sizes (about 40 KB of weights per CTA so every phase keeps its bytes in
+// flight), dispatch the template instantiation that matches the layer's bit
+// widths and row lengths, and carve the caller's workspace. Nothing here
+// allocates device memory.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <string>
+#include <utility>
+
+#include "yn_common.cuh"
+#include "yn_moe.cuh"
+#include "yn_qdot.cuh"
+#include "yn_kernels.cuh"
+
+
+using namespace ynb;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_err;
+static int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+#define YN_CUDA(call)                                                                         \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess) return fail(YN_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+extern "C" const char* yn_last_error(void) { return g_err.c_str(); }
+extern "C" const char* yn_version(void) { return "yanah_b200 0.1 (sm_100a)"; }
+
+// --------------------------------------------------------------- helpers
+static cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static QM to_qm(const yn_qmat& m) {
+  QM q;
+  q.w = reinterpret_cast<const uint8_t*>(m.weight);
+  q.s = reinterpret_cast<const uint16_t*>(m.scales);
+  q.b = reinterpret_cast<const uint16_t*>(m.biases);
+  q.rows = m.rows;
+  q.cols = m.cols;
+  q.bits = m.bits;
+  q.gs = m.group_size;
+  return q;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int check_qmat(const yn_qmat& m, int rows, int cols, int bits, const char* what) {
+  if (!m.weight || !m.scales || !m.biases) return fail(YN_E_INVALID, std::string(what) + ": null pointer");
+  if (m.rows != rows || m.cols != cols)
+    return fail(YN_E_INVALID, std::string(what) + ": shape " + std::to_string(m.rows) + "x" + std::to_string(m.cols) +
+                                  ", expected " + std::to_string(rows) + "x" + std::to_string(cols));
+  if (bits && m.bits != bits)
+    return fail(YN_E_UNSUPPORTED, std::string(what) + ": " + std::to_string(m.bits) + "-bit not supported here");
+  if (m.group_size < 16 || (m.group_size & (m.group_size - 1)) || cols % m.group_size)
+    return fail(YN_E_UNSUPPORTED, std::string(what) + ": group size " + std::to_string(m.group_size));
+  if ((cols * m.bits / 8) % 16) return fail(YN_E_UNSUPPORTED, std::string(what) + ": row bytes not a multiple of 16");
+  if (!aligned16(m.weight) || !aligned16(m.scales) || !aligned16(m.biases))
+    return fail(YN_E_INVALID, std::string(what) + ": pointers must be 16-byte aligned");
+  return YN_OK;
+}
+
+static int lanes(int rowbytes) { return lanes_per_row(rowbytes); }
+static int cpl_of(int rowbytes) { return (rowbytes / 16) / lanes(rowbytes); }
+
+// Rows per tile: the largest power of two R <= limit dividing n whose tile
+// stays under the budget, preferring R whose scale block (R * scale_row_bytes)
+// is a multiple of 16 bytes so that every piece can use the bulk engine.
+static int pick_rows(int n, int limit, size_t row_bytes, size_t scale_row_bytes) {
+  const size_t budget = 40 * 1024;
+  int best_aligned = 0, best_any = 1;
+  for (int R = 1; R <= limit && R <= n; R *= 2) {
+    if (n % R) continue;
+    if (R > 1 && (size_t)R * row_bytes > budget) break;
+    best_any = R;
+    if (((size_t)R * scale_row_bytes) % 16 == 0) best_aligned = R;
+  }
+  return best_aligned ? best_aligned : best_any;
+}
+
+// Raise the dynamic shared-memory limit of a kernel once per device (the
+// first call must come before any stream capture that launches it).
+template <typename K>
+static int set_smem(K kernel, size_t bytes) {
+  if (bytes > 227 * 1024) return fail(YN_E_UNSUPPORTED, "tile needs " + std::to_string(bytes) + " B of shared memory");
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  if (done.count(key)) return YN_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227 * 1024));
+  if (e != cudaSuccess) return fail(YN_E_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  done.insert(key);
+  return YN_OK;
+}
+
+static RecGeom rec_geom(const yn_record& r) {
+  RecGeom g;
+  for (int i = 0; i < 9; ++i) g.off[i] = r.piece_offset[i];
+  g.bytes = r.record_bytes;
+  g.bits = r.bits;
+  g.gs = r.group_size;
+  return g;
+}
+
+static int check_dims(const yn_dims* d, int T) {
+  if (!d) return fail(YN_E_INVALID, "dims is null");
+  if (T < 1 || T > YN_MAX_ROWS) return fail(YN_E_UNSUPPORTED, "rows T must be in [1, " + std::to_string(YN_MAX_ROWS) + "]");
+  if (d->hidden < 128 || d->hidden % 128) return fail(YN_E_UNSUPPORTED, "hidden must be a multiple of 128");
+  if (d->n_experts < 1 || d->n_experts > 1024) return fail(YN_E_UNSUPPORTED, "n_experts must be in [1, 1024]");
+  if (d->top_k < 1 || d->top_k > 16 || d->top_k > d->n_experts) return fail(YN_E_UNSUPPORTED, "top_k must be in [1, 16]");
+  if (d->moe_inter < 64 || d->moe_inter % 64) return fail(YN_E_UNSUPPORTED, "moe_inter must be a multiple of 64");
+  if (d->shared_inter < 0 || d->shared_inter % 64) return fail(YN_E_UNSUPPORTED, "shared_inter must be a multiple of 64");
+  int cbr = d->hidden < CB_ROWS ? d->hidden : CB_ROWS;
+  if (d->hidden % cbr) return fail(YN_E_UNSUPPORTED, "hidden must be a multiple of 256 (or below 256)");
+  return YN_OK;
+}
+
+// ------------------------------------------------------------- workspace
+extern "C" size_t yn_workspace_bytes(const yn_dims* dims) {
+  if (!dims) return 0;
+  return ws_layout(*dims).total;
+}
+
+extern "C" int yn_workspace_init(void* ws, size_t ws_bytes, const yn_dims* dims, void* stream) {
+  int rc = check_dims(dims, 1);
+  if (rc) return rc;
+  WsLayout L = ws_layout(*dims);
+  if (!ws || ws_bytes < L.total) return fail(YN_E_INVALID, "workspace too small");
+  YN_CUDA(cudaMemsetAsync(ws, 0, L.total, as_stream(stream)));
+  return YN_OK;
+}
+
+extern "C" int yn_workspace_view(void* ws, const yn_dims* dims, yn_ws_view* out) {
+  int rc = check_dims(dims, 1);
+  if (rc) return rc;
+  if (!ws || !out) return fail(YN_E_INVALID, "null workspace or view");
+  WsLayout L = ws_layout(*dims);
+  uint8_t* b = reinterpret_cast<uint8_t*>(ws);
+  out->x = b + L.x;
+  out->logits = reinterpret_cast<float*>(b + L.logits);
+  out->ids = reinterpret_cast<int32_t*>(b + L.ids);
+  out->weights = reinterpret_cast<float*>(b + L.w);
+  out->fprobs = reinterpret_cast<float*>(b + L.fprobs);
+  out->act = b + L.act;
+  out->act_sh = b + L.act_sh;
+  out->sgate = reinterpret_cast<float*>(b + L.sgate);
+  out->y = b + L.y;
+  out->y_shared = b + L.y + (size_t)YN_MAX_ROWS * dims->top_k * dims->hidden * 2;
+  out->flogits = reinterpret_cast<float*>(b + L.flogits);
+  out->error = reinterpret_cast<int32_t*>(b + L.err);
+  return YN_OK;
+}
+
+extern "C" int yn_workspace_error(void* ws, const yn_dims* dims, void* stream, int32_t* code_out) {
+  if (!ws || !dims) return fail(YN_E_INVALID, "null argument");
+  WsLayout L = ws_layout(*dims);
+  int32_t code = 0;
+  uint8_t* b = reinterpret_cast<uint8_t*>(ws);
+  YN_CUDA(cudaMemcpyAsync(&code, b + L.err, 4, cudaMemcpyDeviceToHost, as_stream(stream)));
+  YN_CUDA(cudaStreamSynchronize(as_stream(stream)));
+  if (code) YN_CUDA(cudaMemsetAsync(b + L.err, 0, 4, as_stream(stream)));
+  if (code_out) *code_out = code;
+  return code ? fail(YN_E_DEVICE, "kernel error code " + std::to_string(code)) : YN_OK;
+}
+
+// ----------------------------------------------------------- standalone
+extern "C" int yn_dequantize(const yn_qmat* m, float* out, void* stream) {
+  if (!m || !out) return fail(YN_E_INVALID, "null argument");
+  int rc = check_qmat(*m, m->rows, m->cols, 0, "yn_dequantize");
+  if (rc) return rc;
+  const size_t n = (size_t)m->rows * m->cols;
+  const int threads = 256;
+  const int blocks = (int)((n + threads - 1) / threads < 148 * 16 ? (n + threads - 1) / threads : 148 * 16);
+  auto w = reinterpret_cast<const uint32_t*>(m->weight);
+  auto s = reinterpret_cast<const uint16_t*>(m->scales);
+  auto b = reinterpret_cast<const uint16_t*>(m->biases);
+  switch (m->bits) {
+    case 2: k_dequant<2><<<blocks, threads, 0, as_stream(stream)>>>(w, s, b, m->rows, m->cols, m->group_size, out); break;
+    case 4: k_dequant<4><<<blocks, threads, 0, as_stream(stream)>>>(w, s, b, m->rows, m->cols, m->group_size, out); break;
+    case 8: k_dequant<8><<<blocks, threads, 0, as_stream(stream)>>>(w, s, b, m->rows, m->cols, m->group_size, out); break;
+    default: return fail(YN_E_UNSUPPORTED, "bits must be 2, 4 or 8");
+  }
+  YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_qlinear(const yn_qmat* m, const void* x, int32_t T, float* y, void* stream) {
+  if (!m || !x || !y) return fail(YN_E_INVALID, "null argument");
+  if (T < 1 || T > YN_MAX_ROWS) return fail(YN_E_UNSUPPORTED, "T out of range");
+  int rc = check_qmat(*m, m->rows, m->cols, 8, "yn_qlinear");
+  if (rc) return rc;
+  const int rb = m->cols;
+  const int lpr = lanes(rb), rpi = 32 / lpr, cpl = cpl_of(rb);
+  const int rows_per_cta = 4 * rpi;
+  const int grid = (m->rows + rows_per_cta - 1) / rows_per_cta;
+  const size_t smem = (size_t)T * m->cols * 2;
+  QM q = to_qm(*m);
+  auto xx = reinterpret_cast<const uint16_t*>(x);
+  switch (cpl) {
+#define QL(C)                                                                       \
+  case C:                                                                           \
+    if ((rc = set_smem(k_qlinear8<C>, smem))) return rc;                            \
+    k_qlinear8<C><<<grid, THREADS, smem, as_stream(stream)>>>(q, xx, T, y);         \
+    break;
+    QL(1) QL(2) QL(3) QL(4) QL(8)
+#undef QL
+    default: return fail(YN_E_UNSUPPORTED, "row length not supported");
+  }
+  YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_route(const float* logits, int32_t T, const yn_dims* dims, int32_t* ids, float* weights,
+                        void* stream) {
+  if (!logits || !dims || !ids || !weights) return fail(YN_E_INVALID, "null argument");
+  if (dims->n_experts < 1 || dims->n_experts > 1024) return fail(YN_E_UNSUPPORTED, "n_experts must be in [1, 1024]");
+  if (dims->top_k < 1 || dims->top_k > 16 || dims->top_k > dims->n_experts) return fail(YN_E_UNSUPPORTED, "top_k out of range");
+  if (T < 1) return fail(YN_E_INVALID, "T must be >= 1");
+  const int warps = 4;
+  k_route<<<(T + warps - 1) / warps, warps * 32, 0, as_stream(stream)>>>(logits, T, dims->n_experts, dims->top_k,
+                                                                           dims->norm_topk, ids, weights);
+  YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+// -------------------------------------------------------- layer kernels
+static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void* h1, int T, const yn_layer* tg,
+                                 int NT, uint8_t* ws, const WsLayout& W, cudaStream_t st) {
+  int rc;
+  const int H = d.hidden, E = d.n_experts;
+  if (!h1 || !L.post_norm) return fail(YN_E_INVALID, "post_attention: null input or norm");
+  if ((rc = check_qmat(L.router, E, H, 8, "router"))) return rc;
+  const bool sh = d.shared_inter > 0;
+  if (sh) {
+    if ((rc = check_qmat(L.shared_gate, d.shared_inter, H, 8, "shared_gate"))) return rc;
+    if ((rc = check_qmat(L.shared_up, d.shared_inter, H, 8, "shared_up"))) return rc;
+    if ((rc = check_qmat(L.shared_expert_gate, 1, H, 8, "shared_expert_gate"))) return rc;
+  }
+  if (NT < 0 || NT > YN_MAX_TARGETS) return fail(YN_E_UNSUPPORTED, "at most 2 lookahead targets");
+  PostAttnArgs a{};
+  a.T = T; a.H = H; a.E = E; a.K = d.top_k; a.Ish = d.shared_inter; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
+  a.h1 = reinterpret_cast<const uint16_t*>(h1);
+  a.norm = reinterpret_cast<const uint16_t*>(L.post_norm);
+  a.router = to_qm(L.router);
+  a.rbias = L.router_bias;
+  a.has_shared = sh;
+  if (sh) {
+    a.sh_gate = to_qm(L.shared_gate);
+    a.sh_up = to_qm(L.shared_up);
+    a.sg = to_qm(L.shared_expert_gate);
+  }
+  a.n_targets = NT;
+  for (int g = 0; g < NT; ++g) {
+    if ((rc = check_qmat(tg[g].router, E, H, 8, "target router"))) return rc;
+    if (!tg[g].post_norm) return fail(YN_E_INVALID, "target norm is null");
+    a.tnorm[g] = reinterpret_cast<const uint16_t*>(tg[g].post_norm);
+    a.trouter[g] = to_qm(tg[g].router);
+    a.tbias[g] = tg[g].router_bias;
+  }
+  const size_t rowb = (size_t)H + 2 * (size_t)(H / L.router.group_size) * 2;
+  const size_t srow = (size_t)(H / L.router.group_size) * 2;
+  a.r_router = pick_rows(E, 64, rowb, srow);
+  a.nt_router = E / a.r_router;
+  if (sh) {
+    const size_t srow_s = (size_t)(H / L.shared_gate.group_size) * 2;
+    a.r_shared = pick_rows(d.shared_inter, 64, 2 * ((size_t)H + 2 * srow_s), srow_s);
+    a.nt_shared = d.shared_inter / a.r_shared;
+    a.nt_sg = 1;
+  }
+  a.r_target = a.r_router;
+  a.nt_target = NT ? E / a.r_target : 0;
+  a.n_tiles = a.nt_router + a.nt_shared + a.nt_sg + NT * a.nt_target;
+  auto part = [](size_t R, size_t rb, size_t sb) { return (R * rb + 15) / 16 * 16 + 2 * ((R * sb + 15) / 16 * 16); };
+  size_t tile = part(a.r_router, H, srow);
+  if (sh) {
+    const size_t srow_s = (size_t)(H / L.shared_gate.group_size) * 2;
+    const size_t ts = 2 * part(a.r_shared, H, srow_s);
+    const size_t tsg = part(1, H, (size_t)(H / L.shared_expert_gate.group_size) * 2);
+    if (ts > tile) tile = ts;
+    if (tsg > tile) tile = tsg;
+  }
+  for (int g = 0; g < NT; ++g) {
+    const size_t tt = part(a.r_target, H, (size_t)(H / tg[g].router.group_size) * 2);
+    if (tt > tile) tile = tt;
+  }
+  a.tile_bytes = tile;
+  a.x = reinterpret_cast<uint16_t*>(ws + W.x);
+  a.logits = reinterpret_cast<float*>(ws + W.logits);
+  a.act_sh = reinterpret_cast<uint16_t*>(ws + W.act_sh);
+  a.sgate = reinterpret_cast<float*>(ws + W.sgate);
+  a.ids = reinterpret_cast<int32_t*>(ws + W.ids);
+  a.wts = reinterpret_cast<float*>(ws + W.w);
+  a.flogits = reinterpret_cast<float*>(ws + W.flogits);
+  a.fprobs = reinterpret_cast<float*>(ws + W.fprobs);
+  a.counter = reinterpret_cast<int*>(ws + W.counters);
+  a.err = reinterpret_cast<int*>(ws + W.err);
+  const size_t smem = 256 + ((size_t)T * H * 2 + 15) / 16 * 16 + tile;
+  const int cpl = cpl_of(H);
+  switch (cpl) {
+#define PA(C)                                                                        \
+  case C:                                                                            \
+    if ((rc = set_smem(k_post_attention<C>, smem))) return rc;                       \
+    k_post_attention<C><<<a.n_tiles, THREADS, smem, st>>>(a);                        \
+    break;
+    PA(1) PA(2) PA(3) PA(4) PA(8)
+#undef PA
+    default: return fail(YN_E_UNSUPPORTED, "hidden size not supported by the router kernel");
+  }
+  YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+static int check_layer_experts(const yn_dims& d, const yn_layer& L) {
+  const yn_record& r = L.record;
+  if (!L.expert_base) return fail(YN_E_INVALID, "expert_base is null");
+  if (r.bits != 2 && r.bits != 4) return fail(YN_E_UNSUPPORTED, "routed experts must be 2- or 4-bit");
+  if (r.group_size != 32 && r.group_size != 64 && r.group_size != 128)
+    return fail(YN_E_UNSUPPORTED, "routed expert group size must be 32, 64 or 128");
+  if (d.hidden % r.group_size || d.moe_inter % r.group_size) return fail(YN_E_INVALID, "group size must divide H and I");
+  if (!aligned16(L.expert_base) || L.slot_stride % 16) return fail(YN_E_INVALID, "slot arena must be 16-byte aligned");
+  for (int i = 0; i < 9; ++i)
+    if (r.piece_offset[i] % 16) return fail(YN_E_INVALID, "record piece offsets must be multiples of 16");
+  if (L.n_slots < 1) return fail(YN_E_INVALID, "n_slots must be >= 1");
+  if (!L.expert_slot && L.n_slots < d.n_experts) return fail(YN_E_INVALID, "identity slot map needs n_slots >= n_experts");
+  return YN_OK;
+}
+
+static int launch_expert_up(const yn_dims& d, const yn_layer& L, const void* x, const int32_t* ids, int T,
+                            const int32_t* cols, int ncols, uint8_t* ws, const WsLayout& W, cudaStream_t st) {
+  int rc;
+  if ((rc = check_layer_experts(d, L))) return rc;
+  ExpertUpArgs a{};
+  a.T = T; a.H = d.hidden; a.I = d.moe_inter; a.K = d.top_k; a.E = d.n_experts; a.n_slots = L.n_slots;
+  a.x = reinterpret_cast<const uint16_t*>(x ? x : ws + W.x);
+  a.ids = ids ? ids : reinterpret_cast<const int32_t*>(ws + W.ids);
+  a.slot_of = L.expert_slot;
+  a.base = reinterpret_cast<const uint8_t*>(L.expert_base);
+  a.stride = L.slot_stride;
+  a.rg = rec_geom(L.record);
+  if (!cols) ncols = d.top_k;
+  if (ncols < 0 || ncols > 16) return fail(YN_E_INVALID, "n_cols must be in [0, 16]");
+  if (ncols == 0) return YN_OK;
+  a.ncols = ncols;
+  for (int i = 0; i < ncols; ++i) {
+    a.cols[i] = cols ? cols[i] : i;
+    if (a.cols[i] < 0 || a.cols[i] >= d.top_k) return fail(YN_E_INVALID, "column index out of range");
+  }
+  const int bits = L.record.bits, gs = L.record.group_size;
+  const int rb = d.hidden * bits / 8;
+  const size_t srow = (size_t)(d.hidden / gs) * 2;
+  a.rows = pick_rows(d.moe_inter, 64, 2 * ((size_t)rb + 2 * srow), srow);
+  a.tiles_per_task = d.moe_inter / a.rows;
+  a.act = reinterpret_cast<uint16_t*>(ws + W.act);
+  a.err = reinterpret_cast<int*>(ws + W.err);
+  const size_t tile = 2 * ((((size_t)a.rows * rb + 15) / 16 * 16) + 2 * (((size_t)a.rows * srow + 15) / 16 * 16));
+  const size_t smem = 256 + ((size_t)d.hidden * 2 + 15) / 16 * 16 + tile;
+  const int grid = T * ncols * a.tiles_per_task;
+  const int cpl = cpl_of(rb);
+  const int nseg = (bits == 2 && gs == 32) ? 2 : 1;
+  bool done = false;
+#define EU(B, C, S)                                                              \
+  if (!done && bits == B && cpl == C && nseg == S) {                             \
+    if ((rc = set_smem(k_expert_up<B, C, S>, smem))) return rc;                  \
+    k_expert_up<B, C, S><<<grid, THREADS, smem, st>>>(a);                        \
+    done = true;                                                                 \
+  }
+  EU(4, 1, 1) EU(4, 2, 1) EU(4, 3, 1) EU(4, 4, 1)
+  EU(2, 1, 1) EU(2, 2, 1) EU(2, 3, 1) EU(2, 1, 2) EU(2, 2, 2) EU(2, 3, 2)
+#undef EU
+  if (!done) return fail(YN_E_UNSUPPORTED, "expert up: no kernel for this bit width / hidden size");
+  YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+static int launch_expert_down(const yn_dims& d, const yn_layer& L, const int32_t* ids, const float* wts, int T,
+                              const void* h_res, int mode, void* out, uint8_t* ws, const WsLayout& W,
+                              cudaStream_t st) {
+  int rc;
+  if ((rc = check_layer_experts(d, L))) return rc;
+  if (!out) return fail(YN_E_INVALID, "out is null");
+  if (mode < 0 || mode > 2) return fail(YN_E_INVALID, "mode must be 0, 1 or 2");
+  if (mode == 2 && !h_res) return fail(YN_E_INVALID, "mode 2 needs h_res");
+  const bool sh = (mode >= 1) && d.shared_inter > 0;
+  if (sh && (rc = check_qmat(L.shared_down, d.hidden, d.shared_inter, 8, "shared_down"))) return rc;
+  ExpertDownArgs a{};
+  a.T = T; a.H = d.hidden; a.I = d.moe_inter; a.K = d.top_k; a.E = d.n_experts; a.n_slots = L.n_slots;
+  a.Ish = sh ? d.shared_inter : 0;
+  a.has_shared = sh;
+  a.mode = mode;
+  a.act = reinterpret_cast<const uint16_t*>(ws + W.act);
+  a.ids = ids ? ids : reinterpret_cast<const int32_t*>(ws + W.ids);
+  a.wts = wts ? wts : reinterpret_cast<const float*>(ws + W.w);
+  a.slot_of = L.expert_slot;
+  a.base = reinterpret_cast<const uint8_t*>(L.expert_base);
+  a.stride = L.slot_stride;
+  a.rg = rec_geom(L.record);
+  if (sh) a.sh_down = to_qm(L.shared_down);
+  a.act_sh = reinterpret_cast<const uint16_t*>(ws + W.act_sh);
+  a.sgate = reinterpret_cast<const float*>(ws + W.sgate);
+  a.h_res = reinterpret_cast<const uint16_t*>(h_res);
+  a.y = reinterpret_cast<uint16_t*>(ws + W.y);
+  a.ysh = a.y + (size_t)YN_MAX_ROWS * d.top_k * d.hidden;
+  a.out = reinterpret_cast<uint16_t*>(out);
+  a.counters = reinterpret_cast<int*>(ws + W.counters) + 1;
+  a.n_cb = W.n_cb;
+  a.err = reinterpret_cast<int*>(ws + W.err);
+  const int bits = L.record.bits, gs = L.record.group_size;
+  const int cbr = d.hidden < CB_ROWS ? d.hidden : CB_ROWS;
+  const int rb = d.moe_inter * bits / 8;
+  const size_t srow = (size_t)(d.moe_inter / gs) * 2;
+  a.rows_routed = pick_rows(cbr, cbr, (size_t)rb + 2 * srow, srow);
+  a.tiles_routed_per_task = d.hidden / a.rows_routed;
+  a.n_routed_tiles = T * d.top_k * a.tiles_routed_per_task;
+  size_t tile = ((size_t)a.rows_routed * rb + 15) / 16 * 16 + 2 * (((size_t)a.rows_routed * srow + 15) / 16 * 16);
+  int cpls = 1;
+  if (sh) {
+    const size_t srow_s = (size_t)(d.shared_inter / L.shared_down.group_size) * 2;
+    a.rows_shared = pick_rows(cbr, cbr, (size_t)d.shared_inter + 2 * srow_s, srow_s);
+    a.tiles_shared_per_token = d.hidden / a.rows_shared;
+    const size_t ts = ((size_t)a.rows_shared * d.shared_inter + 15) / 16 * 16 + 2 * (((size_t)a.rows_shared * srow_s + 15) / 16 * 16);
+    if (ts > tile) tile = ts;
+    cpls = cpl_of(d.shared_inter);
+  } else {
+    a.rows_shared = 1;
+  }
+  const int kx = d.moe_inter > d.shared_inter ? d.moe_inter : d.shared_inter;
+  const size_t smem = 256 + ((size_t)kx * 2 + 15) / 16 * 16 + tile;
+  const int grid = a.n_routed_tiles + (sh ? T * a.tiles_shared_per_token : 0);
+  const int cpl = cpl_of(rb);
+  const int nseg = (bits == 2 && gs == 32) ? 2 : 1;
+  bool done = false;
+#define ED(B, C, S, CS)                                                          \
+  if (!done && bits == B && cpl == C && nseg == S && cpls == CS) {               \
+    if ((rc = set_smem(k_expert_down<B, C, S, CS>, smem))) return rc;            \
+    k_expert_down<B, C, S, CS><<<grid, THREADS, smem, st>>>(a);                  \
+    done = true;                                                                 \
+  }
+  ED(4, 1, 1, 1) ED(4, 2, 1, 1) ED(4, 3, 1, 1) ED(4, 1, 1, 2) ED(4, 2, 1, 2) ED(4, 3, 1, 2)
+  ED(2, 1, 1, 1) ED(2, 2, 1, 1) ED(2, 3, 1, 1) ED(2, 1, 1, 2) ED(2, 3, 1, 2)
+  ED(2, 1, 2, 1) ED(2, 3, 2, 1) ED(2, 1, 2, 2)
+#undef ED
+  if (!done) return fail(YN_E_UNSUPPORTED, "expert down: no kernel for this bit width / intermediate size");
+  YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_post_attention(const yn_dims* dims, const yn_layer* layer, const void* h1, int32_t T,
+                                 const yn_layer* targets, int32_t n_targets, void* ws, void* stream) {
+  int rc = check_dims(dims, T);
+  if (rc) return rc;
+  if (!layer || !ws) return fail(YN_E_INVALID, "null layer or workspace");
+  if (n_targets && !targets) return fail(YN_E_INVALID, "targets is null");
+  WsLayout W = ws_layout(*dims);
+  return launch_post_attention(*dims, *layer, h1, T, targets, n_targets, reinterpret_cast<uint8_t*>(ws), W,
+                               as_stream(stream));
+}
+
+extern "C" int yn_moe_up(const yn_dims* dims, const yn_layer* layer, const void* x, const int32_t* ids, int32_t T,
+                         const int32_t* cols, int32_t n_cols, void* ws, void* stream) {
+  int rc = check_dims(dims, T);
+  if (rc) return rc;
+  if (!layer || !ws) return fail(YN_E_INVALID, "null layer or workspace");
+  WsLayout W = ws_layout(*dims);
+  return launch_expert_up(*dims, *layer, x, ids, T, cols, n_cols, reinterpret_cast<uint8_t*>(ws), W,
+                          as_stream(stream));
+}
+
+extern "C" int yn_moe_down(const yn_dims* dims, const yn_layer* layer, const int32_t* ids, const float* weights,
+                           int32_t T, const void* h_res, int32_t mode, void* out, void* ws, void* stream) {
+  int rc = check_dims(dims, T);
+  if (rc) return rc;
+  if (!layer || !ws) return fail(YN_E_INVALID, "null layer or workspace");
+  WsLayout W = ws_layout(*dims);
+  return launch_expert_down(*dims, *layer, ids, weights, T, h_res, mode, out, reinterpret_cast<uint8_t*>(ws), W,
+                            as_stream(stream));
+}
+
+extern "C" int yn_moe_layer(const yn_dims* dims, const yn_layer* layer, const void* h_in, int32_t T,
+                            const yn_layer* targets, int32_t n_targets, void* h_out, void* ws, void* stream) {
+  int rc = check_dims(dims, T);
+  if (rc) return rc;
+  if (!layer || !ws || !h_in || !h_out) return fail(YN_E_INVALID, "null argument");
+  if (h_in == h_out) return fail(YN_E_INVALID, "h_in and h_out must not alias");
+  WsLayout W = ws_layout(*dims);
+  uint8_t* b = reinterpret_cast<uint8_t*>(ws);
+  cudaStream_t st = as_stream(stream);
+  if ((rc = launch_post_attention(*dims, *layer, h_in, T, targets, n_targets, b, W, st))) return rc;
+  if ((rc = launch_expert_up(*dims, *layer, nullptr, nullptr, T, nullptr, 0, b, W, st))) return rc;
+  return launch_expert_down(*dims, *layer, nullptr, nullptr, T, h_in, 2, h_out, b, W, st);
+}
+
+// ------------------------------------------------------------ slot copy
+extern "C" int yn_slot_copy(void* arena, int64_t slot_stride, const int32_t* slots, const void* const* host_src,
+                            int32_t n, int64_t record_bytes, void* stream) {
+  if (n < 0) return fail(YN_E_INVALID, "n < 0");
+  if (n && (!arena || !slots || !host_src)) return fail(YN_E_INVALID, "null argument");
+  if (record_bytes > slot_stride) return fail(YN_E_INVALID, "record larger than a slot");
+  for (int i = 0; i < n; ++i) {
+    if (slots[i] < 0) return fail(YN_E_INVALID, "negative slot index");
+    uint8_t* dst = reinterpret_cast<uint8_t*>(arena) + (size_t)slots[i] * (size_t)slot_stride;
+    YN_CUDA(cudaMemcpyAsync(dst, host_src[i], (size_t)record_bytes, cudaMemcpyHostToDevice, as_stream(stream)));
+  }
+  return YN_OK;
+}
