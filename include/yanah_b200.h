@@ -163,6 +163,25 @@ int yn_moe_down(const yn_dims* dims, const yn_layer* layer, const int32_t* ids, 
 int yn_moe_layer(const yn_dims* dims, const yn_layer* layer, const void* h_in, int32_t T,
                  const yn_layer* targets, int32_t n_targets, void* h_out, void* ws, void* stream);
 
+/* ------------------------------------------------ whole-stack bs1 decode */
+
+/* Persistent decode of `n_tokens` sequential bs1 tokens through `n_layers`
+ * resident MoE layers (orchestrator.py:308-343 with every expert resident):
+ * one cooperative launch, one CTA per SM, three grid barriers per layer.
+ * Prepare once: yn_stack_prepare copies the layer descriptors into a device
+ * table of yn_stack_table_bytes(n_layers) bytes. layer_bits: host array of
+ * each layer's routed-expert bit width. inputs/outputs: (n_tokens, H) bf16.
+ * trace_ids: (n_tokens, n_layers, k) routed ids or NULL. timing: (n_layers,
+ * 8) int64 nanosecond stamps of token 0 or NULL. */
+size_t yn_stack_table_bytes(int32_t n_layers);
+size_t yn_stack_scratch_bytes(const yn_dims* dims);
+int yn_stack_prepare(const yn_dims* dims, const yn_layer* layers, int32_t n_layers, void* table, size_t table_bytes);
+int yn_stack_decode(const yn_dims* dims, const void* table, int32_t n_layers, const int32_t* layer_bits,
+                    const void* inputs, int32_t n_tokens, void* outputs, void* scratch, size_t scratch_bytes,
+                    int32_t* trace_ids, int64_t* timing, void* stream);
+/* Read and clear the stack decode error word (synchronises the stream). */
+int yn_stack_error(void* scratch, const yn_dims* dims, void* stream, int32_t* code_out);
+
 /* ---------------------------------------------------------- slot copies */
 
 /* Copy `n` expert records host -> slot arena (io_lanes.py:121-126
@@ -184,6 +203,16 @@ int yn_synth_f16(void* dst, int64_t n, uint64_t seed, uint64_t stream_id, float 
 /* Same for bf16 outputs. */
 int yn_synth_bf16(void* dst, int64_t n, uint64_t seed, uint64_t stream_id, float std, float mean,
                   void* stream);
+
+/* Record a CUDA timing event (cudaEvent_t as void*) on `stream`. While the
+ * stream is being captured into a CUDA graph the record is captured as an
+ * external event node, so kernel durations can be read per graph replay.
+ * Benchmark instrumentation; no counterpart in the reference. */
+int yn_record_event(void* event, void* stream);
+/* Create / destroy a timing event; elapsed milliseconds between two records. */
+int yn_event_create(void** event);
+int yn_event_destroy(void* event);
+int yn_event_elapsed_ms(void* start, void* end, float* ms);
 
 /* Library version string. */
 const char* yn_version(void);

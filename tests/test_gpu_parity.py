@@ -166,3 +166,27 @@ def test_stack_teacher_forced_routing():
         assert rel_l2(bf16_np(hout), ref["out"]) < REL_L2_TOL, l
         h = hout
     assert dm.ws.check_error() == 0
+
+
+def test_persistent_decode_matches_layer_kernels():
+    """The persistent whole-stack kernel gives bit-identical outputs and routing
+    to the per-layer kernels, token after token (4 layers: 4,2,2,4-bit)."""
+    from yanah_b200.stack import ResidentStack
+    cfg = small_config(bits=(4, 2, 2, 4), hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=4)
+    st = ResidentStack(cfg, "cuda")
+    N = 3
+    x = bf16_dev(hidden_rows(cfg, N, stream=2))
+    ref = torch.empty_like(x)
+    st.run(x, ref)
+    got = torch.empty_like(x)
+    trace = torch.full((N, cfg.n_layers, cfg.top_k), -1, dtype=torch.int32, device="cuda")
+    st.decode(x, got, trace=trace)
+    torch.cuda.synchronize()
+    assert st.decode_error() == 0
+    assert np.array_equal(bf16_np(got), bf16_np(ref))
+    # layer 0 routing of every token equals the oracle's on the same input
+    o = cpu.OracleStack(cfg)
+    for t in range(N):
+        r = o.post_attention(0, bf16_np(x[t:t + 1]))
+        assert np.array_equal(trace[t, 0].cpu().numpy(), r["ids"][0]), t
+    assert (trace >= 0).all()

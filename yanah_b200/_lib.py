@@ -67,7 +67,17 @@ _SIGS = {
     "yn_moe_up": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _P, _I, C.POINTER(C.c_int32), _I, _P, _P]),
     "yn_moe_down": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _P, _I, _P, _I, _P, _P, _P]),
     "yn_moe_layer": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _I, C.POINTER(Layer), _I, _P, _P, _P]),
+    "yn_stack_table_bytes": (C.c_size_t, [_I]),
+    "yn_stack_scratch_bytes": (C.c_size_t, [C.POINTER(Dims)]),
+    "yn_stack_prepare": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _I, _P, C.c_size_t]),
+    "yn_stack_decode": (C.c_int, [C.POINTER(Dims), _P, _I, C.POINTER(C.c_int32), _P, _I, _P, _P, C.c_size_t, _P, _P,
+                                  _P]),
+    "yn_stack_error": (C.c_int, [_P, C.POINTER(Dims), _P, C.POINTER(C.c_int32)]),
     "yn_slot_copy": (C.c_int, [_P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_void_p), _I, C.c_int64, _P]),
+    "yn_record_event": (C.c_int, [_P, _P]),
+    "yn_event_create": (C.c_int, [C.POINTER(C.c_void_p)]),
+    "yn_event_destroy": (C.c_int, [_P]),
+    "yn_event_elapsed_ms": (C.c_int, [_P, _P, C.POINTER(C.c_float)]),
     "yn_synth_u32": (C.c_int, [_P, C.c_int64, C.c_uint64, C.c_uint64, _P]),
     "yn_synth_f16": (C.c_int, [_P, C.c_int64, C.c_uint64, C.c_uint64, C.c_float, _I, _P]),
     "yn_synth_bf16": (C.c_int, [_P, C.c_int64, C.c_uint64, C.c_uint64, C.c_float, C.c_float, _P]),

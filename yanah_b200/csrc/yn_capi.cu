@@ -13,11 +13,14 @@
 #include <set>
 #include <string>
 #include <utility>
+#include <vector>
+#include <algorithm>
 
 #include "yn_common.cuh"
 #include "yn_moe.cuh"
 #include "yn_qdot.cuh"
 #include "yn_kernels.cuh"
+#include "yn_decode.cuh"
 
 
 using namespace ynb;
@@ -90,14 +93,18 @@ static int pick_rows(int n, int limit, size_t row_bytes, size_t scale_row_bytes)
 // Raise the dynamic shared-memory limit of a kernel once per device (the
 // first call must come before any stream capture that launches it).
 template <typename K>
-static int set_smem(K kernel, size_t bytes) {
+static int set_smem(K kernel, size_t bytes);
+static int set_smem_ptr(const void* kernel, size_t bytes);
+template <typename K>
+static int set_smem(K kernel, size_t bytes) { return set_smem_ptr(reinterpret_cast<const void*>(kernel), bytes); }
+static int set_smem_ptr(const void* kernel, size_t bytes) {
   if (bytes > 227 * 1024) return fail(YN_E_UNSUPPORTED, "tile needs " + std::to_string(bytes) + " B of shared memory");
   static std::mutex mu;
   static std::set<std::pair<const void*, int>> done;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
-  auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  auto key = std::make_pair(kernel, dev);
   if (done.count(key)) return YN_OK;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227 * 1024));
   if (e != cudaSuccess) return fail(YN_E_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
@@ -306,7 +313,8 @@ static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void
   a.fprobs = reinterpret_cast<float*>(ws + W.fprobs);
   a.counter = reinterpret_cast<int*>(ws + W.counters);
   a.err = reinterpret_cast<int*>(ws + W.err);
-  const size_t smem = 256 + ((size_t)T * H * 2 + 15) / 16 * 16 + tile;
+  const size_t rows_b = ((size_t)T * H * 2 + 15) / 16 * 16;
+  const size_t smem = 256 + 2 * rows_b + ((size_t)H * 2 + 15) / 16 * 16 + tile;
   const int cpl = cpl_of(H);
   switch (cpl) {
 #define PA(C)                                                                        \
@@ -513,4 +521,221 @@ extern "C" int yn_slot_copy(void* arena, int64_t slot_stride, const int32_t* slo
     YN_CUDA(cudaMemcpyAsync(dst, host_src[i], (size_t)record_bytes, cudaMemcpyHostToDevice, as_stream(stream)));
   }
   return YN_OK;
+}
+
+// ---------------------------------------------------------------- timing
+// Record a timing event on `stream`; inside a stream capture the record
+// becomes an external event node, so per-kernel durations can be read after
+// each replay of the graph.
+extern "C" int yn_record_event(void* event, void* stream) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  YN_CUDA(cudaStreamIsCapturing(as_stream(stream), &cs));
+  if (cs == cudaStreamCaptureStatusActive)
+    YN_CUDA(cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(event), as_stream(stream), cudaEventRecordExternal));
+  else
+    YN_CUDA(cudaEventRecord(reinterpret_cast<cudaEvent_t>(event), as_stream(stream)));
+  return YN_OK;
+}
+
+extern "C" int yn_event_create(void** event) {
+  if (!event) return fail(YN_E_INVALID, "null argument");
+  cudaEvent_t e;
+  YN_CUDA(cudaEventCreate(&e));
+  *event = reinterpret_cast<void*>(e);
+  return YN_OK;
+}
+extern "C" int yn_event_destroy(void* event) {
+  YN_CUDA(cudaEventDestroy(reinterpret_cast<cudaEvent_t>(event)));
+  return YN_OK;
+}
+extern "C" int yn_event_elapsed_ms(void* start, void* end, float* ms) {
+  if (!ms) return fail(YN_E_INVALID, "null argument");
+  YN_CUDA(cudaEventElapsedTime(ms, reinterpret_cast<cudaEvent_t>(start), reinterpret_cast<cudaEvent_t>(end)));
+  return YN_OK;
+}
+
+// ------------------------------------------------- persistent stack decode
+static size_t a16h(size_t v) { return (v + 15) / 16 * 16; }
+
+extern "C" size_t yn_stack_table_bytes(int32_t n_layers) { return (size_t)(n_layers > 0 ? n_layers : 0) * sizeof(DecLayer); }
+
+struct StackScratch {
+  size_t hbuf, logits, act, act_sh, sgate, bar, err, total;
+};
+static StackScratch stack_scratch(const yn_dims& d) {
+  StackScratch S{};
+  size_t o = 0;
+  auto take = [&](size_t b) { size_t at = o; o = (o + b + 255) / 256 * 256; return at; };
+  S.err = take(4);
+  S.bar = take(4);
+  S.hbuf = take(2 * (size_t)d.hidden * 2);
+  S.logits = take((size_t)d.n_experts * 4);
+  S.act = take((size_t)d.top_k * d.moe_inter * 2);
+  S.act_sh = take((size_t)(d.shared_inter ? d.shared_inter : 8) * 2);
+  S.sgate = take(4);
+  S.total = o;
+  return S;
+}
+extern "C" size_t yn_stack_scratch_bytes(const yn_dims* dims) { return dims ? stack_scratch(*dims).total : 0; }
+
+extern "C" int yn_stack_prepare(const yn_dims* dims, const yn_layer* layers, int32_t n_layers, void* table,
+                                size_t table_bytes) {
+  int rc = check_dims(dims, 1);
+  if (rc) return rc;
+  if (!layers || n_layers < 1 || !table) return fail(YN_E_INVALID, "null layers/table or n_layers < 1");
+  if (table_bytes < yn_stack_table_bytes(n_layers)) return fail(YN_E_INVALID, "layer table too small");
+  std::vector<DecLayer> t(n_layers);
+  for (int l = 0; l < n_layers; ++l) {
+    const yn_layer& L = layers[l];
+    if ((rc = check_qmat(L.router, dims->n_experts, dims->hidden, 8, "router"))) return rc;
+    if (dims->shared_inter) {
+      if ((rc = check_qmat(L.shared_gate, dims->shared_inter, dims->hidden, 8, "shared_gate"))) return rc;
+      if ((rc = check_qmat(L.shared_up, dims->shared_inter, dims->hidden, 8, "shared_up"))) return rc;
+      if ((rc = check_qmat(L.shared_down, dims->hidden, dims->shared_inter, 8, "shared_down"))) return rc;
+      if ((rc = check_qmat(L.shared_expert_gate, 1, dims->hidden, 8, "shared_expert_gate"))) return rc;
+    }
+    if ((rc = check_layer_experts(*dims, L))) return rc;
+    if (!L.post_norm) return fail(YN_E_INVALID, "post_norm is null");
+    DecLayer& D = t[l];
+    memset(&D, 0, sizeof(D));
+    D.norm = reinterpret_cast<const uint16_t*>(L.post_norm);
+    D.router = to_qm(L.router);
+    D.rbias = L.router_bias;
+    if (dims->shared_inter) {
+      D.sg = to_qm(L.shared_gate);
+      D.su = to_qm(L.shared_up);
+      D.sd = to_qm(L.shared_down);
+      D.sgt = to_qm(L.shared_expert_gate);
+    }
+    D.ebase = reinterpret_cast<const uint8_t*>(L.expert_base);
+    D.stride = L.slot_stride;
+    D.slot_of = L.expert_slot;
+    D.n_slots = L.n_slots;
+    D.rg = rec_geom(L.record);
+  }
+  YN_CUDA(cudaMemcpy(table, t.data(), t.size() * sizeof(DecLayer), cudaMemcpyHostToDevice));
+  return YN_OK;
+}
+
+// Host mirror of the device P1 partition, for buffer sizing.
+static size_t p1_tile_bytes_max(const yn_dims& d, int G, int gs_r, int gs_s) {
+  size_t best = 0;
+  const int E = d.n_experts, Ish = d.shared_inter, H = d.hidden;
+  auto unit_at = [&](int c) {
+    if (c <= E) return c;
+    if (c <= E + 2 * Ish) return E + (c - E + 1) / 2;
+    return E + Ish + (c - E - 2 * Ish);
+  };
+  const int C = E + 2 * Ish + (Ish ? 1 : 0);
+  for (int b = 0; b < G; ++b) {
+    const int lo = (int)((long long)b * C / G), hi = (int)((long long)(b + 1) * C / G);
+    const int u0 = unit_at(lo), u1 = unit_at(hi);
+    const size_t nr = std::min(u1, E) - std::min(u0, E);
+    const size_t np = std::min(std::max(u1 - E, 0), Ish) - std::min(std::max(u0 - E, 0), Ish);
+    const int sg = (Ish > 0 && u0 <= E + Ish && u1 > E + Ish) ? 1 : 0;
+    const size_t sbr = (size_t)(H / gs_r) * 2, sbs = (size_t)(H / gs_s) * 2;
+    size_t o = a16h(nr * H) + 2 * a16h(nr * sbr) + 2 * (a16h(np * H) + 2 * a16h(np * sbs)) +
+               (sg ? a16h(H) + 2 * a16h(sbs) : 0);
+    best = std::max(best, o);
+  }
+  return best;
+}
+
+extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, int32_t n_layers, const int32_t* layer_bits,
+                               const void* inputs, int32_t n_tokens, void* outputs, void* scratch,
+                               size_t scratch_bytes, int32_t* trace_ids, int64_t* timing, void* stream) {
+  int rc = check_dims(dims, 1);
+  if (rc) return rc;
+  const yn_dims& d = *dims;
+  if (!table || !inputs || !outputs || !scratch || !layer_bits) return fail(YN_E_INVALID, "null argument");
+  if (n_layers < 1 || n_tokens < 1) return fail(YN_E_INVALID, "n_layers and n_tokens must be >= 1");
+  StackScratch S = stack_scratch(d);
+  if (scratch_bytes < S.total) return fail(YN_E_INVALID, "scratch too small");
+  if (d.top_k > DEC_MAX_K || d.n_experts % 4) return fail(YN_E_UNSUPPORTED, "top_k <= 16 and n_experts % 4 == 0 required");
+  // The persistent kernel is instantiated for rows whose lane mapping matches
+  // H = 2048-class rows (8-bit router CPL from H, routed gate/up CPL 2 at 4-bit
+  // and 1 at 2-bit, down rows CPL 1).
+  const int cpl8 = cpl_of(d.hidden), cpls = d.shared_inter ? cpl_of(d.shared_inter) : 1;
+  bool any4 = false;
+  for (int l = 0; l < n_layers; ++l) {
+    const int b = layer_bits[l];
+    if (b != 2 && b != 4) return fail(YN_E_UNSUPPORTED, "stack decode: experts must be 2- or 4-bit");
+    if (cpl_of(d.hidden * b / 8) != (b == 4 ? 2 : 1) || cpl_of(d.moe_inter * b / 8) != 1)
+      return fail(YN_E_UNSUPPORTED, "stack decode: hidden/moe_inter outside the compiled row mapping");
+    any4 |= (b == 4);
+  }
+  int dev = 0, sms = 0;
+  YN_CUDA(cudaGetDevice(&dev));
+  YN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int G = sms;
+  const int nd_max = (d.hidden + G - 1) / G;
+  if (nd_max > DEC_MAX_DROWS) return fail(YN_E_UNSUPPORTED, "hidden too large for the per-CTA row block");
+  // shared-memory carve
+  const int H = d.hidden, E = d.n_experts, K = d.top_k, I = d.moe_inter, Ish = d.shared_inter;
+  const int gs_max_bits = any4 ? 4 : 2;
+  size_t o = 256;
+  DecodeArgs a{};
+  a.off_hs = (int)o; o += a16h((size_t)H * 2);
+  a.off_xs = (int)o; o += a16h((size_t)H * 2);
+  a.off_act = (int)o; o += a16h((size_t)K * I * 2);
+  a.off_actsh = (int)o; o += a16h((size_t)(Ish ? Ish : 8) * 2);
+  a.off_route = (int)o; o += a16h(8 * (size_t)E + 4 * DEC_WARPS * DEC_MAX_K + 4 * 4 * DEC_MAX_K + 32 + 4 * sizeof(CSeg) +
+                                  3 * (DEC_MAX_K + 1) * sizeof(void*) + 16);
+  a.off_y = (int)o; o += a16h((size_t)(K + 1) * DEC_MAX_DROWS * 4);
+  const size_t ta = p1_tile_bytes_max(d, G, 32, 32);
+  a.off_A0 = (int)o; o += a16h(ta);
+  a.off_A1 = (int)o; o += a16h(ta);
+  // C: at most ceil(K*I/G) (j, n) units in at most 3 segments, each 6 pieces
+  const int umax = (K * I + G - 1) / G + 1;
+  const size_t rbH = (size_t)H * gs_max_bits / 8, sbH = (size_t)(H / 32) * 2;
+  const size_t tc = 2 * (a16h(umax * rbH) + 2 * a16h(umax * sbH)) + 3 * 6 * 16;
+  a.off_C = (int)o; o += a16h(tc);
+  const size_t rbI = (size_t)I * gs_max_bits / 8, sbI = (size_t)(I / 32) * 2, sbS = Ish ? (size_t)(Ish / 32) * 2 : 0;
+  const size_t td = K * (a16h(nd_max * rbI) + 2 * a16h(nd_max * sbI)) + (Ish ? a16h((size_t)nd_max * Ish) + 2 * a16h(nd_max * sbS) : 0);
+  a.off_D = (int)o; o += a16h(td);
+  const size_t smem = o;
+  if (smem > 227 * 1024) return fail(YN_E_UNSUPPORTED, "stack decode needs " + std::to_string(smem) + " B of shared memory");
+
+  uint8_t* sc = reinterpret_cast<uint8_t*>(scratch);
+  a.H = H; a.E = E; a.K = K; a.I = I; a.Ish = Ish; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
+  a.layers = reinterpret_cast<const DecLayer*>(table);
+  a.n_layers = n_layers;
+  a.inputs = reinterpret_cast<const uint16_t*>(inputs);
+  a.n_tokens = n_tokens;
+  a.outputs = reinterpret_cast<uint16_t*>(outputs);
+  a.hbuf = reinterpret_cast<uint16_t*>(sc + S.hbuf);
+  a.logits = reinterpret_cast<float*>(sc + S.logits);
+  a.act = reinterpret_cast<uint16_t*>(sc + S.act);
+  a.act_sh = reinterpret_cast<uint16_t*>(sc + S.act_sh);
+  a.sgate = reinterpret_cast<float*>(sc + S.sgate);
+  a.trace_ids = trace_ids;
+  a.bar = reinterpret_cast<unsigned*>(sc + S.bar);
+  a.err = reinterpret_cast<int*>(sc + S.err);
+  a.timing = reinterpret_cast<long long*>(timing);
+  cudaStream_t st = as_stream(stream);
+  YN_CUDA(cudaMemsetAsync(a.bar, 0, 4, st));
+  void* kernel = nullptr;
+#define SD(C8, CS) if (!kernel && cpl8 == C8 && cpls == CS) kernel = reinterpret_cast<void*>(&k_stack_decode<C8, CS>);
+  SD(4, 1) SD(4, 2) SD(2, 1) SD(2, 2)
+#undef SD
+  if (!kernel) return fail(YN_E_UNSUPPORTED, "stack decode: no kernel for this hidden / shared size");
+  if ((rc = set_smem(reinterpret_cast<const void*>(kernel), smem))) return rc;
+  int per_sm = 0;
+  YN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, DEC_THREADS, smem));
+  if (per_sm < 1) return fail(YN_E_UNSUPPORTED, "stack decode kernel does not fit on an SM");
+  void* args[] = {&a};
+  YN_CUDA(cudaLaunchCooperativeKernel(kernel, dim3(G), dim3(DEC_THREADS), args, smem, st));
+  return YN_OK;
+}
+
+extern "C" int yn_stack_error(void* scratch, const yn_dims* dims, void* stream, int32_t* code_out) {
+  if (!scratch || !dims) return fail(YN_E_INVALID, "null argument");
+  StackScratch S = stack_scratch(*dims);
+  int32_t code = 0;
+  uint8_t* b = reinterpret_cast<uint8_t*>(scratch);
+  YN_CUDA(cudaMemcpyAsync(&code, b + S.err, 4, cudaMemcpyDeviceToHost, as_stream(stream)));
+  YN_CUDA(cudaStreamSynchronize(as_stream(stream)));
+  if (code) YN_CUDA(cudaMemsetAsync(b + S.err, 0, 4, as_stream(stream)));
+  if (code_out) *code_out = code;
+  return code ? fail(YN_E_DEVICE, "stack decode kernel error code " + std::to_string(code)) : YN_OK;
 }

@@ -57,9 +57,12 @@ YN_DEV void stage_pieces(const Piece* pc, int n, uint64_t* bar) {
     if (!bulk_ok(pc[i].dst, pc[i].src, pc[i].bytes)) coop_copy(pc[i].dst, pc[i].src, pc[i].bytes);
 }
 
-YN_DEV void init_bar(uint64_t* bar) {
+// Shared-memory header: [0] weight barrier, [8] activation barrier,
+// [16] last-CTA flag, [32..64) reduction scratch.
+YN_DEV void init_bars(uint64_t* bar_w, uint64_t* bar_a) {
   if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
+    mbar_init(bar_w, 1);
+    mbar_init(bar_a, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -85,7 +88,7 @@ YN_DEV float block_max4(float v, float* red) {
 // RMSNorm (canonical order, 128 threads): out = bf16(w * bf16(x * r)),
 // r = 1/sqrt(mean(x^2) + eps), sum of squares per thread over i = tid + 128 j.
 YN_DEV void rmsnorm_row(const uint16_t* h, const uint16_t* w, int H, float eps, uint16_t* out_smem,
-                        uint16_t* out_global, float* red) {
+                        uint16_t* out_global, float* red) {  // h, w in shared memory
   float ss = 0.0f;
   for (int i = threadIdx.x; i < H; i += THREADS) {
     const float v = bf16_to_f32(h[i]);
@@ -212,10 +215,13 @@ template <int CPL>
 __global__ void __launch_bounds__(THREADS) k_post_attention(const PostAttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  int* flag = reinterpret_cast<int*>(smem + 8);
-  float* red = reinterpret_cast<float*>(smem + 16);
-  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + SMEM_HDR);
-  uint8_t* tile = smem + SMEM_HDR + a16((size_t)a.T * a.H * 2);
+  uint64_t* bar_a = reinterpret_cast<uint64_t*>(smem + 8);
+  int* flag = reinterpret_cast<int*>(smem + 16);
+  float* red = reinterpret_cast<float*>(smem + 32);
+  uint16_t* hs = reinterpret_cast<uint16_t*>(smem + SMEM_HDR);                 // (T, H) h1 rows
+  uint16_t* ns = hs + a16((size_t)a.T * a.H * 2) / 2;                           // (H) norm weight
+  uint16_t* xs = ns + a16((size_t)a.H * 2) / 2;                                 // (T, H) normed rows
+  uint8_t* tile = reinterpret_cast<uint8_t*>(xs) + a16((size_t)a.T * a.H * 2);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int t = blockIdx.x;
@@ -249,8 +255,11 @@ __global__ void __launch_bounds__(THREADS) k_post_attention(const PostAttnArgs a
       pc_b[p] = reinterpret_cast<uint16_t*>(tile + o); o += a16((size_t)nrows * sb);
     }
   }
-  init_bar(bar);
+  init_bars(bar, bar_a);
   {
+    Piece act[2] = {{reinterpret_cast<uint8_t*>(hs), reinterpret_cast<const uint8_t*>(a.h1), (uint32_t)(a.T * H * 2)},
+                    {reinterpret_cast<uint8_t*>(ns), reinterpret_cast<const uint8_t*>(normw), (uint32_t)(H * 2)}};
+    stage_pieces(act, 2, bar_a);
     Piece pc[6];
     int n = 0;
     for (int p = 0; p < nparts; ++p) {
@@ -264,11 +273,14 @@ __global__ void __launch_bounds__(THREADS) k_post_attention(const PostAttnArgs a
     stage_pieces(pc, n, bar);
   }
   // RMSNorm of every row while the weights are in flight.
-  for (int tt = 0; tt < a.T; ++tt)
-    rmsnorm_row(a.h1 + (size_t)tt * H, normw, H, a.eps, xs + (size_t)tt * H,
-                (blockIdx.x == 0) ? a.x + (size_t)tt * H : nullptr, red);
   __syncthreads();
-  const bool ok = mbar_wait_bounded(bar, 0, a.err);
+  const bool act_ok = mbar_wait_bounded(bar_a, 0, a.err);
+  if (act_ok)
+    for (int tt = 0; tt < a.T; ++tt)
+      rmsnorm_row(hs + (size_t)tt * H, ns, H, a.eps, xs + (size_t)tt * H,
+                  (blockIdx.x == 0) ? a.x + (size_t)tt * H : nullptr, red);
+  __syncthreads();
+  const bool ok = mbar_wait_bounded(bar, 0, a.err) && act_ok;
 
   if (ok) {
     const int lpr = lanes_per_row((int)rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
@@ -347,7 +359,8 @@ template <int BITS, int CPL, int NSEG>
 __global__ void __launch_bounds__(THREADS) k_expert_up(const ExpertUpArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  float* red = reinterpret_cast<float*>(smem + 16);
+  uint64_t* bar_a = reinterpret_cast<uint64_t*>(smem + 8);
+  float* red = reinterpret_cast<float*>(smem + 32);
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + SMEM_HDR);
   uint8_t* tile = smem + SMEM_HDR + a16((size_t)a.H * 2);
 
@@ -370,8 +383,11 @@ __global__ void __launch_bounds__(THREADS) k_expert_up(const ExpertUpArgs a) {
   uint16_t* usc = reinterpret_cast<uint16_t*>(uc + a16((size_t)R * rb));
   uint16_t* ubi = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(usc) + a16((size_t)R * sb));
 
-  init_bar(bar);
+  init_bars(bar, bar_a);
   {
+    Piece act[1] = {{reinterpret_cast<uint8_t*>(xs), reinterpret_cast<const uint8_t*>(a.x + (size_t)tt * H),
+                     (uint32_t)(H * 2)}};
+    stage_pieces(act, 1, bar_a);
     Piece pc[6] = {
         {gc, rec + a.rg.off[0] + (size_t)n0 * rb, (uint32_t)(R * rb)},
         {reinterpret_cast<uint8_t*>(gsc), rec + a.rg.off[1] + (size_t)n0 * sb, (uint32_t)(R * sb)},
@@ -382,14 +398,11 @@ __global__ void __launch_bounds__(THREADS) k_expert_up(const ExpertUpArgs a) {
     };
     stage_pieces(pc, 6, bar);
   }
-  // x row into shared memory and its max |x| (scale for the fp16 path).
-  const uint16_t* xg = a.x + (size_t)tt * H;
+  // max |x| of the staged row (power-of-two scale for the fp16 path).
+  __syncthreads();
+  if (!mbar_wait_bounded(bar_a, 0, a.err)) return;
   float mx = 0.0f;
-  for (int i = tid; i < H; i += THREADS) {
-    const uint16_t v = xg[i];
-    xs[i] = v;
-    mx = fmaxf(mx, fabsf(bf16_to_f32(v)));
-  }
+  for (int i = tid; i < H; i += THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
   mx = block_max4(mx, red);
   const float scale = fp16_input_scale(mx);
   const float inv_scale = __fdiv_rn(1.0f, scale);
@@ -418,8 +431,9 @@ template <int BITS, int CPL, int NSEG, int CPLS>
 __global__ void __launch_bounds__(THREADS) k_expert_down(const ExpertDownArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  int* flag = reinterpret_cast<int*>(smem + 8);
-  float* red = reinterpret_cast<float*>(smem + 16);
+  uint64_t* bar_a = reinterpret_cast<uint64_t*>(smem + 8);
+  int* flag = reinterpret_cast<int*>(smem + 16);
+  float* red = reinterpret_cast<float*>(smem + 32);
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + SMEM_HDR);
   const int Kx = (a.I > a.Ish) ? a.I : a.Ish;
   uint8_t* tile = smem + SMEM_HDR + a16((size_t)Kx * 2);
@@ -471,22 +485,25 @@ __global__ void __launch_bounds__(THREADS) k_expert_down(const ExpertDownArgs a)
   uint16_t* wsc = reinterpret_cast<uint16_t*>(wc + a16((size_t)R * rb));
   uint16_t* wbi = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(wsc) + a16((size_t)R * sb));
 
-  init_bar(bar);
+  init_bars(bar, bar_a);
   const bool have = (wsrc != nullptr);
+  {
+    Piece act[1] = {{reinterpret_cast<uint8_t*>(xs), reinterpret_cast<const uint8_t*>(xg), (uint32_t)(Kin * 2)}};
+    stage_pieces(act, 1, bar_a);
+  }
   if (have) {
     Piece pc[3] = {{wc, wsrc, R * rb}, {reinterpret_cast<uint8_t*>(wsc), ssrc, R * sb},
                    {reinterpret_cast<uint8_t*>(wbi), bsrc, R * sb}};
     stage_pieces(pc, 3, bar);
   }
+  __syncthreads();
+  const bool act_ok = mbar_wait_bounded(bar_a, 0, a.err);
   float mx = 0.0f;
-  for (int i = tid; i < Kin; i += THREADS) {
-    const uint16_t v = xg[i];
-    xs[i] = v;
-    mx = fmaxf(mx, fabsf(bf16_to_f32(v)));
-  }
+  if (act_ok)
+    for (int i = tid; i < Kin; i += THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
   mx = block_max4(mx, red);
   __syncthreads();
-  const bool ok = have && mbar_wait_bounded(bar, 0, a.err);
+  const bool ok = have && act_ok && mbar_wait_bounded(bar, 0, a.err);
 
   if (ok) {
     const int lpr = lanes_per_row((int)rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
@@ -534,15 +551,22 @@ __global__ void __launch_bounds__(THREADS) k_expert_down(const ExpertDownArgs a)
   if (*flag) {
     __threadfence();
     const float* wrow = a.wts + (size_t)tt * a.K;
+    float wv[16];
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) wv[jj] = (jj < a.K) ? __ldcg(wrow + jj) : 0.0f;
     for (int r = cb * cbr + tid; r < (cb + 1) * cbr; r += THREADS) {
+      uint16_t yv[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) yv[jj] = (jj < a.K) ? __ldcg(a.y + ((size_t)tt * a.K + jj) * H + r) : 0;
+      const uint16_t sh = (a.mode >= 1 && a.has_shared) ? __ldcg(a.ysh + (size_t)tt * H + r) : 0;
+      const uint16_t hr = (a.mode == 2) ? a.h_res[(size_t)tt * H + r] : 0;
       float acc = 0.0f;
-      for (int jj = 0; jj < a.K; ++jj) {
-        const float y = bf16_to_f32(__ldcg(a.y + ((size_t)tt * a.K + jj) * H + r));
-        acc = __fadd_rn(acc, bf16r(__fmul_rn(y, __ldcg(wrow + jj))));
-      }
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj)
+        if (jj < a.K) acc = __fadd_rn(acc, bf16r(__fmul_rn(bf16_to_f32(yv[jj]), wv[jj])));
       float o = bf16r(acc);
-      if (a.mode >= 1 && a.has_shared) o = bf16r(__fadd_rn(o, bf16_to_f32(__ldcg(a.ysh + (size_t)tt * H + r))));
-      if (a.mode == 2) o = bf16r(__fadd_rn(bf16_to_f32(a.h_res[(size_t)tt * H + r]), o));
+      if (a.mode >= 1 && a.has_shared) o = bf16r(__fadd_rn(o, bf16_to_f32(sh)));
+      if (a.mode == 2) o = bf16r(__fadd_rn(bf16_to_f32(hr), o));
       a.out[(size_t)tt * H + r] = f32_to_bf16(o);
     }
     __syncthreads();

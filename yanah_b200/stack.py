@@ -40,6 +40,16 @@ class ResidentStack:
         self.ws = Workspace(self.dims, self.device)
         H = cfg.hidden
         self._ping = torch.empty((2, 1, H), dtype=torch.bfloat16, device=self.device)
+        # persistent decode: device layer table + scratch
+        lib = _lib.lib()
+        n = len(self.structs)
+        tb = int(lib.yn_stack_table_bytes(n))
+        self.table = torch.empty(tb, dtype=torch.uint8, device=self.device)
+        arr = (_lib.Layer * n)(*self.structs)
+        _lib.check(lib.yn_stack_prepare(C.byref(self.dims), arr, n, self.table.data_ptr(), tb))
+        sb = int(lib.yn_stack_scratch_bytes(C.byref(self.dims)))
+        self.scratch = torch.zeros(sb, dtype=torch.uint8, device=self.device)
+        self.layer_bits = (C.c_int32 * n)(*[cfg.expert_bits[l] for l in self.layer_ids])
         torch.cuda.synchronize(self.device)
 
     @property
@@ -75,3 +85,100 @@ class ResidentStack:
 
     def kernel_launches_per_token(self) -> int:
         return 3 * len(self.structs)
+
+    # ------------------------------------------------- persistent decode
+    def decode(self, inputs: torch.Tensor, outputs: torch.Tensor, trace: Optional[torch.Tensor] = None,
+               timing: Optional[torch.Tensor] = None, stream=None) -> None:
+        """Sequential bs1 decode of inputs (N,H) -> outputs (N,H) in ONE
+        persistent cooperative launch. trace: (N, L, k) int32 routed ids;
+        timing: (L, 8) int64 phase stamps of token 0."""
+        lib = _lib.lib()
+        n = len(self.structs)
+        _lib.check(lib.yn_stack_decode(C.byref(self.dims), self.table.data_ptr(), n, self.layer_bits,
+                                       inputs.data_ptr(), inputs.shape[0], outputs.data_ptr(), self.scratch.data_ptr(),
+                                       self.scratch.numel(), trace.data_ptr() if trace is not None else None,
+                                       timing.data_ptr() if timing is not None else None, stream_ptr(stream)))
+
+    def decode_error(self, stream=None) -> int:
+        code = C.c_int32(0)
+        rc = _lib.lib().yn_stack_error(self.scratch.data_ptr(), C.byref(self.dims), stream_ptr(stream), C.byref(code))
+        if rc != _lib.YN_OK and code.value == 0:
+            _lib.check(rc)
+        return code.value
+
+    def decode_host(self, host_inputs: torch.Tensor, host_outputs: torch.Tensor, dev_in: torch.Tensor,
+                    dev_out: torch.Tensor, stream=None) -> None:
+        """End-to-end call with host buffers: copy pinned inputs in, decode,
+        copy outputs back (all on `stream`, asynchronous)."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(s):
+            dev_in.copy_(host_inputs, non_blocking=True)
+            self.decode(dev_in, dev_out, stream=s)
+            host_outputs.copy_(dev_out, non_blocking=True)
+
+    # ------------------------------------------------------ kernel timing
+    def run_token_timed(self, h_in: torch.Tensor, h_out: torch.Tensor, events: List[int], stream=None) -> None:
+        """run_token with an event recorded before the first kernel and after
+        every kernel (4 events per layer boundary set: pre, post_attention,
+        expert_up, expert_down), so each kernel's duration can be read."""
+        lib = _lib.lib()
+        st = stream_ptr(stream)
+        n = len(self.structs)
+        src = h_in.data_ptr()
+        d = C.byref(self.dims)
+        _lib.check(lib.yn_record_event(events[0], st))
+        for i, L in enumerate(self.structs):
+            dst = h_out.data_ptr() if i == n - 1 else self._ping[i % 2].data_ptr()
+            Lr = C.byref(L)
+            _lib.check(lib.yn_post_attention(d, Lr, src, 1, None, 0, self.ws.ptr, st))
+            _lib.check(lib.yn_record_event(events[3 * i + 1], st))
+            _lib.check(lib.yn_moe_up(d, Lr, None, None, 1, None, 0, self.ws.ptr, st))
+            _lib.check(lib.yn_record_event(events[3 * i + 2], st))
+            _lib.check(lib.yn_moe_down(d, Lr, None, None, 1, src, 2, dst, self.ws.ptr, st))
+            _lib.check(lib.yn_record_event(events[3 * i + 3], st))
+            src = dst
+
+    def profile_kernels(self, inputs: torch.Tensor, outputs: torch.Tensor, replays: int = 3):
+        """Per-kernel device durations (ms) of a graph-captured decode of
+        inputs, with external event nodes between kernels. Returns
+        {"post_attention": [...], "expert_up": [...], "expert_down": [...]}
+        with one entry per (replay, token, layer)."""
+        lib = _lib.lib()
+        n_ev = 3 * len(self.structs) + 1
+        T = inputs.shape[0]
+        evs = []
+        for _ in range(T * n_ev):
+            e = C.c_void_p()
+            _lib.check(lib.yn_event_create(C.byref(e)))
+            evs.append(e.value)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+
+        def body(stream):
+            for t in range(T):
+                self.run_token_timed(inputs[t:t + 1], outputs[t:t + 1], evs[t * n_ev:(t + 1) * n_ev], stream)
+
+        with torch.cuda.stream(s):
+            body(s)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                body(s)
+        out = {"post_attention": [], "expert_up": [], "expert_down": []}
+        names = list(out)
+        ms = C.c_float()
+        for _ in range(replays):
+            g.replay()
+            torch.cuda.synchronize(self.device)
+            for t in range(T):
+                base = t * n_ev
+                for i in range(len(self.structs)):
+                    for k in range(3):
+                        _lib.check(lib.yn_event_elapsed_ms(evs[base + 3 * i + k], evs[base + 3 * i + k + 1],
+                                                           C.byref(ms)))
+                        out[names[k]].append((self.layer_ids[i], ms.value))
+        del g
+        for e in evs:
+            lib.yn_event_destroy(e)
+        return out
