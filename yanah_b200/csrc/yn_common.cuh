@@ -144,6 +144,13 @@ YN_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t phase, int* err) {
   }
 }
 
+// Every thread of the block waits; the result is made block-uniform so that
+// no thread skips work (or returns) while others continue.
+YN_DEV bool mbar_wait_block(uint64_t* bar, uint32_t phase, int* err) {
+  const bool ok = mbar_wait_bounded(bar, phase, err);
+  return __syncthreads_and(ok ? 1 : 0) != 0;
+}
+
 // Global -> shared bulk copy (non-tensor TMA path). dst/src 16-byte aligned,
 // bytes a multiple of 16. Completion is signalled as transaction bytes on bar.
 YN_DEV void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -63,7 +63,8 @@ struct DecodeArgs {
 };
 
 // ---------------------------------------------------------------- barrier
-YN_DEV void grid_barrier(const DecodeArgs& a, unsigned& gen) {
+// Returns true (block-uniform) when the error word is set after the barrier.
+YN_DEV bool grid_barrier(const DecodeArgs& a, unsigned& gen, int* flag) {
   __syncthreads();
   gen += 1;
   if (threadIdx.x == 0) {
@@ -82,11 +83,11 @@ YN_DEV void grid_barrier(const DecodeArgs& a, unsigned& gen) {
         }
       }
     }
+    *flag = *reinterpret_cast<volatile int*>(a.err);
   }
   __syncthreads();
+  return *flag != 0;
 }
-
-YN_DEV bool dec_error(const DecodeArgs& a) { return *reinterpret_cast<volatile int*>(a.err) != 0; }
 
 YN_DEV void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -502,6 +503,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
   uint64_t* barC = reinterpret_cast<uint64_t*>(smem + 16);
   uint64_t* barD = reinterpret_cast<uint64_t*>(smem + 24);
   float* red = reinterpret_cast<float*>(smem + 32);           // 16 floats
+  int* eflag = reinterpret_cast<int*>(smem + 128);
   uint16_t* hs = reinterpret_cast<uint16_t*>(smem + a.off_hs);
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + a.off_xs);
   uint16_t* acts = reinterpret_cast<uint16_t*>(smem + a.off_act);   // (K, I)
@@ -544,7 +546,16 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
   }
   unsigned gen = 0;
   uint32_t phA[2] = {0, 0}, phC = 0, phD = 0;
+  bool pendA[2] = {true, false}, pendC = false, pendD = false;  // armed, not yet waited on
   int step = 0;  // global layer step counter (selects the A buffer)
+  // Error exit: wait (bounded) for every bulk copy still landing in this
+  // CTA's shared memory, then leave.
+  auto drain = [&]() {
+    for (int i = 0; i < 2; ++i)
+      if (pendA[i]) mbar_wait_block(&barA[i], phA[i], nullptr);
+    if (pendC) mbar_wait_block(barC, phC, nullptr);
+    if (pendD) mbar_wait_block(barD, phD, nullptr);
+  };
 
   for (int tok = 0; tok < a.n_tokens; ++tok) {
     for (int layer = 0; layer < a.n_layers; ++layer, ++step) {
@@ -561,17 +572,20 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
           issue_p1(N, r1, p1_tile(Abuf[ab ^ 1], r1, H, N.router.gs, N.sg.gs ? N.sg.gs : 64), H, &barA[ab ^ 1]);
         }
       }
+      pendA[ab ^ 1] = (layer + 1 < a.n_layers) || (tok + 1 < a.n_tokens);
       const uint16_t* hin = (layer == 0) ? a.inputs + (size_t)tok * H : a.hbuf + (size_t)(step & 1) * H;
       for (int i = tid; i < H / 8; i += DEC_THREADS)
         reinterpret_cast<uint4*>(hs)[i] = __ldcg(reinterpret_cast<const uint4*>(hin) + i);
       __syncthreads();
       rmsnorm_smem(hs, L.norm, H, a.eps, xs, red);
-      if (!mbar_wait_bounded(&barA[ab], phA[ab], a.err)) {}
-      phA[ab] ^= 1;
-      if (!dec_error(a)) p1_compute<CPL8>(a, L, r1, p1_tile(Abuf[ab], r1, H, L.router.gs, L.sg.gs ? L.sg.gs : 64), xs);
+      const bool a_ok = mbar_wait_block(&barA[ab], phA[ab], a.err);
+      if (a_ok) {
+        phA[ab] ^= 1;
+        pendA[ab] = false;
+      }
+      if (a_ok) p1_compute<CPL8>(a, L, r1, p1_tile(Abuf[ab], r1, H, L.router.gs, L.sg.gs ? L.sg.gs : 64), xs);
       stamp(a, tok, layer, 1);
-      grid_barrier(a, gen);
-      if (dec_error(a)) return;
+      if (grid_barrier(a, gen, eflag)) { drain(); return; }
       stamp(a, tok, layer, 2);
       // -------- P2: routing, issue C and D tiles, gate/up rows
       route_block(a.logits, E, K, a.norm_topk, rv, keys, cand, red, ids, wts);
@@ -585,7 +599,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
         }
         if (!ok) {
           raise_error(a.err, YN_ERR_BAD_SLOT);
-          *nseg_s = 0;
+          *nseg_s = -1;
         } else {
           int nseg = 0;
           proxy_fence();
@@ -603,9 +617,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
 #pragma unroll
       for (int w = 1; w < DEC_WARPS; ++w) mx = fmaxf(mx, red[w]);
       const float xscale = fp16_input_scale(mx);
-      const bool cd_ok = !dec_error(a);
-      if (cd_ok) {
-        mbar_wait_bounded(barC, phC, a.err);
+      const bool cd_ok = (*nseg_s >= 0);  // uniform: written by thread 0 before the sync above
+      pendC = pendD = cd_ok;
+      const bool c_ok = cd_ok && mbar_wait_block(barC, phC, a.err);
+      if (c_ok) {
+        phC ^= 1;
+        pendC = false;
         const int bits = L.rg.bits, gs = L.rg.gs;
         const int nseg = *nseg_s;
         if (bits == 2) {
@@ -615,10 +632,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
           p2_compute<4, 2, 1>(a, seg, nseg, xs, xscale, gs);
         }
       }
-      phC ^= 1;
       stamp(a, tok, layer, 3);
-      grid_barrier(a, gen);
-      if (dec_error(a)) return;
+      if (grid_barrier(a, gen, eflag)) { drain(); return; }
       stamp(a, tok, layer, 4);
       // -------- P3: down rows [d0, d1) of every expert + shared, combine, residual
       for (int i = tid; i < K * I / 8; i += DEC_THREADS)
@@ -636,9 +651,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
         }
       }
       __syncthreads();
-      mbar_wait_bounded(barD, phD, a.err);
-      phD ^= 1;
-      if (!dec_error(a)) {
+      const bool d_ok = mbar_wait_block(barD, phD, a.err);
+      if (d_ok) {
+        phD ^= 1;
+        pendD = false;
+      }
+      if (d_ok) {
         const int bits = L.rg.bits, gs = L.rg.gs;
         if (bits == 2) {
           if (gs == 32) p3_routed<2, 1, 2>(a, dptr, nd, acts, ascale, ybuf, gs);
@@ -661,8 +679,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
         }
       }
       stamp(a, tok, layer, 5);
-      grid_barrier(a, gen);
-      if (dec_error(a)) return;
+      if (grid_barrier(a, gen, eflag)) { drain(); return; }
     }
   }
 }

@@ -274,13 +274,13 @@ __global__ void __launch_bounds__(THREADS) k_post_attention(const PostAttnArgs a
   }
   // RMSNorm of every row while the weights are in flight.
   __syncthreads();
-  const bool act_ok = mbar_wait_bounded(bar_a, 0, a.err);
+  const bool act_ok = mbar_wait_block(bar_a, 0, a.err);
   if (act_ok)
     for (int tt = 0; tt < a.T; ++tt)
       rmsnorm_row(hs + (size_t)tt * H, ns, H, a.eps, xs + (size_t)tt * H,
                   (blockIdx.x == 0) ? a.x + (size_t)tt * H : nullptr, red);
   __syncthreads();
-  const bool ok = mbar_wait_bounded(bar, 0, a.err) && act_ok;
+  const bool ok = mbar_wait_block(bar, 0, a.err) && act_ok;
 
   if (ok) {
     const int lpr = lanes_per_row((int)rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
@@ -400,14 +400,14 @@ __global__ void __launch_bounds__(THREADS) k_expert_up(const ExpertUpArgs a) {
   }
   // max |x| of the staged row (power-of-two scale for the fp16 path).
   __syncthreads();
-  if (!mbar_wait_bounded(bar_a, 0, a.err)) return;
+  if (!mbar_wait_block(bar_a, 0, a.err)) return;
   float mx = 0.0f;
   for (int i = tid; i < H; i += THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
   mx = block_max4(mx, red);
   const float scale = fp16_input_scale(mx);
   const float inv_scale = __fdiv_rn(1.0f, scale);
   __syncthreads();
-  if (!mbar_wait_bounded(bar, 0, a.err)) return;
+  if (!mbar_wait_block(bar, 0, a.err)) return;
 
   const int lpr = lanes_per_row((int)rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
   XF16<BITS, CPL, NSEG> X;
@@ -497,13 +497,14 @@ __global__ void __launch_bounds__(THREADS) k_expert_down(const ExpertDownArgs a)
     stage_pieces(pc, 3, bar);
   }
   __syncthreads();
-  const bool act_ok = mbar_wait_bounded(bar_a, 0, a.err);
+  const bool act_ok = mbar_wait_block(bar_a, 0, a.err);
   float mx = 0.0f;
   if (act_ok)
     for (int i = tid; i < Kin; i += THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
   mx = block_max4(mx, red);
   __syncthreads();
-  const bool ok = have && act_ok && mbar_wait_bounded(bar, 0, a.err);
+  const bool wok = have ? mbar_wait_block(bar, 0, a.err) : false;
+  const bool ok = have && act_ok && wok;
 
   if (ok) {
     const int lpr = lanes_per_row((int)rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
