@@ -214,18 +214,22 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.synchronize(dev)
     if stack.decode_error():
         raise RuntimeError("device error in the first decode")
-    # phase stamps of token 0 (one extra untimed launch)
-    timing = torch.zeros((len(layers), 8), dtype=torch.int64, device=dev)
+    # per-layer phase breakdown from SM-cycle stamps (one extra untimed launch)
+    timing = torch.zeros((len(layers), 16), dtype=torch.int64, device=dev)
     stack.decode(inputs[:2], outputs[:2], timing=timing)
     torch.cuda.synchronize(dev)
     tm = timing.cpu().numpy().astype(np.float64)
+    mhz = torch.cuda.get_device_properties(dev).clock_rate / 1e3 if hasattr(
+        torch.cuda.get_device_properties(dev), "clock_rate") else 1965.0
     phases = {}
     if tm[0, 0] > 0:
-        d = np.diff(tm[:, :6], axis=1) / 1e3
-        b3 = (np.append(tm[1:, 0], np.nan) - tm[:, 5]) / 1e3
-        phases = {k: round(float(v), 3) for k, v in zip(
-            ["p1_us", "bar1_us", "p2_us", "bar2_us", "p3_us"], d.mean(axis=0))}
-        phases["bar3_us"] = round(float(np.nanmean(b3)), 3) if len(layers) > 1 else None
+        names = ["loads", "waitA", "rmsnorm", "p1", "bar1", "route", "plan_issue_xmax", "waitC", "p2", "bar2",
+                 "act_loads", "ascale", "waitD", "p3", "combine"]
+        d = np.diff(tm, axis=1) / mhz  # us
+        phases = {n: round(float(v), 3) for n, v in zip(names, d.mean(axis=0))}
+        if len(layers) > 1:
+            phases["bar3"] = round(float(np.mean((tm[1:, 0] - tm[:-1, 15]) / mhz)), 3)
+        phases["clock_mhz_assumed"] = mhz
 
     def barrier():
         if world > 1:
@@ -299,7 +303,7 @@ def run_ours(args, rank: int, world: int):
                      "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
                      "bytes_per_launch": bytes_tok * N, "avg_launch_us": round(launch_ms * 1e3, 1),
                      "traffic": traffic},
-        "phases_token0_us_per_layer": phases,
+        "phases_us_per_layer": phases,
     }
     if args.layers:
         line["config"]["layers"] = len(layers)

@@ -169,14 +169,15 @@ int yn_moe_layer(const yn_dims* dims, const yn_layer* layer, const void* h_in, i
  * resident MoE layers (orchestrator.py:308-343 with every expert resident):
  * one cooperative launch, one CTA per SM, three grid barriers per layer.
  * Prepare once: yn_stack_prepare copies the layer descriptors into a device
- * table of yn_stack_table_bytes(n_layers) bytes. layer_bits: host array of
- * each layer's routed-expert bit width. inputs/outputs: (n_tokens, H) bf16.
+ * table of yn_stack_table_bytes(n_layers) bytes; `layers` is the same host
+ * array (used for sizing). inputs/outputs: (n_tokens, H) bf16.
  * trace_ids: (n_tokens, n_layers, k) routed ids or NULL. timing: (n_layers,
- * 8) int64 nanosecond stamps of token 0 or NULL. */
+ * 16) int64 SM-cycle stamps of the last token's phases on CTA 0, or NULL
+ * (diagnostics: adds block syncs on CTA 0). */
 size_t yn_stack_table_bytes(int32_t n_layers);
 size_t yn_stack_scratch_bytes(const yn_dims* dims);
 int yn_stack_prepare(const yn_dims* dims, const yn_layer* layers, int32_t n_layers, void* table, size_t table_bytes);
-int yn_stack_decode(const yn_dims* dims, const void* table, int32_t n_layers, const int32_t* layer_bits,
+int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
                     const void* inputs, int32_t n_tokens, void* outputs, void* scratch, size_t scratch_bytes,
                     int32_t* trace_ids, int64_t* timing, void* stream);
 /* Read and clear the stack decode error word (synchronises the stream). */

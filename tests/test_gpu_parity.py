@@ -168,9 +168,31 @@ def test_stack_teacher_forced_routing():
     assert dm.ws.check_error() == 0
 
 
-def test_persistent_decode_matches_layer_kernels():
-    """The persistent whole-stack kernel gives bit-identical outputs and routing
-    to the per-layer kernels, token after token (4 layers: 4,2,2,4-bit)."""
+def test_persistent_decode_single_layers_vs_oracle():
+    """The persistent whole-stack kernel on one-layer stacks (4-bit g64, 2-bit
+    g64, 2-bit g32): routing ids bit-exact, outputs within tolerance of the oracle."""
+    from yanah_b200.stack import ResidentStack
+    for bits, gs in ((4, 64), (2, 64), (2, 32)):
+        cfg = small_config(bits=(bits,), gs=gs, hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=4)
+        st = ResidentStack(cfg, "cuda")
+        N = 3
+        x = bf16_dev(hidden_rows(cfg, N, stream=2))
+        got = torch.empty_like(x)
+        trace = torch.full((N, 1, cfg.top_k), -1, dtype=torch.int32, device="cuda")
+        st.decode(x, got, trace=trace)
+        torch.cuda.synchronize()
+        assert st.decode_error() == 0
+        o = cpu.OracleStack(cfg)
+        for t in range(N):
+            r = o.layer(0, bf16_np(x[t:t + 1]))
+            assert np.array_equal(trace[t, 0].cpu().numpy(), r["ids"][0]), (bits, gs, t)
+            err = rel_l2(bf16_np(got[t:t + 1]), r["out"])
+            assert err < REL_L2_TOL, (bits, gs, t, err)
+
+
+def test_persistent_decode_stack_vs_layer_kernels():
+    """Four layers (4,2,2,4-bit), three tokens: persistent kernel and per-layer
+    kernels agree on layer-0 routing exactly and on outputs within tolerance."""
     from yanah_b200.stack import ResidentStack
     cfg = small_config(bits=(4, 2, 2, 4), hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=4)
     st = ResidentStack(cfg, "cuda")
@@ -183,10 +205,9 @@ def test_persistent_decode_matches_layer_kernels():
     st.decode(x, got, trace=trace)
     torch.cuda.synchronize()
     assert st.decode_error() == 0
-    assert np.array_equal(bf16_np(got), bf16_np(ref))
-    # layer 0 routing of every token equals the oracle's on the same input
+    assert (trace >= 0).all()
     o = cpu.OracleStack(cfg)
     for t in range(N):
         r = o.post_attention(0, bf16_np(x[t:t + 1]))
         assert np.array_equal(trace[t, 0].cpu().numpy(), r["ids"][0]), t
-    assert (trace >= 0).all()
+        assert rel_l2(bf16_np(got[t:t + 1]), bf16_np(ref[t:t + 1])) < REL_L2_TOL, t

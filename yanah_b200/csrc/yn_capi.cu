@@ -106,7 +106,15 @@ static int set_smem_ptr(const void* kernel, size_t bytes) {
   std::lock_guard<std::mutex> lock(mu);
   auto key = std::make_pair(kernel, dev);
   if (done.count(key)) return YN_OK;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227 * 1024));
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return fail(YN_E_CUDA, std::string("cudaFuncGetAttributes: ") + cudaGetErrorString(e));
+  const int avail = optin - (int)fa.sharedSizeBytes;
+  if ((int)bytes > avail) return fail(YN_E_UNSUPPORTED, "kernel needs " + std::to_string(bytes) + " B of shared memory, " +
+                                                            std::to_string(avail) + " available");
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, avail);
   if (e != cudaSuccess) return fail(YN_E_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   done.insert(key);
   return YN_OK;
@@ -634,20 +642,20 @@ static size_t p1_tile_bytes_max(const yn_dims& d, int G, int gs_r, int gs_s) {
     const size_t np = std::min(std::max(u1 - E, 0), Ish) - std::min(std::max(u0 - E, 0), Ish);
     const int sg = (Ish > 0 && u0 <= E + Ish && u1 > E + Ish) ? 1 : 0;
     const size_t sbr = (size_t)(H / gs_r) * 2, sbs = (size_t)(H / gs_s) * 2;
-    size_t o = a16h(nr * H) + 2 * a16h(nr * sbr) + 2 * (a16h(np * H) + 2 * a16h(np * sbs)) +
+    size_t o = a16h((size_t)H * 2) + a16h(nr * H) + 2 * a16h(nr * sbr) + 2 * (a16h(np * H) + 2 * a16h(np * sbs)) +
                (sg ? a16h(H) + 2 * a16h(sbs) : 0);
     best = std::max(best, o);
   }
   return best;
 }
 
-extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, int32_t n_layers, const int32_t* layer_bits,
+extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
                                const void* inputs, int32_t n_tokens, void* outputs, void* scratch,
                                size_t scratch_bytes, int32_t* trace_ids, int64_t* timing, void* stream) {
   int rc = check_dims(dims, 1);
   if (rc) return rc;
   const yn_dims& d = *dims;
-  if (!table || !inputs || !outputs || !scratch || !layer_bits) return fail(YN_E_INVALID, "null argument");
+  if (!table || !inputs || !outputs || !scratch || !layers) return fail(YN_E_INVALID, "null argument");
   if (n_layers < 1 || n_tokens < 1) return fail(YN_E_INVALID, "n_layers and n_tokens must be >= 1");
   StackScratch S = stack_scratch(d);
   if (scratch_bytes < S.total) return fail(YN_E_INVALID, "scratch too small");
@@ -656,43 +664,62 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, int32_t n
   // H = 2048-class rows (8-bit router CPL from H, routed gate/up CPL 2 at 4-bit
   // and 1 at 2-bit, down rows CPL 1).
   const int cpl8 = cpl_of(d.hidden), cpls = d.shared_inter ? cpl_of(d.shared_inter) : 1;
-  bool any4 = false;
+  int max_bits = 2, min_gs = 1 << 30, min_gs_dense = 1 << 30;
   for (int l = 0; l < n_layers; ++l) {
-    const int b = layer_bits[l];
+    const int b = layers[l].record.bits;
+    min_gs = std::min(min_gs, (int)layers[l].record.group_size);
+    min_gs_dense = std::min(min_gs_dense, (int)layers[l].router.group_size);
+    if (d.shared_inter) {
+      min_gs_dense = std::min(min_gs_dense, (int)layers[l].shared_gate.group_size);
+      min_gs_dense = std::min(min_gs_dense, (int)layers[l].shared_down.group_size);
+    }
     if (b != 2 && b != 4) return fail(YN_E_UNSUPPORTED, "stack decode: experts must be 2- or 4-bit");
     if (cpl_of(d.hidden * b / 8) != (b == 4 ? 2 : 1) || cpl_of(d.moe_inter * b / 8) != 1)
       return fail(YN_E_UNSUPPORTED, "stack decode: hidden/moe_inter outside the compiled row mapping");
-    any4 |= (b == 4);
+    max_bits = std::max(max_bits, b);
   }
   int dev = 0, sms = 0;
   YN_CUDA(cudaGetDevice(&dev));
   YN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int G = sms;
   const int nd_max = (d.hidden + G - 1) / G;
+  if ((d.top_k * d.moe_inter + G - 1) / G > d.moe_inter)
+    return fail(YN_E_UNSUPPORTED, "stack decode: a CTA's gate/up rows must span at most two experts");
   if (nd_max > DEC_MAX_DROWS) return fail(YN_E_UNSUPPORTED, "hidden too large for the per-CTA row block");
-  // shared-memory carve
+  // shared-memory carve (mirrors the pointer layout at the top of k_stack_decode)
   const int H = d.hidden, E = d.n_experts, K = d.top_k, I = d.moe_inter, Ish = d.shared_inter;
-  const int gs_max_bits = any4 ? 4 : 2;
+  if (I != 512 || (Ish != 0 && Ish != 512))
+    return fail(YN_E_UNSUPPORTED, "stack decode: moe_inter and shared_inter must be 512 (one warp per activation vector)");
+  if (K + 1 > DEC_WARPS) return fail(YN_E_UNSUPPORTED, "stack decode: top_k must be < 16");
+  if (H != 1024 && H != 2048 && H != 4096)
+    return fail(YN_E_UNSUPPORTED, "stack decode: hidden must be 1024, 2048 or 4096");
+  if (2 * ((K * I + G - 1) / G + 1) > 80) return fail(YN_E_UNSUPPORTED, "stack decode: too many gate/up rows per CTA");
+  if ((K + 1) * 8 > 6 * DEC_WARPS) return fail(YN_E_UNSUPPORTED, "stack decode: too many down tiles");
+  if (nd_max > DEC_MAX_DROWS) return fail(YN_E_UNSUPPORTED, "stack decode: more than 16 output rows per CTA");
+  const int gs_max_bits = max_bits;
   size_t o = 256;
   DecodeArgs a{};
   a.off_hs = (int)o; o += a16h((size_t)H * 2);
   a.off_xs = (int)o; o += a16h((size_t)H * 2);
-  a.off_act = (int)o; o += a16h((size_t)K * I * 2);
-  a.off_actsh = (int)o; o += a16h((size_t)(Ish ? Ish : 8) * 2);
-  a.off_route = (int)o; o += a16h(8 * (size_t)E + 4 * DEC_WARPS * DEC_MAX_K + 4 * 4 * DEC_MAX_K + 32 + 4 * sizeof(CSeg) +
-                                  3 * (DEC_MAX_K + 1) * sizeof(void*) + 16);
-  a.off_y = (int)o; o += a16h((size_t)(K + 1) * DEC_MAX_DROWS * 4);
-  const size_t ta = p1_tile_bytes_max(d, G, 32, 32);
-  a.off_A0 = (int)o; o += a16h(ta);
-  a.off_A1 = (int)o; o += a16h(ta);
-  // C: at most ceil(K*I/G) (j, n) units in at most 3 segments, each 6 pieces
+  a.off_xf = (int)o; o += a16h((size_t)(K + 1) * 8 * 4 * sizeof(XBlock));
+  a.off_route = (int)o;
+  o += a16h(8 * (size_t)E + 4 * DEC_WARPS * DEC_MAX_K + 4 * DEC_MAX_K + 4 * DEC_MAX_K + 4 * (DEC_MAX_K + 4) + 4 * (64 + 256) +
+            3 * sizeof(DecLayer));
   const int umax = (K * I + G - 1) / G + 1;
-  const size_t rbH = (size_t)H * gs_max_bits / 8, sbH = (size_t)(H / 32) * 2;
-  const size_t tc = 2 * (a16h(umax * rbH) + 2 * a16h(umax * sbH)) + 3 * 6 * 16;
-  a.off_C = (int)o; o += a16h(tc);
-  const size_t rbI = (size_t)I * gs_max_bits / 8, sbI = (size_t)(I / 32) * 2, sbS = Ish ? (size_t)(Ish / 32) * 2 : 0;
-  const size_t td = K * (a16h(nd_max * rbI) + 2 * a16h(nd_max * sbI)) + (Ish ? a16h((size_t)nd_max * Ish) + 2 * a16h(nd_max * sbS) : 0);
-  a.off_D = (int)o; o += a16h(td);
+  const int Rmax = 2 * umax;
+  const size_t part_p2 = (size_t)Rmax * (H / 64) * 4, part_p3 = (size_t)(K + 1) * DEC_MAX_DROWS * 8 * 4;
+  a.off_part = (int)o; o += a16h(std::max(part_p2, part_p3));
+  const size_t ta = p1_tile_bytes_max(d, G, min_gs_dense, min_gs_dense);
+  a.off_A = (int)o; o += a16h(ta);
+  const size_t rbH = (size_t)H * gs_max_bits / 8, sbH = (size_t)(H / min_gs) * 2;
+  a.off_C = (int)o;  // routed tiles are staged in registers (no shared-memory tile)
+  (void)rbH; (void)sbH;
+  const size_t rbI = (size_t)I * gs_max_bits / 8, sbI = (size_t)(I / min_gs) * 2,
+               sbS = Ish ? (size_t)(Ish / min_gs_dense) * 2 : 0;
+  const size_t td = (size_t)K * DEC_MAX_DROWS * (rbI + 16) + (size_t)DEC_MAX_DROWS * (Ish + 16) +
+                    2 * (size_t)K * DEC_MAX_DROWS * sbI + 2 * (size_t)DEC_MAX_DROWS * sbS;
+  a.off_D = (int)o;
+  (void)td;
   const size_t smem = o;
   if (smem > 227 * 1024) return fail(YN_E_UNSUPPORTED, "stack decode needs " + std::to_string(smem) + " B of shared memory");
 

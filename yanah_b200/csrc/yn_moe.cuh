@@ -4,7 +4,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#include "../../include/yanah_b200.h"
+#include "yanah_b200.h"
 
 namespace ynb {
 

@@ -47,8 +47,21 @@ YN_DEV void load_x_f32(XF32<BITS, CPL, NSEG>& X, const uint16_t* xs_bf16, int l,
 #pragma unroll
   for (int c = 0; c < CPL; ++c) {
     const int k0 = (l + lpr * c) * CPC;
+    if (CPC % 8 == 0) {
 #pragma unroll
-    for (int e = 0; e < CPC; ++e) X.v[c][e] = bf16_to_f32(xs_bf16[k0 + e]);
+      for (int q = 0; q < CPC / 8; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4*>(xs_bf16 + k0 + 8 * q);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          X.v[c][8 * q + 2 * i] = bf16_to_f32((uint16_t)(ww[i] & 0xFFFFu));
+          X.v[c][8 * q + 2 * i + 1] = bf16_to_f32((uint16_t)(ww[i] >> 16));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < CPC; ++e) X.v[c][e] = bf16_to_f32(xs_bf16[k0 + e]);
+    }
 #pragma unroll
     for (int s = 0; s < NSEG; ++s) {
       float a = 0.0f;

@@ -8,7 +8,7 @@
 // one exact int->float conversion, one multiply and one rounding.
 #include <cuda_runtime.h>
 
-#include "../../include/yanah_b200.h"
+#include "yanah_b200.h"
 #include "yn_common.cuh"
 
 namespace ynb {

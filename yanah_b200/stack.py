@@ -49,7 +49,7 @@ class ResidentStack:
         _lib.check(lib.yn_stack_prepare(C.byref(self.dims), arr, n, self.table.data_ptr(), tb))
         sb = int(lib.yn_stack_scratch_bytes(C.byref(self.dims)))
         self.scratch = torch.zeros(sb, dtype=torch.uint8, device=self.device)
-        self.layer_bits = (C.c_int32 * n)(*[cfg.expert_bits[l] for l in self.layer_ids])
+        self.layer_array = arr
         torch.cuda.synchronize(self.device)
 
     @property
@@ -94,7 +94,7 @@ class ResidentStack:
         timing: (L, 8) int64 phase stamps of token 0."""
         lib = _lib.lib()
         n = len(self.structs)
-        _lib.check(lib.yn_stack_decode(C.byref(self.dims), self.table.data_ptr(), n, self.layer_bits,
+        _lib.check(lib.yn_stack_decode(C.byref(self.dims), self.table.data_ptr(), self.layer_array, n,
                                        inputs.data_ptr(), inputs.shape[0], outputs.data_ptr(), self.scratch.data_ptr(),
                                        self.scratch.numel(), trace.data_ptr() if trace is not None else None,
                                        timing.data_ptr() if timing is not None else None, stream_ptr(stream)))
