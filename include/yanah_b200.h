@@ -163,6 +163,29 @@ int yn_moe_down(const yn_dims* dims, const yn_layer* layer, const int32_t* ids, 
 int yn_moe_layer(const yn_dims* dims, const yn_layer* layer, const void* h_in, int32_t T,
                  const yn_layer* targets, int32_t n_targets, void* h_out, void* ws, void* stream);
 
+/* yn_moe_layer without a caller workspace: no counterpart in the reference
+ * (its MLX backend allocates lazily). For callers that cannot allocate device
+ * memory at call time or hand one over: an FFI binding (cgo, ctypes, JNI)
+ * that owns no device allocator, or a process that has already given all free
+ * HBM to the expert slot pool, where a cudaMalloc would fail or fragment it.
+ * Nothing is allocated: the workspace is a file-scope device array of
+ * YN_NOALLOC_SCRATCH_BYTES per device (yn_workspace_bytes(dims) larger than
+ * that returns YN_E_UNSUPPORTED with the two sizes in yn_last_error).
+ * The first call on each device looks up the array's address and zeroes it
+ * with cudaMemsetAsync on `stream`; make that first call before any stream
+ * capture. The error word and the combine counters at the front of the
+ * workspace must start at zero: the counters return to zero at the end of
+ * every call, the error word stays set until yn_workspace_error clears it, and
+ * a call whose counter region reaches further than the last call's zeroes the
+ * extension first. All calls share the one array per device: calls that
+ * overlap in time (different streams, host threads without ordering) race and
+ * give wrong results. scratch_out (optional) receives the array's device
+ * address, for yn_workspace_view / yn_workspace_error. */
+#define YN_NOALLOC_SCRATCH_BYTES (1u << 20)
+int yn_moe_layer_noalloc(const yn_dims* dims, const yn_layer* layer, const void* h_in, int32_t T,
+                         const yn_layer* targets, int32_t n_targets, void* h_out, void* stream,
+                         void** scratch_out);
+
 /* ------------------------------------------------ whole-stack bs1 decode */
 
 /* Persistent decode of `n_tokens` sequential bs1 tokens through `n_layers`

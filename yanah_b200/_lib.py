@@ -67,6 +67,8 @@ _SIGS = {
     "yn_moe_up": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _P, _I, C.POINTER(C.c_int32), _I, _P, _P]),
     "yn_moe_down": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _P, _I, _P, _I, _P, _P, _P]),
     "yn_moe_layer": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _I, C.POINTER(Layer), _I, _P, _P, _P]),
+    "yn_moe_layer_noalloc": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _I, C.POINTER(Layer), _I, _P, _P,
+                                       C.POINTER(C.c_void_p)]),
     "yn_stack_table_bytes": (C.c_size_t, [_I]),
     "yn_stack_scratch_bytes": (C.c_size_t, [C.POINTER(Dims)]),
     "yn_stack_prepare": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _I, _P, C.c_size_t]),

@@ -517,6 +517,57 @@ extern "C" int yn_moe_layer(const yn_dims* dims, const yn_layer* layer, const vo
   return launch_expert_down(*dims, *layer, nullptr, nullptr, T, h_in, 2, h_out, b, W, st);
 }
 
+// ------------------------------------------------- no-allocation variant
+// One workspace per device in static device memory (zero at module load,
+// zeroed again explicitly at set-up). g_na_clean[dev] is the byte offset up
+// to which the front of the array is known to hold zero counters: the
+// counters reset themselves at the end of each call, the bytes behind them
+// may hold a previous call's activations.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[YN_NOALLOC_SCRATCH_BYTES];
+static constexpr int kNaMaxDevices = 64;
+static std::mutex g_na_mu;
+static uint8_t* g_na_ptr[kNaMaxDevices];
+static size_t g_na_clean[kNaMaxDevices];
+
+extern "C" int yn_moe_layer_noalloc(const yn_dims* dims, const yn_layer* layer, const void* h_in, int32_t T,
+                                    const yn_layer* targets, int32_t n_targets, void* h_out, void* stream,
+                                    void** scratch_out) {
+  int rc = check_dims(dims, T);
+  if (rc) return rc;
+  if (!layer || !h_in || !h_out) return fail(YN_E_INVALID, "null argument");
+  if (h_in == h_out) return fail(YN_E_INVALID, "h_in and h_out must not alias");
+  if (n_targets && !targets) return fail(YN_E_INVALID, "targets is null");
+  WsLayout W = ws_layout(*dims);
+  if (W.total > YN_NOALLOC_SCRATCH_BYTES)
+    return fail(YN_E_UNSUPPORTED, "yn_moe_layer_noalloc: workspace of " + std::to_string(W.total) +
+                                      " bytes exceeds the static scratch of " +
+                                      std::to_string((size_t)YN_NOALLOC_SCRATCH_BYTES) + " bytes");
+  int dev = 0;
+  YN_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNaMaxDevices) return fail(YN_E_UNSUPPORTED, "device ordinal out of range");
+  cudaStream_t st = as_stream(stream);
+  const size_t counters_end = W.counters + (size_t)(1 + YN_MAX_ROWS * W.n_cb) * 4;
+  uint8_t* b = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_na_mu);
+    if (!g_na_ptr[dev]) {
+      void* p = nullptr;
+      YN_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+      YN_CUDA(cudaMemsetAsync(p, 0, YN_NOALLOC_SCRATCH_BYTES, st));
+      g_na_ptr[dev] = reinterpret_cast<uint8_t*>(p);
+      g_na_clean[dev] = counters_end;
+    } else if (counters_end > g_na_clean[dev]) {
+      YN_CUDA(cudaMemsetAsync(g_na_ptr[dev] + g_na_clean[dev], 0, counters_end - g_na_clean[dev], st));
+    }
+    g_na_clean[dev] = counters_end;
+    b = g_na_ptr[dev];
+  }
+  if (scratch_out) *scratch_out = b;
+  if ((rc = launch_post_attention(*dims, *layer, h_in, T, targets, n_targets, b, W, st))) return rc;
+  if ((rc = launch_expert_up(*dims, *layer, nullptr, nullptr, T, nullptr, 0, b, W, st))) return rc;
+  return launch_expert_down(*dims, *layer, nullptr, nullptr, T, h_in, 2, h_out, b, W, st);
+}
+
 // ------------------------------------------------------------ slot copy
 extern "C" int yn_slot_copy(void* arena, int64_t slot_stride, const int32_t* slots, const void* const* host_src,
                             int32_t n, int64_t record_bytes, void* stream) {
