@@ -223,8 +223,8 @@ def run_ours(args, rank: int, world: int):
         torch.cuda.get_device_properties(dev), "clock_rate") else 1965.0
     phases = {}
     if tm[0, 0] > 0:
-        names = ["loads", "waitA", "rmsnorm", "p1", "bar1", "route", "plan_issue_xmax", "waitC", "p2", "bar2",
-                 "act_loads", "ascale", "waitD", "p3", "combine"]
+        names = ["loads", "waitA", "rmsnorm", "p1", "bar1", "route", "issue_xmax", "waitC", "p2", "bar2",
+                 "frags", "sgate", "waitD", "p3", "combine"]
         d = np.diff(tm, axis=1) / mhz  # us
         phases = {n: round(float(v), 3) for n, v in zip(names, d.mean(axis=0))}
         if len(layers) > 1:

@@ -1,0 +1,183 @@
+"""Generate the golden fixtures in this directory from the reference's own code.
+
+Run in a container that has the reference checkout (read-only) at
+``/root/reference``; the fixtures it writes are committed, so nothing that
+runs on a GPU machine needs the reference:
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+
+What each fixture pins (the reference function that produced it):
+
+* ``layout.json`` — ``moe_prefetch/layout.py:28-61`` ``ModelGeometry``
+  record/slot sizes and ``quantize_2bit.py:90-103`` ``out_spec`` piece lists
+  (order ``moe_prefetch/repack.py:27-29``) for the record formats the kernels
+  read.
+* ``route.npz`` — ``moe_prefetch/orchestrator.py:141-150`` fallback routing
+  (softmax, top-k by argpartition, renormalise) on tie-free logits.
+* ``rmsnorm.npz`` — ``moe_prefetch/predictor.py:31-34`` ``rms_norm`` (fp32,
+  eps 1e-6) on bf16-valued rows.
+* ``select.npz`` — ``moe_prefetch/predictor.py:100-111``
+  ``RouterForecast.select`` (top candidates in descending probability) on
+  tie-free probability vectors, plus ``observe`` recall counters.
+* ``softmax.npz`` — the fp32 softmax of ``predictor.py:95-97`` (lookahead
+  probabilities) on random logits.
+* ``expert_mlp.npz`` — ``moe_prefetch/test_synthetic.py:46-51``
+  ``expert_mlp`` (fp16 weights, fp32 SwiGLU MLP) on weights that are exactly
+  representable as 4-bit affine codes, so the quantised CUDA/oracle path and
+  the reference's float MLP compute with identical weights.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+
+
+def _bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to the nearest bf16 value (ties to even), returned as fp32."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16 << 16
+    return u.astype(np.uint32).view(np.float32)
+
+
+def _tie_free_logits(rng, T: int, E: int, k: int, gap: float = 0.05) -> np.ndarray:
+    """bf16-valued logits whose k-th and (k+1)-th largest differ by > gap
+    (ties elsewhere do not change the routed set)."""
+    rows = []
+    for _ in range(1000):
+        lg = _bf16_round((rng.standard_normal(E) * 2.0).astype(np.float32))
+        s = np.sort(lg)[::-1]
+        if s[k - 1] - s[k] > gap:
+            rows.append(lg)
+        if len(rows) == T:
+            return np.stack(rows)
+    raise RuntimeError("no tie-free rows found")
+
+
+def make_layout(ref) -> dict:
+    from moe_prefetch.layout import ModelGeometry
+    from moe_prefetch.repack import Piece, RecordSpec
+    from quantize_2bit import out_spec
+
+    geoms = []
+    for kw in (dict(), dict(bits=2, group_size=32), dict(bits=2, group_size=64), dict(bits=8, group_size=64),
+               dict(hidden=2048, moe_inter=1536, n_experts=64, top_k=4, n_layers=40, bits=4, group_size=64)):
+        g = ModelGeometry(**kw)
+        geoms.append({"kwargs": kw, "expert_nbytes": g.expert_nbytes, "slot_nbytes": g.slot_nbytes,
+                      "total_moe_layers": g.total_moe_layers})
+    # the MLX 4-bit g64 source record of a Qwen3-Next expert (H=2048, I=512)
+    H, I = 2048, 512
+    src = []
+    for proj in ("gate_proj", "up_proj", "down_proj"):
+        rows, cols = (H, I) if proj == "down_proj" else (I, H)
+        src += [Piece(f"{proj}.weight", "U32", [rows, cols * 4 // 32], rows * cols // 2),
+                Piece(f"{proj}.scales", "F16", [rows, cols // 64], rows * cols // 64 * 2),
+                Piece(f"{proj}.biases", "F16", [rows, cols // 64], rows * cols // 64 * 2)]
+    src_spec = RecordSpec(src, 64, 4, 48, 1, 512)
+    specs = [{"bits": 4, "group_size": 64, "spec": src_spec.to_json()}]
+    for bits, group in ((2, 32), (2, 64), (4, 128), (8, 64)):
+        specs.append({"bits": bits, "group_size": group, "spec": out_spec(src_spec, 4, bits, group).to_json()})
+    return {"geometries": geoms, "record_specs": specs}
+
+
+def make_route(rng):
+    from moe_prefetch.orchestrator import MoEOrchestrator
+
+    class _G:
+        pass
+
+    out = {}
+    for name, (T, E, k) in {"e512_k10": (6, 512, 10), "e64_k4": (5, 64, 4), "e100_k8": (4, 100, 8)}.items():
+        lg = _tie_free_logits(rng, T, E, k)
+        me = _G()
+        me.b = object()          # a backend without its own `route`
+        me.g = _G()
+        me.g.top_k = k
+        ids, w = MoEOrchestrator.route(me, lg)
+        out[f"{name}_logits"] = lg
+        out[f"{name}_ids"] = np.asarray(ids, np.int64)
+        out[f"{name}_w"] = np.asarray(w, np.float32)
+    return out
+
+
+def make_rmsnorm(rng):
+    from moe_prefetch.predictor import rms_norm
+    h = _bf16_round(rng.standard_normal((3, 2048)).astype(np.float32) * 1.5)
+    w = _bf16_round((1.0 + 0.1 * rng.standard_normal(2048)).astype(np.float32))
+    return {"h": h, "w": w, "out": rms_norm(h, w, 1e-6).astype(np.float32)}
+
+
+def make_select(rng):
+    from moe_prefetch.layout import ModelGeometry
+    from moe_prefetch.predictor import RouterForecast
+    out = {}
+    fc = RouterForecast(ModelGeometry())
+    scores, picks, probs = [], [], []
+    for i in range(6):
+        for _ in range(100):
+            lg = rng.standard_normal(512).astype(np.float32) * 2
+            p = np.exp(lg - lg.max())
+            p = (p / p.sum()).astype(np.float32)
+            if len(np.unique(np.sort(p)[-25:])) == 25:   # the top 25 are distinct
+                break
+        sel = fc.select(3, p, 24)
+        scores.append(p)
+        picks.append([e for e, _ in sel])
+        probs.append([q for _, q in sel])
+        routed = np.argsort(-p)[: 10] if i % 2 == 0 else rng.choice(512, 10, replace=False)
+        fc.observe(3, routed)
+    out["scores"] = np.stack(scores)
+    out["ids"] = np.asarray(picks, np.int64)
+    out["probs"] = np.asarray(probs, np.float64)
+    out["stats"] = np.asarray([fc.stats.forecasts, fc.stats.candidates, fc.stats.actual, fc.stats.covered])
+    return out
+
+
+def make_softmax(rng):
+    lg = (rng.standard_normal((4, 512)) * 3).astype(np.float32)
+    z = lg - lg.max(axis=-1, keepdims=True)
+    p = np.exp(z)
+    p /= p.sum(axis=-1, keepdims=True)
+    return {"logits": lg, "probs": p.astype(np.float32)}
+
+
+def make_expert_mlp(rng):
+    """Codes q in [0,16), scale 2^-5, bias -8*2^-5 per group of 32: every
+    weight (q-8)/32 is exact in fp16, bf16 and fp32."""
+    import moe_prefetch.test_synthetic as ts
+    H, I, gs = ts.G.hidden, ts.G.moe_inter, 32
+    codes = {"gate_proj": rng.integers(0, 16, (I, H)), "up_proj": rng.integers(0, 16, (I, H)),
+             "down_proj": rng.integers(0, 16, (H, I))}
+    w = {k: ((v - 8) / 32.0).astype(np.float16) for k, v in codes.items()}
+    blob = np.concatenate([w["gate_proj"].ravel(), w["up_proj"].ravel(), w["down_proj"].ravel()])
+    x = (np.round(rng.standard_normal((3, H)) * 32) / 32).clip(-4, 4).astype(np.float32)
+    y = np.stack([ts.expert_mlp(blob, x[t]) for t in range(3)]).astype(np.float32)
+    return {"gate_codes": codes["gate_proj"].astype(np.uint8), "up_codes": codes["up_proj"].astype(np.uint8),
+            "down_codes": codes["down_proj"].astype(np.uint8), "group_size": np.int64(gs),
+            "scale": np.float32(1 / 32), "bias": np.float32(-8 / 32), "x": x, "y": y}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    ref = Path(args.reference)
+    sys.path.insert(0, str(ref))
+    rng = np.random.default_rng(20260101)
+    (HERE / "layout.json").write_text(json.dumps(make_layout(ref), indent=1) + "\n")
+    np.savez_compressed(HERE / "route.npz", **make_route(rng))
+    np.savez_compressed(HERE / "rmsnorm.npz", **make_rmsnorm(rng))
+    np.savez_compressed(HERE / "select.npz", **make_select(rng))
+    np.savez_compressed(HERE / "softmax.npz", **make_softmax(rng))
+    np.savez_compressed(HERE / "expert_mlp.npz", **make_expert_mlp(rng))
+    print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
+
+
+if __name__ == "__main__":
+    main()
