@@ -677,9 +677,9 @@ extern "C" int yn_stack_prepare(const yn_dims* dims, const yn_layer* layers, int
 }
 
 // Host mirror of the device P1 partition, for buffer sizing.
-static size_t p1_tile_bytes_max(const yn_dims& d, int G, int gs_r, int gs_s) {
+static size_t p1_tile_bytes_max(int Ish, int G) {
   size_t best = 0;
-  const int E = d.n_experts, Ish = d.shared_inter, H = d.hidden;
+  const int E = DEC_E, H = DEC_H;
   auto unit_at = [&](int c) {
     if (c <= E) return c;
     if (c <= E + 2 * Ish) return E + (c - E + 1) / 2;
@@ -692,13 +692,15 @@ static size_t p1_tile_bytes_max(const yn_dims& d, int G, int gs_r, int gs_s) {
     const size_t nr = std::min(u1, E) - std::min(u0, E);
     const size_t np = std::min(std::max(u1 - E, 0), Ish) - std::min(std::max(u0 - E, 0), Ish);
     const int sg = (Ish > 0 && u0 <= E + Ish && u1 > E + Ish) ? 1 : 0;
-    const size_t sbr = (size_t)(H / gs_r) * 2, sbs = (size_t)(H / gs_s) * 2;
-    size_t o = a16h((size_t)H * 2) + a16h(nr * H) + 2 * a16h(nr * sbr) + 2 * (a16h(np * H) + 2 * a16h(np * sbs)) +
-               (sg ? a16h(H) + 2 * a16h(sbs) : 0);
+    const size_t sb = DEC_DSB;
+    size_t o = a16h((size_t)H * 2) + a16h(nr * H) + 2 * a16h(nr * sb) + 2 * (a16h(np * H) + 2 * a16h(np * sb)) +
+               (sg ? a16h(H) + 2 * a16h(sb) : 0);
     best = std::max(best, o);
   }
   return best;
 }
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
                                const void* inputs, int32_t n_tokens, void* outputs, void* scratch,
@@ -710,72 +712,80 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   if (n_layers < 1 || n_tokens < 1) return fail(YN_E_INVALID, "n_layers and n_tokens must be >= 1");
   StackScratch S = stack_scratch(d);
   if (scratch_bytes < S.total) return fail(YN_E_INVALID, "scratch too small");
-  if (d.top_k > DEC_MAX_K || d.n_experts % 4) return fail(YN_E_UNSUPPORTED, "top_k <= 16 and n_experts % 4 == 0 required");
-  // The persistent kernel is instantiated for rows whose lane mapping matches
-  // H = 2048-class rows (8-bit router CPL from H, routed gate/up CPL 2 at 4-bit
-  // and 1 at 2-bit, down rows CPL 1).
-  const int cpl8 = cpl_of(d.hidden), cpls = d.shared_inter ? cpl_of(d.shared_inter) : 1;
-  int max_bits = 2, min_gs = 1 << 30, min_gs_dense = 1 << 30;
+  const int K = d.top_k, Ish = d.shared_inter;
+  // The persistent kernel is compiled for one shape (index arithmetic on constants).
+  if (d.hidden != DEC_H || d.n_experts != DEC_E || d.moe_inter != DEC_I || (Ish != 0 && Ish != DEC_I) ||
+      K > DEC_MAX_K)
+    return fail(YN_E_UNSUPPORTED, "stack decode is compiled for hidden 2048, 512 experts, intermediate 512 "
+                                  "(shared 0 or 512), top_k <= 16");
+  int rb_max = 0, sb_max = 0, rbi_max = 0, sbi_max = 0;
   for (int l = 0; l < n_layers; ++l) {
-    const int b = layers[l].record.bits;
-    min_gs = std::min(min_gs, (int)layers[l].record.group_size);
-    min_gs_dense = std::min(min_gs_dense, (int)layers[l].router.group_size);
-    if (d.shared_inter) {
-      min_gs_dense = std::min(min_gs_dense, (int)layers[l].shared_gate.group_size);
-      min_gs_dense = std::min(min_gs_dense, (int)layers[l].shared_down.group_size);
-    }
-    if (b != 2 && b != 4) return fail(YN_E_UNSUPPORTED, "stack decode: experts must be 2- or 4-bit");
-    if (cpl_of(d.hidden * b / 8) != (b == 4 ? 2 : 1) || cpl_of(d.moe_inter * b / 8) != 1)
-      return fail(YN_E_UNSUPPORTED, "stack decode: hidden/moe_inter outside the compiled row mapping");
-    max_bits = std::max(max_bits, b);
+    const yn_layer& L = layers[l];
+    const int bits = L.record.bits, gs = L.record.group_size;
+    if ((bits != 2 && bits != 4) || (gs != 32 && gs != 64))
+      return fail(YN_E_UNSUPPORTED, "stack decode: routed experts must be 2- or 4-bit with groups of 32 or 64");
+    if (L.router.group_size != DEC_DGS ||
+        (Ish && (L.shared_gate.group_size != DEC_DGS || L.shared_up.group_size != DEC_DGS ||
+                 L.shared_down.group_size != DEC_DGS || L.shared_expert_gate.group_size != DEC_DGS)))
+      return fail(YN_E_UNSUPPORTED, "stack decode: dense 8-bit matrices must use groups of 64");
+    for (int i = 0; i < 9; ++i)
+      if (L.record.piece_offset[i] % 16) return fail(YN_E_UNSUPPORTED, "stack decode: record pieces must be 16-byte aligned");
+    if (!al16(L.expert_base) || L.slot_stride % 16)
+      return fail(YN_E_UNSUPPORTED, "stack decode: slot arena and stride must be 16-byte aligned");
+    if (!al16(L.router.weight) || !al16(L.router.scales) || !al16(L.router.biases) || !al16(L.post_norm))
+      return fail(YN_E_UNSUPPORTED, "stack decode: router pieces must be 16-byte aligned");
+    if (Ish && (!al16(L.shared_gate.weight) || !al16(L.shared_gate.scales) || !al16(L.shared_gate.biases) ||
+                !al16(L.shared_up.weight) || !al16(L.shared_up.scales) || !al16(L.shared_up.biases) ||
+                !al16(L.shared_down.weight) || !al16(L.shared_down.scales) || !al16(L.shared_down.biases) ||
+                !al16(L.shared_expert_gate.weight) || !al16(L.shared_expert_gate.scales) ||
+                !al16(L.shared_expert_gate.biases)))
+      return fail(YN_E_UNSUPPORTED, "stack decode: shared-expert pieces must be 16-byte aligned");
+    rb_max = std::max(rb_max, DEC_H * bits / 8);
+    sb_max = std::max(sb_max, DEC_H / gs * 2);
+    rbi_max = std::max(rbi_max, DEC_I * bits / 8);
+    sbi_max = std::max(sbi_max, DEC_I / gs * 2);
   }
   int dev = 0, sms = 0;
   YN_CUDA(cudaGetDevice(&dev));
   YN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int G = sms;
-  const int nd_max = (d.hidden + G - 1) / G;
-  if ((d.top_k * d.moe_inter + G - 1) / G > d.moe_inter)
-    return fail(YN_E_UNSUPPORTED, "stack decode: a CTA's gate/up rows must span at most two experts");
-  if (nd_max > DEC_MAX_DROWS) return fail(YN_E_UNSUPPORTED, "hidden too large for the per-CTA row block");
+  const int noct = K * (DEC_I / 8);
+  const int oct_max = (noct + G - 1) / G;
+  if (oct_max > DEC_MAX_OCT) return fail(YN_E_UNSUPPORTED, "stack decode: too many gate/up tiles per CTA");
+  if ((DEC_H + G - 1) / G > DEC_MAX_DROWS) return fail(YN_E_UNSUPPORTED, "stack decode: more than 16 output rows per CTA");
   // shared-memory carve (mirrors the pointer layout at the top of k_stack_decode)
-  const int H = d.hidden, E = d.n_experts, K = d.top_k, I = d.moe_inter, Ish = d.shared_inter;
-  if (I != 512 || (Ish != 0 && Ish != 512))
-    return fail(YN_E_UNSUPPORTED, "stack decode: moe_inter and shared_inter must be 512 (one warp per activation vector)");
-  if (K + 1 > DEC_WARPS) return fail(YN_E_UNSUPPORTED, "stack decode: top_k must be < 16");
-  if (H != 1024 && H != 2048 && H != 4096)
-    return fail(YN_E_UNSUPPORTED, "stack decode: hidden must be 1024, 2048 or 4096");
-  if (2 * ((K * I + G - 1) / G + 1) > 80) return fail(YN_E_UNSUPPORTED, "stack decode: too many gate/up rows per CTA");
-  if ((K + 1) * 8 > 6 * DEC_WARPS) return fail(YN_E_UNSUPPORTED, "stack decode: too many down tiles");
-  if (nd_max > DEC_MAX_DROWS) return fail(YN_E_UNSUPPORTED, "stack decode: more than 16 output rows per CTA");
-  const int gs_max_bits = max_bits;
-  size_t o = 256;
   DecodeArgs a{};
-  a.off_hs = (int)o; o += a16h((size_t)H * 2);
-  a.off_xs = (int)o; o += a16h((size_t)H * 2);
-  a.off_xf = (int)o; o += a16h((size_t)(K + 1) * 8 * 4 * sizeof(XBlock));
+  size_t o = 256;
+  a.off_hs = (int)o; o += a16h((size_t)DEC_H * 2);
+  a.off_xs = (int)o; o += a16h((size_t)DEC_H * 2);
   a.off_route = (int)o;
-  o += a16h(8 * (size_t)E + 4 * DEC_WARPS * DEC_MAX_K + 4 * DEC_MAX_K + 4 * DEC_MAX_K + 4 * (DEC_MAX_K + 4) + 4 * (64 + 256) +
-            3 * sizeof(DecLayer));
-  const int umax = (K * I + G - 1) / G + 1;
-  const int Rmax = 2 * umax;
-  const size_t part_p2 = (size_t)Rmax * (H / 64) * 4, part_p3 = (size_t)(K + 1) * DEC_MAX_DROWS * 8 * 4;
+  o += a16h(4 * (size_t)DEC_E + 4 * DEC_WARPS * DEC_MAX_K + 4 * DEC_MAX_K + 4 * DEC_MAX_K + 4 * (DEC_MAX_K + 4) +
+            4 * 64 + 4 * 256 + 3 * sizeof(DecLayer));
+  a.off_xf2 = (int)o; o += a16h((size_t)DEC_H / 2 * 4 + (size_t)DEC_H / 32 * 4);
+  a.off_xf3 = (int)o; o += a16h((size_t)(DEC_MAX_K + 1) * (DEC_I / 2) * 4 + (size_t)(DEC_MAX_K + 1) * 16 * 4);
+  const size_t part_p2 = (size_t)oct_max * 8 * 2 * 16 * 4, part_p3 = (size_t)(K + 1) * 16 * 8 * 4;
   a.off_part = (int)o; o += a16h(std::max(part_p2, part_p3));
-  const size_t ta = p1_tile_bytes_max(d, G, min_gs_dense, min_gs_dense);
-  a.off_A = (int)o; o += a16h(ta);
-  const size_t rbH = (size_t)H * gs_max_bits / 8, sbH = (size_t)(H / min_gs) * 2;
-  a.off_C = (int)o;  // routed tiles are staged in registers (no shared-memory tile)
-  (void)rbH; (void)sbH;
-  const size_t rbI = (size_t)I * gs_max_bits / 8, sbI = (size_t)(I / min_gs) * 2,
-               sbS = Ish ? (size_t)(Ish / min_gs_dense) * 2 : 0;
-  const size_t td = (size_t)K * DEC_MAX_DROWS * (rbI + 16) + (size_t)DEC_MAX_DROWS * (Ish + 16) +
-                    2 * (size_t)K * DEC_MAX_DROWS * sbI + 2 * (size_t)DEC_MAX_DROWS * sbS;
-  a.off_D = (int)o;
-  (void)td;
+  a.off_A = (int)o; o += a16h(p1_tile_bytes_max(Ish, G));
+  a.c_rows = 8 * oct_max;
+  a.c_rb = rb_max;
+  a.c_sb = sb_max;
+  const size_t c_bytes = std::max((size_t)2 * a.c_rows * a.c_rb + (size_t)4 * a.c_rows * a.c_sb,
+                                  (size_t)(K + 1) * DEC_I * 2);
+  a.off_C = (int)o; o += a16h(c_bytes);
+  a.d_rb = rbi_max;
+  a.d_sb = sbi_max;
+  const size_t d_bytes = (size_t)K * DEC_MAX_DROWS * a.d_rb + (size_t)DEC_MAX_DROWS * DEC_I +
+                         2 * (size_t)K * DEC_MAX_DROWS * a.d_sb + 2 * (size_t)DEC_MAX_DROWS * DEC_DSBI;
+  a.off_D = (int)o; o += a16h(d_bytes);
   const size_t smem = o;
-  if (smem > 227 * 1024) return fail(YN_E_UNSUPPORTED, "stack decode needs " + std::to_string(smem) + " B of shared memory");
+  int optin = 0;
+  YN_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (smem > (size_t)optin)
+    return fail(YN_E_UNSUPPORTED, "stack decode needs " + std::to_string(smem) + " B of shared memory (" +
+                                      std::to_string(optin) + " available)");
 
   uint8_t* sc = reinterpret_cast<uint8_t*>(scratch);
-  a.H = H; a.E = E; a.K = K; a.I = I; a.Ish = Ish; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
+  a.K = K; a.Ish = Ish; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
   a.layers = reinterpret_cast<const DecLayer*>(table);
   a.n_layers = n_layers;
   a.inputs = reinterpret_cast<const uint16_t*>(inputs);
@@ -790,14 +800,12 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   a.bar = reinterpret_cast<unsigned*>(sc + S.bar);
   a.err = reinterpret_cast<int*>(sc + S.err);
   a.timing = reinterpret_cast<long long*>(timing);
+  if (!al16(inputs) || !al16(outputs) || !al16(a.hbuf) || !al16(a.act))
+    return fail(YN_E_INVALID, "stack decode: inputs, outputs and scratch must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
   YN_CUDA(cudaMemsetAsync(a.bar, 0, 4, st));
-  void* kernel = nullptr;
-#define SD(C8, CS) if (!kernel && cpl8 == C8 && cpls == CS) kernel = reinterpret_cast<void*>(&k_stack_decode<C8, CS>);
-  SD(4, 1) SD(4, 2) SD(2, 1) SD(2, 2)
-#undef SD
-  if (!kernel) return fail(YN_E_UNSUPPORTED, "stack decode: no kernel for this hidden / shared size");
-  if ((rc = set_smem(reinterpret_cast<const void*>(kernel), smem))) return rc;
+  const void* kernel = reinterpret_cast<const void*>(&k_stack_decode);
+  if ((rc = set_smem_ptr(kernel, smem))) return rc;
   int per_sm = 0;
   YN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, DEC_THREADS, smem));
   if (per_sm < 1) return fail(YN_E_UNSUPPORTED, "stack decode kernel does not fit on an SM");

@@ -1,22 +1,37 @@
 // Persistent whole-stack bs1 decode kernel (one cooperative launch decodes
 // n_tokens tokens sequentially through every layer).
 //
-// Grid = one CTA per SM (co-resident, cooperative launch), 256 threads.
+// Compiled shape: hidden 2048, 512 experts, expert and shared-expert
+// intermediate 512, top-k <= 16, routed experts 2- or 4-bit with groups of 32
+// or 64, dense matrices (router, shared expert) 8-bit with groups of 64. All
+// index arithmetic uses these constants, and every phase is a short rolled
+// loop, so the hot code of a layer stays small.
+//
+// Grid = one CTA per SM (co-resident, cooperative launch), 512 threads.
 // Per layer three phases separated by grid barriers:
 //   P1  RMSNorm(h) -> router logits, shared-expert gate/up/SwiGLU, shared gate
-//       (each CTA owns a byte-balanced slice of those rows; the tiles were
-//       prefetched into shared memory one whole layer earlier)
-//   P2  routing (every CTA, redundantly, from the 512 logits) -> each CTA
-//       issues bulk copies for its slice of routed gate/up rows (C tiles) and
-//       of the down rows it will need in P3 (D tiles), then computes its
-//       gate/up rows -> SwiGLU activations
-//   P3  each CTA owns a contiguous block of output rows: routed + shared down
-//       projections for those rows, the weighted combine in column order and
-//       the residual -> next h
+//       (each CTA owns a cost-balanced slice of those rows; its tile was
+//       bulk-copied into shared memory during the previous layer). The
+//       tensor-core fragments of the normed row are built here too.
+//   P2  routing (every CTA, redundantly, from the 512 logits); each CTA then
+//       bulk-copies its gate/up rows (tiles of 8 units: 8 gate rows + 8 up
+//       rows of one expert) and the down rows it needs in P3, and computes its
+//       units' SwiGLU activations.
+//   P3  each CTA owns <= 16 consecutive output rows: routed + shared down
+//       projections of those rows, the weighted combine and the residual.
 // Grid barriers are a global counter (release add / acquire poll) with a
 // wall-clock limit; on any error every CTA skips work and leaves at the next
-// barrier. Reference behaviour: orchestrator.py:308-343 layer loop with
-// every expert resident; arithmetic as in the separate layer kernels.
+// barrier. Reference behaviour: moe_prefetch/orchestrator.py:308-343 layer
+// loop with every expert resident (mlx_backend.py:302-316 post-attention and
+// routing, :442-459 routed experts, :438-440 shared expert and combine).
+//
+// Tensor-core GEMV ("super-block" form). A lane owns 16 contiguous bytes of a
+// weight row per super-block (4 lanes = 64 bytes of a row); a 16-row tile of
+// one super-block is a chain of m16n8k16 MMAs in which the 8 N columns of B
+// carry the activation masked to one quantisation group each: column n is
+// nonzero only at the k-slots whose codes belong to group n. D then holds the
+// per-group dot products of each row in separate columns, and the group scale
+// and bias are applied in fp32 afterwards (y = s*D/x_scale + b*sum(x_group)).
 #pragma once
 #include "yn_common.cuh"
 #include "yn_moe.cuh"
@@ -27,8 +42,12 @@ namespace ynb {
 
 constexpr int DEC_THREADS = 512;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
+constexpr int DEC_H = 2048, DEC_E = 512, DEC_I = 512;
 constexpr int DEC_MAX_K = 16;
-constexpr int DEC_MAX_DROWS = 16;  // output rows per CTA in P3 (one MMA tile)
+constexpr int DEC_MAX_OCT = 8;       // gate/up tiles (8 units each) per CTA
+constexpr int DEC_MAX_DROWS = 16;    // output rows per CTA in P3 (one MMA tile)
+constexpr int DEC_DGS = 64;          // group size of the 8-bit dense matrices
+constexpr int DEC_STAMPS = 16;
 
 struct DecLayer {
   const uint16_t* norm;
@@ -43,7 +62,7 @@ struct DecLayer {
 };
 
 struct DecodeArgs {
-  int H, E, K, I, Ish, norm_topk;
+  int K, Ish, norm_topk;
   float eps;
   const DecLayer* layers;
   int n_layers;
@@ -58,9 +77,12 @@ struct DecodeArgs {
   int32_t* trace_ids;  // (n_tokens, n_layers, K) or null
   unsigned* bar;
   int* err;
-  long long* timing;   // (n_layers, 8) for token 0, or null
+  long long* timing;   // (n_layers, DEC_STAMPS) for the last token, or null
   // shared-memory carve (byte offsets)
-  int off_hs, off_xs, off_xf, off_route, off_part, off_A, off_C, off_D;
+  int off_hs, off_xs, off_route, off_xf2, off_xf3, off_part, off_A, off_C, off_D;
+  int c_rows;          // rows reserved per code / scale block of the C tile (8 * max tiles)
+  int c_rb, c_sb;      // bytes reserved per C code row / scale row
+  int d_rb, d_sb;      // bytes reserved per D code row / scale row (routed)
 };
 
 // ---------------------------------------------------------------- barrier
@@ -90,9 +112,7 @@ YN_DEV bool grid_barrier(const DecodeArgs& a, unsigned& gen, int* flag) {
   return *flag != 0;
 }
 
-YN_DEV void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// --------------------------------------------------------------- partition
+// --------------------------------------------------------------- P1 slices
 // P1 units: router rows (cost 1), shared gate/up row pairs (cost 2), the
 // shared_expert_gate row (cost 1); CTA b takes the units whose cumulative
 // cost starts in [b*C/G, (b+1)*C/G).
@@ -101,21 +121,21 @@ struct P1Range {
   int p0, p1;   // shared pairs
   int sg;       // 1 if this CTA owns the shared_expert_gate row
 };
-YN_DEV int p1_unit_at(int c, int E, int Ish) {
-  if (c <= E) return c;
-  if (c <= E + 2 * Ish) return E + (c - E + 1) / 2;
-  return E + Ish + (c - E - 2 * Ish);
+YN_DEV int p1_unit_at(int c, int Ish) {
+  if (c <= DEC_E) return c;
+  if (c <= DEC_E + 2 * Ish) return DEC_E + (c - DEC_E + 1) / 2;
+  return DEC_E + Ish + (c - DEC_E - 2 * Ish);
 }
-YN_DEV P1Range p1_range(int b, int G, int E, int Ish) {
-  const int C = E + 2 * Ish + (Ish ? 1 : 0);
+YN_DEV P1Range p1_range(int b, int G, int Ish) {
+  const int C = DEC_E + 2 * Ish + (Ish ? 1 : 0);
   const int lo = (int)((long long)b * C / G), hi = (int)((long long)(b + 1) * C / G);
-  const int u0 = p1_unit_at(lo, E, Ish), u1 = p1_unit_at(hi, E, Ish);
+  const int u0 = p1_unit_at(lo, Ish), u1 = p1_unit_at(hi, Ish);
   P1Range r;
-  r.r0 = min(u0, E);
-  r.r1 = min(u1, E);
-  r.p0 = min(max(u0 - E, 0), Ish);
-  r.p1 = min(max(u1 - E, 0), Ish);
-  r.sg = (Ish > 0 && u0 <= E + Ish && u1 > E + Ish) ? 1 : 0;
+  r.r0 = min(u0, DEC_E);
+  r.r1 = min(u1, DEC_E);
+  r.p0 = min(max(u0 - DEC_E, 0), Ish);
+  r.p1 = min(max(u1 - DEC_E, 0), Ish);
+  r.sg = (Ish > 0 && u0 <= DEC_E + Ish && u1 > DEC_E + Ish) ? 1 : 0;
   return r;
 }
 
@@ -130,38 +150,35 @@ struct P1Tile {
 };
 
 YN_DEV size_t a16d(size_t v) { return (v + 15) & ~size_t(15); }
+constexpr int DEC_DSB = DEC_H / DEC_DGS * 2;   // scale-row bytes of a dense 2048-column matrix
 
-YN_DEV P1Tile p1_tile(uint8_t* base, const P1Range& r, int H, int gs_r, int gs_s) {
+YN_DEV P1Tile p1_tile(uint8_t* base, const P1Range& r) {
   P1Tile t;
   size_t o = 0;
   const size_t nr = r.r1 - r.r0, np = r.p1 - r.p0;
-  const size_t sbr = (size_t)(H / gs_r) * 2, sbs = (size_t)(H / gs_s) * 2;
-  t.norm = (uint16_t*)(base + o); o += a16d((size_t)H * 2);
-  t.rc = base + o; o += a16d(nr * H);
-  t.rs = (uint16_t*)(base + o); o += a16d(nr * sbr);
-  t.rbv = (uint16_t*)(base + o); o += a16d(nr * sbr);
-  t.gc = base + o; o += a16d(np * H);
-  t.gsc = (uint16_t*)(base + o); o += a16d(np * sbs);
-  t.gbi = (uint16_t*)(base + o); o += a16d(np * sbs);
-  t.uc = base + o; o += a16d(np * H);
-  t.usc = (uint16_t*)(base + o); o += a16d(np * sbs);
-  t.ubi = (uint16_t*)(base + o); o += a16d(np * sbs);
-  t.sc = base + o; o += a16d(r.sg ? (size_t)H : 0);
-  t.ssc = (uint16_t*)(base + o); o += a16d(r.sg ? sbs : 0);
-  t.sbi = (uint16_t*)(base + o); o += a16d(r.sg ? sbs : 0);
+  t.norm = (uint16_t*)(base + o); o += a16d((size_t)DEC_H * 2);
+  t.rc = base + o; o += a16d(nr * DEC_H);
+  t.rs = (uint16_t*)(base + o); o += a16d(nr * DEC_DSB);
+  t.rbv = (uint16_t*)(base + o); o += a16d(nr * DEC_DSB);
+  t.gc = base + o; o += a16d(np * DEC_H);
+  t.gsc = (uint16_t*)(base + o); o += a16d(np * DEC_DSB);
+  t.gbi = (uint16_t*)(base + o); o += a16d(np * DEC_DSB);
+  t.uc = base + o; o += a16d(np * DEC_H);
+  t.usc = (uint16_t*)(base + o); o += a16d(np * DEC_DSB);
+  t.ubi = (uint16_t*)(base + o); o += a16d(np * DEC_DSB);
+  t.sc = base + o; o += a16d(r.sg ? (size_t)DEC_H : 0);
+  t.ssc = (uint16_t*)(base + o); o += a16d(r.sg ? DEC_DSB : 0);
+  t.sbi = (uint16_t*)(base + o); o += a16d(r.sg ? DEC_DSB : 0);
   return t;
 }
 
-YN_DEV int shared_gs(const DecLayer& L) { return L.sg.gs ? L.sg.gs : 64; }
-
 // One warp: issue the bulk copies of one layer's P1 tile (every CTA also
 // takes the whole norm weight); lane i issues piece i.
-YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, int H, uint64_t* bar) {
+YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint64_t* bar) {
   const int lane = threadIdx.x & 31;
-  const uint32_t sbr = (uint32_t)(H / L.router.gs) * 2;
   const uint32_t nr = r.r1 - r.r0, np = r.p1 - r.p0;
-  const uint32_t sbs = L.sg.gs ? (uint32_t)(H / L.sg.gs) * 2 : 0;
-  const uint32_t tx = (uint32_t)H * 2 + nr * (H + 2 * sbr) + np * 2 * (H + 2 * sbs) + (r.sg ? H + 2 * sbs : 0);
+  const uint32_t tx = (uint32_t)DEC_H * 2 + nr * (DEC_H + 2 * DEC_DSB) + np * 2 * (DEC_H + 2 * DEC_DSB) +
+                      (r.sg ? DEC_H + 2 * DEC_DSB : 0);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   if (lane == 0) mbar_arrive_expect_tx(bar, tx);
   __syncwarp();
@@ -171,105 +188,139 @@ YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, int H
   const uint8_t* rs = reinterpret_cast<const uint8_t*>(L.router.s);
   const uint8_t* rb = reinterpret_cast<const uint8_t*>(L.router.b);
   switch (lane) {
-    case 0: dst = t.norm; src = L.norm; bytes = (uint32_t)H * 2; break;
-    case 1: dst = t.rc; src = L.router.w + (size_t)r.r0 * H; bytes = nr * H; break;
-    case 2: dst = t.rs; src = rs + (size_t)r.r0 * sbr; bytes = nr * sbr; break;
-    case 3: dst = t.rbv; src = rb + (size_t)r.r0 * sbr; bytes = nr * sbr; break;
-    case 4: dst = t.gc; src = L.sg.w + (size_t)r.p0 * H; bytes = np * H; break;
-    case 5: dst = t.gsc; src = reinterpret_cast<const uint8_t*>(L.sg.s) + (size_t)r.p0 * sbs; bytes = np * sbs; break;
-    case 6: dst = t.gbi; src = reinterpret_cast<const uint8_t*>(L.sg.b) + (size_t)r.p0 * sbs; bytes = np * sbs; break;
-    case 7: dst = t.uc; src = L.su.w + (size_t)r.p0 * H; bytes = np * H; break;
-    case 8: dst = t.usc; src = reinterpret_cast<const uint8_t*>(L.su.s) + (size_t)r.p0 * sbs; bytes = np * sbs; break;
-    case 9: dst = t.ubi; src = reinterpret_cast<const uint8_t*>(L.su.b) + (size_t)r.p0 * sbs; bytes = np * sbs; break;
-    case 10: dst = t.sc; src = L.sgt.w; bytes = r.sg ? (uint32_t)H : 0u; break;
-    case 11: dst = t.ssc; src = L.sgt.s; bytes = r.sg ? sbs : 0u; break;
-    case 12: dst = t.sbi; src = L.sgt.b; bytes = r.sg ? sbs : 0u; break;
+    case 0: dst = t.norm; src = L.norm; bytes = (uint32_t)DEC_H * 2; break;
+    case 1: dst = t.rc; src = L.router.w + (size_t)r.r0 * DEC_H; bytes = nr * DEC_H; break;
+    case 2: dst = t.rs; src = rs + (size_t)r.r0 * DEC_DSB; bytes = nr * DEC_DSB; break;
+    case 3: dst = t.rbv; src = rb + (size_t)r.r0 * DEC_DSB; bytes = nr * DEC_DSB; break;
+    case 4: dst = t.gc; src = L.sg.w + (size_t)r.p0 * DEC_H; bytes = np * DEC_H; break;
+    case 5: dst = t.gsc; src = reinterpret_cast<const uint8_t*>(L.sg.s) + (size_t)r.p0 * DEC_DSB; bytes = np * DEC_DSB; break;
+    case 6: dst = t.gbi; src = reinterpret_cast<const uint8_t*>(L.sg.b) + (size_t)r.p0 * DEC_DSB; bytes = np * DEC_DSB; break;
+    case 7: dst = t.uc; src = L.su.w + (size_t)r.p0 * DEC_H; bytes = np * DEC_H; break;
+    case 8: dst = t.usc; src = reinterpret_cast<const uint8_t*>(L.su.s) + (size_t)r.p0 * DEC_DSB; bytes = np * DEC_DSB; break;
+    case 9: dst = t.ubi; src = reinterpret_cast<const uint8_t*>(L.su.b) + (size_t)r.p0 * DEC_DSB; bytes = np * DEC_DSB; break;
+    case 10: dst = t.sc; src = L.sgt.w; bytes = r.sg ? (uint32_t)DEC_H : 0u; break;
+    case 11: dst = t.ssc; src = L.sgt.s; bytes = r.sg ? (uint32_t)DEC_DSB : 0u; break;
+    case 12: dst = t.sbi; src = L.sgt.b; bytes = r.sg ? (uint32_t)DEC_DSB : 0u; break;
     default: break;
   }
   if (bytes) bulk_g2s(dst, src, bytes, bar);
   __syncwarp();
 }
 
+// RMSNorm in the canonical 128-thread order (threads 128.. idle in the sum).
+YN_DEV void rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uint16_t* out, float* red) {
+  const int tid = threadIdx.x;
+  float ss = 0.0f;
+  if (tid < 128)
+    for (int i = tid; i < DEC_H; i += 128) {
+      const float v = bf16_to_f32(h[i]);
+      ss = __fmaf_rn(v, v, ss);
+    }
+  if (tid < 128) {
+    ss = group_sum_bfly(ss, 32);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+  }
+  __syncthreads();
+  const float tot = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)DEC_H), eps));
+  for (int i = tid; i < DEC_H; i += DEC_THREADS)
+    out[i] = f32_to_bf16(__fmul_rn(bf16_to_f32(w_g[i]), bf16r(__fmul_rn(bf16_to_f32(h[i]), r))));
+  __syncthreads();
+}
+
+// P1 compute: router rows, shared pairs, shared_expert_gate (canonical fp32
+// row dot, one row per warp step, bit-exact with the oracle).
+YN_DEV void p1_compute(const DecodeArgs& a, const P1Range& r, const P1Tile& t, const uint16_t* xs,
+                       const float* rbias_s, float* gu) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int LPR = 32, CPL = DEC_H / 16 / LPR;
+  constexpr int NGD = DEC_H / DEC_DGS;
+  XF32<8, CPL, 1> X;
+  load_x_f32<8, CPL, 1>(X, xs, lane, LPR);
+  const int nr = r.r1 - r.r0, np = r.p1 - r.p0;
+  const int ntask = nr + 2 * np + r.sg;
+  for (int k = warp; k < ntask; k += DEC_WARPS) {
+    const uint8_t* cr;
+    const uint16_t* sr;
+    const uint16_t* br;
+    if (k < nr) {
+      cr = t.rc + (size_t)k * DEC_H; sr = t.rs + k * NGD; br = t.rbv + k * NGD;
+    } else if (k < nr + 2 * np) {
+      const int q = k - nr, p = q >> 1;
+      if (q & 1) { cr = t.uc + (size_t)p * DEC_H; sr = t.usc + p * NGD; br = t.ubi + p * NGD; }
+      else { cr = t.gc + (size_t)p * DEC_H; sr = t.gsc + p * NGD; br = t.gbi + p * NGD; }
+    } else {
+      cr = t.sc; sr = t.ssc; br = t.sbi;
+    }
+    float v = row_dot_f32<8, CPL, 1>(cr, sr, br, X, lane, LPR, DEC_DGS);
+    v = group_sum_bfly(v, LPR);
+    if (lane == 0) {
+      if (k < nr) a.logits[r.r0 + k] = bf16r(__fadd_rn(v, rbias_s[k]));
+      else if (k < nr + 2 * np) gu[k - nr] = bf16r(v);
+      else a.sgate[0] = bf16r(sigmoid_f32(bf16r(v)));
+    }
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < np; p += DEC_THREADS)
+    a.act_sh[r.p0 + p] = f32_to_bf16(swiglu_bf16(gu[2 * p], gu[2 * p + 1]));
+}
+
 // ------------------------------------------------------------------ routing
-// Block-wide routing of one row of logits (global, E <= 1024) with the
+// Block-wide routing of the 512 logits (thread t <-> expert t) in the
 // canonical order of the oracle: max (order-free), exp per element, sum per
 // lane over e = lane + 32 i then a butterfly (warp 0), bf16 probabilities,
 // then top-k by the unique key (bf16 prob << 16 | 0xFFFF - id): per-warp
-// top-k over a slice, merged by warp 0. Results in shared memory.
-YN_DEV void route_block(const float* logits_g, int E, int K, int norm, float* v /* E */, uint32_t* keys /* E */,
-                        uint32_t* cand /* DEC_WARPS*K */, float* red, int32_t* ids_out, float* w_out) {
+// top-k over its 32 experts, merged by warp 0. Results in shared memory.
+YN_DEV void route_block(const float* logits_g, int K, int norm, float* v /* E */, uint32_t* cand /* 16*16 */,
+                        float* red, int32_t* ids_out, float* w_out) {
+  static_assert(DEC_E == DEC_THREADS, "one expert per thread");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float m = -INFINITY;
-  for (int e = tid; e < E; e += DEC_THREADS) {
-    const float x = __ldcg(logits_g + e);
-    v[e] = x;
-    m = fmaxf(m, x);
-  }
-  m = warp_max(m);
+  const float x = __ldcg(logits_g + tid);
+  float m = warp_max(x);
   if (lane == 0) red[warp] = m;
   __syncthreads();
-  m = red[0];
-#pragma unroll
-  for (int w = 1; w < DEC_WARPS; ++w) m = fmaxf(m, red[w]);
-  for (int e = tid; e < E; e += DEC_THREADS) v[e] = yn_expf(__fsub_rn(v[e], m));
+  m = red[lane & 15];
+  m = warp_max(m);
+  v[tid] = yn_expf(__fsub_rn(x, m));
   __syncthreads();
   if (warp == 0) {
     float s = 0.0f;
-    for (int e = lane; e < E; e += 32) s = __fadd_rn(s, v[e]);
+#pragma unroll
+    for (int i = 0; i < DEC_E / 32; ++i) s = __fadd_rn(s, v[lane + 32 * i]);
     s = group_sum_bfly(s, 32);
-    if (lane == 0) red[8] = s;
+    if (lane == 0) red[16] = s;
   }
   __syncthreads();
-  const float S = red[8];
-  for (int e = tid; e < E; e += DEC_THREADS) {
-    const float p = bf16r(__fdiv_rn(v[e], S));
-    v[e] = p;
-    keys[e] = ((uint32_t)f32_to_bf16(p) << 16) | (uint32_t)(0xFFFF - e);
-  }
-  __syncthreads();
-  // per-warp top-K over slice [w*E/8, (w+1)*E/8)
-  {
-    const int lo = warp * E / DEC_WARPS, hi = (warp + 1) * E / DEC_WARPS;
-    uint32_t mine[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = lo + lane + 32 * i;
-      mine[i] = (e < hi) ? keys[e] : 0u;
-    }
-    for (int j = 0; j < K; ++j) {
-      uint32_t best = 0;
-      int bi = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (mine[i] > best) { best = mine[i]; bi = i; }
-      const uint32_t top = __reduce_max_sync(0xffffffffu, best);
-      if (best == top && top != 0u) mine[bi] = 0u;
-      if (lane == 0) cand[warp * K + j] = top;
-    }
+  const float p = bf16r(__fdiv_rn(v[tid], red[16]));
+  uint32_t key = ((uint32_t)f32_to_bf16(p) << 16) | (uint32_t)(0xFFFF - tid);
+  for (int j = 0; j < K; ++j) {
+    const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+    if (key == top) key = 0u;
+    if (lane == 0) cand[warp * DEC_MAX_K + j] = top;
   }
   __syncthreads();
   if (warp == 0) {
-    uint32_t mine[(DEC_WARPS * DEC_MAX_K + 31) / 32];
-    const int nc = DEC_WARPS * K;
+    constexpr int NC = DEC_WARPS * DEC_MAX_K / 32;
+    uint32_t mine[NC];
 #pragma unroll
-    for (int i = 0; i < (DEC_WARPS * DEC_MAX_K + 31) / 32; ++i) {
-      const int c = lane + 32 * i;
-      mine[i] = (c < nc) ? cand[c] : 0u;
+    for (int i = 0; i < NC; ++i) {
+      const int cix = lane + 32 * i;
+      mine[i] = ((cix % DEC_MAX_K) < K) ? cand[cix] : 0u;
     }
     float wsum = 0.0f, myp = 0.0f;
     int myid = 0;
     for (int j = 0; j < K; ++j) {
       uint32_t best = 0;
-      int bi = 0;
 #pragma unroll
-      for (int i = 0; i < (DEC_WARPS * DEC_MAX_K + 31) / 32; ++i)
-        if (mine[i] > best) { best = mine[i]; bi = i; }
+      for (int i = 0; i < NC; ++i) best = max(best, mine[i]);
       const uint32_t top = __reduce_max_sync(0xffffffffu, best);
-      if (best == top) mine[bi] = 0u;
-      const float p = bf16_to_f32((uint16_t)(top >> 16));
-      wsum = __fadd_rn(wsum, p);
+#pragma unroll
+      for (int i = 0; i < NC; ++i)
+        if (mine[i] == top) mine[i] = 0u;
+      const float pj = bf16_to_f32((uint16_t)(top >> 16));
+      wsum = __fadd_rn(wsum, pj);
       if (lane == j) {
-        myp = p;
+        myp = pj;
         myid = 0xFFFF - (int)(top & 0xFFFFu);
       }
     }
@@ -282,425 +333,363 @@ YN_DEV void route_block(const float* logits_g, int E, int K, int norm, float* v 
   __syncthreads();
 }
 
-// RMSNorm in the canonical 128-thread order (threads 128.. idle in the sum).
-YN_DEV void rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, int H, float eps, uint16_t* out, float* red) {
-  const int tid = threadIdx.x;
-  float ss = 0.0f;
-  if (tid < 128)
-    for (int i = tid; i < H; i += 128) {
-      const float v = bf16_to_f32(h[i]);
-      ss = __fmaf_rn(v, v, ss);
+// ------------------------------------------------------- super-block GEMV
+template <int BITS>
+struct Sb {
+  static constexpr int W = MmaFmt<BITS>::WORDS;  // code words per 8-pair unpack unit
+  static constexpr int U = 4 / W;                 // units per lane per super-block
+  static constexpr int CPL = 16 * U;              // codes per lane
+  static constexpr int CODES = 4 * CPL;           // codes per row per super-block (64 bytes)
+  static constexpr int FRAG = 8 * U;              // activation fragment words per lane
+};
+
+// Fragment word w of lane c of super-block sb of a bf16 vector x: the pair
+// (x[lo], x[hi]) of unpack pair p = w % 8 of unit u = w / 8, pre-scaled by
+// `scale` and divided by the pair's code multiplier, as fp16.
+template <int BITS>
+YN_DEV uint32_t frag_word(const uint16_t* x, float scale, int sb, int c, int w) {
+  using S = Sb<BITS>;
+  const int u = w >> 3, p = w & 7;
+  const int base = sb * S::CODES + c * S::CPL + 16 * u;
+  const float m = __fmul_rn(scale, MmaFmt<BITS>::inv_mult(p));
+  __half2 h = __floats2half2_rn(__fmul_rn(bf16_to_f32(x[base + MmaFmt<BITS>::lo(p)]), m),
+                                __fmul_rn(bf16_to_f32(x[base + MmaFmt<BITS>::hi(p)]), m));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Fragments of an n-code vector: word index i = ((sb * 4 + c) * FRAG + w).
+template <int BITS>
+YN_DEV void build_frags(const uint16_t* x, int n, float scale, uint32_t* out, int t0, int nthreads) {
+  using S = Sb<BITS>;
+  for (int i = t0; i < n / 2; i += nthreads) {
+    const int sb = i / (4 * S::FRAG), rem = i % (4 * S::FRAG);
+    out[i] = frag_word<BITS>(x, scale, sb, rem / S::FRAG, rem % S::FRAG);
+  }
+}
+
+// One 16-row tile x one super-block. rg / rg8: this lane's 16 bytes of rows g
+// and g+8; xf: lane c's fragment words. d = D[g][2c], D[g][2c+1],
+// D[g+8][2c], D[g+8][2c+1]; column n = dot over group n of the super-block
+// (times the activation scale).
+template <int BITS, int GS>
+YN_DEV void sb_mma(const uint8_t* rg, const uint8_t* rg8, const uint32_t* xf, int g, int c, float (&d)[4]) {
+  using S = Sb<BITS>;
+  const uint4 va = *reinterpret_cast<const uint4*>(rg);
+  const uint4 vb = *reinterpret_cast<const uint4*>(rg8);
+  const uint32_t wa[4] = {va.x, va.y, va.z, va.w}, wb[4] = {vb.x, vb.y, vb.z, vb.w};
+  float acc[S::U][4];
+#pragma unroll
+  for (int u = 0; u < S::U; ++u) {
+    acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
+    uint32_t pa[8], pb[8];
+    MmaFmt<BITS>::unpack(wa + u * S::W, pa);
+    MmaFmt<BITS>::unpack(wb + u * S::W, pb);
+    uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
+    if ((c * S::CPL + 16 * u) / GS == g) {
+      x0 = reinterpret_cast<const uint4*>(xf)[2 * u];
+      x1 = reinterpret_cast<const uint4*>(xf)[2 * u + 1];
     }
-  ss = group_sum_bfly(ss, 32);
-  __syncthreads();
-  if ((tid & 31) == 0 && tid < 128) red[tid >> 5] = ss;
-  __syncthreads();
-  const float tot = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), eps)));
-  for (int i = tid; i < H; i += DEC_THREADS)
-    out[i] = f32_to_bf16(__fmul_rn(bf16_to_f32(w_g[i]), bf16r(__fmul_rn(bf16_to_f32(h[i]), r))));
-  __syncthreads();
+    const uint32_t xb[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t A[4] = {pa[2 * m], pb[2 * m], pa[2 * m + 1], pb[2 * m + 1]};
+      const uint32_t B[2] = {xb[2 * m], xb[2 * m + 1]};
+      mma16816(acc[u], A, B);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float s = acc[0][i];
+#pragma unroll
+    for (int u = 1; u < S::U; ++u) s = __fadd_rn(s, acc[u][i]);
+    d[i] = s;
+  }
+}
+
+// Scale and bias of one row's two groups (columns 2c, 2c+1 of super-block sb),
+// summed over the lane quad: every lane of the quad returns the row's
+// super-block partial. s_row / b_row: fp16 scale / bias rows; xsum: group sums.
+template <int BITS, int GS>
+YN_DEV float sb_apply(float d0, float d1, const uint16_t* s_row, const uint16_t* b_row, const float* xsum, int sb,
+                      int c, float inv) {
+  constexpr int NG = Sb<BITS>::CODES / GS;
+  float v = 0.0f;
+  if (2 * c < NG) {
+    const int gi = sb * NG + 2 * c;
+    if (NG >= 2) {
+      const uint32_t s2 = *reinterpret_cast<const uint32_t*>(s_row + gi);
+      const uint32_t b2 = *reinterpret_cast<const uint32_t*>(b_row + gi);
+      v = __fmaf_rn(f16_to_f32((uint16_t)(s2 & 0xFFFFu)), __fmul_rn(d0, inv),
+                    __fmul_rn(f16_to_f32((uint16_t)(b2 & 0xFFFFu)), xsum[gi]));
+      v = __fadd_rn(v, __fmaf_rn(f16_to_f32((uint16_t)(s2 >> 16)), __fmul_rn(d1, inv),
+                                 __fmul_rn(f16_to_f32((uint16_t)(b2 >> 16)), xsum[gi + 1])));
+    } else {
+      v = __fmaf_rn(f16_to_f32(s_row[gi]), __fmul_rn(d0, inv), __fmul_rn(f16_to_f32(b_row[gi]), xsum[gi]));
+    }
+  }
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  return v;
+}
+
+// Group sums over groups of GS codes: thread i sums codes [16i, 16i+16) of
+// x, then a butterfly over the GS/16 consecutive threads of a group; the
+// first of them writes out[i / (GS/16)]. Every lane of the calling warp
+// takes part (valid = false contributes nothing and writes nothing).
+template <int GS>
+YN_DEV void group_sums16(const uint16_t* x, int i, bool valid, float* out) {
+  float s = 0.0f;
+  if (valid) {
+    const uint4 q0 = reinterpret_cast<const uint4*>(x + 16 * i)[0];
+    const uint4 q1 = reinterpret_cast<const uint4*>(x + 16 * i)[1];
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      s = __fadd_rn(s, bf16_to_f32((uint16_t)(w[k] & 0xFFFFu)));
+      s = __fadd_rn(s, bf16_to_f32((uint16_t)(w[k] >> 16)));
+    }
+  }
+  s = group_sum_bfly(s, GS / 16);
+  if (valid && i % (GS / 16) == 0) out[i / (GS / 16)] = s;
 }
 
 // ------------------------------------------------------------ P2 / P3 tiles
-// Shared-memory layout of this CTA's routed gate/up rows ("C rows"): the
-// rows of at most two (column, row-range) segments, ordered seg0 gate, seg0
-// up, seg1 gate, seg1 up; codes with a padded stride, scales and biases dense.
-struct CPlan {
-  int nseg;
-  int j[2], n0[2], nr[2];   // column, first row, rows
-  int R;                    // total C rows (2 * sum nr)
-  int rs;                   // padded code-row stride
+// C tile (gate/up rows of this CTA's units), in shared memory:
+//   codes: gate rows [c_rows][c_rb] then up rows [c_rows][c_rb];
+//   scales/biases: gate scales, gate biases, up scales, up biases [c_rows][c_sb].
+// Tile t (8 units) = C rows 8t..8t+7; a CTA's tiles span at most two experts
+// ("segments"), whose rows are copied back to back.
+struct CSeg {
+  int n;       // segments (0..2)
+  int j[2];    // routed column of each segment
+  int n0[2];   // first unit row inside the expert
+  int rows[2]; // units in the segment
 };
-
-YN_DEV CPlan c_plan(int u0, int u1, int I, int rbH) {
-  CPlan p;
-  p.nseg = 0;
-  p.R = 0;
-  p.rs = rbH + 16;
-  for (int u = u0; u < u1 && p.nseg < 2;) {
-    const int j = u / I, n0 = u % I, n1 = min(I, n0 + (u1 - u));
-    p.j[p.nseg] = j; p.n0[p.nseg] = n0; p.nr[p.nseg] = n1 - n0;
-    p.R += 2 * (n1 - n0);
-    ++p.nseg;
-    u += n1 - n0;
+YN_DEV CSeg c_segments(int o0, int o1) {
+  CSeg s;
+  s.n = 0;
+  for (int o = o0; o < o1 && s.n < 2;) {
+    const int j = o / (DEC_I / 8), oe = min(o1, (j + 1) * (DEC_I / 8));
+    s.j[s.n] = j;
+    s.n0[s.n] = (o % (DEC_I / 8)) * 8;
+    s.rows[s.n] = (oe - o) * 8;
+    ++s.n;
+    o = oe;
   }
-  return p;
-}
-// C row r -> (segment, up?, row inside the segment)
-YN_DEV void c_row(const CPlan& p, int r, int& s, int& up, int& n) {
-  const int r0 = 2 * p.nr[0];
-  s = (r >= r0) ? 1 : 0;
-  const int rr = s ? r - r0 : r;
-  up = rr >= p.nr[s] ? 1 : 0;
-  n = up ? rr - p.nr[s] : rr;
+  return s;
 }
 
-// All warps: 16-byte asynchronous copies of this CTA's C rows (one commit
-// group) then D rows (a second group). A warp takes a row at a time; its
-// lanes take the row's 16-byte chunks, so rows land at a padded stride.
-struct DLayout {  // D tile: per column a 16-row block at stride rsI, then the shared tile
-  uint32_t rbI, sbI, rsI, rsS, sbS;
-  size_t dsh, dsc, dbi, ssc, sbi;
+YN_DEV const uint8_t* expert_record(const DecLayer& L, int e) {
+  return L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
+}
+
+// Lanes of one warp issue this CTA's C-tile copies (one piece per lane).
+template <int BITS, int GS>
+YN_DEV void issue_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, uint8_t* C,
+                    uint64_t* bar) {
+  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rows = (uint32_t)(sg.rows[0] + (sg.n > 1 ? sg.rows[1] : 0));
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (lane == 0) mbar_arrive_expect_tx(bar, rows * (2u * RB + 4u * SBH));
+  __syncwarp();
+  if (lane < 6 * sg.n) {
+    const int s = lane / 6, piece = lane % 6;  // gate w, s, b, up w, s, b
+    const uint8_t* rec = expert_record(L, ids[sg.j[s]]);
+    const int prow = s ? sg.rows[0] : 0;       // destination row of the segment
+    const int kind = piece % 3, up = piece / 3;
+    uint8_t* dst;
+    uint32_t rb;
+    if (kind == 0) {
+      rb = RB;
+      dst = C + (size_t)up * a.c_rows * a.c_rb + (size_t)prow * RB;
+    } else {
+      rb = SBH;
+      dst = C + (size_t)2 * a.c_rows * a.c_rb + (size_t)(2 * up + kind - 1) * a.c_rows * a.c_sb + (size_t)prow * SBH;
+    }
+    const uint8_t* src = rec + L.rg.off[3 * up + kind] + (size_t)sg.n0[s] * rb;
+    bulk_g2s(dst, src, (uint32_t)sg.rows[s] * rb, bar);
+  }
+  __syncwarp();
+}
+
+// D tile (down rows [d0, d0+nd) of every routed column and of the shared
+// expert): codes [K][16][RBI] then shared [16][Ish]; scales / biases
+// [K][16][SBI] each, then shared scales / biases [16][DEC_DSBI].
+constexpr int DEC_DSBI = DEC_I / DEC_DGS * 2;  // scale-row bytes of the shared down_proj
+struct DOff {
+  size_t sh, rs, rb, ss, sb;
 };
-YN_DEV DLayout d_layout(const DecodeArgs& a, const DecLayer& L) {
-  DLayout d;
-  const int bits = L.rg.bits, gs = L.rg.gs, K = a.K, Ish = a.Ish;
-  d.rbI = (uint32_t)(a.I * bits / 8);
-  d.sbI = (uint32_t)(a.I / gs) * 2;
-  d.rsI = d.rbI + 16;
-  d.rsS = (uint32_t)Ish + 16;
-  d.sbS = Ish ? (uint32_t)(Ish / L.sd.gs) * 2 : 0;
-  d.dsh = (size_t)K * DEC_MAX_DROWS * d.rsI;
-  d.dsc = d.dsh + (size_t)DEC_MAX_DROWS * d.rsS;
-  d.dbi = d.dsc + (size_t)K * DEC_MAX_DROWS * d.sbI;
-  d.ssc = d.dbi + (size_t)K * DEC_MAX_DROWS * d.sbI;
-  d.sbi = d.ssc + (size_t)DEC_MAX_DROWS * d.sbS;
-  return d;
+YN_DEV DOff d_offsets(const DecodeArgs& a) {
+  DOff o;
+  o.sh = (size_t)a.K * DEC_MAX_DROWS * a.d_rb;
+  o.rs = o.sh + (size_t)DEC_MAX_DROWS * DEC_I;
+  o.rb = o.rs + (size_t)a.K * DEC_MAX_DROWS * a.d_sb;
+  o.ss = o.rb + (size_t)a.K * DEC_MAX_DROWS * a.d_sb;
+  o.sb = o.ss + (size_t)DEC_MAX_DROWS * DEC_DSBI;
+  return o;
 }
 
-// One warp: pull this CTA's D pieces (rows [d0, d0+nd) of every column's
-// down_proj codes/scales/biases and of the shared down_proj) into L2 with
-// bulk prefetches, so the P3 register loads hit L2.
-YN_DEV void prefetch_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd) {
+// Lanes of one warp issue the D-tile copies: piece i = (column j = i / 3,
+// kind = i % 3); j == K is the shared expert.
+template <int BITS, int GS>
+YN_DEV void issue_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd, uint8_t* D,
+                    uint64_t* bar) {
+  constexpr int RBI = DEC_I * BITS / 8, SBI = DEC_I / GS * 2;
   const int lane = threadIdx.x & 31, K = a.K;
-  const DLayout dl = d_layout(a, L);
-  for (int i = lane; i < 3 * K + (a.Ish ? 3 : 0); i += 32) {
-    const int j = i / 3, piece = i % 3;
+  const DOff o = d_offsets(a);
+  const uint32_t tx = (uint32_t)nd * ((uint32_t)K * (RBI + 2 * SBI) + (a.Ish ? DEC_I + 2 * DEC_DSBI : 0));
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (lane == 0) mbar_arrive_expect_tx(bar, tx);
+  __syncwarp();
+  const int npieces = 3 * K + (a.Ish ? 3 : 0);
+  for (int i = lane; i < npieces; i += 32) {
+    const int j = i / 3, kind = i % 3;
     const uint8_t* src;
-    uint32_t bytes;
+    uint8_t* dst;
+    uint32_t rb;
     if (j < K) {
-      const int e = ids[j];
-      const uint8_t* rec = L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
-      const uint32_t rb = piece == 0 ? dl.rbI : dl.sbI;
-      src = rec + L.rg.off[6 + piece] + (size_t)d0 * rb;
-      bytes = (uint32_t)nd * rb;
+      const uint8_t* rec = expert_record(L, ids[j]);
+      rb = kind == 0 ? RBI : SBI;
+      src = rec + L.rg.off[6 + kind] + (size_t)d0 * rb;
+      dst = D + (kind == 0 ? (size_t)j * DEC_MAX_DROWS * a.d_rb
+                           : (kind == 1 ? o.rs : o.rb) + (size_t)j * DEC_MAX_DROWS * a.d_sb);
     } else {
-      const uint8_t* base = piece == 0 ? L.sd.w : reinterpret_cast<const uint8_t*>(piece == 1 ? L.sd.s : L.sd.b);
-      const uint32_t rb = piece == 0 ? (uint32_t)a.Ish : dl.sbS;
+      rb = kind == 0 ? DEC_I : DEC_DSBI;
+      const uint8_t* base = kind == 0 ? L.sd.w : reinterpret_cast<const uint8_t*>(kind == 1 ? L.sd.s : L.sd.b);
       src = base + (size_t)d0 * rb;
-      bytes = (uint32_t)nd * rb;
+      dst = D + (kind == 0 ? o.sh : (kind == 1 ? o.ss : o.sb));
     }
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+    bulk_g2s(dst, src, (uint32_t)nd * rb, bar);
   }
+  __syncwarp();
 }
 
-// Scale/bias contribution of one block for one row.
-YN_DEV float block_contrib(const uint16_t* srow, const uint16_t* brow, int blk, int gs, const float (&d)[2],
-                           const XBlock& X, float inv_scale, int nseg) {
-  if (nseg == 1) {
-    const int g = blk * 64 / gs;
-    return __fmaf_rn(f16_to_f32(srow[g]), __fmul_rn(d[0], inv_scale),
-                     __fmul_rn(f16_to_f32(brow[g]), __fadd_rn(X.xs_lo, X.xs_hi)));
-  }
-  const int g = blk * 2;
-  const float lo = __fmaf_rn(f16_to_f32(srow[g]), __fmul_rn(d[0], inv_scale), __fmul_rn(f16_to_f32(brow[g]), X.xs_lo));
-  const float hi = __fmaf_rn(f16_to_f32(srow[g + 1]), __fmul_rn(d[1], inv_scale),
-                             __fmul_rn(f16_to_f32(brow[g + 1]), X.xs_hi));
-  return __fadd_rn(lo, hi);
-}
-
-// Global address of one lane's code words for (row of the C list, block).
-YN_DEV const uint8_t* c_row_ptr(const DecLayer& L, const int32_t* ids, const CPlan& cp, int r, uint32_t rbH) {
-  int sgi, up, n;
-  c_row(cp, r, sgi, up, n);
-  const int e = ids[cp.j[sgi]];
-  const uint8_t* rec = L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
-  return rec + L.rg.off[up ? 3 : 0] + (size_t)(cp.n0[sgi] + n) * rbH;
-}
-YN_DEV const uint16_t* c_scale_ptr(const DecLayer& L, const int32_t* ids, const CPlan& cp, int r, uint32_t sbH,
-                                   int bias) {
-  int sgi, up, n;
-  c_row(cp, r, sgi, up, n);
-  const int e = ids[cp.j[sgi]];
-  const uint8_t* rec = L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
-  return reinterpret_cast<const uint16_t*>(rec + L.rg.off[(up ? 4 : 1) + bias] + (size_t)(cp.n0[sgi] + n) * sbH);
-}
-
-template <int BITS>
-YN_DEV void ldg_codes(const uint8_t* p, uint32_t (&w)[4]) {
-  constexpr int W = MmaFmt<BITS>::WORDS;
-  if (W == 1) {
-    w[0] = __ldg(reinterpret_cast<const unsigned int*>(p));
-  } else if (W == 2) {
-    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-    w[0] = v.x; w[1] = v.y;
-  } else {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
-    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-  }
-}
-
-// P2: warp w owns blocks [NBW*w, NBW*w + NBW) of the hidden dimension for
-// every C row. All code words and scales a lane needs are loaded from global
-// memory into registers up front (one memory round trip), then unpacked and
-// multiplied. Contributions go to part[blk * R + row].
-template <int BITS, int NSEG, int NBW, int MAXT>
-YN_DEV void p2_regs(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CPlan& cp, int gs,
-                    const uint16_t* xs, float xscale, float* part) {
+// P2: gate/up dots of this CTA's tiles. Items (tile t, super-block sb) go
+// round-robin over the warps; partial sums land in
+// part[((t * 8 + row) * 2 + up) * NSB + sb].
+template <int BITS, int GS>
+YN_DEV void p2_tiles(const DecodeArgs& a, int ntile, const uint8_t* C, const uint32_t* xf, const float* xsum,
+                     float inv, float* part) {
+  using S = Sb<BITS>;
+  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, NSB = RB / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  constexpr int W = MmaFmt<BITS>::WORDS;
-  const int H = a.H, R = cp.R;
-  const uint32_t rbH = (uint32_t)(H * BITS / 8), sbH = (uint32_t)(H / gs) * 2;
-  const int ntile = (R + 15) / 16;
-  const int blk0 = warp * NBW;
-  uint32_t w[MAXT][2][NBW][4];
-  uint2 sc[MAXT][2][2];      // scales / biases of an aligned 4-group window (fp16) for rows g, g+8
-  const int grp0 = (blk0 * 64 / gs) & ~3;
-#pragma unroll
-  for (int t = 0; t < MAXT; ++t) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = t * 16 + g + 8 * h;
-      const bool ok = (t < ntile) && (r < R);
-      if (ok) {
-        const uint8_t* rp = c_row_ptr(L, ids, cp, r, rbH);
-#pragma unroll
-        for (int q = 0; q < NBW; ++q) ldg_codes<BITS>(rp + (blk0 + q) * 8 * BITS + c * 4 * W, w[t][h][q]);
-        const uint16_t* sp = c_scale_ptr(L, ids, cp, r, sbH, 0);
-        const uint16_t* bp = c_scale_ptr(L, ids, cp, r, sbH, 1);
-        sc[t][h][0] = __ldg(reinterpret_cast<const uint2*>(sp + grp0));
-        sc[t][h][1] = __ldg(reinterpret_cast<const uint2*>(bp + grp0));
-      } else {
-#pragma unroll
-        for (int q = 0; q < NBW; ++q) w[t][h][q][0] = w[t][h][q][1] = w[t][h][q][2] = w[t][h][q][3] = 0u;
-        sc[t][h][0] = sc[t][h][1] = make_uint2(0u, 0u);
-      }
-    }
-  }
-  const float inv = __fdiv_rn(1.0f, xscale);
-#pragma unroll
-  for (int q = 0; q < NBW; ++q) {
-    const int blk = blk0 + q;
-    XBlock X;
-    build_xblock<BITS>(X, xs, blk, xscale, c);
-    float* pb = part + (size_t)blk * R;
-#pragma unroll
-    for (int t = 0; t < MAXT; ++t) {
-      if (t >= ntile) break;
-      float da[2], db[2];
-      mma_block<BITS, NSEG>(w[t][0][q], w[t][1][q], X, c, da, db);
-      if (c == 0) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = t * 16 + g + 8 * h;
-          if (r < R) {
-            // scales of group index blk*64/gs inside the loaded 4-group window
-            const uint2 s4 = sc[t][h][0], b4 = sc[t][h][1];
-            auto pick = [](uint2 v, int i) -> float {
-              const uint32_t wv = (i < 2) ? v.x : v.y;
-              return f16_to_f32((uint16_t)((i & 1) ? wv >> 16 : wv & 0xFFFFu));
-            };
-            const float* dd = h ? db : da;
-            float v;
-            if (NSEG == 1) {
-              const int gi = blk * 64 / gs - grp0;
-              v = __fmaf_rn(pick(s4, gi), __fmul_rn(dd[0], inv), __fmul_rn(pick(b4, gi), __fadd_rn(X.xs_lo, X.xs_hi)));
-            } else {
-              const int gi = 2 * blk - grp0;
-              v = __fadd_rn(__fmaf_rn(pick(s4, gi), __fmul_rn(dd[0], inv), __fmul_rn(pick(b4, gi), X.xs_lo)),
-                            __fmaf_rn(pick(s4, gi + 1), __fmul_rn(dd[1], inv), __fmul_rn(pick(b4, gi + 1), X.xs_hi)));
-            }
-            pb[r] = v;
-          }
-        }
-      }
-    }
-  }
-}
-
-// P3 prologue: warp j < K builds the fragments of routed column j's
-// activations (from global), warp K those of the shared expert's; each lane
-// (blk = lane/4, c = lane%4) owns one block fragment.
-template <int BITS>
-YN_DEV void p3_frags(const DecodeArgs& a, XBlock* xf, float* xscale) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, blk = lane >> 2, c = lane & 3;
-  const int K = a.K;
-  if (warp > K || (warp == K && !a.Ish)) return;
-  const int n = (warp < K) ? a.I : a.Ish;
-  if (n != 512) return;  // one warp covers 8 blocks of 64 codes (checked on the host)
-  const uint16_t* src = (warp < K) ? a.act + (size_t)warp * a.I : a.act_sh;
-  uint16_t v[16];
-  {
-    const uint4 q0 = __ldcg(reinterpret_cast<const uint4*>(src + blk * 64 + 16 * c));
-    const uint4 q1 = __ldcg(reinterpret_cast<const uint4*>(src + blk * 64 + 16 * c + 8));
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[2 * i] = (uint16_t)(w[i] & 0xFFFFu);
-      v[2 * i + 1] = (uint16_t)(w[i] >> 16);
-    }
-  }
-  float m = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(bf16_to_f32(v[i])));
-  m = warp_max(m);
-  const float scale = fp16_input_scale(m);
-  // fragment from registers (same construction as build_xblock)
-  XBlock X;
-  const bool eight = (warp == K);
-#pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    const int lo = eight ? MmaFmt<8>::lo(p) : MmaFmt<BITS>::lo(p);
-    const int hi = eight ? MmaFmt<8>::hi(p) : MmaFmt<BITS>::hi(p);
-    const float im = eight ? MmaFmt<8>::inv_mult(p) : MmaFmt<BITS>::inv_mult(p);
-    const float mm = __fmul_rn(scale, im);
-    float va = 0.f, vb = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (i == lo) va = bf16_to_f32(v[i]);
-      if (i == hi) vb = bf16_to_f32(v[i]);
-    }
-    __half2 h = __floats2half2_rn(__fmul_rn(va, mm), __fmul_rn(vb, mm));
-    X.b[p] = *reinterpret_cast<uint32_t*>(&h);
-  }
-  float s = 0.0f;
-#pragma unroll
-  for (int e = 0; e < 16; ++e) s = __fadd_rn(s, bf16_to_f32(v[e]));
-  const float s1 = __shfl_xor_sync(0xffffffffu, s, 1);
-  const float s01 = __fadd_rn(s, s1);
-  const float s23 = __shfl_xor_sync(0xffffffffu, s01, 2);
-  X.xs_lo = (c < 2) ? s01 : s23;
-  X.xs_hi = (c < 2) ? s23 : s01;
-  xf[(size_t)(warp * 8 + blk) * 4 + c] = X;
-  if (lane == 0) xscale[warp] = scale;
-}
-
-// P3: (tile, block) items over all warps; tiles 0..K-1 routed (BITS), tile K
-// the shared expert (8-bit). Code words and scales come straight from global
-// memory (prefetched into L2 during P2), all items' loads issued up front.
-// Contributions to part[(tile * 8 + blk) * 16 + row].
-template <int BITS, int NSEG, int MAXI>
-YN_DEV void p3_regs(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd, const XBlock* xf,
-                    const float* xscale, float* part) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  const int K = a.K, I = a.I, Ish = a.Ish, gs = L.rg.gs;
-  const DLayout dl = d_layout(a, L);
-  const int nblk = 8;  // I = Ish = 512
-  const int ntile = K + (Ish ? 1 : 0);
-  const int nitems = ntile * nblk;
-  uint32_t w[MAXI][2][4];
-  uint32_t sc[MAXI][2][2];
-#pragma unroll
-  for (int k = 0; k < MAXI; ++k) {
-    const int item = warp + k * DEC_WARPS;
-    const int t = item / nblk, blk = item % nblk;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = g + 8 * h;
-      w[k][h][0] = w[k][h][1] = w[k][h][2] = w[k][h][3] = 0u;
-      sc[k][h][0] = sc[k][h][1] = 0u;
-      if (item < nitems && r < nd) {
-        if (t < K) {
-          const int e = ids[t];
-          const uint8_t* rec = L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
-          const uint8_t* rp = rec + L.rg.off[6] + (size_t)(d0 + r) * dl.rbI;
-          ldg_codes<BITS>(rp + blk * 8 * BITS + c * 4 * MmaFmt<BITS>::WORDS, w[k][h]);
-          const int gi = (blk * 64 / gs) & ~1;
-          sc[k][h][0] = __ldg(reinterpret_cast<const unsigned int*>(rec + L.rg.off[7] + (size_t)(d0 + r) * dl.sbI) + gi / 2);
-          sc[k][h][1] = __ldg(reinterpret_cast<const unsigned int*>(rec + L.rg.off[8] + (size_t)(d0 + r) * dl.sbI) + gi / 2);
-        } else {
-          const uint8_t* rp = L.sd.w + (size_t)(d0 + r) * Ish;
-          ldg_codes<8>(rp + blk * 64 + c * 16, w[k][h]);
-          const int gi = (blk * 64 / L.sd.gs) & ~1;
-          sc[k][h][0] = __ldg(reinterpret_cast<const unsigned int*>(L.sd.s + (size_t)(d0 + r) * (Ish / L.sd.gs)) + gi / 2);
-          sc[k][h][1] = __ldg(reinterpret_cast<const unsigned int*>(L.sd.b + (size_t)(d0 + r) * (Ish / L.sd.gs)) + gi / 2);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < MAXI; ++k) {
-    const int item = warp + k * DEC_WARPS;
-    if (item >= nitems) break;
-    const int t = item / nblk, blk = item % nblk;
-    const XBlock& X = xf[(size_t)(t * 8 + blk) * 4 + c];
-    const float inv = __fdiv_rn(1.0f, xscale[t]);
-    const bool routed = t < K;
-    float da[2], db[2];
-    if (routed) mma_block<BITS, NSEG>(w[k][0], w[k][1], X, c, da, db);
-    else mma_block<8, 1>(w[k][0], w[k][1], X, c, da, db);
+  const uint8_t* cg = C;
+  const uint8_t* cu = C + (size_t)a.c_rows * a.c_rb;
+  const uint8_t* sc = C + (size_t)2 * a.c_rows * a.c_rb;
+  for (int it = warp; it < ntile * NSB; it += DEC_WARPS) {
+    const int t = it / NSB, sb = it % NSB;
+    const int row = t * 8 + g;
+    float d[4];
+    sb_mma<BITS, GS>(cg + (size_t)row * RB + sb * 64 + c * 16, cu + (size_t)row * RB + sb * 64 + c * 16,
+                     xf + (sb * 4 + c) * S::FRAG, g, c, d);
+    const uint16_t* gs_ = reinterpret_cast<const uint16_t*>(sc + (size_t)row * SBH);
+    const uint16_t* gb_ = reinterpret_cast<const uint16_t*>(sc + (size_t)a.c_rows * a.c_sb + (size_t)row * SBH);
+    const uint16_t* us_ = reinterpret_cast<const uint16_t*>(sc + (size_t)2 * a.c_rows * a.c_sb + (size_t)row * SBH);
+    const uint16_t* ub_ = reinterpret_cast<const uint16_t*>(sc + (size_t)3 * a.c_rows * a.c_sb + (size_t)row * SBH);
+    const float vg = sb_apply<BITS, GS>(d[0], d[1], gs_, gb_, xsum, sb, c, inv);
+    const float vu = sb_apply<BITS, GS>(d[2], d[3], us_, ub_, xsum, sb, c, inv);
     if (c == 0) {
-      const int gsx = routed ? gs : L.sd.gs;
-      const int nsx = routed ? NSEG : 1;
-      float* pp = part + (size_t)(t * nblk + blk) * DEC_MAX_DROWS;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int r = g + 8 * h;
-        if (r < nd) {
-          const uint32_t s2 = sc[k][h][0], b2 = sc[k][h][1];
-          const float* dd = h ? db : da;
-          float v;
-          if (nsx == 1) {
-            const int gi = (blk * 64 / gsx) & 1;
-            const float sv = f16_to_f32((uint16_t)(gi ? s2 >> 16 : s2 & 0xFFFFu));
-            const float bv = f16_to_f32((uint16_t)(gi ? b2 >> 16 : b2 & 0xFFFFu));
-            v = __fmaf_rn(sv, __fmul_rn(dd[0], inv), __fmul_rn(bv, __fadd_rn(X.xs_lo, X.xs_hi)));
-          } else {
-            const float s0 = f16_to_f32((uint16_t)(s2 & 0xFFFFu)), s1 = f16_to_f32((uint16_t)(s2 >> 16));
-            const float b0 = f16_to_f32((uint16_t)(b2 & 0xFFFFu)), b1 = f16_to_f32((uint16_t)(b2 >> 16));
-            v = __fadd_rn(__fmaf_rn(s0, __fmul_rn(dd[0], inv), __fmul_rn(b0, X.xs_lo)),
-                          __fmaf_rn(s1, __fmul_rn(dd[1], inv), __fmul_rn(b1, X.xs_hi)));
-          }
-          pp[r] = v;
-        }
+      part[(row * 2 + 0) * NSB + sb] = vg;
+      part[(row * 2 + 1) * NSB + sb] = vu;
+    }
+  }
+}
+
+// P3: down dots of rows [d0, d0+16) for every routed column (BITS, GS) and
+// the shared expert (8-bit, DEC_DGS). part[(j * 16 + row) * 8 + sb].
+template <int BITS, int GS>
+YN_DEV void p3_tiles(const DecodeArgs& a, const uint8_t* D, const uint32_t* xf3, const float* xsum3,
+                     const float* xsc3, float* part) {
+  constexpr int RBI = DEC_I * BITS / 8, SBI = DEC_I / GS * 2, NSBR = RBI / 64, NSBS = DEC_I / 64;
+  constexpr int NGR = DEC_I / GS, NGS = DEC_I / DEC_DGS;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int K = a.K;
+  const DOff o = d_offsets(a);
+  const int nr = K * NSBR, nitems = nr + (a.Ish ? NSBS : 0);
+  for (int it = warp; it < nitems; it += DEC_WARPS) {
+    float d[4];
+    int j, sb;
+    if (it < nr) {
+      j = it / NSBR;
+      sb = it % NSBR;
+      const uint8_t* cb = D + (size_t)j * DEC_MAX_DROWS * a.d_rb + sb * 64 + c * 16;
+      sb_mma<BITS, GS>(cb + (size_t)g * RBI, cb + (size_t)(g + 8) * RBI, xf3 + j * (DEC_I / 2) + (sb * 4 + c) * Sb<BITS>::FRAG,
+                       g, c, d);
+      const size_t srow = (size_t)j * DEC_MAX_DROWS * a.d_sb + (size_t)g * SBI;
+      const uint16_t* s0 = reinterpret_cast<const uint16_t*>(D + o.rs + srow);
+      const uint16_t* b0 = reinterpret_cast<const uint16_t*>(D + o.rb + srow);
+      const float inv = __frcp_rn(xsc3[j]);
+      const float v0 = sb_apply<BITS, GS>(d[0], d[1], s0, b0, xsum3 + j * 16, sb, c, inv);
+      const float v1 = sb_apply<BITS, GS>(d[2], d[3], s0 + 8 * NGR, b0 + 8 * NGR, xsum3 + j * 16, sb, c, inv);
+      if (c == 0) {
+        part[(j * 16 + g) * 8 + sb] = v0;
+        part[(j * 16 + g + 8) * 8 + sb] = v1;
+      }
+    } else {
+      j = K;
+      sb = it - nr;
+      const uint8_t* cb = D + o.sh + sb * 64 + c * 16;
+      sb_mma<8, DEC_DGS>(cb + (size_t)g * DEC_I, cb + (size_t)(g + 8) * DEC_I,
+                         xf3 + K * (DEC_I / 2) + (sb * 4 + c) * Sb<8>::FRAG, g, c, d);
+      const uint16_t* s0 = reinterpret_cast<const uint16_t*>(D + o.ss + (size_t)g * DEC_DSBI);
+      const uint16_t* b0 = reinterpret_cast<const uint16_t*>(D + o.sb + (size_t)g * DEC_DSBI);
+      const float inv = __frcp_rn(xsc3[K]);
+      const float v0 = sb_apply<8, DEC_DGS>(d[0], d[1], s0, b0, xsum3 + K * 16, sb, c, inv);
+      const float v1 = sb_apply<8, DEC_DGS>(d[2], d[3], s0 + 8 * NGS, b0 + 8 * NGS, xsum3 + K * 16, sb, c, inv);
+      if (c == 0) {
+        part[(K * 16 + g) * 8 + sb] = v0;
+        part[(K * 16 + g + 8) * 8 + sb] = v1;
       }
     }
   }
-  (void)I;
 }
 
-// P1 compute: router rows, shared pairs, shared_expert_gate (fp32 path, 8-bit).
-template <int CPL8>
-YN_DEV void p1_compute(const DecodeArgs& a, const DecLayer& L, const P1Range& r, const P1Tile& t, const uint16_t* xs,
-                       const float* rbias_s) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int H = a.H, rb = H;
-  const int lpr = lanes_per_row(rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
-  XF32<8, CPL8, 1> X;
-  load_x_f32<8, CPL8, 1>(X, xs, l, lpr);
-  const int nr = r.r1 - r.r0, np = r.p1 - r.p0;
-  const int ntask = nr + 2 * np + r.sg;  // shared pairs as two rows (gate, up)
-  const int ngr = H / L.router.gs, ngs = L.sg.gs ? H / L.sg.gs : 1;
-  float* gu = const_cast<float*>(rbias_s) + 64;  // shared gate/up dots (bf16-rounded) [2][np]
-  for (int base = warp * rpi; base < ntask; base += DEC_WARPS * rpi) {
-    int k = base + u;
-    const bool valid = k < ntask;
-    if (!valid) k = 0;
-    float v;
-    if (k < nr) {
-      v = row_dot_f32<8, CPL8, 1>(t.rc + (size_t)k * rb, t.rs + (size_t)k * ngr, t.rbv + (size_t)k * ngr, X, l, lpr,
-                                  L.router.gs);
-    } else if (k < nr + 2 * np) {
-      const int q = k - nr, p = q >> 1, up = q & 1;
-      v = up ? row_dot_f32<8, CPL8, 1>(t.uc + (size_t)p * rb, t.usc + (size_t)p * ngs, t.ubi + (size_t)p * ngs, X, l,
-                                       lpr, L.su.gs)
-             : row_dot_f32<8, CPL8, 1>(t.gc + (size_t)p * rb, t.gsc + (size_t)p * ngs, t.gbi + (size_t)p * ngs, X, l,
-                                       lpr, L.sg.gs);
+// Activation fragments for P3: routed columns (BITS) from act, the shared
+// expert (8-bit) from act_sh. stage: (K+1) x 512 bf16 staging in shared memory.
+template <int BITS, int GS>
+YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float* xsum3, float* xsc3) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.K;
+  const int nvec = K + (a.Ish ? 1 : 0);
+  // (a) stage the activation vectors (16-byte chunks)
+  for (int i = tid; i < nvec * (DEC_I / 8); i += DEC_THREADS) {
+    const int j = i / (DEC_I / 8), q = i % (DEC_I / 8);
+    const uint16_t* src = j < K ? a.act + (size_t)j * DEC_I : a.act_sh;
+    reinterpret_cast<uint4*>(stage + j * DEC_I)[q] = __ldcg(reinterpret_cast<const uint4*>(src) + q);
+  }
+  __syncthreads();
+  // (b) per vector: power-of-two scale and group sums (warp j)
+  for (int j = warp; j < nvec; j += DEC_WARPS) {
+    const uint16_t* x = stage + j * DEC_I;
+    float m = 0.0f;
+#pragma unroll
+    for (int e = 0; e < DEC_I / 32; ++e) m = fmaxf(m, fabsf(bf16_to_f32(x[lane + 32 * e])));
+    m = warp_max(m);
+    if (lane == 0) xsc3[j] = fp16_input_scale(m);
+    if (j < K) group_sums16<GS>(x, lane, true, xsum3 + j * 16);
+    else group_sums16<DEC_DGS>(x, lane, true, xsum3 + j * 16);
+  }
+  __syncthreads();
+  // (c) fragments: vector j occupies words [j * 256, (j + 1) * 256)
+  for (int i = tid; i < nvec * (DEC_I / 2); i += DEC_THREADS) {
+    const int j = i / (DEC_I / 2), w = i % (DEC_I / 2);
+    const uint16_t* x = stage + j * DEC_I;
+    if (j < K) {
+      using S = Sb<BITS>;
+      const int sb = w / (4 * S::FRAG), rem = w % (4 * S::FRAG);
+      xf3[i] = frag_word<BITS>(x, xsc3[j], sb, rem / S::FRAG, rem % S::FRAG);
     } else {
-      v = row_dot_f32<8, CPL8, 1>(t.sc, t.ssc, t.sbi, X, l, lpr, L.sgt.gs);
-    }
-    v = group_sum_bfly(v, lpr);
-    if (valid && l == 0) {
-      if (k < nr) {
-        a.logits[r.r0 + k] = bf16r(__fadd_rn(v, rbias_s[k]));
-      } else if (k < nr + 2 * np) {
-        const int q = k - nr;
-        gu[q] = bf16r(v);
-      } else {
-        a.sgate[0] = bf16r(sigmoid_f32(bf16r(v)));
-      }
+      using S = Sb<8>;
+      const int sb = w / (4 * S::FRAG), rem = w % (4 * S::FRAG);
+      xf3[i] = frag_word<8>(x, xsc3[j], sb, rem / S::FRAG, rem % S::FRAG);
     }
   }
   __syncthreads();
-  for (int p = threadIdx.x; p < np; p += DEC_THREADS)
-    a.act_sh[r.p0 + p] = f32_to_bf16(swiglu_bf16(gu[2 * p], gu[2 * p + 1]));
 }
 
 // Diagnostics: SM-cycle stamps of CTA 0 for one token (the last one decoded),
 // 16 per layer; a block-wide sync before each stamp attributes the time of the
 // slowest warp of the CTA.
-constexpr int DEC_STAMPS = 16;
 YN_DEV void stamp(const DecodeArgs& a, int tok, int layer, int slot) {
   if (a.timing && blockIdx.x == 0 && tok == a.n_tokens - 1) {
     __syncthreads();
@@ -708,7 +697,7 @@ YN_DEV void stamp(const DecodeArgs& a, int tok, int layer, int slot) {
   }
 }
 
-// Copy descriptor of layer `idx` into a shared-memory slot (threads 0..20).
+// Copy descriptor of layer `idx` into a shared-memory slot.
 YN_DEV void load_layer(DecLayer* slot, const DecLayer* table, int idx) {
   constexpr int NW = sizeof(DecLayer) / 16;
   static_assert(sizeof(DecLayer) % 16 == 0, "DecLayer must be a multiple of 16 bytes");
@@ -716,40 +705,74 @@ YN_DEV void load_layer(DecLayer* slot, const DecLayer* table, int idx) {
     reinterpret_cast<uint4*>(slot)[threadIdx.x] = __ldcg(reinterpret_cast<const uint4*>(table + idx) + threadIdx.x);
 }
 
-template <int CPL8, int CPLS>
+// Layer format index: bits 2/4 x group 32/64.
+YN_DEV int fmt_of(const DecLayer& L) { return (L.rg.bits == 4 ? 2 : 0) + (L.rg.gs == 32 ? 1 : 0); }
+
+// Fragments and group sums of the normed row for P2 (format of layer L).
+template <int BITS, int GS>
+YN_DEV void p2_frags(const uint16_t* xs, float scale, uint32_t* xf2, float* xsum2) {
+  build_frags<BITS>(xs, DEC_H, scale, xf2, threadIdx.x, DEC_THREADS);
+  if (threadIdx.x < DEC_H / 16) group_sums16<GS>(xs, threadIdx.x, true, xsum2);
+}
+
+// P2 after the C tile landed: tile dots, then per unit gate/up sums over the
+// super-blocks in order, SwiGLU, activation row to global memory.
+template <int BITS, int GS>
+YN_DEV void p2_finish(const DecodeArgs& a, const CSeg& sg, int ntile, const uint8_t* C, const uint32_t* xf2,
+                      const float* xsum2, float inv, float* part) {
+  constexpr int NSB = DEC_H * BITS / 8 / 64;
+  p2_tiles<BITS, GS>(a, ntile, C, xf2, xsum2, inv, part);
+  __syncthreads();
+  const int u = threadIdx.x;
+  if (u < ntile * 8) {
+    float gsum = 0.0f, usum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NSB; ++q) {
+      gsum = __fadd_rn(gsum, part[(u * 2 + 0) * NSB + q]);
+      usum = __fadd_rn(usum, part[(u * 2 + 1) * NSB + q]);
+    }
+    const int s = (sg.n > 1 && u >= sg.rows[0]) ? 1 : 0;
+    const int n = sg.n0[s] + (s ? u - sg.rows[0] : u);
+    a.act[(size_t)sg.j[s] * DEC_I + n] = f32_to_bf16(swiglu_bf16(bf16r(gsum), bf16r(usum)));
+  }
+}
+
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArgs a) {
-  constexpr int NBW = (CPL8 + 1) / 2;  // 64-code blocks of the hidden dimension per warp in P2
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* barA = reinterpret_cast<uint64_t*>(smem);
   uint64_t* barC = reinterpret_cast<uint64_t*>(smem + 16);
   uint64_t* barD = reinterpret_cast<uint64_t*>(smem + 24);
-  float* red = reinterpret_cast<float*>(smem + 32);           // 16 floats
+  float* red = reinterpret_cast<float*>(smem + 32);           // 24 floats
   int* eflag = reinterpret_cast<int*>(smem + 128);
   uint16_t* hs = reinterpret_cast<uint16_t*>(smem + a.off_hs);
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + a.off_xs);
-  XBlock* xf = reinterpret_cast<XBlock*>(smem + a.off_xf);           // [(K+1) * 8 blocks * 4 lanes]
   uint8_t* rt = smem + a.off_route;
-  float* rv = reinterpret_cast<float*>(rt);                             // E
-  uint32_t* keys = reinterpret_cast<uint32_t*>(rt + 4 * a.E);           // E
-  uint32_t* cand = keys + a.E;                                          // WARPS*K
+  float* rv = reinterpret_cast<float*>(rt);                              // E
+  uint32_t* cand = reinterpret_cast<uint32_t*>(rt + 4 * DEC_E);          // 16 * 16
   int32_t* ids = reinterpret_cast<int32_t*>(cand + DEC_WARPS * DEC_MAX_K);
   float* wts = reinterpret_cast<float*>(ids + DEC_MAX_K);
-  float* xsc = wts + DEC_MAX_K;                                         // K+1 fragment scales
-  float* rbias_s = xsc + DEC_MAX_K + 4;                                 // 64 + shared gate/up scratch
-  DecLayer* lay = reinterpret_cast<DecLayer*>(rbias_s + 64 + 256);      // 3 slots
+  float* xsc3 = wts + DEC_MAX_K;                                         // K + 1
+  float* rbias_s = xsc3 + DEC_MAX_K + 4;                                 // 64
+  float* gu = rbias_s + 64;                                              // 256
+  DecLayer* lay = reinterpret_cast<DecLayer*>(gu + 256);                 // 3 slots
+  uint32_t* xf2 = reinterpret_cast<uint32_t*>(smem + a.off_xf2);         // H / 2 words
+  float* xsum2 = reinterpret_cast<float*>(xf2 + DEC_H / 2);              // H / 32
+  uint32_t* xf3 = reinterpret_cast<uint32_t*>(smem + a.off_xf3);         // (K+1) * I / 2 words
+  float* xsum3 = reinterpret_cast<float*>(xf3 + (DEC_MAX_K + 1) * (DEC_I / 2));  // (K+1) * 16
   float* part = reinterpret_cast<float*>(smem + a.off_part);
   uint8_t* Abuf = smem + a.off_A;
-  uint8_t* cbuf = smem + a.off_C;
-  uint8_t* dbuf = smem + a.off_D;
+  uint8_t* C = smem + a.off_C;
+  uint8_t* D = smem + a.off_D;
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int G = gridDim.x, b = blockIdx.x;
-  const int H = a.H, E = a.E, K = a.K, I = a.I;
-  const P1Range r1 = p1_range(b, G, E, a.Ish);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int G = gridDim.x, b = blockIdx.x, K = a.K;
+  const P1Range r1 = p1_range(b, G, a.Ish);
   const int nr1 = r1.r1 - r1.r0;
-  const int U = K * I;
-  const int u0 = (int)((long long)b * U / G), u1 = (int)((long long)(b + 1) * U / G);
-  const int d0 = (int)((long long)b * H / G), d1 = (int)((long long)(b + 1) * H / G);
+  const int noct = K * (DEC_I / 8);
+  const int o0 = (int)((long long)b * noct / G), o1 = (int)((long long)(b + 1) * noct / G);
+  const int ntile = o1 - o0;
+  const CSeg sg = c_segments(o0, o1);
+  const int d0 = (int)((long long)b * DEC_H / G), d1 = (int)((long long)(b + 1) * DEC_H / G);
   const int nd = d1 - d0;
   const int total_steps = a.n_tokens * a.n_layers;
 
@@ -762,12 +785,15 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
   load_layer(&lay[0], a.layers, 0);
   load_layer(&lay[1], a.layers, a.n_layers > 1 ? 1 : 0);
   __syncthreads();
-  if (warp == 0) issue_p1(lay[0], r1, p1_tile(Abuf, r1, H, lay[0].router.gs, shared_gs(lay[0])), H, barA);
+  if (warp == 0) issue_p1(lay[0], r1, p1_tile(Abuf, r1), barA);
   unsigned gen = 0;
-  uint32_t phA = 0;
-  bool pendA = true;
+  uint32_t phA = 0, phC = 0, phD = 0;
+  bool pendA = true, pendC = false, pendD = false;
+  // before leaving on an error: let every copy in flight land (bounded)
   auto drain = [&]() {
     if (pendA) mbar_wait_block(barA, phA, nullptr);
+    if (pendC) mbar_wait_block(barC, phC, nullptr);
+    if (pendD) mbar_wait_block(barD, phD, nullptr);
   };
 
   for (int step = 0; step < total_steps; ++step) {
@@ -775,127 +801,143 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     const DecLayer& L = lay[step % 3];
     const DecLayer& Ln = lay[(step + 1) % 3];
     const bool more = step + 1 < total_steps;
+    const int fmt = fmt_of(L);
     stamp(a, tok, layer, 0);
     // -------- P1: norm; router + shared rows (tile prefetched during the previous layer)
     {
-      const uint16_t* hin = (layer == 0) ? a.inputs + (size_t)tok * H : a.hbuf + (size_t)(step & 1) * H;
+      const uint16_t* hin = (layer == 0) ? a.inputs + (size_t)tok * DEC_H : a.hbuf + (size_t)(step & 1) * DEC_H;
       const float bv = (tid < nr1 && L.rbias) ? __ldcg(L.rbias + r1.r0 + tid) : 0.0f;
-      if (tid < H / 8) reinterpret_cast<uint4*>(hs)[tid] = __ldcg(reinterpret_cast<const uint4*>(hin) + tid);
+      if (tid < DEC_H / 8) reinterpret_cast<uint4*>(hs)[tid] = __ldcg(reinterpret_cast<const uint4*>(hin) + tid);
       if (tid < 64) rbias_s[tid] = bv;
     }
-    const P1Tile t1 = p1_tile(Abuf, r1, H, L.router.gs, shared_gs(L));
+    const P1Tile t1 = p1_tile(Abuf, r1);
     stamp(a, tok, layer, 1);
     const bool a_ok = mbar_wait_block(barA, phA, a.err);
     stamp(a, tok, layer, 2);
+    float xscale2 = 1.0f;
     if (a_ok) {
       phA ^= 1;
       pendA = false;
-      rmsnorm_smem(hs, t1.norm, H, a.eps, xs, red);
+      rmsnorm_smem(hs, t1.norm, a.eps, xs, red);
+      // power-of-two scale of the normed row, fragments and group sums for P2
+      float mx = 0.0f;
+      for (int i = tid; i < DEC_H; i += DEC_THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
+      mx = warp_max(mx);
+      if ((tid & 31) == 0) red[8 + warp] = mx;
+      __syncthreads();
+      mx = warp_max(red[8 + (tid & 15)]);
+      xscale2 = fp16_input_scale(mx);
+      switch (fmt) {
+        case 0: p2_frags<2, 64>(xs, xscale2, xf2, xsum2); break;
+        case 1: p2_frags<2, 32>(xs, xscale2, xf2, xsum2); break;
+        case 2: p2_frags<4, 64>(xs, xscale2, xf2, xsum2); break;
+        default: p2_frags<4, 32>(xs, xscale2, xf2, xsum2); break;
+      }
       stamp(a, tok, layer, 3);
-      p1_compute<CPL8>(a, L, r1, t1, xs, rbias_s);
+      p1_compute(a, r1, t1, xs, rbias_s, gu);
     }
     stamp(a, tok, layer, 4);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }
     stamp(a, tok, layer, 5);
-    // -------- P2: prefetch next layer's P1 tile, route, C/D tiles, gate/up rows
-    if (warp == 2 && more)
-      issue_p1(Ln, r1, p1_tile(Abuf, r1, H, Ln.router.gs, shared_gs(Ln)), H, barA);
+    // -------- P2: route; C / D copies; next layer's P1 tile; gate/up rows
+    if (warp == 2 && more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA);
     pendA = more;
     if (step + 2 < total_steps) load_layer(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
-    route_block(a.logits, E, K, a.norm_topk, rv, keys, cand, red, ids, wts);
+    route_block(a.logits, K, a.norm_topk, rv, cand, red, ids, wts);
     if (a.trace_ids && b == 0 && tid < K) a.trace_ids[((size_t)tok * a.n_layers + layer) * K + tid] = ids[tid];
     stamp(a, tok, layer, 6);
     bool ids_ok = true;
     for (int j = 0; j < K; ++j) {
       const int e = ids[j];
-      const int sl = (e >= 0 && e < E) ? (L.slot_of ? L.slot_of[e] : e) : -1;
+      const int sl = (e >= 0 && e < DEC_E) ? (L.slot_of ? L.slot_of[e] : e) : -1;
       if (sl < 0 || sl >= L.n_slots) ids_ok = false;
     }
+    ids_ok = __syncthreads_and(ids_ok ? 1 : 0) != 0;
     if (!ids_ok && tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
-    const int bits = L.rg.bits, gs = L.rg.gs;
-    const CPlan cp = c_plan(u0, u1, I, H * bits / 8);
-    if (ids_ok && warp == DEC_WARPS - 1) prefetch_d(a, L, ids, d0, nd);
-    // max |x| of the normed row (power-of-two scale for the fp16 fragments)
-    float mx = 0.0f;
-    for (int i = tid; i < H; i += DEC_THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
-#pragma unroll
-    for (int w = 1; w < DEC_WARPS; ++w) mx = fmaxf(mx, red[w]);
-    const float xscale = fp16_input_scale(mx);
-    stamp(a, tok, layer, 7);
-    stamp(a, tok, layer, 8);
-    const bool c_ok = ids_ok;
-    if (c_ok) {
-      if (bits == 2) {
-        if (gs == 32) p2_regs<2, 2, NBW, 5>(a, L, ids, cp, gs, xs, xscale, part);
-        else p2_regs<2, 1, NBW, 5>(a, L, ids, cp, gs, xs, xscale, part);
-      } else {
-        if (gs == 32) p2_regs<4, 2, NBW, 5>(a, L, ids, cp, gs, xs, xscale, part);
-        else p2_regs<4, 1, NBW, 5>(a, L, ids, cp, gs, xs, xscale, part);
-      }
-      __syncthreads();
-      // gate/up rows of each n: sum the per-block contributions in block order
-      const int nblk = H / 64;
-      int off = 0;
-      for (int s = 0; s < cp.nseg; ++s) {
-        for (int i = tid; i < cp.nr[s]; i += DEC_THREADS) {
-          float gsum = 0.0f, usum = 0.0f;
-          for (int q = 0; q < nblk; ++q) {
-            gsum = __fadd_rn(gsum, part[(size_t)q * cp.R + off + i]);
-            usum = __fadd_rn(usum, part[(size_t)q * cp.R + off + cp.nr[s] + i]);
-          }
-          a.act[(size_t)cp.j[s] * I + cp.n0[s] + i] = f32_to_bf16(swiglu_bf16(bf16r(gsum), bf16r(usum)));
+    if (ids_ok) {
+      if (warp == 0) {
+        switch (fmt) {
+          case 0: issue_c<2, 64>(a, L, ids, sg, C, barC); break;
+          case 1: issue_c<2, 32>(a, L, ids, sg, C, barC); break;
+          case 2: issue_c<4, 64>(a, L, ids, sg, C, barC); break;
+          default: issue_c<4, 32>(a, L, ids, sg, C, barC); break;
         }
-        off += 2 * cp.nr[s];
+      } else if (warp == 1) {
+        switch (fmt) {
+          case 0: issue_d<2, 64>(a, L, ids, d0, nd, D, barD); break;
+          case 1: issue_d<2, 32>(a, L, ids, d0, nd, D, barD); break;
+          case 2: issue_d<4, 64>(a, L, ids, d0, nd, D, barD); break;
+          default: issue_d<4, 32>(a, L, ids, d0, nd, D, barD); break;
+        }
+      }
+      pendC = pendD = true;
+    }
+    stamp(a, tok, layer, 7);
+    const bool c_ok = ids_ok && mbar_wait_block(barC, phC, a.err);
+    stamp(a, tok, layer, 8);
+    if (c_ok) {
+      phC ^= 1;
+      pendC = false;
+      const float inv = __frcp_rn(xscale2);
+      switch (fmt) {
+        case 0: p2_finish<2, 64>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
+        case 1: p2_finish<2, 32>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
+        case 2: p2_finish<4, 64>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
+        default: p2_finish<4, 32>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
       }
     }
     stamp(a, tok, layer, 9);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }
     stamp(a, tok, layer, 10);
-    // -------- P3: fragments of every column's activations, down rows, combine
-    if (bits == 2) p3_frags<2>(a, xf, xsc);
-    else p3_frags<4>(a, xf, xsc);
-    __syncthreads();
+    // -------- P3: activation fragments (staged in the free C tile), down rows, combine
+    uint16_t* stage = reinterpret_cast<uint16_t*>(C);
+    switch (fmt) {
+      case 0: p3_frags<2, 64>(a, stage, xf3, xsum3, xsc3); break;
+      case 1: p3_frags<2, 32>(a, stage, xf3, xsum3, xsc3); break;
+      case 2: p3_frags<4, 64>(a, stage, xf3, xsum3, xsc3); break;
+      default: p3_frags<4, 32>(a, stage, xf3, xsum3, xsc3); break;
+    }
     stamp(a, tok, layer, 11);
-    const float sgv = a.Ish ? __ldcg(a.sgate) : 0.0f;
+    const bool d_ok = ids_ok && mbar_wait_block(barD, phD, a.err);
     stamp(a, tok, layer, 12);
-    stamp(a, tok, layer, 13);
-    const bool d_ok = ids_ok;
     if (d_ok) {
-      if (bits == 2) {
-        if (gs == 32) p3_regs<2, 2, 6>(a, L, ids, d0, nd, xf, xsc, part);
-        else p3_regs<2, 1, 6>(a, L, ids, d0, nd, xf, xsc, part);
-      } else {
-        if (gs == 32) p3_regs<4, 2, 6>(a, L, ids, d0, nd, xf, xsc, part);
-        else p3_regs<4, 1, 6>(a, L, ids, d0, nd, xf, xsc, part);
+      phD ^= 1;
+      pendD = false;
+      switch (fmt) {
+        case 0: p3_tiles<2, 64>(a, D, xf3, xsum3, xsc3, part); break;
+        case 1: p3_tiles<2, 32>(a, D, xf3, xsum3, xsc3, part); break;
+        case 2: p3_tiles<4, 64>(a, D, xf3, xsum3, xsc3, part); break;
+        default: p3_tiles<4, 32>(a, D, xf3, xsum3, xsc3, part); break;
       }
     }
     __syncthreads();
-    stamp(a, tok, layer, 14);
+    stamp(a, tok, layer, 13);
     if (d_ok) {
-      uint16_t* hout = (layer == a.n_layers - 1) ? a.outputs + (size_t)tok * H : a.hbuf + (size_t)((step + 1) & 1) * H;
+      const int nsbr = (L.rg.bits * DEC_I / 8) / 64;
+      const float sgv = a.Ish ? __ldcg(a.sgate) : 0.0f;
+      uint16_t* hout = (layer == a.n_layers - 1) ? a.outputs + (size_t)tok * DEC_H : a.hbuf + (size_t)((step + 1) & 1) * DEC_H;
       for (int t = tid; t < nd; t += DEC_THREADS) {
         float acc = 0.0f;
         for (int j = 0; j < K; ++j) {
           float y = 0.0f;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) y = __fadd_rn(y, part[(size_t)(j * 8 + q) * DEC_MAX_DROWS + t]);
+          for (int q = 0; q < nsbr; ++q) y = __fadd_rn(y, part[(j * 16 + t) * 8 + q]);
           acc = __fadd_rn(acc, bf16r(__fmul_rn(bf16r(y), wts[j])));
         }
         float o = bf16r(acc);
         if (a.Ish) {
           float y = 0.0f;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) y = __fadd_rn(y, part[(size_t)(K * 8 + q) * DEC_MAX_DROWS + t]);
+          for (int q = 0; q < DEC_I / 64; ++q) y = __fadd_rn(y, part[(K * 16 + t) * 8 + q]);
           o = bf16r(__fadd_rn(o, bf16r(__fmul_rn(sgv, bf16r(y)))));
         }
         o = bf16r(__fadd_rn(bf16_to_f32(hs[d0 + t]), o));
         hout[d0 + t] = f32_to_bf16(o);
       }
     }
+    // generic-proxy writes to the C tile (activation staging) before the
+    // next layer's bulk copies into it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    stamp(a, tok, layer, 14);
     stamp(a, tok, layer, 15);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }
   }
