@@ -11,10 +11,10 @@
 // Per layer three phases separated by grid barriers:
 //   P1  RMSNorm(h) -> router logits, shared-expert gate/up/SwiGLU, shared gate
 //       (each CTA owns a cost-balanced slice of those rows; its tile was
-//       bulk-copied into shared memory during the previous layer). The
+//       copied into shared memory during the previous layer). The
 //       tensor-core fragments of the normed row are built here too.
 //   P2  routing (every CTA, redundantly, from the 512 logits); each CTA then
-//       bulk-copies its gate/up rows (tiles of 8 units: 8 gate rows + 8 up
+//       copies its gate/up rows (tiles of 8 units: 8 gate rows + 8 up
 //       rows of one expert) and the down rows it needs in P3, and computes its
 //       units' SwiGLU activations.
 //   P3  each CTA owns <= 16 consecutive output rows: routed + shared down
@@ -150,6 +150,20 @@ struct P1Tile {
 };
 
 YN_DEV size_t a16d(size_t v) { return (v + 15) & ~size_t(15); }
+
+// Tiles move with 16-byte cp.async (L2 -> shared, no L1 allocation): every
+// thread issues a few, then arrives on the tile's mbarrier with
+// cp.async.mbarrier.arrive.noinc, which fires when all of that thread's
+// earlier copies have landed (barrier count = DEC_THREADS).
+YN_DEV void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+YN_DEV void cp_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+YN_DEV void warp_copy(uint8_t* dst, const uint8_t* src, uint32_t bytes, int lane) {
+  for (uint32_t o = (uint32_t)lane * 16; o < bytes; o += 512) cp16(dst + o, src + o);
+}
 constexpr int DEC_DSB = DEC_H / DEC_DGS * 2;   // scale-row bytes of a dense 2048-column matrix
 
 YN_DEV P1Tile p1_tile(uint8_t* base, const P1Range& r) {
@@ -172,22 +186,17 @@ YN_DEV P1Tile p1_tile(uint8_t* base, const P1Range& r) {
   return t;
 }
 
-// One warp: issue the bulk copies of one layer's P1 tile (every CTA also
-// takes the whole norm weight); lane i issues piece i.
+// Copies of one layer's P1 tile (every CTA also takes the whole norm
+// weight): warp p copies piece p; then every thread arrives on `bar`.
 YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint64_t* bar) {
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t nr = r.r1 - r.r0, np = r.p1 - r.p0;
-  const uint32_t tx = (uint32_t)DEC_H * 2 + nr * (DEC_H + 2 * DEC_DSB) + np * 2 * (DEC_H + 2 * DEC_DSB) +
-                      (r.sg ? DEC_H + 2 * DEC_DSB : 0);
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  if (lane == 0) mbar_arrive_expect_tx(bar, tx);
-  __syncwarp();
   void* dst = nullptr;
   const void* src = nullptr;
   uint32_t bytes = 0;
   const uint8_t* rs = reinterpret_cast<const uint8_t*>(L.router.s);
   const uint8_t* rb = reinterpret_cast<const uint8_t*>(L.router.b);
-  switch (lane) {
+  switch (warp) {
     case 0: dst = t.norm; src = L.norm; bytes = (uint32_t)DEC_H * 2; break;
     case 1: dst = t.rc; src = L.router.w + (size_t)r.r0 * DEC_H; bytes = nr * DEC_H; break;
     case 2: dst = t.rs; src = rs + (size_t)r.r0 * DEC_DSB; bytes = nr * DEC_DSB; break;
@@ -203,8 +212,8 @@ YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint6
     case 12: dst = t.sbi; src = L.sgt.b; bytes = r.sg ? (uint32_t)DEC_DSB : 0u; break;
     default: break;
   }
-  if (bytes) bulk_g2s(dst, src, bytes, bar);
-  __syncwarp();
+  warp_copy(reinterpret_cast<uint8_t*>(dst), reinterpret_cast<const uint8_t*>(src), bytes, lane);
+  cp_arrive(bar);
 }
 
 // RMSNorm in the canonical 128-thread order (threads 128.. idle in the sum).
@@ -483,34 +492,35 @@ YN_DEV const uint8_t* expert_record(const DecLayer& L, int e) {
   return L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
 }
 
-// Lanes of one warp issue this CTA's C-tile copies (one piece per lane).
+// Copies of this CTA's C tile. Chunks (16 bytes) are numbered row-major over
+// (row, [gate codes | up codes | gate scales | gate biases | up scales |
+// up biases]), so consecutive threads copy consecutive bytes of a piece row.
 template <int BITS, int GS>
-YN_DEV void issue_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, uint8_t* C,
-                    uint64_t* bar) {
-  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rows = (uint32_t)(sg.rows[0] + (sg.n > 1 ? sg.rows[1] : 0));
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  if (lane == 0) mbar_arrive_expect_tx(bar, rows * (2u * RB + 4u * SBH));
-  __syncwarp();
-  if (lane < 6 * sg.n) {
-    const int s = lane / 6, piece = lane % 6;  // gate w, s, b, up w, s, b
-    const uint8_t* rec = expert_record(L, ids[sg.j[s]]);
-    const int prow = s ? sg.rows[0] : 0;       // destination row of the segment
-    const int kind = piece % 3, up = piece / 3;
+YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, uint8_t* C) {
+  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, CR = RB / 16, CS = SBH / 16, PER_ROW = 2 * CR + 4 * CS;
+  const int R0 = sg.rows[0], R = sg.n ? R0 + (sg.n > 1 ? sg.rows[1] : 0) : 0;
+  if (!R) return;
+  const uint8_t* rec0 = expert_record(L, ids[sg.j[0]]);
+  const uint8_t* rec1 = sg.n > 1 ? expert_record(L, ids[sg.j[1]]) : rec0;
+  const size_t sbase = (size_t)2 * a.c_rows * a.c_rb;
+  for (int ci = threadIdx.x; ci < R * PER_ROW; ci += DEC_THREADS) {
+    const int row = ci / PER_ROW, k = ci % PER_ROW;
+    const int seg = row >= R0 ? 1 : 0;
+    const int n = sg.n0[seg] + (seg ? row - R0 : row);
+    const uint8_t* rec = seg ? rec1 : rec0;
+    const uint8_t* src;
     uint8_t* dst;
-    uint32_t rb;
-    if (kind == 0) {
-      rb = RB;
-      dst = C + (size_t)up * a.c_rows * a.c_rb + (size_t)prow * RB;
+    if (k < 2 * CR) {
+      const int up = k >= CR ? 1 : 0, col = k - up * CR;
+      src = rec + L.rg.off[3 * up] + (size_t)n * RB + col * 16;
+      dst = C + (size_t)up * a.c_rows * a.c_rb + (size_t)row * RB + col * 16;
     } else {
-      rb = SBH;
-      dst = C + (size_t)2 * a.c_rows * a.c_rb + (size_t)(2 * up + kind - 1) * a.c_rows * a.c_sb + (size_t)prow * SBH;
+      const int q = (k - 2 * CR) / CS, col = (k - 2 * CR) % CS;  // q: gate s, gate b, up s, up b
+      src = rec + L.rg.off[3 * (q >> 1) + 1 + (q & 1)] + (size_t)n * SBH + col * 16;
+      dst = C + sbase + (size_t)q * a.c_rows * a.c_sb + (size_t)row * SBH + col * 16;
     }
-    const uint8_t* src = rec + L.rg.off[3 * up + kind] + (size_t)sg.n0[s] * rb;
-    bulk_g2s(dst, src, (uint32_t)sg.rows[s] * rb, bar);
+    cp16(dst, src);
   }
-  __syncwarp();
 }
 
 // D tile (down rows [d0, d0+nd) of every routed column and of the shared
@@ -530,39 +540,25 @@ YN_DEV DOff d_offsets(const DecodeArgs& a) {
   return o;
 }
 
-// Lanes of one warp issue the D-tile copies: piece i = (column j = i / 3,
-// kind = i % 3); j == K is the shared expert.
+// Copies of the D tile: warp j < K copies column j's three pieces, warp K
+// the shared expert's.
 template <int BITS, int GS>
-YN_DEV void issue_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd, uint8_t* D,
-                    uint64_t* bar) {
+YN_DEV void copy_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd, uint8_t* D) {
   constexpr int RBI = DEC_I * BITS / 8, SBI = DEC_I / GS * 2;
-  const int lane = threadIdx.x & 31, K = a.K;
+  const int lane = threadIdx.x & 31, j = threadIdx.x >> 5, K = a.K;
   const DOff o = d_offsets(a);
-  const uint32_t tx = (uint32_t)nd * ((uint32_t)K * (RBI + 2 * SBI) + (a.Ish ? DEC_I + 2 * DEC_DSBI : 0));
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  if (lane == 0) mbar_arrive_expect_tx(bar, tx);
-  __syncwarp();
-  const int npieces = 3 * K + (a.Ish ? 3 : 0);
-  for (int i = lane; i < npieces; i += 32) {
-    const int j = i / 3, kind = i % 3;
-    const uint8_t* src;
-    uint8_t* dst;
-    uint32_t rb;
-    if (j < K) {
-      const uint8_t* rec = expert_record(L, ids[j]);
-      rb = kind == 0 ? RBI : SBI;
-      src = rec + L.rg.off[6 + kind] + (size_t)d0 * rb;
-      dst = D + (kind == 0 ? (size_t)j * DEC_MAX_DROWS * a.d_rb
-                           : (kind == 1 ? o.rs : o.rb) + (size_t)j * DEC_MAX_DROWS * a.d_sb);
-    } else {
-      rb = kind == 0 ? DEC_I : DEC_DSBI;
-      const uint8_t* base = kind == 0 ? L.sd.w : reinterpret_cast<const uint8_t*>(kind == 1 ? L.sd.s : L.sd.b);
-      src = base + (size_t)d0 * rb;
-      dst = D + (kind == 0 ? o.sh : (kind == 1 ? o.ss : o.sb));
-    }
-    bulk_g2s(dst, src, (uint32_t)nd * rb, bar);
+  if (j < K) {
+    const uint8_t* rec = expert_record(L, ids[j]);
+    warp_copy(D + (size_t)j * DEC_MAX_DROWS * a.d_rb, rec + L.rg.off[6] + (size_t)d0 * RBI, (uint32_t)nd * RBI, lane);
+    warp_copy(D + o.rs + (size_t)j * DEC_MAX_DROWS * a.d_sb, rec + L.rg.off[7] + (size_t)d0 * SBI, (uint32_t)nd * SBI,
+              lane);
+    warp_copy(D + o.rb + (size_t)j * DEC_MAX_DROWS * a.d_sb, rec + L.rg.off[8] + (size_t)d0 * SBI, (uint32_t)nd * SBI,
+              lane);
+  } else if (j == K && a.Ish) {
+    warp_copy(D + o.sh, L.sd.w + (size_t)d0 * DEC_I, (uint32_t)nd * DEC_I, lane);
+    warp_copy(D + o.ss, reinterpret_cast<const uint8_t*>(L.sd.s) + (size_t)d0 * DEC_DSBI, (uint32_t)nd * DEC_DSBI, lane);
+    warp_copy(D + o.sb, reinterpret_cast<const uint8_t*>(L.sd.b) + (size_t)d0 * DEC_DSBI, (uint32_t)nd * DEC_DSBI, lane);
   }
-  __syncwarp();
 }
 
 // P2: gate/up dots of this CTA's tiles. Items (tile t, super-block sb) go
@@ -646,43 +642,47 @@ YN_DEV void p3_tiles(const DecodeArgs& a, const uint8_t* D, const uint32_t* xf3,
 }
 
 // Activation fragments for P3: routed columns (BITS) from act, the shared
-// expert (8-bit) from act_sh. stage: (K+1) x 512 bf16 staging in shared memory.
+// expert (8-bit) from act_sh. Warp j takes vector j: lane l holds values
+// [16l, 16l+16), takes the vector's power-of-two scale (warp max) and its
+// group sums, stages the values in shared memory and builds 8 fragment words.
+// stage: (K+1) x 512 bf16 in shared memory.
 template <int BITS, int GS>
 YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float* xsum3, float* xsc3) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = a.K;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, K = a.K;
   const int nvec = K + (a.Ish ? 1 : 0);
-  // (a) stage the activation vectors (16-byte chunks)
-  for (int i = tid; i < nvec * (DEC_I / 8); i += DEC_THREADS) {
-    const int j = i / (DEC_I / 8), q = i % (DEC_I / 8);
-    const uint16_t* src = j < K ? a.act + (size_t)j * DEC_I : a.act_sh;
-    reinterpret_cast<uint4*>(stage + j * DEC_I)[q] = __ldcg(reinterpret_cast<const uint4*>(src) + q);
-  }
-  __syncthreads();
-  // (b) per vector: power-of-two scale and group sums (warp j)
   for (int j = warp; j < nvec; j += DEC_WARPS) {
-    const uint16_t* x = stage + j * DEC_I;
+    const uint16_t* src = j < K ? a.act + (size_t)j * DEC_I : a.act_sh;
+    uint16_t* x = stage + j * DEC_I;
+    const uint4 q0 = __ldcg(reinterpret_cast<const uint4*>(src) + 2 * lane);
+    const uint4 q1 = __ldcg(reinterpret_cast<const uint4*>(src) + 2 * lane + 1);
+    reinterpret_cast<uint4*>(x)[2 * lane] = q0;
+    reinterpret_cast<uint4*>(x)[2 * lane + 1] = q1;
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     float m = 0.0f;
 #pragma unroll
-    for (int e = 0; e < DEC_I / 32; ++e) m = fmaxf(m, fabsf(bf16_to_f32(x[lane + 32 * e])));
-    m = warp_max(m);
-    if (lane == 0) xsc3[j] = fp16_input_scale(m);
-    if (j < K) group_sums16<GS>(x, lane, true, xsum3 + j * 16);
-    else group_sums16<DEC_DGS>(x, lane, true, xsum3 + j * 16);
-  }
-  __syncthreads();
-  // (c) fragments: vector j occupies words [j * 256, (j + 1) * 256)
-  for (int i = tid; i < nvec * (DEC_I / 2); i += DEC_THREADS) {
-    const int j = i / (DEC_I / 2), w = i % (DEC_I / 2);
-    const uint16_t* x = stage + j * DEC_I;
+    for (int k = 0; k < 8; ++k)
+      m = fmaxf(m, fmaxf(fabsf(bf16_to_f32((uint16_t)(w[k] & 0xFFFFu))), fabsf(bf16_to_f32((uint16_t)(w[k] >> 16)))));
+    const float scale = fp16_input_scale(warp_max(m));
+    __syncwarp();
+    uint32_t* out = xf3 + j * (DEC_I / 2);
     if (j < K) {
       using S = Sb<BITS>;
-      const int sb = w / (4 * S::FRAG), rem = w % (4 * S::FRAG);
-      xf3[i] = frag_word<BITS>(x, xsc3[j], sb, rem / S::FRAG, rem % S::FRAG);
+      group_sums16<GS>(x, lane, true, xsum3 + j * 16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int wd = lane + 32 * i, sb = wd / (4 * S::FRAG), rem = wd % (4 * S::FRAG);
+        out[wd] = frag_word<BITS>(x, scale, sb, rem / S::FRAG, rem % S::FRAG);
+      }
     } else {
       using S = Sb<8>;
-      const int sb = w / (4 * S::FRAG), rem = w % (4 * S::FRAG);
-      xf3[i] = frag_word<8>(x, xsc3[j], sb, rem / S::FRAG, rem % S::FRAG);
+      group_sums16<DEC_DGS>(x, lane, true, xsum3 + j * 16);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int wd = lane + 32 * i, sb = wd / (4 * S::FRAG), rem = wd % (4 * S::FRAG);
+        out[wd] = frag_word<8>(x, scale, sb, rem / S::FRAG, rem % S::FRAG);
+      }
     }
+    if (lane == 0) xsc3[j] = scale;
   }
   __syncthreads();
 }
@@ -777,20 +777,21 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
   const int total_steps = a.n_tokens * a.n_layers;
 
   if (tid == 0) {
-    mbar_init(barA, 1);
-    mbar_init(barC, 1);
-    mbar_init(barD, 1);
+    mbar_init(barA, DEC_THREADS);
+    mbar_init(barC, DEC_THREADS);
+    mbar_init(barD, DEC_THREADS);
     fence_mbar_init();
   }
   load_layer(&lay[0], a.layers, 0);
   load_layer(&lay[1], a.layers, a.n_layers > 1 ? 1 : 0);
   __syncthreads();
-  if (warp == 0) issue_p1(lay[0], r1, p1_tile(Abuf, r1), barA);
+  issue_p1(lay[0], r1, p1_tile(Abuf, r1), barA);
   unsigned gen = 0;
   uint32_t phA = 0, phC = 0, phD = 0;
   bool pendA = true, pendC = false, pendD = false;
   // before leaving on an error: let every copy in flight land (bounded)
   auto drain = [&]() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
     if (pendA) mbar_wait_block(barA, phA, nullptr);
     if (pendC) mbar_wait_block(barC, phC, nullptr);
     if (pendD) mbar_wait_block(barD, phD, nullptr);
@@ -836,13 +837,15 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
       stamp(a, tok, layer, 3);
       p1_compute(a, r1, t1, xs, rbias_s, gu);
     }
+    // the P1 tile is no longer read: prefetch the next layer's into it while
+    // the grid barrier is pending
+    if (more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA);
+    pendA = more;
+    if (step + 2 < total_steps) load_layer(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
     stamp(a, tok, layer, 4);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }
     stamp(a, tok, layer, 5);
     // -------- P2: route; C / D copies; next layer's P1 tile; gate/up rows
-    if (warp == 2 && more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA);
-    pendA = more;
-    if (step + 2 < total_steps) load_layer(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
     route_block(a.logits, K, a.norm_topk, rv, cand, red, ids, wts);
     if (a.trace_ids && b == 0 && tid < K) a.trace_ids[((size_t)tok * a.n_layers + layer) * K + tid] = ids[tid];
     stamp(a, tok, layer, 6);
@@ -855,21 +858,20 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     ids_ok = __syncthreads_and(ids_ok ? 1 : 0) != 0;
     if (!ids_ok && tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
     if (ids_ok) {
-      if (warp == 0) {
-        switch (fmt) {
-          case 0: issue_c<2, 64>(a, L, ids, sg, C, barC); break;
-          case 1: issue_c<2, 32>(a, L, ids, sg, C, barC); break;
-          case 2: issue_c<4, 64>(a, L, ids, sg, C, barC); break;
-          default: issue_c<4, 32>(a, L, ids, sg, C, barC); break;
-        }
-      } else if (warp == 1) {
-        switch (fmt) {
-          case 0: issue_d<2, 64>(a, L, ids, d0, nd, D, barD); break;
-          case 1: issue_d<2, 32>(a, L, ids, d0, nd, D, barD); break;
-          case 2: issue_d<4, 64>(a, L, ids, d0, nd, D, barD); break;
-          default: issue_d<4, 32>(a, L, ids, d0, nd, D, barD); break;
-        }
+      switch (fmt) {
+        case 0: copy_c<2, 64>(a, L, ids, sg, C); break;
+        case 1: copy_c<2, 32>(a, L, ids, sg, C); break;
+        case 2: copy_c<4, 64>(a, L, ids, sg, C); break;
+        default: copy_c<4, 32>(a, L, ids, sg, C); break;
       }
+      cp_arrive(barC);
+      switch (fmt) {
+        case 0: copy_d<2, 64>(a, L, ids, d0, nd, D); break;
+        case 1: copy_d<2, 32>(a, L, ids, d0, nd, D); break;
+        case 2: copy_d<4, 64>(a, L, ids, d0, nd, D); break;
+        default: copy_d<4, 32>(a, L, ids, d0, nd, D); break;
+      }
+      cp_arrive(barD);
       pendC = pendD = true;
     }
     stamp(a, tok, layer, 7);
@@ -913,30 +915,34 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     __syncthreads();
     stamp(a, tok, layer, 13);
     if (d_ok) {
+      // warp t combines output row d0 + t: lane j < K holds routed column j's
+      // weighted term, lane K the gated shared term; sums in column order.
       const int nsbr = (L.rg.bits * DEC_I / 8) / 64;
-      const float sgv = a.Ish ? __ldcg(a.sgate) : 0.0f;
+      const int lane = tid & 31;
       uint16_t* hout = (layer == a.n_layers - 1) ? a.outputs + (size_t)tok * DEC_H : a.hbuf + (size_t)((step + 1) & 1) * DEC_H;
-      for (int t = tid; t < nd; t += DEC_THREADS) {
-        float acc = 0.0f;
-        for (int j = 0; j < K; ++j) {
+      for (int t = warp; t < nd; t += DEC_WARPS) {
+        float term = 0.0f;
+        if (lane < K) {
           float y = 0.0f;
-          for (int q = 0; q < nsbr; ++q) y = __fadd_rn(y, part[(j * 16 + t) * 8 + q]);
-          acc = __fadd_rn(acc, bf16r(__fmul_rn(bf16r(y), wts[j])));
-        }
-        float o = bf16r(acc);
-        if (a.Ish) {
+          for (int q = 0; q < nsbr; ++q) y = __fadd_rn(y, part[(lane * 16 + t) * 8 + q]);
+          term = bf16r(__fmul_rn(bf16r(y), wts[lane]));
+        } else if (lane == K && a.Ish) {
           float y = 0.0f;
 #pragma unroll
           for (int q = 0; q < DEC_I / 64; ++q) y = __fadd_rn(y, part[(K * 16 + t) * 8 + q]);
-          o = bf16r(__fadd_rn(o, bf16r(__fmul_rn(sgv, bf16r(y)))));
+          term = bf16r(__fmul_rn(__ldcg(a.sgate), bf16r(y)));
         }
-        o = bf16r(__fadd_rn(bf16_to_f32(hs[d0 + t]), o));
-        hout[d0 + t] = f32_to_bf16(o);
+        float acc = 0.0f;
+        for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, j));
+        const float sh = __shfl_sync(0xffffffffu, term, K);
+        if (lane == 0) {
+          float o = bf16r(acc);
+          if (a.Ish) o = bf16r(__fadd_rn(o, sh));
+          o = bf16r(__fadd_rn(bf16_to_f32(hs[d0 + t]), o));
+          hout[d0 + t] = f32_to_bf16(o);
+        }
       }
     }
-    // generic-proxy writes to the C tile (activation staging) before the
-    // next layer's bulk copies into it
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     stamp(a, tok, layer, 14);
     stamp(a, tok, layer, 15);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }
