@@ -196,7 +196,7 @@ def run_ours(args, rank: int, world: int):
 
     from yanah_b200 import _lib
     from yanah_b200.device import stream_ptr
-    from yanah_b200.stack import ResidentStack
+    from yanah_b200.stack import DECODE_STAMPS, ResidentStack, decode_phase_report
     from yanah_b200.synthetic import hidden_stream_id, qwen3_next_stack
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -214,22 +214,13 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.synchronize(dev)
     if stack.decode_error():
         raise RuntimeError("device error in the first decode")
-    # per-layer phase breakdown from SM-cycle stamps (one extra untimed launch)
-    timing = torch.zeros((len(layers), 16), dtype=torch.int64, device=dev)
+    # per-layer phase breakdown from global-timer stamps of every CTA (one
+    # extra untimed launch)
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    timing = torch.zeros((len(layers), DECODE_STAMPS, n_sm), dtype=torch.int64, device=dev)
     stack.decode(inputs[:2], outputs[:2], timing=timing)
     torch.cuda.synchronize(dev)
-    tm = timing.cpu().numpy().astype(np.float64)
-    mhz = torch.cuda.get_device_properties(dev).clock_rate / 1e3 if hasattr(
-        torch.cuda.get_device_properties(dev), "clock_rate") else 1965.0
-    phases = {}
-    if tm[0, 0] > 0:
-        names = ["loads", "waitA", "rmsnorm", "p1", "bar1", "route", "issue_xmax", "waitC", "p2", "bar2",
-                 "frags", "sgate", "waitD", "p3", "combine"]
-        d = np.diff(tm, axis=1) / mhz  # us
-        phases = {n: round(float(v), 3) for n, v in zip(names, d.mean(axis=0))}
-        if len(layers) > 1:
-            phases["bar3"] = round(float(np.mean((tm[1:, 0] - tm[:-1, 15]) / mhz)), 3)
-        phases["clock_mhz_assumed"] = mhz
+    phases = decode_phase_report(timing.cpu().numpy())
 
     def barrier():
         if world > 1:
@@ -303,7 +294,7 @@ def run_ours(args, rank: int, world: int):
                      "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
                      "bytes_per_launch": bytes_tok * N, "avg_launch_us": round(launch_ms * 1e3, 1),
                      "traffic": traffic},
-        "phases_us_per_layer": phases,
+        "phases": phases,
     }
     if args.layers:
         line["config"]["layers"] = len(layers)

@@ -195,8 +195,8 @@ int yn_moe_layer_noalloc(const yn_dims* dims, const yn_layer* layer, const void*
  * table of yn_stack_table_bytes(n_layers) bytes; `layers` is the same host
  * array (used for sizing). inputs/outputs: (n_tokens, H) bf16.
  * trace_ids: (n_tokens, n_layers, k) routed ids or NULL. timing: (n_layers,
- * 16) int64 SM-cycle stamps of the last token's phases on CTA 0, or NULL
- * (diagnostics: adds block syncs on CTA 0). */
+ * 16, n_SMs) int64 global-timer stamps (ns) of the last token's phases on
+ * every CTA, or NULL (diagnostics: adds a block sync per stamp). */
 size_t yn_stack_table_bytes(int32_t n_layers);
 size_t yn_stack_scratch_bytes(const yn_dims* dims);
 int yn_stack_prepare(const yn_dims* dims, const yn_layer* layers, int32_t n_layers, void* table, size_t table_bytes);

@@ -619,16 +619,19 @@ static size_t a16h(size_t v) { return (v + 15) / 16 * 16; }
 extern "C" size_t yn_stack_table_bytes(int32_t n_layers) { return (size_t)(n_layers > 0 ? n_layers : 0) * sizeof(DecLayer); }
 
 struct StackScratch {
-  size_t hbuf, logits, act, act_sh, sgate, bar, err, total;
+  size_t err, bar, f_logits, zero_end, hbuf, act, act_sh, sgate, total;
 };
+// Error word; barrier counter and flagged logits (zeroed before every launch);
+// buffers passed between phases.
 static StackScratch stack_scratch(const yn_dims& d) {
   StackScratch S{};
   size_t o = 0;
   auto take = [&](size_t b) { size_t at = o; o = (o + b + 255) / 256 * 256; return at; };
   S.err = take(4);
   S.bar = take(4);
+  S.f_logits = take(2 * (size_t)d.n_experts * 8);
+  S.zero_end = o;
   S.hbuf = take(2 * (size_t)d.hidden * 2);
-  S.logits = take((size_t)d.n_experts * 4);
   S.act = take((size_t)d.top_k * d.moe_inter * 2);
   S.act_sh = take((size_t)(d.shared_inter ? d.shared_inter : 8) * 2);
   S.sgate = take(4);
@@ -761,8 +764,9 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   a.off_route = (int)o;
   o += a16h(4 * (size_t)DEC_E + 4 * DEC_WARPS * DEC_MAX_K + 4 * DEC_MAX_K + 4 * DEC_MAX_K + 4 * (DEC_MAX_K + 4) +
             4 * 64 + 4 * 256 + 3 * sizeof(DecLayer));
-  a.off_xf2 = (int)o; o += a16h((size_t)DEC_H / 2 * 4 + (size_t)DEC_H / 32 * 4);
-  a.off_xf3 = (int)o; o += a16h((size_t)(DEC_MAX_K + 1) * (DEC_I / 2) * 4 + (size_t)(DEC_MAX_K + 1) * 16 * 4);
+  // fragments + group sums + group unpack offsets
+  a.off_xf2 = (int)o; o += a16h((size_t)DEC_H / 2 * 4 + 2 * (size_t)DEC_H / 32 * 4);
+  a.off_xf3 = (int)o; o += a16h((size_t)(DEC_MAX_K + 1) * (DEC_I / 2) * 4 + 2 * (size_t)(DEC_MAX_K + 1) * 16 * 4);
   const size_t part_p2 = (size_t)oct_max * 8 * 2 * 16 * 4, part_p3 = (size_t)(K + 1) * 16 * 8 * 4;
   a.off_part = (int)o; o += a16h(std::max(part_p2, part_p3));
   a.off_A = (int)o; o += a16h(p1_tile_bytes_max(Ish, G));
@@ -791,8 +795,8 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   a.inputs = reinterpret_cast<const uint16_t*>(inputs);
   a.n_tokens = n_tokens;
   a.outputs = reinterpret_cast<uint16_t*>(outputs);
+  a.f_logits = reinterpret_cast<unsigned long long*>(sc + S.f_logits);
   a.hbuf = reinterpret_cast<uint16_t*>(sc + S.hbuf);
-  a.logits = reinterpret_cast<float*>(sc + S.logits);
   a.act = reinterpret_cast<uint16_t*>(sc + S.act);
   a.act_sh = reinterpret_cast<uint16_t*>(sc + S.act_sh);
   a.sgate = reinterpret_cast<float*>(sc + S.sgate);
@@ -800,10 +804,12 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   a.bar = reinterpret_cast<unsigned*>(sc + S.bar);
   a.err = reinterpret_cast<int*>(sc + S.err);
   a.timing = reinterpret_cast<long long*>(timing);
-  if (!al16(inputs) || !al16(outputs) || !al16(a.hbuf) || !al16(a.act))
+  if (!al16(inputs) || !al16(outputs) || !al16(scratch))
     return fail(YN_E_INVALID, "stack decode: inputs, outputs and scratch must be 16-byte aligned");
   cudaStream_t st = as_stream(stream);
-  YN_CUDA(cudaMemsetAsync(a.bar, 0, 4, st));
+  // barrier counter, and stale logit epochs of an earlier launch that must not
+  // match this launch's steps
+  YN_CUDA(cudaMemsetAsync(sc + S.bar, 0, S.zero_end - S.bar, st));
   const void* kernel = reinterpret_cast<const void*>(&k_stack_decode);
   if ((rc = set_smem_ptr(kernel, smem))) return rc;
   int per_sm = 0;

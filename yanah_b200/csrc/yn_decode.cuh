@@ -8,7 +8,8 @@
 // loop, so the hot code of a layer stays small.
 //
 // Grid = one CTA per SM (co-resident, cooperative launch), 512 threads.
-// Per layer three phases separated by grid barriers:
+// Per layer three phases; P1 -> P2 passes the router logits as "flagged
+// words" (below), P2 -> P3 and P3 -> next P1 are grid barriers:
 //   P1  RMSNorm(h) -> router logits, shared-expert gate/up/SwiGLU, shared gate
 //       (each CTA owns a cost-balanced slice of those rows; its tile was
 //       copied into shared memory during the previous layer). The
@@ -19,9 +20,17 @@
 //       units' SwiGLU activations.
 //   P3  each CTA owns <= 16 consecutive output rows: routed + shared down
 //       projections of those rows, the weighted combine and the residual.
-// Grid barriers are a global counter (release add / acquire poll) with a
-// wall-clock limit; on any error every CTA skips work and leaves at the next
-// barrier. Reference behaviour: moe_prefetch/orchestrator.py:308-343 layer
+// Flagged words: each router logit is stored as one aligned 64-bit word
+// {fp32 payload, epoch} with a relaxed gpu-scope store, epoch = decode step
+// + 1; in routing every thread polls its expert's word with relaxed gpu-scope
+// loads until the epoch matches, so the data read is the synchronisation (no
+// fence, no counter, one load in flight per thread). The words are
+// double-buffered by step parity: at a token boundary a CTA may start the next
+// token's first layer while others still route the last one.
+// Grid barriers are a global counter (release add / acquire poll; the poll
+// also watches the error word). Every wait has a wall-clock limit; on any
+// error each CTA waits for its copies in flight and returns. Reference
+// behaviour: moe_prefetch/orchestrator.py:308-343 layer
 // loop with every expert resident (mlx_backend.py:302-316 post-attention and
 // routing, :442-459 routed experts, :438-440 shared expert and combine).
 //
@@ -69,15 +78,17 @@ struct DecodeArgs {
   const uint16_t* inputs;
   int n_tokens;
   uint16_t* outputs;
-  uint16_t* hbuf;      // (2, H)
-  float* logits;       // (E)
-  uint16_t* act;       // (K, I)
-  uint16_t* act_sh;    // (Ish)
-  float* sgate;        // (1)
+  // flagged router logits {fp32 (low 32 bits), epoch (high 32 bits)},
+  // two buffers (step parity); zeroed before every launch
+  unsigned long long* f_logits;  // (2, E)
+  uint16_t* hbuf;      // (2, H) hidden row between layers
+  uint16_t* act;       // (K, I) routed SwiGLU activations
+  uint16_t* act_sh;    // (Ish) shared-expert SwiGLU activations
+  float* sgate;        // (1) shared-expert gate
   int32_t* trace_ids;  // (n_tokens, n_layers, K) or null
-  unsigned* bar;
+  unsigned* bar;       // grid barrier counter (zeroed before every launch)
   int* err;
-  long long* timing;   // (n_layers, DEC_STAMPS) for the last token, or null
+  long long* timing;   // (n_layers, DEC_STAMPS, grid) for the last token, or null
   // shared-memory carve (byte offsets)
   int off_hs, off_xs, off_route, off_xf2, off_xf3, off_part, off_A, off_C, off_D;
   int c_rows;          // rows reserved per code / scale block of the C tile (8 * max tiles)
@@ -85,28 +96,66 @@ struct DecodeArgs {
   int d_rb, d_sb;      // bytes reserved per D code row / scale row (routed)
 };
 
+// ------------------------------------------------------------ flagged words
+using u64 = unsigned long long;
+YN_DEV void put_flag(u64* p, uint32_t payload, uint32_t epoch) {
+  const u64 v = ((u64)epoch << 32) | payload;
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+YN_DEV u64 get_flag(const u64* p) {
+  u64 v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Payload of *p once it carries `epoch`. On an error raised elsewhere, or
+// after 2 s (then the error is raised here), sets `fail` and returns 0.
+YN_DEV uint32_t wait_flag(const u64* p, uint32_t epoch, int* err, bool& fail) {
+  u64 v = get_flag(p);
+  if ((uint32_t)(v >> 32) == epoch) return (uint32_t)v;
+  const uint64_t t0 = globaltimer_ns();
+  for (unsigned it = 1;; ++it) {
+    v = get_flag(p);
+    if ((uint32_t)(v >> 32) == epoch) return (uint32_t)v;
+    if ((it & 63) == 0) {
+      if (*reinterpret_cast<volatile int*>(err)) break;
+      if (globaltimer_ns() - t0 > 2000000000ull) {
+        raise_error(err, YN_ERR_BULK_TIMEOUT);
+        break;
+      }
+    }
+  }
+  fail = true;
+  return 0;
+}
+
 // ---------------------------------------------------------------- barrier
-// Returns true (block-uniform) when the error word is set after the barrier.
+// Returns true (block-uniform) when the decode must stop: an error was seen
+// while waiting, or the wait ran out (then the error is raised here).
 YN_DEV bool grid_barrier(const DecodeArgs& a, unsigned& gen, int* flag) {
   __syncthreads();
   gen += 1;
   if (threadIdx.x == 0) {
     const unsigned target = gen * gridDim.x;
+    int stop = 0;
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
     if (v < target) {
       const uint64_t t0 = globaltimer_ns();
-      while (true) {
+      for (unsigned it = 1;; ++it) {
         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
         if (v >= target) break;
-        if (globaltimer_ns() - t0 > 2000000000ull) {
-          raise_error(a.err, YN_ERR_BULK_TIMEOUT);
-          break;
+        if ((it & 63) == 0) {
+          if (*reinterpret_cast<volatile int*>(a.err)) { stop = 1; break; }
+          if (globaltimer_ns() - t0 > 2000000000ull) {
+            raise_error(a.err, YN_ERR_BULK_TIMEOUT);
+            stop = 1;
+            break;
+          }
         }
       }
     }
-    *flag = *reinterpret_cast<volatile int*>(a.err);
+    *flag = stop;
   }
   __syncthreads();
   return *flag != 0;
@@ -187,16 +236,18 @@ YN_DEV P1Tile p1_tile(uint8_t* base, const P1Range& r) {
 }
 
 // Copies of one layer's P1 tile (every CTA also takes the whole norm
-// weight): warp p copies piece p; then every thread arrives on `bar`.
-YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint64_t* bar) {
+// weight): warps w0.. copy the 13 pieces round-robin; then every thread of
+// the CTA arrives on `bar` (once per layer).
+YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint64_t* bar, int w0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t nr = r.r1 - r.r0, np = r.p1 - r.p0;
+  const uint8_t* rs = reinterpret_cast<const uint8_t*>(L.router.s);
+  const uint8_t* rb = reinterpret_cast<const uint8_t*>(L.router.b);
+  for (int piece = warp - w0; warp >= w0 && piece < 13; piece += DEC_WARPS - w0) {
   void* dst = nullptr;
   const void* src = nullptr;
   uint32_t bytes = 0;
-  const uint8_t* rs = reinterpret_cast<const uint8_t*>(L.router.s);
-  const uint8_t* rb = reinterpret_cast<const uint8_t*>(L.router.b);
-  switch (warp) {
+  switch (piece) {
     case 0: dst = t.norm; src = L.norm; bytes = (uint32_t)DEC_H * 2; break;
     case 1: dst = t.rc; src = L.router.w + (size_t)r.r0 * DEC_H; bytes = nr * DEC_H; break;
     case 2: dst = t.rs; src = rs + (size_t)r.r0 * DEC_DSB; bytes = nr * DEC_DSB; break;
@@ -213,6 +264,7 @@ YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint6
     default: break;
   }
   warp_copy(reinterpret_cast<uint8_t*>(dst), reinterpret_cast<const uint8_t*>(src), bytes, lane);
+  }
   cp_arrive(bar);
 }
 
@@ -240,7 +292,7 @@ YN_DEV void rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uint
 // P1 compute: router rows, shared pairs, shared_expert_gate (canonical fp32
 // row dot, one row per warp step, bit-exact with the oracle).
 YN_DEV void p1_compute(const DecodeArgs& a, const P1Range& r, const P1Tile& t, const uint16_t* xs,
-                       const float* rbias_s, float* gu) {
+                       const float* rbias_s, float* gu, int par, uint32_t ep) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int LPR = 32, CPL = DEC_H / 16 / LPR;
   constexpr int NGD = DEC_H / DEC_DGS;
@@ -264,7 +316,7 @@ YN_DEV void p1_compute(const DecodeArgs& a, const P1Range& r, const P1Tile& t, c
     float v = row_dot_f32<8, CPL, 1>(cr, sr, br, X, lane, LPR, DEC_DGS);
     v = group_sum_bfly(v, LPR);
     if (lane == 0) {
-      if (k < nr) a.logits[r.r0 + k] = bf16r(__fadd_rn(v, rbias_s[k]));
+      if (k < nr) put_flag(a.f_logits + par * DEC_E + r.r0 + k, __float_as_uint(bf16r(__fadd_rn(v, rbias_s[k]))), ep);
       else if (k < nr + 2 * np) gu[k - nr] = bf16r(v);
       else a.sgate[0] = bf16r(sigmoid_f32(bf16r(v)));
     }
@@ -275,16 +327,19 @@ YN_DEV void p1_compute(const DecodeArgs& a, const P1Range& r, const P1Tile& t, c
 }
 
 // ------------------------------------------------------------------ routing
-// Block-wide routing of the 512 logits (thread t <-> expert t) in the
+// Block-wide routing of the 512 logits (thread t <-> expert t; each thread
+// waits for its flagged logit; false when that wait failed) in the
 // canonical order of the oracle: max (order-free), exp per element, sum per
 // lane over e = lane + 32 i then a butterfly (warp 0), bf16 probabilities,
 // then top-k by the unique key (bf16 prob << 16 | 0xFFFF - id): per-warp
 // top-k over its 32 experts, merged by warp 0. Results in shared memory.
-YN_DEV void route_block(const float* logits_g, int K, int norm, float* v /* E */, uint32_t* cand /* 16*16 */,
-                        float* red, int32_t* ids_out, float* w_out) {
+YN_DEV bool route_block(const u64* f_logits, uint32_t ep, int* err, int K, int norm, float* v /* E */,
+                        uint32_t* cand /* 16*16 */, float* red, int32_t* ids_out, float* w_out) {
   static_assert(DEC_E == DEC_THREADS, "one expert per thread");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float x = __ldcg(logits_g + tid);
+  bool fail = false;
+  const float x = __uint_as_float(wait_flag(f_logits + tid, ep, err, fail));
+  if (__syncthreads_or(fail)) return false;
   float m = warp_max(x);
   if (lane == 0) red[warp] = m;
   __syncthreads();
@@ -340,6 +395,7 @@ YN_DEV void route_block(const float* logits_g, int K, int norm, float* v /* E */
     }
   }
   __syncthreads();
+  return true;
 }
 
 // ------------------------------------------------------- super-block GEMV
@@ -379,7 +435,7 @@ YN_DEV void build_frags(const uint16_t* x, int n, float scale, uint32_t* out, in
 // One 16-row tile x one super-block. rg / rg8: this lane's 16 bytes of rows g
 // and g+8; xf: lane c's fragment words. d = D[g][2c], D[g][2c+1],
 // D[g+8][2c], D[g+8][2c+1]; column n = dot over group n of the super-block
-// (times the activation scale).
+// (times the activation scale) plus the group's unpack offset.
 template <int BITS, int GS>
 YN_DEV void sb_mma(const uint8_t* rg, const uint8_t* rg8, const uint32_t* xf, int g, int c, float (&d)[4]) {
   using S = Sb<BITS>;
@@ -391,8 +447,8 @@ YN_DEV void sb_mma(const uint8_t* rg, const uint8_t* rg8, const uint32_t* xf, in
   for (int u = 0; u < S::U; ++u) {
     acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
     uint32_t pa[8], pb[8];
-    MmaFmt<BITS>::unpack(wa + u * S::W, pa);
-    MmaFmt<BITS>::unpack(wb + u * S::W, pb);
+    MmaFmt<BITS>::unpack_raw(wa + u * S::W, pa);
+    MmaFmt<BITS>::unpack_raw(wb + u * S::W, pb);
     uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
     if ((c * S::CPL + 16 * u) / GS == g) {
       x0 = reinterpret_cast<const uint4*>(xf)[2 * u];
@@ -417,14 +473,17 @@ YN_DEV void sb_mma(const uint8_t* rg, const uint8_t* rg8, const uint32_t* xf, in
 
 // Scale and bias of one row's two groups (columns 2c, 2c+1 of super-block sb),
 // summed over the lane quad: every lane of the quad returns the row's
-// super-block partial. s_row / b_row: fp16 scale / bias rows; xsum: group sums.
+// super-block partial. s_row / b_row: fp16 scale / bias rows; xsum: group sums
+// of x; off: group unpack offsets (removed from D first).
 template <int BITS, int GS>
-YN_DEV float sb_apply(float d0, float d1, const uint16_t* s_row, const uint16_t* b_row, const float* xsum, int sb,
-                      int c, float inv) {
+YN_DEV float sb_apply(float d0, float d1, const uint16_t* s_row, const uint16_t* b_row, const float* xsum,
+                      const float* off, int sb, int c, float inv) {
   constexpr int NG = Sb<BITS>::CODES / GS;
   float v = 0.0f;
   if (2 * c < NG) {
     const int gi = sb * NG + 2 * c;
+    d0 = __fsub_rn(d0, off[gi]);
+    if (NG >= 2) d1 = __fsub_rn(d1, off[gi + 1]);
     if (NG >= 2) {
       const uint32_t s2 = *reinterpret_cast<const uint32_t*>(s_row + gi);
       const uint32_t b2 = *reinterpret_cast<const uint32_t*>(b_row + gi);
@@ -441,25 +500,39 @@ YN_DEV float sb_apply(float d0, float d1, const uint16_t* s_row, const uint16_t*
   return v;
 }
 
-// Group sums over groups of GS codes: thread i sums codes [16i, 16i+16) of
-// x, then a butterfly over the GS/16 consecutive threads of a group; the
-// first of them writes out[i / (GS/16)]. Every lane of the calling warp
-// takes part (valid = false contributes nothing and writes nothing).
-template <int GS>
-YN_DEV void group_sums16(const uint16_t* x, int i, bool valid, float* out) {
-  float s = 0.0f;
+// Per group of GS codes: the sum of x (fp32) and the unpack offset
+// 1024 * sum(fp16(x * scale / mult)) of the fragment values fed to the MMA.
+// Thread i takes codes [16i, 16i+16) (one unpack unit of one lane), then a
+// butterfly over the GS/16 consecutive threads of a group; the first of them
+// writes entry i / (GS/16). Every lane of the calling warp takes part.
+template <int BITS, int GS>
+YN_DEV void group_sums16(const uint16_t* x, int i, bool valid, float scale, float* xsum, float* off) {
+  float s = 0.0f, o = 0.0f;
   if (valid) {
     const uint4 q0 = reinterpret_cast<const uint4*>(x + 16 * i)[0];
     const uint4 q1 = reinterpret_cast<const uint4*>(x + 16 * i)[1];
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      s = __fadd_rn(s, bf16_to_f32((uint16_t)(w[k] & 0xFFFFu)));
-      s = __fadd_rn(s, bf16_to_f32((uint16_t)(w[k] >> 16)));
+    for (int k = 0; k < 16; ++k) {
+      const float v = bf16_to_f32((uint16_t)((k & 1) ? w[k >> 1] >> 16 : w[k >> 1] & 0xFFFFu));
+      s = __fadd_rn(s, v);
+      const float m = __fmul_rn(scale, MmaFmt<BITS>::inv_mult(MmaFmt<BITS>::pair_of(k)));
+      o = __fadd_rn(o, __half2float(__float2half_rn(__fmul_rn(v, m))));
     }
+    o = __fmul_rn(o, 1024.0f);
   }
   s = group_sum_bfly(s, GS / 16);
-  if (valid && i % (GS / 16) == 0) out[i / (GS / 16)] = s;
+  o = group_sum_bfly(o, GS / 16);
+  if (valid && i % (GS / 16) == 0) {
+    xsum[i / (GS / 16)] = s;
+    off[i / (GS / 16)] = o;
+  }
+}
+
+// Warp-level bounded wait (the result is warp-uniform).
+YN_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t phase, int* err) {
+  const bool ok = mbar_wait_bounded(bar, phase, err);
+  return __all_sync(0xffffffffu, ok ? 1 : 0) != 0;
 }
 
 // ------------------------------------------------------------ P2 / P3 tiles
@@ -492,34 +565,40 @@ YN_DEV const uint8_t* expert_record(const DecLayer& L, int e) {
   return L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
 }
 
-// Copies of this CTA's C tile. Chunks (16 bytes) are numbered row-major over
-// (row, [gate codes | up codes | gate scales | gate biases | up scales |
-// up biases]), so consecutive threads copy consecutive bytes of a piece row.
+// Bulk copies of this CTA's C tile, issued by a few warps tile by tile
+// (warp i of n takes tiles i, i+n, ...; lane k
+// issues piece k: gate codes, gate scales, gate biases, up codes, up scales,
+// up biases of the tile's 8 rows); tile t completes on its own mbarrier, so
+// P2 starts on tile 0 while later tiles are in flight. A tile (8 units) never
+// crosses an expert boundary.
 template <int BITS, int GS>
-YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, uint8_t* C) {
-  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, CR = RB / 16, CS = SBH / 16, PER_ROW = 2 * CR + 4 * CS;
-  const int R0 = sg.rows[0], R = sg.n ? R0 + (sg.n > 1 ? sg.rows[1] : 0) : 0;
-  if (!R) return;
+YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, int ntile, uint8_t* C,
+                   uint64_t* barT, int t0, int tstep) {
+  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2;
+  constexpr uint32_t TILE_BYTES = 8u * (2u * RB + 4u * SBH);
+  const int lane = threadIdx.x & 31;
+  if (!ntile) return;
   const uint8_t* rec0 = expert_record(L, ids[sg.j[0]]);
   const uint8_t* rec1 = sg.n > 1 ? expert_record(L, ids[sg.j[1]]) : rec0;
   const size_t sbase = (size_t)2 * a.c_rows * a.c_rb;
-  for (int ci = threadIdx.x; ci < R * PER_ROW; ci += DEC_THREADS) {
-    const int row = ci / PER_ROW, k = ci % PER_ROW;
-    const int seg = row >= R0 ? 1 : 0;
-    const int n = sg.n0[seg] + (seg ? row - R0 : row);
-    const uint8_t* rec = seg ? rec1 : rec0;
-    const uint8_t* src;
-    uint8_t* dst;
-    if (k < 2 * CR) {
-      const int up = k >= CR ? 1 : 0, col = k - up * CR;
-      src = rec + L.rg.off[3 * up] + (size_t)n * RB + col * 16;
-      dst = C + (size_t)up * a.c_rows * a.c_rb + (size_t)row * RB + col * 16;
-    } else {
-      const int q = (k - 2 * CR) / CS, col = (k - 2 * CR) % CS;  // q: gate s, gate b, up s, up b
-      src = rec + L.rg.off[3 * (q >> 1) + 1 + (q & 1)] + (size_t)n * SBH + col * 16;
-      dst = C + sbase + (size_t)q * a.c_rows * a.c_sb + (size_t)row * SBH + col * 16;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  for (int t = t0; t < ntile; t += tstep) {
+    if (lane == 0) mbar_arrive_expect_tx(&barT[t], TILE_BYTES);
+    __syncwarp();
+    if (lane < 6) {
+      const int row = 8 * t, seg = row >= sg.rows[0] ? 1 : 0;
+      const int n = sg.n0[seg] + (seg ? row - sg.rows[0] : row);
+      const uint8_t* rec = seg ? rec1 : rec0;
+      const int up = lane / 3, kind = lane % 3;
+      if (kind == 0) {
+        bulk_g2s(C + (size_t)up * a.c_rows * a.c_rb + (size_t)row * RB, rec + L.rg.off[3 * up] + (size_t)n * RB,
+                 8u * RB, &barT[t]);
+      } else {
+        bulk_g2s(C + sbase + (size_t)(2 * up + kind - 1) * a.c_rows * a.c_sb + (size_t)row * SBH,
+                 rec + L.rg.off[3 * up + kind] + (size_t)n * SBH, 8u * SBH, &barT[t]);
+      }
     }
-    cp16(dst, src);
+    __syncwarp();
   }
 }
 
@@ -540,12 +619,12 @@ YN_DEV DOff d_offsets(const DecodeArgs& a) {
   return o;
 }
 
-// Copies of the D tile: warp j < K copies column j's three pieces, warp K
-// the shared expert's.
+// Copies of the D tile by one warp: column j < K (three pieces), or the
+// shared expert's pieces for j == K.
 template <int BITS, int GS>
-YN_DEV void copy_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd, uint8_t* D) {
+YN_DEV void copy_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, int d0, int nd, uint8_t* D, int j) {
   constexpr int RBI = DEC_I * BITS / 8, SBI = DEC_I / GS * 2;
-  const int lane = threadIdx.x & 31, j = threadIdx.x >> 5, K = a.K;
+  const int lane = threadIdx.x & 31, K = a.K;
   const DOff o = d_offsets(a);
   if (j < K) {
     const uint8_t* rec = expert_record(L, ids[j]);
@@ -566,15 +645,23 @@ YN_DEV void copy_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, i
 // part[((t * 8 + row) * 2 + up) * NSB + sb].
 template <int BITS, int GS>
 YN_DEV void p2_tiles(const DecodeArgs& a, int ntile, const uint8_t* C, const uint32_t* xf, const float* xsum,
-                     float inv, float* part) {
+                     float inv, float* part, uint64_t* barT, uint32_t phT) {
   using S = Sb<BITS>;
   constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, NSB = RB / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const float* xoff = xsum + DEC_H / 32;
   const uint8_t* cg = C;
   const uint8_t* cu = C + (size_t)a.c_rows * a.c_rb;
   const uint8_t* sc = C + (size_t)2 * a.c_rows * a.c_rb;
+  int waited = -1;
+  bool ok = true;
   for (int it = warp; it < ntile * NSB; it += DEC_WARPS) {
     const int t = it / NSB, sb = it % NSB;
+    if (t != waited) {
+      ok = mbar_wait_warp(&barT[t], phT, a.err);
+      waited = t;
+    }
+    if (!ok) continue;  // error raised; the grid barrier ends the decode
     const int row = t * 8 + g;
     float d[4];
     sb_mma<BITS, GS>(cg + (size_t)row * RB + sb * 64 + c * 16, cu + (size_t)row * RB + sb * 64 + c * 16,
@@ -583,8 +670,8 @@ YN_DEV void p2_tiles(const DecodeArgs& a, int ntile, const uint8_t* C, const uin
     const uint16_t* gb_ = reinterpret_cast<const uint16_t*>(sc + (size_t)a.c_rows * a.c_sb + (size_t)row * SBH);
     const uint16_t* us_ = reinterpret_cast<const uint16_t*>(sc + (size_t)2 * a.c_rows * a.c_sb + (size_t)row * SBH);
     const uint16_t* ub_ = reinterpret_cast<const uint16_t*>(sc + (size_t)3 * a.c_rows * a.c_sb + (size_t)row * SBH);
-    const float vg = sb_apply<BITS, GS>(d[0], d[1], gs_, gb_, xsum, sb, c, inv);
-    const float vu = sb_apply<BITS, GS>(d[2], d[3], us_, ub_, xsum, sb, c, inv);
+    const float vg = sb_apply<BITS, GS>(d[0], d[1], gs_, gb_, xsum, xoff, sb, c, inv);
+    const float vu = sb_apply<BITS, GS>(d[2], d[3], us_, ub_, xsum, xoff, sb, c, inv);
     if (c == 0) {
       part[(row * 2 + 0) * NSB + sb] = vg;
       part[(row * 2 + 1) * NSB + sb] = vu;
@@ -602,6 +689,7 @@ YN_DEV void p3_tiles(const DecodeArgs& a, const uint8_t* D, const uint32_t* xf3,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int K = a.K;
   const DOff o = d_offsets(a);
+  const float* off3 = xsum3 + (DEC_MAX_K + 1) * 16;
   const int nr = K * NSBR, nitems = nr + (a.Ish ? NSBS : 0);
   for (int it = warp; it < nitems; it += DEC_WARPS) {
     float d[4];
@@ -616,8 +704,9 @@ YN_DEV void p3_tiles(const DecodeArgs& a, const uint8_t* D, const uint32_t* xf3,
       const uint16_t* s0 = reinterpret_cast<const uint16_t*>(D + o.rs + srow);
       const uint16_t* b0 = reinterpret_cast<const uint16_t*>(D + o.rb + srow);
       const float inv = __frcp_rn(xsc3[j]);
-      const float v0 = sb_apply<BITS, GS>(d[0], d[1], s0, b0, xsum3 + j * 16, sb, c, inv);
-      const float v1 = sb_apply<BITS, GS>(d[2], d[3], s0 + 8 * NGR, b0 + 8 * NGR, xsum3 + j * 16, sb, c, inv);
+      const float v0 = sb_apply<BITS, GS>(d[0], d[1], s0, b0, xsum3 + j * 16, off3 + j * 16, sb, c, inv);
+      const float v1 = sb_apply<BITS, GS>(d[2], d[3], s0 + 8 * NGR, b0 + 8 * NGR, xsum3 + j * 16, off3 + j * 16, sb, c,
+                                          inv);
       if (c == 0) {
         part[(j * 16 + g) * 8 + sb] = v0;
         part[(j * 16 + g + 8) * 8 + sb] = v1;
@@ -631,8 +720,9 @@ YN_DEV void p3_tiles(const DecodeArgs& a, const uint8_t* D, const uint32_t* xf3,
       const uint16_t* s0 = reinterpret_cast<const uint16_t*>(D + o.ss + (size_t)g * DEC_DSBI);
       const uint16_t* b0 = reinterpret_cast<const uint16_t*>(D + o.sb + (size_t)g * DEC_DSBI);
       const float inv = __frcp_rn(xsc3[K]);
-      const float v0 = sb_apply<8, DEC_DGS>(d[0], d[1], s0, b0, xsum3 + K * 16, sb, c, inv);
-      const float v1 = sb_apply<8, DEC_DGS>(d[2], d[3], s0 + 8 * NGS, b0 + 8 * NGS, xsum3 + K * 16, sb, c, inv);
+      const float v0 = sb_apply<8, DEC_DGS>(d[0], d[1], s0, b0, xsum3 + K * 16, off3 + K * 16, sb, c, inv);
+      const float v1 = sb_apply<8, DEC_DGS>(d[2], d[3], s0 + 8 * NGS, b0 + 8 * NGS, xsum3 + K * 16, off3 + K * 16, sb,
+                                            c, inv);
       if (c == 0) {
         part[(K * 16 + g) * 8 + sb] = v0;
         part[(K * 16 + g + 8) * 8 + sb] = v1;
@@ -650,6 +740,7 @@ template <int BITS, int GS>
 YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float* xsum3, float* xsc3) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, K = a.K;
   const int nvec = K + (a.Ish ? 1 : 0);
+  float* off3 = xsum3 + (DEC_MAX_K + 1) * 16;
   for (int j = warp; j < nvec; j += DEC_WARPS) {
     const uint16_t* src = j < K ? a.act + (size_t)j * DEC_I : a.act_sh;
     uint16_t* x = stage + j * DEC_I;
@@ -667,7 +758,7 @@ YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float*
     uint32_t* out = xf3 + j * (DEC_I / 2);
     if (j < K) {
       using S = Sb<BITS>;
-      group_sums16<GS>(x, lane, true, xsum3 + j * 16);
+      group_sums16<BITS, GS>(x, lane, true, scale, xsum3 + j * 16, off3 + j * 16);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int wd = lane + 32 * i, sb = wd / (4 * S::FRAG), rem = wd % (4 * S::FRAG);
@@ -675,7 +766,7 @@ YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float*
       }
     } else {
       using S = Sb<8>;
-      group_sums16<DEC_DGS>(x, lane, true, xsum3 + j * 16);
+      group_sums16<8, DEC_DGS>(x, lane, true, scale, xsum3 + j * 16, off3 + j * 16);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int wd = lane + 32 * i, sb = wd / (4 * S::FRAG), rem = wd % (4 * S::FRAG);
@@ -687,13 +778,15 @@ YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float*
   __syncthreads();
 }
 
-// Diagnostics: SM-cycle stamps of CTA 0 for one token (the last one decoded),
-// 16 per layer; a block-wide sync before each stamp attributes the time of the
-// slowest warp of the CTA.
+// Diagnostics: global-timer stamps (ns) of every CTA for one token (the last
+// one decoded), DEC_STAMPS per layer, at timing[(layer * DEC_STAMPS + slot) *
+// gridDim.x + blockIdx.x]; a block-wide sync before each stamp attributes the
+// time of the slowest warp of the CTA.
 YN_DEV void stamp(const DecodeArgs& a, int tok, int layer, int slot) {
-  if (a.timing && blockIdx.x == 0 && tok == a.n_tokens - 1) {
+  if (a.timing && tok == a.n_tokens - 1) {
     __syncthreads();
-    if (threadIdx.x == 0) a.timing[(size_t)layer * DEC_STAMPS + slot] = (long long)clock64();
+    if (threadIdx.x == 0)
+      a.timing[((size_t)layer * DEC_STAMPS + slot) * gridDim.x + blockIdx.x] = (long long)globaltimer_ns();
   }
 }
 
@@ -711,36 +804,40 @@ YN_DEV int fmt_of(const DecLayer& L) { return (L.rg.bits == 4 ? 2 : 0) + (L.rg.g
 // Fragments and group sums of the normed row for P2 (format of layer L).
 template <int BITS, int GS>
 YN_DEV void p2_frags(const uint16_t* xs, float scale, uint32_t* xf2, float* xsum2) {
+  float* off2 = xsum2 + DEC_H / 32;
   build_frags<BITS>(xs, DEC_H, scale, xf2, threadIdx.x, DEC_THREADS);
-  if (threadIdx.x < DEC_H / 16) group_sums16<GS>(xs, threadIdx.x, true, xsum2);
+  if (threadIdx.x < DEC_H / 16) group_sums16<BITS, GS>(xs, threadIdx.x, true, scale, xsum2, off2);
 }
 
-// P2 after the C tile landed: tile dots, then per unit gate/up sums over the
-// super-blocks in order, SwiGLU, activation row to global memory.
-template <int BITS, int GS>
-YN_DEV void p2_finish(const DecodeArgs& a, const CSeg& sg, int ntile, const uint8_t* C, const uint32_t* xf2,
-                      const float* xsum2, float inv, float* part) {
+// P2 after the tile dots: thread v takes units 2v and 2v+1 (same tile, so
+// the same expert): gate/up sums over the super-blocks in order, SwiGLU, both
+// bf16 activations in one 32-bit store.
+template <int BITS>
+YN_DEV void p2_swiglu(const DecodeArgs& a, const CSeg& sg, int ntile, const float* part, int v) {
   constexpr int NSB = DEC_H * BITS / 8 / 64;
-  p2_tiles<BITS, GS>(a, ntile, C, xf2, xsum2, inv, part);
-  __syncthreads();
-  const int u = threadIdx.x;
-  if (u < ntile * 8) {
+  if (v >= ntile * 4) return;
+  uint32_t pk = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int u = 2 * v + h;
     float gsum = 0.0f, usum = 0.0f;
 #pragma unroll
     for (int q = 0; q < NSB; ++q) {
       gsum = __fadd_rn(gsum, part[(u * 2 + 0) * NSB + q]);
       usum = __fadd_rn(usum, part[(u * 2 + 1) * NSB + q]);
     }
-    const int s = (sg.n > 1 && u >= sg.rows[0]) ? 1 : 0;
-    const int n = sg.n0[s] + (s ? u - sg.rows[0] : u);
-    a.act[(size_t)sg.j[s] * DEC_I + n] = f32_to_bf16(swiglu_bf16(bf16r(gsum), bf16r(usum)));
+    pk |= (uint32_t)f32_to_bf16(swiglu_bf16(bf16r(gsum), bf16r(usum))) << (16 * h);
   }
+  const int u = 2 * v;
+  const int s = (sg.n > 1 && u >= sg.rows[0]) ? 1 : 0;
+  const int n = sg.n0[s] + (s ? u - sg.rows[0] : u);
+  reinterpret_cast<uint32_t*>(a.act)[((size_t)sg.j[s] * DEC_I + n) / 2] = pk;
 }
 
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* barA = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* barC = reinterpret_cast<uint64_t*>(smem + 16);
+  uint64_t* barT = reinterpret_cast<uint64_t*>(smem + 136);   // DEC_MAX_OCT tile barriers
   uint64_t* barD = reinterpret_cast<uint64_t*>(smem + 24);
   float* red = reinterpret_cast<float*>(smem + 32);           // 24 floats
   int* eflag = reinterpret_cast<int*>(smem + 128);
@@ -778,35 +875,38 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
 
   if (tid == 0) {
     mbar_init(barA, DEC_THREADS);
-    mbar_init(barC, DEC_THREADS);
+    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1);
     mbar_init(barD, DEC_THREADS);
     fence_mbar_init();
   }
   load_layer(&lay[0], a.layers, 0);
   load_layer(&lay[1], a.layers, a.n_layers > 1 ? 1 : 0);
   __syncthreads();
-  issue_p1(lay[0], r1, p1_tile(Abuf, r1), barA);
-  unsigned gen = 0;
-  uint32_t phA = 0, phC = 0, phD = 0;
-  bool pendA = true, pendC = false, pendD = false;
+  issue_p1(lay[0], r1, p1_tile(Abuf, r1), barA, 0);
+  uint32_t phA = 0, phT = 0, phD = 0;
+  bool pendA = true, pendT = false, pendD = false;
   // before leaving on an error: let every copy in flight land (bounded)
   auto drain = [&]() {
     asm volatile("cp.async.wait_all;" ::: "memory");
     if (pendA) mbar_wait_block(barA, phA, nullptr);
-    if (pendC) mbar_wait_block(barC, phC, nullptr);
+    if (pendT)
+      for (int t = 0; t < ntile; ++t) mbar_wait_block(&barT[t], phT, nullptr);
     if (pendD) mbar_wait_block(barD, phD, nullptr);
   };
 
+  unsigned gen = 0;
   for (int step = 0; step < total_steps; ++step) {
     const int tok = step / a.n_layers, layer = step % a.n_layers;
     const DecLayer& L = lay[step % 3];
     const DecLayer& Ln = lay[(step + 1) % 3];
     const bool more = step + 1 < total_steps;
     const int fmt = fmt_of(L);
+    const int par = step & 1;
+    const uint32_t ep = (uint32_t)step + 1;  // epoch of the words this step produces
     stamp(a, tok, layer, 0);
     // -------- P1: norm; router + shared rows (tile prefetched during the previous layer)
     {
-      const uint16_t* hin = (layer == 0) ? a.inputs + (size_t)tok * DEC_H : a.hbuf + (size_t)(step & 1) * DEC_H;
+      const uint16_t* hin = (layer == 0) ? a.inputs + (size_t)tok * DEC_H : a.hbuf + (size_t)par * DEC_H;
       const float bv = (tid < nr1 && L.rbias) ? __ldcg(L.rbias + r1.r0 + tid) : 0.0f;
       if (tid < DEC_H / 8) reinterpret_cast<uint4*>(hs)[tid] = __ldcg(reinterpret_cast<const uint4*>(hin) + tid);
       if (tid < 64) rbias_s[tid] = bv;
@@ -835,18 +935,17 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
         default: p2_frags<4, 32>(xs, xscale2, xf2, xsum2); break;
       }
       stamp(a, tok, layer, 3);
-      p1_compute(a, r1, t1, xs, rbias_s, gu);
+      p1_compute(a, r1, t1, xs, rbias_s, gu, par, ep);
     }
-    // the P1 tile is no longer read: prefetch the next layer's into it while
-    // the grid barrier is pending
-    if (more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA);
-    pendA = more;
     if (step + 2 < total_steps) load_layer(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
     stamp(a, tok, layer, 4);
-    if (grid_barrier(a, gen, eflag)) { drain(); return; }
+    if (!a_ok) { drain(); return; }
     stamp(a, tok, layer, 5);
     // -------- P2: route; C / D copies; next layer's P1 tile; gate/up rows
-    route_block(a.logits, K, a.norm_topk, rv, cand, red, ids, wts);
+    if (!route_block(a.f_logits + par * DEC_E, ep, a.err, K, a.norm_topk, rv, cand, red, ids, wts)) {
+      drain();
+      return;
+    }
     if (a.trace_ids && b == 0 && tid < K) a.trace_ids[((size_t)tok * a.n_layers + layer) * K + tid] = ids[tid];
     stamp(a, tok, layer, 6);
     bool ids_ok = true;
@@ -858,40 +957,58 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     ids_ok = __syncthreads_and(ids_ok ? 1 : 0) != 0;
     if (!ids_ok && tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
     if (ids_ok) {
-      switch (fmt) {
-        case 0: copy_c<2, 64>(a, L, ids, sg, C); break;
-        case 1: copy_c<2, 32>(a, L, ids, sg, C); break;
-        case 2: copy_c<4, 64>(a, L, ids, sg, C); break;
-        default: copy_c<4, 32>(a, L, ids, sg, C); break;
+      constexpr int CW = 3;  // issuing warps (the last three)
+      if (warp >= DEC_WARPS - CW) {
+        const int t0 = warp - (DEC_WARPS - CW);
+        switch (fmt) {
+          case 0: copy_c<2, 64>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
+          case 1: copy_c<2, 32>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
+          case 2: copy_c<4, 64>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
+          default: copy_c<4, 32>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
+        }
       }
-      cp_arrive(barC);
-      switch (fmt) {
-        case 0: copy_d<2, 64>(a, L, ids, d0, nd, D); break;
-        case 1: copy_d<2, 32>(a, L, ids, d0, nd, D); break;
-        case 2: copy_d<4, 64>(a, L, ids, d0, nd, D); break;
-        default: copy_d<4, 32>(a, L, ids, d0, nd, D); break;
-      }
-      cp_arrive(barD);
-      pendC = pendD = true;
+      pendT = true;
     }
     stamp(a, tok, layer, 7);
-    const bool c_ok = ids_ok && mbar_wait_block(barC, phC, a.err);
-    stamp(a, tok, layer, 8);
-    if (c_ok) {
-      phC ^= 1;
-      pendC = false;
+    if (ids_ok) {
       const float inv = __frcp_rn(xscale2);
       switch (fmt) {
-        case 0: p2_finish<2, 64>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
-        case 1: p2_finish<2, 32>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
-        case 2: p2_finish<4, 64>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
-        default: p2_finish<4, 32>(a, sg, ntile, C, xf2, xsum2, inv, part); break;
+        case 0: p2_tiles<2, 64>(a, ntile, C, xf2, xsum2, inv, part, barT, phT); break;
+        case 1: p2_tiles<2, 32>(a, ntile, C, xf2, xsum2, inv, part, barT, phT); break;
+        case 2: p2_tiles<4, 64>(a, ntile, C, xf2, xsum2, inv, part, barT, phT); break;
+        default: p2_tiles<4, 32>(a, ntile, C, xf2, xsum2, inv, part, barT, phT); break;
       }
+      phT ^= 1;
+      pendT = false;
+    }
+    __syncthreads();
+    stamp(a, tok, layer, 8);
+    if (ids_ok) {
+      // warps 0-1: SwiGLU of this CTA's units; warps 2..: the D-tile copies
+      // for P3 (they land during the grid barrier)
+      if (warp < 2) {
+        if (L.rg.bits == 2) p2_swiglu<2>(a, sg, ntile, part, tid);
+        else p2_swiglu<4>(a, sg, ntile, part, tid);
+      } else {
+        for (int j = warp - 2; j <= K; j += DEC_WARPS - 2) {
+          switch (fmt) {
+            case 0: copy_d<2, 64>(a, L, ids, d0, nd, D, j); break;
+            case 1: copy_d<2, 32>(a, L, ids, d0, nd, D, j); break;
+            case 2: copy_d<4, 64>(a, L, ids, d0, nd, D, j); break;
+            default: copy_d<4, 32>(a, L, ids, d0, nd, D, j); break;
+          }
+        }
+      }
+      cp_arrive(barD);
+      pendD = true;
     }
     stamp(a, tok, layer, 9);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }
     stamp(a, tok, layer, 10);
-    // -------- P3: activation fragments (staged in the free C tile), down rows, combine
+    // -------- P3: next layer's P1 tile (idle warps), activation fragments
+    // (staged in the free C tile), down rows, combine
+    if (more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA, min(K + 1, DEC_WARPS - 4));
+    pendA = more;
     uint16_t* stage = reinterpret_cast<uint16_t*>(C);
     switch (fmt) {
       case 0: p3_frags<2, 64>(a, stage, xf3, xsum3, xsc3); break;
@@ -919,7 +1036,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
       // weighted term, lane K the gated shared term; sums in column order.
       const int nsbr = (L.rg.bits * DEC_I / 8) / 64;
       const int lane = tid & 31;
-      uint16_t* hout = (layer == a.n_layers - 1) ? a.outputs + (size_t)tok * DEC_H : a.hbuf + (size_t)((step + 1) & 1) * DEC_H;
+      const bool last = layer == a.n_layers - 1;
       for (int t = warp; t < nd; t += DEC_WARPS) {
         float term = 0.0f;
         if (lane < K) {
@@ -939,10 +1056,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
           float o = bf16r(acc);
           if (a.Ish) o = bf16r(__fadd_rn(o, sh));
           o = bf16r(__fadd_rn(bf16_to_f32(hs[d0 + t]), o));
-          hout[d0 + t] = f32_to_bf16(o);
+          (last ? a.outputs + (size_t)tok * DEC_H : a.hbuf + (size_t)(par ^ 1) * DEC_H)[d0 + t] = f32_to_bf16(o);
         }
       }
     }
+    // the C tile held generic-proxy writes (activation staging): order them
+    // before the next layer's bulk copies into it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     stamp(a, tok, layer, 14);
     stamp(a, tok, layer, 15);
     if (grid_barrier(a, gen, eflag)) { drain(); return; }

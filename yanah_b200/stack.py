@@ -21,6 +21,39 @@ from . import _lib
 from .device import DeviceLayer, ExpertArena, Workspace, dims_struct, fill_synthetic_experts, stream_ptr
 from .synthetic import StackConfig, dense_layer
 
+# Stamp slots of the persistent decode kernel (16 per layer; phase i runs from
+# slot i to slot i+1). Grid barriers end phases 4 (bar1) and 9 (bar2); bar3
+# runs from slot 15 of a layer to slot 0 of the next.
+DECODE_STAMPS = 16
+DECODE_PHASES = ["loads", "wait_p1_tile", "norm_frags", "p1_rows", "bar1", "route", "issue_c", "p2_tiles",
+                 "swiglu_issue_d", "bar2", "p3_frags", "wait_d", "p3_tiles", "combine", "end"]
+
+
+def decode_phase_report(timing: np.ndarray) -> dict:
+    """Summarise (L, 16, G) global-timer stamps (ns) of one decoded token.
+
+    Per phase: mean over layers of the mean and of the max over CTAs (us).
+    Per grid barrier: the arrival skew (last arrival - first arrival) and the
+    release latency (first CTA through - last arrival). `layer_us`: mean
+    time from one layer's first stamp to the next layer's."""
+    t = np.asarray(timing, dtype=np.float64) / 1e3
+    L, S, G = t.shape
+    d = np.diff(t, axis=1)                       # (L, S-1, G)
+    out = {"phases_mean_us": {n: round(float(d[:, i].mean()), 3) for i, n in enumerate(DECODE_PHASES)},
+           "phases_max_us": {n: round(float(d[:, i].max(axis=1).mean()), 3) for i, n in enumerate(DECODE_PHASES)}}
+    bars = {}
+    for name, arr_slot, exit_slot in (("bar1", 4, 5), ("bar2", 9, 10)):
+        arr, ext = t[:, arr_slot], t[:, exit_slot]
+        bars[name] = {"skew_us": round(float((arr.max(1) - arr.min(1)).mean()), 3),
+                      "release_us": round(float((ext.min(1) - arr.max(1)).mean()), 3)}
+    if L > 1:
+        arr, ext = t[:-1, 15], t[1:, 0]
+        bars["bar3"] = {"skew_us": round(float((arr.max(1) - arr.min(1)).mean()), 3),
+                        "release_us": round(float((ext.min(1) - arr.max(1)).mean()), 3)}
+        out["layer_us"] = round(float(np.diff(t[:, 0].min(1)).mean()), 3)
+    out["barriers"] = bars
+    return out
+
 
 class ResidentStack:
     def __init__(self, cfg: StackConfig, device: str = "cuda", layers: Optional[List[int]] = None):
@@ -91,7 +124,8 @@ class ResidentStack:
                timing: Optional[torch.Tensor] = None, stream=None) -> None:
         """Sequential bs1 decode of inputs (N,H) -> outputs (N,H) in ONE
         persistent cooperative launch. trace: (N, L, k) int32 routed ids;
-        timing: (L, 8) int64 phase stamps of token 0."""
+        timing: (L, 16, n_SM) int64 global-timer stamps (ns) of every CTA
+        for the last token."""
         lib = _lib.lib()
         n = len(self.structs)
         _lib.check(lib.yn_stack_decode(C.byref(self.dims), self.table.data_ptr(), self.layer_array, n,
