@@ -602,6 +602,9 @@ YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, c
   }
 }
 
+constexpr int DEC_CW = 1;  // warps that issue the C-tile copies
+
+
 // D tile (down rows [d0, d0+nd) of every routed column and of the shared
 // expert): codes [K][16][RBI] then shared [16][Ish]; scales / biases
 // [K][16][SBI] each, then shared scales / biases [16][DEC_DSBI].
@@ -957,14 +960,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     ids_ok = __syncthreads_and(ids_ok ? 1 : 0) != 0;
     if (!ids_ok && tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
     if (ids_ok) {
-      constexpr int CW = 3;  // issuing warps (the last three)
-      if (warp >= DEC_WARPS - CW) {
-        const int t0 = warp - (DEC_WARPS - CW);
+      if (warp >= DEC_WARPS - DEC_CW) {  // the last DEC_CW warps issue the C-tile copies
+        const int t0 = warp - (DEC_WARPS - DEC_CW);
         switch (fmt) {
-          case 0: copy_c<2, 64>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
-          case 1: copy_c<2, 32>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
-          case 2: copy_c<4, 64>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
-          default: copy_c<4, 32>(a, L, ids, sg, ntile, C, barT, t0, CW); break;
+          case 0: copy_c<2, 64>(a, L, ids, sg, ntile, C, barT, t0, DEC_CW); break;
+          case 1: copy_c<2, 32>(a, L, ids, sg, ntile, C, barT, t0, DEC_CW); break;
+          case 2: copy_c<4, 64>(a, L, ids, sg, ntile, C, barT, t0, DEC_CW); break;
+          default: copy_c<4, 32>(a, L, ids, sg, ntile, C, barT, t0, DEC_CW); break;
         }
       }
       pendT = true;
