@@ -21,6 +21,12 @@ What each fixture pins (the reference function that produced it):
   tie-free probability vectors, plus ``observe`` recall counters.
 * ``softmax.npz`` — the fp32 softmax of ``predictor.py:95-97`` (lookahead
   probabilities) on random logits.
+* ``pool_small.npz``, ``pool_wide.npz`` — ``moe_prefetch/pool.py:90-282``
+  ``SlotPool`` driven by ``tests/pool_driver.drive_slot_pool`` (slot
+  decisions and stats), and ``moe_prefetch/cache_sim.py:88-200`` ``PoolSim``
+  + ``ForecastPolicy`` replaying the same seeded routing trace in
+  ``simulate``'s order (:296-323), with per-(step, layer) counters, the
+  final dictionary and the demand-miss log.
 * ``expert_mlp.npz`` — ``moe_prefetch/test_synthetic.py:46-51``
   ``expert_mlp`` (fp16 weights, fp32 SwiGLU MLP) on weights that are exactly
   representable as 4-bit affine codes, so the quantised CUDA/oracle path and
@@ -163,6 +169,50 @@ def make_expert_mlp(rng):
             "scale": np.float32(1 / 32), "bias": np.float32(-8 / 32), "x": x, "y": y}
 
 
+def make_pool(rng, S: int, L: int, E: int, k: int, n_cand: int, spec: int):
+    """Reference SlotPool driven by tests/pool_driver.drive_slot_pool and the
+    reference cache_sim replay (PoolSim + ForecastPolicy, the loop order of
+    cache_sim.simulate) with per-(step, layer) counter snapshots."""
+    sys.path.insert(0, str(REPO))
+    from tests.pool_driver import NullMemory, drive_slot_pool, fc_to_arrays, make_trace, stats_tuple
+    from moe_prefetch import cache_sim
+    from moe_prefetch.layout import ModelGeometry
+    from moe_prefetch.pool import SlotPool
+
+    routed, fc = make_trace(rng, S, L, E, k, n_cand=n_cand)
+    slots = int(0.2 * E * L)
+    g = ModelGeometry(n_layers=L, n_mtp_layers=0, n_experts=E, top_k=k, hidden=64, moe_inter=32, bits=4,
+                      group_size=32)
+    pool = SlotPool(g, slots, spec_slot_cap=spec, memory=NullMemory())
+    log = drive_slot_pool(pool, routed, fc)
+    trace = cache_sim.Trace(routed, np.zeros(S, np.int64), fc, {"n_layers": L})
+    test = (np.arange(S) >= S // 4).astype(np.int8)
+    names = ["uses", "hits", "adopted", "demand", "prefetch", "wasted", "refused", "tokens"]
+    sim = cache_sim.PoolSim(slots, spec)
+    miss_log = []
+    sim.miss_log = miss_log
+    pol = cache_sim.ForecastPolicy(trace, 0.062, 32)
+    snaps = []
+    for s in range(S):
+        sim.measure = bool(test[s])
+        for l in range(L):
+            sim.layer(l, trace.routed[s, l])
+            pol.issue(sim, s, l)
+            sim.expire(l)
+            snaps.append([sim.c[n] for n in names])
+        sim.end_token()
+    final = cache_sim.simulate(trace, test, slots, spec, forecast=cache_sim.ForecastPolicy(trace, 0.062, 32))
+    assert all(final[n] == sim.c[n] for n in names)
+    ml_layer = np.array([l for l, m in miss_log for _ in m], np.int16)
+    ml_expert = np.array([e for _, m in miss_log for e in m], np.int16)
+    ml_len = np.array([len(m) for _, m in miss_log], np.int16)
+    return {"routed": routed.astype(np.int16), "test": test, "slots": np.int64(slots), "spec": np.int64(spec),
+            "pool_log": np.array(log, np.int64), "pool_stats": np.array(stats_tuple(pool.stats), np.int64),
+            "snaps": np.array(snaps, np.int64).reshape(S, L, len(names)),
+            "final_keys": np.array(sorted(final)), "final_vals": np.array([final[k2] for k2 in sorted(final)], np.float64),
+            "miss_layer": ml_layer, "miss_expert": ml_expert, "miss_len": ml_len, **fc_to_arrays(fc)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -176,6 +226,8 @@ def main():
     np.savez_compressed(HERE / "select.npz", **make_select(rng))
     np.savez_compressed(HERE / "softmax.npz", **make_softmax(rng))
     np.savez_compressed(HERE / "expert_mlp.npz", **make_expert_mlp(rng))
+    np.savez_compressed(HERE / "pool_small.npz", **make_pool(rng, S=40, L=12, E=128, k=8, n_cand=16, spec=32))
+    np.savez_compressed(HERE / "pool_wide.npz", **make_pool(rng, S=12, L=24, E=512, k=10, n_cand=12, spec=64))
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 
