@@ -102,6 +102,10 @@ class CudaMoEBackend:
                        for l in range(cfg.n_layers)]
         self.ws = Workspace(self.dims, self.device, self.stream)
         self._lut = torch.zeros(cfg.n_experts, dtype=torch.int32, device=self.device)
+        # expert -> slot tables go up through a ring of pinned buffers (no host sync)
+        self._lut_host = [torch.empty(cfg.n_experts, dtype=torch.int32, pin_memory=True) for _ in range(8)]
+        self._lut_ev: List[Optional[torch.cuda.Event]] = [None] * len(self._lut_host)
+        self._lut_i = 0
         self._pre: Dict[int, dict] = {}
         self._unfenced: Optional[torch.cuda.Event] = None
 
@@ -114,11 +118,21 @@ class CudaMoEBackend:
 
     def _layer_struct(self, layer: int, memory: CudaExpertMemory, rows: Dict[int, int]) -> _lib.Layer:
         """Layer descriptor whose routed experts live in `memory` at `rows`."""
-        lut = np.zeros(self.cfg.n_experts, np.int32)
+        i = self._lut_i
+        self._lut_i = (i + 1) % len(self._lut_host)
+        if self._lut_ev[i] is not None:
+            self._lut_ev[i].synchronize()        # the copy out of this buffer has run
+        lut = self._lut_host[i].numpy()
+        lut[:] = 0
         if rows:
             lut[np.fromiter(rows.keys(), dtype=np.int64)] = np.fromiter(rows.values(), dtype=np.int64)
         with torch.cuda.stream(self.stream):
-            self._lut = torch.from_numpy(lut).to(self.device, non_blocking=False)
+            dev = torch.empty(self.cfg.n_experts, dtype=torch.int32, device=self.device)
+            dev.copy_(self._lut_host[i], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(self.stream)
+        self._lut_ev[i] = ev
+        self._lut = dev   # freed tensors are reused in stream order by the caching allocator
         L = self.layers[layer].struct()
         L.expert_base = memory.arena.base
         L.slot_stride = memory.arena.slot_bytes
