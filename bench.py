@@ -188,6 +188,99 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------- streaming leg
+STREAM_METRIC = "decode tok/s (bs1) streaming: 20% HBM slot pool + pinned host tier, Qwen3-Next-80B-A3B-shaped"
+
+
+def host_link_gbs(dev, nbytes: int = 1 << 30) -> float:
+    """Pinned host -> device copy bandwidth (one large cudaMemcpyAsync, events)."""
+    import torch
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        d.copy_(h, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = max(best, nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    return best
+
+
+def run_streaming(args, rank: int, world: int):
+    """Config 2: the 48-layer stack with the slot pool at 20% of the experts;
+    the rest in pinned host memory; lookahead-2 forecasts (threshold 0.062,
+    at most 32 per target, top 24) copy on a side stream. Input rows follow
+    an AR(1) process (rho = args.rho) so consecutive tokens route alike."""
+    import numpy as np
+    import torch
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.streaming import HostTier, StreamingDecoder
+    from yanah_b200.synthetic import hidden_stream_id, qwen3_next_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = qwen3_next_stack(seed=0)
+    link = host_link_gbs(dev)
+    host = HostTier(cfg, dev)
+    dec = StreamingDecoder(cfg, slot_fraction=0.2, spec_slot_cap=64, lookahead=2, threshold=0.062, issue_cap=32,
+                           top=24, device=dev, host=host)
+    H, N = cfg.hidden, args.stream_tokens
+    total = N * (args.warmup + args.steps)
+    noise = torch.empty((total, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(noise.data_ptr(), total * H, cfg.seed, hidden_stream_id(100 + rank), 1.0, 0.0,
+                                        stream_ptr()))
+    x = noise.float()
+    rho = args.rho
+    for t in range(1, total):
+        x[t] = rho * x[t - 1] + (1 - rho * rho) ** 0.5 * x[t]
+    inputs = x.to(torch.bfloat16)
+    outputs = torch.empty_like(inputs)
+    for w in range(args.warmup):
+        dec.decode(inputs[w * N:(w + 1) * N], outputs[w * N:(w + 1) * N])
+    torch.cuda.synchronize(dev)
+    dec.reset_stats()
+    dec.trace = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    off = args.warmup * N
+    for k in range(args.steps):
+        dec.decode(inputs[off + k * N:off + (k + 1) * N], outputs[off + k * N:off + (k + 1) * N])
+    e1.record()
+    torch.cuda.synchronize(dev)
+    secs = e0.elapsed_time(e1) / 1e3
+    r = dec.report(secs)
+    if dec.be.check_error():
+        raise RuntimeError("device error in the streaming decode")
+    tr = np.array(dec.trace).reshape(-1, cfg.n_layers, cfg.top_k)
+    rep = float(np.mean([len(set(tr[t, l]) & set(tr[t - 1, l])) / cfg.top_k
+                         for t in range(1, tr.shape[0]) for l in range(cfg.n_layers)])) if tr.shape[0] > 1 else 0.0
+    tokens = N * args.steps
+    line = {
+        "metric": STREAM_METRIC, "value": round(tokens / secs, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "qwen3_next_80b_a3b_moe_stack48_bs1_streaming", "pool_slots": r["pool_slots"],
+                   "pool_fraction": 0.2, "spec_slots": r["spec_slots"], "lookahead": 2, "threshold": 0.062,
+                   "issue_cap": 32, "forecast_top": 24, "tokens_per_step": N, "input_ar1_rho": rho,
+                   "host_tier_gb": round(host.nbytes / 1e9, 2)},
+        "streaming": {"hit_rate": round(r["hit_rate"], 4), "adopted": r["adopted"],
+                      "forecast_recall": round(r["forecast_recall"], 4),
+                      "demand_records_per_token": round(r["demand_records"] / tokens, 2),
+                      "spec_records_per_token": round(r["spec_records"] / tokens, 2),
+                      "h2d_gbs": round(r["h2d_gbs"], 2), "stall_ms_per_token": round(r["stall_ms"] / tokens, 3),
+                      "copy_busy_ms_per_token": round(r["copy_busy_ms"] / tokens, 3),
+                      "hidden_fraction": round(r["hidden_fraction"], 4),
+                      "measured_repeat_rate": round(rep, 4), "target_repeat_rate": 0.6},
+        "roofline": {"bound": "host-link", "achieved": round(r["h2d_gbs"], 2), "peak": round(link, 2),
+                     "unit": "GB/s", "frac": round(r["h2d_gbs"] / link, 4),
+                     "peak_source": "pinned host->device cudaMemcpyAsync of 1 GiB, measured in this run"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, rank: int, world: int):
     import numpy as np
@@ -321,6 +414,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
+    ap.add_argument("--workload", choices=["resident", "streaming"], default="resident",
+                    help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier")
+    ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
+    ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -335,6 +432,9 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.workload == "streaming":
+            if rank == 0:
+                run_streaming(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

@@ -100,6 +100,7 @@ class StreamingDecoder:
         self.ev_compute: Optional[torch.cuda.Event] = None
         self.stats = StreamStats()
         self.measure = measure
+        self.trace: Optional[List[np.ndarray]] = None   # routed ids per layer, when set to a list
 
     # ------------------------------------------------------------- copies
     def _copy(self, stream, pairs: List[Tuple[int, int]], layer: int) -> Optional[torch.cuda.Event]:
@@ -130,6 +131,8 @@ class StreamingDecoder:
         h_res, x, logits = be.pre_moe(l, h)
         targets = [t for t in (l + 1, l + 2) if t < self.cfg.n_layers]
         ids, w, probs = be.route_and_forecast(logits, h_res, targets)
+        if self.trace is not None:
+            self.trace.append(ids[0].copy())
         self.fc.observe(l, ids)
         pool.drain_returned()
         out: Dict[int, int] = {}
@@ -231,6 +234,13 @@ class StreamingDecoder:
                 self.stats.stall_ms += max(0.0, ms)
         self.stats._pending = []
         return self.stats
+
+    def reset_stats(self) -> None:
+        """Start counting afresh (after a warm-up that filled the pool)."""
+        self.collect()
+        self.stats = StreamStats()
+        self.pool.stats = type(self.pool.stats)()
+        self.fc.stats = type(self.fc.stats)()
 
     def report(self, seconds: float) -> dict:
         st = self.collect()
