@@ -773,14 +773,19 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   a.c_rows = 8 * oct_max;
   a.c_rb = rb_max;
   a.c_sb = sb_max;
-  const size_t c_bytes = std::max((size_t)2 * a.c_rows * a.c_rb + (size_t)4 * a.c_rows * a.c_sb,
-                                  (size_t)(K + 1) * DEC_I * 2);
-  a.off_C = (int)o; o += a16h(c_bytes);
   a.d_rb = rbi_max;
   a.d_sb = sbi_max;
   const size_t d_bytes = (size_t)K * DEC_MAX_DROWS * a.d_rb + (size_t)DEC_MAX_DROWS * DEC_I +
                          2 * (size_t)K * DEC_MAX_DROWS * a.d_sb + 2 * (size_t)DEC_MAX_DROWS * DEC_DSBI;
-  a.off_D = (int)o; o += a16h(d_bytes);
+  // The C tile (gate/up rows) is dead once P2's dots are done; P3's
+  // activation staging and the D tile (down rows, copied after P2) share its
+  // space, staging first.
+  const size_t stage_bytes = a16h((size_t)(K + 1) * DEC_I * 2);
+  const size_t c_bytes = std::max((size_t)2 * a.c_rows * a.c_rb + (size_t)4 * a.c_rows * a.c_sb,
+                                  stage_bytes + d_bytes);
+  a.off_C = (int)o;
+  a.off_D = (int)(o + stage_bytes);
+  o += a16h(c_bytes);
   const size_t smem = o;
   int optin = 0;
   YN_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));

@@ -129,33 +129,38 @@ YN_DEV uint32_t wait_flag(const u64* p, uint32_t epoch, int* err, bool& fail) {
 }
 
 // ---------------------------------------------------------------- barrier
-// Returns true (block-uniform) when the decode must stop: an error was seen
-// while waiting, or the wait ran out (then the error is raised here).
-YN_DEV bool grid_barrier(const DecodeArgs& a, unsigned& gen, int* flag) {
+// Grid barrier in two halves so that a CTA can issue copies for the next
+// phase between its arrival and the release. Arrival: block sync, then one
+// release add on the counter. Wait: lane 0 of warps 0-3 poll the counter
+// with acquire loads, starting ~150 ns apart so that the release is seen
+// within a quarter of a round trip; the first to see it (or a timeout, or
+// the error word) ends the others' loops through shared memory. Returns true
+// (block-uniform) when the decode must stop.
+YN_DEV void grid_arrive(const DecodeArgs& a) {
   __syncthreads();
-  gen += 1;
-  if (threadIdx.x == 0) {
-    const unsigned target = gen * gridDim.x;
-    int stop = 0;
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
-    if (v < target) {
-      const uint64_t t0 = globaltimer_ns();
-      for (unsigned it = 1;; ++it) {
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
-        if (v >= target) break;
-        if ((it & 63) == 0) {
-          if (*reinterpret_cast<volatile int*>(a.err)) { stop = 1; break; }
-          if (globaltimer_ns() - t0 > 2000000000ull) {
-            raise_error(a.err, YN_ERR_BULK_TIMEOUT);
-            stop = 1;
-            break;
-          }
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+}
+YN_DEV bool grid_wait(const DecodeArgs& a, unsigned target, volatile int* done, int* flag) {
+  const int tid = threadIdx.x;
+  if (tid == 0) { *done = 0; *flag = 0; }
+  __syncthreads();
+  if ((tid & 31) == 0 && tid < 128) {
+    __nanosleep(150u * (unsigned)(tid >> 5));
+    const uint64_t t0 = globaltimer_ns();
+    for (unsigned it = 0; !*done; ++it) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+      if (v >= target) { *done = 1; break; }
+      if ((it & 63) == 63) {
+        if (*reinterpret_cast<volatile int*>(a.err)) { *flag = 1; *done = 1; break; }
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+          raise_error(a.err, YN_ERR_BULK_TIMEOUT);
+          *flag = 1;
+          *done = 1;
+          break;
         }
       }
     }
-    *flag = stop;
   }
   __syncthreads();
   return *flag != 0;
@@ -268,8 +273,9 @@ YN_DEV void issue_p1(const DecLayer& L, const P1Range& r, const P1Tile& t, uint6
   cp_arrive(bar);
 }
 
-// RMSNorm in the canonical 128-thread order (threads 128.. idle in the sum).
-YN_DEV void rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uint16_t* out, float* red) {
+// RMSNorm in the canonical 128-thread order (threads 128.. idle in the sum);
+// returns max |x| of the normed row (every thread).
+YN_DEV float rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uint16_t* out, float* red) {
   const int tid = threadIdx.x;
   float ss = 0.0f;
   if (tid < 128)
@@ -284,9 +290,17 @@ YN_DEV void rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uint
   __syncthreads();
   const float tot = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
   const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)DEC_H), eps));
-  for (int i = tid; i < DEC_H; i += DEC_THREADS)
-    out[i] = f32_to_bf16(__fmul_rn(bf16_to_f32(w_g[i]), bf16r(__fmul_rn(bf16_to_f32(h[i]), r))));
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = tid; i < DEC_H; i += DEC_THREADS) {
+    const uint16_t o = f32_to_bf16(__fmul_rn(bf16_to_f32(w_g[i]), bf16r(__fmul_rn(bf16_to_f32(h[i]), r))));
+    out[i] = o;
+    mx = fmaxf(mx, fabsf(bf16_to_f32(o)));
+  }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[8 + (tid >> 5)] = mx;
   __syncthreads();
+  return warp_max(red[8 + (tid & 15)]);
 }
 
 // P1 compute: router rows, shared pairs, shared_expert_gate (canonical fp32
@@ -328,13 +342,15 @@ YN_DEV void p1_compute(const DecodeArgs& a, const P1Range& r, const P1Tile& t, c
 
 // ------------------------------------------------------------------ routing
 // Block-wide routing of the 512 logits (thread t <-> expert t; each thread
-// waits for its flagged logit; false when that wait failed) in the
+// waits for its flagged logit; false when that wait failed; *ids_ok = whether
+// every routed expert has a slot in layer L) in the
 // canonical order of the oracle: max (order-free), exp per element, sum per
 // lane over e = lane + 32 i then a butterfly (warp 0), bf16 probabilities,
 // then top-k by the unique key (bf16 prob << 16 | 0xFFFF - id): per-warp
 // top-k over its 32 experts, merged by warp 0. Results in shared memory.
 YN_DEV bool route_block(const u64* f_logits, uint32_t ep, int* err, int K, int norm, float* v /* E */,
-                        uint32_t* cand /* 16*16 */, float* red, int32_t* ids_out, float* w_out) {
+                        uint32_t* cand /* 16*16 */, float* red, int32_t* ids_out, float* w_out,
+                        const DecLayer& L, int* ids_ok) {
   static_assert(DEC_E == DEC_THREADS, "one expert per thread");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   bool fail = false;
@@ -389,10 +405,15 @@ YN_DEV bool route_block(const u64* f_logits, uint32_t ep, int* err, int K, int n
       }
     }
     const float sb = bf16r(wsum);
+    bool bad = false;
     if (lane < K) {
       ids_out[lane] = myid;
       w_out[lane] = norm ? bf16r(__fdiv_rn(myp, sb)) : myp;
+      const int sl = L.slot_of ? L.slot_of[myid] : myid;   // the expert's slot must exist
+      bad = sl < 0 || sl >= L.n_slots;
     }
+    const unsigned anybad = __ballot_sync(0xffffffffu, bad);
+    if (lane == 0) *ids_ok = anybad == 0u;
   }
   __syncthreads();
   return true;
@@ -777,6 +798,7 @@ YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float*
       }
     }
     if (lane == 0) xsc3[j] = scale;
+    if (lane == 0 && j == K) xsc3[DEC_MAX_K + 2] = __ldcg(a.sgate);  // shared-expert gate for the combine
   }
   __syncthreads();
 }
@@ -784,13 +806,22 @@ YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float*
 // Diagnostics: global-timer stamps (ns) of every CTA for one token (the last
 // one decoded), DEC_STAMPS per layer, at timing[(layer * DEC_STAMPS + slot) *
 // gridDim.x + blockIdx.x]; a block-wide sync before each stamp attributes the
-// time of the slowest warp of the CTA.
+// time of the slowest warp of the CTA. Out of line: off the hot code path.
+__device__ __noinline__ void stamp_at(long long* timing, int layer, int slot) {
+  __syncthreads();
+  if (threadIdx.x == 0)
+    timing[((size_t)layer * DEC_STAMPS + slot) * gridDim.x + blockIdx.x] = (long long)globaltimer_ns();
+}
 YN_DEV void stamp(const DecodeArgs& a, int tok, int layer, int slot) {
-  if (a.timing && tok == a.n_tokens - 1) {
-    __syncthreads();
-    if (threadIdx.x == 0)
-      a.timing[((size_t)layer * DEC_STAMPS + slot) * gridDim.x + blockIdx.x] = (long long)globaltimer_ns();
-  }
+  if (a.timing && tok == a.n_tokens - 1) stamp_at(a.timing, layer, slot);
+}
+
+// Asynchronous copy of the descriptor of layer `idx` into a shared-memory
+// slot (tracked by the next cp_arrive of the copying threads).
+YN_DEV void load_layer_async(DecLayer* slot, const DecLayer* table, int idx) {
+  constexpr int NW = sizeof(DecLayer) / 16;
+  if (threadIdx.x < NW)
+    cp16(reinterpret_cast<uint4*>(slot) + threadIdx.x, reinterpret_cast<const uint4*>(table + idx) + threadIdx.x);
 }
 
 // Copy descriptor of layer `idx` into a shared-memory slot.
@@ -844,6 +875,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
   uint64_t* barD = reinterpret_cast<uint64_t*>(smem + 24);
   float* red = reinterpret_cast<float*>(smem + 32);           // 24 floats
   int* eflag = reinterpret_cast<int*>(smem + 128);
+  volatile int* done_s = reinterpret_cast<volatile int*>(smem + 132);  // barrier pollers' flag
+  int* ids_ok_s = reinterpret_cast<int*>(smem + 200);                  // routed experts all have slots
   uint16_t* hs = reinterpret_cast<uint16_t*>(smem + a.off_hs);
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + a.off_xs);
   uint8_t* rt = smem + a.off_route;
@@ -922,15 +955,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     if (a_ok) {
       phA ^= 1;
       pendA = false;
-      rmsnorm_smem(hs, t1.norm, a.eps, xs, red);
       // power-of-two scale of the normed row, fragments and group sums for P2
-      float mx = 0.0f;
-      for (int i = tid; i < DEC_H; i += DEC_THREADS) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[i])));
-      mx = warp_max(mx);
-      if ((tid & 31) == 0) red[8 + warp] = mx;
-      __syncthreads();
-      mx = warp_max(red[8 + (tid & 15)]);
-      xscale2 = fp16_input_scale(mx);
+      xscale2 = fp16_input_scale(rmsnorm_smem(hs, t1.norm, a.eps, xs, red));
       switch (fmt) {
         case 0: p2_frags<2, 64>(xs, xscale2, xf2, xsum2); break;
         case 1: p2_frags<2, 32>(xs, xscale2, xf2, xsum2); break;
@@ -940,24 +966,17 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
       stamp(a, tok, layer, 3);
       p1_compute(a, r1, t1, xs, rbias_s, gu, par, ep);
     }
-    if (step + 2 < total_steps) load_layer(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
     stamp(a, tok, layer, 4);
     if (!a_ok) { drain(); return; }
     stamp(a, tok, layer, 5);
     // -------- P2: route; C / D copies; next layer's P1 tile; gate/up rows
-    if (!route_block(a.f_logits + par * DEC_E, ep, a.err, K, a.norm_topk, rv, cand, red, ids, wts)) {
+    if (!route_block(a.f_logits + par * DEC_E, ep, a.err, K, a.norm_topk, rv, cand, red, ids, wts, L, ids_ok_s)) {
       drain();
       return;
     }
     if (a.trace_ids && b == 0 && tid < K) a.trace_ids[((size_t)tok * a.n_layers + layer) * K + tid] = ids[tid];
     stamp(a, tok, layer, 6);
-    bool ids_ok = true;
-    for (int j = 0; j < K; ++j) {
-      const int e = ids[j];
-      const int sl = (e >= 0 && e < DEC_E) ? (L.slot_of ? L.slot_of[e] : e) : -1;
-      if (sl < 0 || sl >= L.n_slots) ids_ok = false;
-    }
-    ids_ok = __syncthreads_and(ids_ok ? 1 : 0) != 0;
+    const bool ids_ok = *ids_ok_s != 0;   // block-uniform (set before routing's last sync)
     if (!ids_ok && tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
     if (ids_ok) {
       if (warp >= DEC_WARPS - DEC_CW) {  // the last DEC_CW warps issue the C-tile copies
@@ -985,30 +1004,33 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     }
     __syncthreads();
     stamp(a, tok, layer, 8);
+    if (ids_ok && warp < 2) {  // SwiGLU of this CTA's units
+      if (L.rg.bits == 2) p2_swiglu<2>(a, sg, ntile, part, tid);
+      else p2_swiglu<4>(a, sg, ntile, part, tid);
+    }
+    stamp(a, tok, layer, 9);
+    grid_arrive(a);
     if (ids_ok) {
-      // warps 0-1: SwiGLU of this CTA's units; warps 2..: the D-tile copies
-      // for P3 (they land during the grid barrier)
-      if (warp < 2) {
-        if (L.rg.bits == 2) p2_swiglu<2>(a, sg, ntile, part, tid);
-        else p2_swiglu<4>(a, sg, ntile, part, tid);
-      } else {
-        for (int j = warp - 2; j <= K; j += DEC_WARPS - 2) {
-          switch (fmt) {
-            case 0: copy_d<2, 64>(a, L, ids, d0, nd, D, j); break;
-            case 1: copy_d<2, 32>(a, L, ids, d0, nd, D, j); break;
-            case 2: copy_d<4, 64>(a, L, ids, d0, nd, D, j); break;
-            default: copy_d<4, 32>(a, L, ids, d0, nd, D, j); break;
-          }
+      // the D-tile copies for P3 go out while the grid barrier is pending
+      for (int j = warp; j <= K; j += DEC_WARPS) {
+        switch (fmt) {
+          case 0: copy_d<2, 64>(a, L, ids, d0, nd, D, j); break;
+          case 1: copy_d<2, 32>(a, L, ids, d0, nd, D, j); break;
+          case 2: copy_d<4, 64>(a, L, ids, d0, nd, D, j); break;
+          default: copy_d<4, 32>(a, L, ids, d0, nd, D, j); break;
         }
       }
       cp_arrive(barD);
       pendD = true;
     }
-    stamp(a, tok, layer, 9);
-    if (grid_barrier(a, gen, eflag)) { drain(); return; }
+    gen += 1;
+    if (grid_wait(a, gen * (unsigned)G, done_s, eflag)) { drain(); return; }
     stamp(a, tok, layer, 10);
     // -------- P3: next layer's P1 tile (idle warps), activation fragments
     // (staged in the free C tile), down rows, combine
+    // descriptor of layer step+2: its copy completes with this P1-tile phase,
+    // which step+1 waits for before using anything of step+2
+    if (step + 2 < total_steps) load_layer_async(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
     if (more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA, min(K + 1, DEC_WARPS - 4));
     pendA = more;
     uint16_t* stage = reinterpret_cast<uint16_t*>(C);
@@ -1049,7 +1071,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
           float y = 0.0f;
 #pragma unroll
           for (int q = 0; q < DEC_I / 64; ++q) y = __fadd_rn(y, part[(K * 16 + t) * 8 + q]);
-          term = bf16r(__fmul_rn(__ldcg(a.sgate), bf16r(y)));
+          term = bf16r(__fmul_rn(xsc3[DEC_MAX_K + 2], bf16r(y)));
         }
         float acc = 0.0f;
         for (int j = 0; j < K; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, term, j));
@@ -1067,7 +1089,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     stamp(a, tok, layer, 14);
     stamp(a, tok, layer, 15);
-    if (grid_barrier(a, gen, eflag)) { drain(); return; }
+    grid_arrive(a);
+    gen += 1;
+    if (grid_wait(a, gen * (unsigned)G, done_s, eflag)) { drain(); return; }
   }
 }
 
