@@ -131,36 +131,31 @@ YN_DEV uint32_t wait_flag(const u64* p, uint32_t epoch, int* err, bool& fail) {
 // ---------------------------------------------------------------- barrier
 // Grid barrier in two halves so that a CTA can issue copies for the next
 // phase between its arrival and the release. Arrival: block sync, then one
-// release add on the counter. Wait: lane 0 of warps 0-3 poll the counter
-// with acquire loads, starting ~150 ns apart so that the release is seen
-// within a quarter of a round trip; the first to see it (or a timeout, or
-// the error word) ends the others' loops through shared memory. Returns true
-// (block-uniform) when the decode must stop.
+// release add on the counter. Wait: thread 0 polls the counter with acquire
+// loads (watching the error word every 64 polls and a 2 s limit), then a
+// block sync. Returns true (block-uniform) when the decode must stop.
 YN_DEV void grid_arrive(const DecodeArgs& a) {
   __syncthreads();
   if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
 }
-YN_DEV bool grid_wait(const DecodeArgs& a, unsigned target, volatile int* done, int* flag) {
-  const int tid = threadIdx.x;
-  if (tid == 0) { *done = 0; *flag = 0; }
-  __syncthreads();
-  if ((tid & 31) == 0 && tid < 128) {
-    __nanosleep(150u * (unsigned)(tid >> 5));
+YN_DEV bool grid_wait(const DecodeArgs& a, unsigned target, int* flag) {
+  if (threadIdx.x == 0) {
+    int stop = 0;
     const uint64_t t0 = globaltimer_ns();
-    for (unsigned it = 0; !*done; ++it) {
+    for (unsigned it = 0;; ++it) {
       unsigned v;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
-      if (v >= target) { *done = 1; break; }
+      if (v >= target) break;
       if ((it & 63) == 63) {
-        if (*reinterpret_cast<volatile int*>(a.err)) { *flag = 1; *done = 1; break; }
+        if (*reinterpret_cast<volatile int*>(a.err)) { stop = 1; break; }
         if (globaltimer_ns() - t0 > 2000000000ull) {
           raise_error(a.err, YN_ERR_BULK_TIMEOUT);
-          *flag = 1;
-          *done = 1;
+          stop = 1;
           break;
         }
       }
     }
+    *flag = stop;
   }
   __syncthreads();
   return *flag != 0;
@@ -875,7 +870,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
   uint64_t* barD = reinterpret_cast<uint64_t*>(smem + 24);
   float* red = reinterpret_cast<float*>(smem + 32);           // 24 floats
   int* eflag = reinterpret_cast<int*>(smem + 128);
-  volatile int* done_s = reinterpret_cast<volatile int*>(smem + 132);  // barrier pollers' flag
   int* ids_ok_s = reinterpret_cast<int*>(smem + 200);                  // routed experts all have slots
   uint16_t* hs = reinterpret_cast<uint16_t*>(smem + a.off_hs);
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + a.off_xs);
@@ -1024,7 +1018,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
       pendD = true;
     }
     gen += 1;
-    if (grid_wait(a, gen * (unsigned)G, done_s, eflag)) { drain(); return; }
+    if (grid_wait(a, gen * (unsigned)G, eflag)) { drain(); return; }
     stamp(a, tok, layer, 10);
     // -------- P3: next layer's P1 tile (idle warps), activation fragments
     // (staged in the free C tile), down rows, combine
@@ -1091,7 +1085,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     stamp(a, tok, layer, 15);
     grid_arrive(a);
     gen += 1;
-    if (grid_wait(a, gen * (unsigned)G, done_s, eflag)) { drain(); return; }
+    if (grid_wait(a, gen * (unsigned)G, eflag)) { drain(); return; }
   }
 }
 
