@@ -581,17 +581,17 @@ YN_DEV const uint8_t* expert_record(const DecLayer& L, int e) {
   return L.ebase + (size_t)(L.slot_of ? L.slot_of[e] : e) * (size_t)L.stride;
 }
 
-// Bulk copies of this CTA's C tile, issued by a few warps tile by tile
-// (warp i of n takes tiles i, i+n, ...; lane k
-// issues piece k: gate codes, gate scales, gate biases, up codes, up scales,
-// up biases of the tile's 8 rows); tile t completes on its own mbarrier, so
-// P2 starts on tile 0 while later tiles are in flight. A tile (8 units) never
-// crosses an expert boundary.
+// Copies of this CTA's C tile, issued by one warp tile by tile; tile t
+// completes on its own mbarrier (count 1 + 32), so P2 starts on tile 0 while
+// later tiles are in flight. Per tile: the gate and up codes of its 8 rows
+// (two contiguous 8-row pieces) go as two bulk copies (lane 0 posts their
+// byte count); the four small scale/bias pieces go as 16-byte cp.async over
+// the 32 lanes, which then arrive on the barrier when their copies land. A
+// tile (8 units) never crosses an expert boundary.
 template <int BITS, int GS>
 YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, int ntile, uint8_t* C,
                    uint64_t* barT, int t0, int tstep) {
-  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2;
-  constexpr uint32_t TILE_BYTES = 8u * (2u * RB + 4u * SBH);
+  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, CS = SBH / 16;
   const int lane = threadIdx.x & 31;
   if (!ntile) return;
   const uint8_t* rec0 = expert_record(L, ids[sg.j[0]]);
@@ -599,22 +599,20 @@ YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, c
   const size_t sbase = (size_t)2 * a.c_rows * a.c_rb;
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   for (int t = t0; t < ntile; t += tstep) {
-    if (lane == 0) mbar_arrive_expect_tx(&barT[t], TILE_BYTES);
+    const int row = 8 * t, seg = row >= sg.rows[0] ? 1 : 0;
+    const int n = sg.n0[seg] + (seg ? row - sg.rows[0] : row);
+    const uint8_t* rec = seg ? rec1 : rec0;
+    if (lane == 0) mbar_arrive_expect_tx(&barT[t], 16u * RB);
     __syncwarp();
-    if (lane < 6) {
-      const int row = 8 * t, seg = row >= sg.rows[0] ? 1 : 0;
-      const int n = sg.n0[seg] + (seg ? row - sg.rows[0] : row);
-      const uint8_t* rec = seg ? rec1 : rec0;
-      const int up = lane / 3, kind = lane % 3;
-      if (kind == 0) {
-        bulk_g2s(C + (size_t)up * a.c_rows * a.c_rb + (size_t)row * RB, rec + L.rg.off[3 * up] + (size_t)n * RB,
-                 8u * RB, &barT[t]);
-      } else {
-        bulk_g2s(C + sbase + (size_t)(2 * up + kind - 1) * a.c_rows * a.c_sb + (size_t)row * SBH,
-                 rec + L.rg.off[3 * up + kind] + (size_t)n * SBH, 8u * SBH, &barT[t]);
-      }
+    if (lane < 2)
+      bulk_g2s(C + (size_t)lane * a.c_rows * a.c_rb + (size_t)row * RB, rec + L.rg.off[3 * lane] + (size_t)n * RB,
+               8u * RB, &barT[t]);
+    for (int c = lane; c < 4 * 8 * CS; c += 32) {   // gate s, gate b, up s, up b: 8 rows x SBH bytes each
+      const int q = c / (8 * CS), o = (c % (8 * CS)) * 16;
+      cp16(C + sbase + (size_t)q * a.c_rows * a.c_sb + (size_t)row * SBH + o,
+           rec + L.rg.off[3 * (q >> 1) + 1 + (q & 1)] + (size_t)n * SBH + o);
     }
-    __syncwarp();
+    cp_arrive(&barT[t]);
   }
 }
 
@@ -905,7 +903,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
 
   if (tid == 0) {
     mbar_init(barA, DEC_THREADS);
-    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1);
+    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1 + 32 * DEC_CW);
     mbar_init(barD, DEC_THREADS);
     fence_mbar_init();
   }
