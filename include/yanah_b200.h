@@ -206,6 +206,86 @@ int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* laye
 /* Read and clear the stack decode error word (synchronises the stream). */
 int yn_stack_error(void* scratch, const yn_dims* dims, void* stream, int32_t* code_out);
 
+/* ------------------------------------- batch decode, expert parallelism */
+
+/* A batch of T = n_ranks * rows_per_rank token rows (at most 64) through
+ * one MoE layer with the routed experts grouped by expert, so each expert
+ * record is read once per layer however many rows chose it
+ * (mlx_backend.py:411-436 `moe` with :111-123 `_gather_sort`;
+ * orchestrator.py:361-405 `generate_batch`). Expert parallelism has no
+ * counterpart in the reference (one MLX device): rank r holds the routed
+ * experts [expert_lo, expert_hi) of every layer in its arena (slot =
+ * expert_slot[e], or e - expert_lo without a table) and rows
+ * [r * rows_per_rank, (r+1) * rows_per_rank) of the batch ("home rows").
+ * With n_ranks = 1 this is the single-GPU batch path. */
+typedef struct yn_ep_config {
+  int32_t rank, n_ranks, rows_per_rank;
+  int32_t expert_lo, expert_hi;
+  int32_t n_layers;  /* layers per step (the per-step flag and counter targets) */
+} yn_ep_config;
+
+/* Per rank two buffers: a peer-visible one of yn_ep_sym_bytes (gather rows,
+ * flags, the home rows' routed outputs and their counter; every rank maps
+ * every other rank's, see yn_ipc_export) and a private one of
+ * yn_ep_local_bytes. Zero both once with yn_ep_init before the first layer
+ * (all ranks, before any rank's first yn_ep_layer). */
+size_t yn_ep_sym_bytes(const yn_dims* dims, const yn_ep_config* cfg);
+size_t yn_ep_local_bytes(const yn_dims* dims, const yn_ep_config* cfg);
+int yn_ep_init(void* sym, void* local, const yn_dims* dims, const yn_ep_config* cfg, void* stream);
+
+/* One layer for this rank's home rows h_in -> h_out ((rows_per_rank, H)
+ * bf16): post-attention and routing of the home rows, the rows and their ids
+ * written into every rank's gather buffer (peer stores + a release flag),
+ * the shared expert of the home rows, then (after every rank's flag) the
+ * pairs of the local experts: gate/up + SwiGLU and the down projection, whose
+ * output rows are stored into the home rank's buffer with a release counter,
+ * and finally the combine of the home rows in column order plus the shared
+ * expert and the residual. peer_sym: n_ranks device pointers, peer_sym[r] =
+ * rank r's peer-visible buffer as mapped in this process (own buffer at
+ * [rank]). Waits on other ranks are bounded (2 s): a timeout sets the error
+ * word (yn_ep_error) and the remaining kernels of the step skip their work.
+ * Call yn_ep_step_end after the last layer of every step (all ranks run the
+ * same number of steps). Launches only kernels: capturable in a graph. */
+int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t layer_index, const yn_ep_config* cfg,
+                const void* h_in, void* h_out, void* const* peer_sym, void* local, void* stream);
+int yn_ep_step_end(void* local, const yn_dims* dims, const yn_ep_config* cfg, void* stream);
+/* Read and clear the error word (synchronises the stream). */
+int yn_ep_error(void* local, const yn_dims* dims, const yn_ep_config* cfg, void* stream, int32_t* code_out);
+
+/* Device pointers into the buffers, for readback. */
+typedef struct yn_ep_local_ptrs {
+  void* x;          /* (rows_per_rank, H) bf16 normalised home rows */
+  int32_t* ids;     /* (rows_per_rank, k) routed ids */
+  float* weights;   /* (rows_per_rank, k) routing weights */
+  void* act_sh;     /* (rows_per_rank, I_sh) shared-expert activations */
+  float* sgate;     /* (rows_per_rank) shared-expert gate */
+  void* y_shared;   /* (rows_per_rank, H) gated shared-expert outputs */
+  int32_t* error;
+  uint64_t* epoch;  /* steps completed */
+} yn_ep_local_ptrs;
+typedef struct yn_ep_sym_ptrs {
+  void* x_all;        /* (n_ranks * rows_per_rank, H) gathered rows */
+  int32_t* ids_all;   /* (n_ranks * rows_per_rank, k) */
+  void* y;            /* (rows_per_rank, k, H) routed outputs of the home rows */
+  uint64_t* flags;    /* (8) arrival stamps, slot = writing rank */
+  uint64_t* counter;  /* finished (pair, 64-row tile) units, cumulative */
+} yn_ep_sym_ptrs;
+int yn_ep_view(void* local, const yn_dims* dims, const yn_ep_config* cfg, yn_ep_local_ptrs* out);
+int yn_ep_sym_view(void* sym, const yn_dims* dims, const yn_ep_config* cfg, yn_ep_sym_ptrs* out);
+
+/* Device memory for the peer-visible buffer (cudaMalloc, so that it can be
+ * exported) and its CUDA IPC handle (YN_IPC_HANDLE_BYTES bytes) for the other
+ * ranks' processes; import maps a peer's buffer with peer access enabled. */
+#define YN_IPC_HANDLE_BYTES 64
+int yn_device_alloc(size_t bytes, void** ptr);
+int yn_device_free(void* ptr);
+int yn_ipc_export(const void* dev_ptr, void* handle_out);
+int yn_ipc_import(const void* handle, void** dev_ptr_out);
+int yn_ipc_close(void* dev_ptr);
+/* Copy between any host/device addresses (cudaMemcpyDefault), then wait for
+ * `stream`: readback for callers that hold raw device pointers. */
+int yn_memcpy(void* dst, const void* src, size_t bytes, void* stream);
+
 /* ---------------------------------------------------------- slot copies */
 
 /* Copy `n` expert records host -> slot arena (io_lanes.py:121-126

@@ -51,6 +51,21 @@ class WsView(C.Structure):
                                           "act_sh", "sgate", "y", "y_shared", "error")]
 
 
+class EpConfig(C.Structure):
+    _fields_ = [("rank", C.c_int32), ("n_ranks", C.c_int32), ("rows_per_rank", C.c_int32),
+                ("expert_lo", C.c_int32), ("expert_hi", C.c_int32), ("n_layers", C.c_int32)]
+
+
+class EpLocalPtrs(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("x", "ids", "weights", "act_sh", "sgate", "y_shared", "error", "epoch")]
+
+
+class EpSymPtrs(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("x_all", "ids_all", "y", "flags", "counter")]
+
+
+YN_IPC_HANDLE_BYTES = 64
+
 _P = C.c_void_p
 _I = C.c_int32
 _SIGS = {
@@ -83,6 +98,21 @@ _SIGS = {
     "yn_synth_u32": (C.c_int, [_P, C.c_int64, C.c_uint64, C.c_uint64, _P]),
     "yn_synth_f16": (C.c_int, [_P, C.c_int64, C.c_uint64, C.c_uint64, C.c_float, _I, _P]),
     "yn_synth_bf16": (C.c_int, [_P, C.c_int64, C.c_uint64, C.c_uint64, C.c_float, C.c_float, _P]),
+    "yn_ep_sym_bytes": (C.c_size_t, [C.POINTER(Dims), C.POINTER(EpConfig)]),
+    "yn_ep_local_bytes": (C.c_size_t, [C.POINTER(Dims), C.POINTER(EpConfig)]),
+    "yn_ep_init": (C.c_int, [_P, _P, C.POINTER(Dims), C.POINTER(EpConfig), _P]),
+    "yn_ep_layer": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _I, C.POINTER(EpConfig), _P, _P,
+                              C.POINTER(C.c_void_p), _P, _P]),
+    "yn_ep_step_end": (C.c_int, [_P, C.POINTER(Dims), C.POINTER(EpConfig), _P]),
+    "yn_ep_error": (C.c_int, [_P, C.POINTER(Dims), C.POINTER(EpConfig), _P, C.POINTER(C.c_int32)]),
+    "yn_ep_view": (C.c_int, [_P, C.POINTER(Dims), C.POINTER(EpConfig), C.POINTER(EpLocalPtrs)]),
+    "yn_ep_sym_view": (C.c_int, [_P, C.POINTER(Dims), C.POINTER(EpConfig), C.POINTER(EpSymPtrs)]),
+    "yn_device_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p)]),
+    "yn_device_free": (C.c_int, [_P]),
+    "yn_ipc_export": (C.c_int, [_P, _P]),
+    "yn_ipc_import": (C.c_int, [_P, C.POINTER(C.c_void_p)]),
+    "yn_ipc_close": (C.c_int, [_P]),
+    "yn_memcpy": (C.c_int, [_P, _P, C.c_size_t, _P]),
 }
 
 _lib = None

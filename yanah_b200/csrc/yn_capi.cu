@@ -21,6 +21,7 @@
 #include "yn_qdot.cuh"
 #include "yn_kernels.cuh"
 #include "yn_decode.cuh"
+#include "yn_internal.h"
 
 
 using namespace ynb;
@@ -31,6 +32,7 @@ static int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
 }
+int ynb::host_fail(int code, const std::string& msg) { return fail(code, msg); }
 #define YN_CUDA(call)                                                                         \
   do {                                                                                        \
     cudaError_t e_ = (call);                                                                  \
@@ -119,6 +121,11 @@ static int set_smem_ptr(const void* kernel, size_t bytes) {
   done.insert(key);
   return YN_OK;
 }
+
+int ynb::host_check_qmat(const yn_qmat& m, int rows, int cols, int bits, const char* what) {
+  return check_qmat(m, rows, cols, bits, what);
+}
+int ynb::host_set_smem(const void* kernel, size_t bytes) { return set_smem_ptr(kernel, bytes); }
 
 static RecGeom rec_geom(const yn_record& r) {
   RecGeom g;
@@ -251,8 +258,8 @@ extern "C" int yn_route(const float* logits, int32_t T, const yn_dims* dims, int
 }
 
 // -------------------------------------------------------- layer kernels
-static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void* h1, int T, const yn_layer* tg,
-                                 int NT, uint8_t* ws, const WsLayout& W, cudaStream_t st) {
+static int launch_post_attention_out(const yn_dims& d, const yn_layer& L, const void* h1, int T, const yn_layer* tg,
+                                     int NT, const PostAttnOut& o, cudaStream_t st) {
   int rc;
   const int H = d.hidden, E = d.n_experts;
   if (!h1 || !L.post_norm) return fail(YN_E_INVALID, "post_attention: null input or norm");
@@ -311,16 +318,16 @@ static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void
     if (tt > tile) tile = tt;
   }
   a.tile_bytes = tile;
-  a.x = reinterpret_cast<uint16_t*>(ws + W.x);
-  a.logits = reinterpret_cast<float*>(ws + W.logits);
-  a.act_sh = reinterpret_cast<uint16_t*>(ws + W.act_sh);
-  a.sgate = reinterpret_cast<float*>(ws + W.sgate);
-  a.ids = reinterpret_cast<int32_t*>(ws + W.ids);
-  a.wts = reinterpret_cast<float*>(ws + W.w);
-  a.flogits = reinterpret_cast<float*>(ws + W.flogits);
-  a.fprobs = reinterpret_cast<float*>(ws + W.fprobs);
-  a.counter = reinterpret_cast<int*>(ws + W.counters);
-  a.err = reinterpret_cast<int*>(ws + W.err);
+  a.x = o.x;
+  a.logits = o.logits;
+  a.act_sh = o.act_sh;
+  a.sgate = o.sgate;
+  a.ids = o.ids;
+  a.wts = o.wts;
+  a.flogits = o.flogits;
+  a.fprobs = o.fprobs;
+  a.counter = o.counter;
+  a.err = o.err;
   const size_t rows_b = ((size_t)T * H * 2 + 15) / 16 * 16;
   const size_t smem = 256 + 2 * rows_b + ((size_t)H * 2 + 15) / 16 * 16 + tile;
   const int cpl = cpl_of(H);
@@ -335,6 +342,40 @@ static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void
     default: return fail(YN_E_UNSUPPORTED, "hidden size not supported by the router kernel");
   }
   YN_CUDA(cudaGetLastError());
+  return YN_OK;
+}
+
+static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void* h1, int T, const yn_layer* tg,
+                                 int NT, uint8_t* ws, const WsLayout& W, cudaStream_t st) {
+  PostAttnOut o;
+  o.x = reinterpret_cast<uint16_t*>(ws + W.x);
+  o.logits = reinterpret_cast<float*>(ws + W.logits);
+  o.act_sh = reinterpret_cast<uint16_t*>(ws + W.act_sh);
+  o.sgate = reinterpret_cast<float*>(ws + W.sgate);
+  o.ids = reinterpret_cast<int32_t*>(ws + W.ids);
+  o.wts = reinterpret_cast<float*>(ws + W.w);
+  o.flogits = reinterpret_cast<float*>(ws + W.flogits);
+  o.fprobs = reinterpret_cast<float*>(ws + W.fprobs);
+  o.counter = reinterpret_cast<int*>(ws + W.counters);
+  o.err = reinterpret_cast<int*>(ws + W.err);
+  return launch_post_attention_out(d, L, h1, T, tg, NT, o, st);
+}
+
+int ynb::host_post_attention_rows(const yn_dims& d, const yn_layer& L, const void* h1, int T, const PostAttnOut& o,
+                                  cudaStream_t st) {
+  for (int t0 = 0; t0 < T; t0 += YN_MAX_ROWS) {
+    const int n = std::min(YN_MAX_ROWS, T - t0);
+    PostAttnOut c = o;
+    c.x = o.x + (size_t)t0 * d.hidden;
+    c.logits = o.logits + (size_t)t0 * d.n_experts;
+    c.act_sh = o.act_sh + (size_t)t0 * (d.shared_inter ? d.shared_inter : 1);
+    c.sgate = o.sgate + t0;
+    c.ids = o.ids + (size_t)t0 * d.top_k;
+    c.wts = o.wts + (size_t)t0 * d.top_k;
+    const int rc = launch_post_attention_out(d, L, reinterpret_cast<const uint16_t*>(h1) + (size_t)t0 * d.hidden, n,
+                                             nullptr, 0, c, st);
+    if (rc) return rc;
+  }
   return YN_OK;
 }
 
