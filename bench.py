@@ -281,6 +281,144 @@ def run_streaming(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------- expert-parallel leg
+EP_METRIC = "decode tok/s, batch of 64 rows, experts sharded over GPUs (Qwen3-Next-80B-A3B-shaped, 48 layers)"
+
+
+def run_ep(args, rank: int, world: int):
+    """Config 4: a decode batch of 64 rows (one token each per step) through
+    the 48-layer stack, experts sharded 512/world per GPU, per-layer dispatch
+    and combine over peer memory (yn_ep_layer). One step = one CUDA graph
+    replay. Inputs differ every step (the previous step's outputs)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.ep import ExpertParallelStack, expert_range
+    from yanah_b200.synthetic import hidden_stream_id, qwen3_next_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = qwen3_next_stack(seed=0)
+    B = args.batch
+    stack = ExpertParallelStack(cfg, batch=B, rank=rank, world=world, device=dev)
+    H, K, L = cfg.hidden, cfg.top_k, cfg.n_layers
+    T_h = B // world
+    rows = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(rows.data_ptr(), B * H, cfg.seed, hidden_stream_id(500), 1.0, 0.0,
+                                        stream_ptr()))
+    home = rows[rank * T_h:(rank + 1) * T_h].contiguous()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # untimed pass, layer by layer: which experts and pairs each layer touches
+    lo, hi = stack.e_lo, stack.e_hi
+    n_local, pairs_out, pairs_in = [], 0, 0
+    ids_all = torch.empty((B, K), dtype=torch.int32)
+    ping = [home.clone(), torch.empty_like(home)]
+    for i in range(L):
+        stack.layer(i, ping[i % 2], ping[(i + 1) % 2])
+        torch.cuda.synchronize(dev)
+        _lib.check(_lib.lib().yn_memcpy(ids_all.data_ptr(), stack.sview.ids_all, B * K * 4, None))
+        ids = ids_all.numpy()
+        local = (ids >= lo) & (ids < hi)
+        n_local.append(len(np.unique(ids[local])))
+        t_home = np.arange(B)[:, None] // T_h
+        pairs_out += int((local & (t_home != rank)).sum())
+        pairs_in += int(((~local) & (t_home == rank)).sum())
+    stack.step_end()
+    barrier()
+    if stack.check_error():
+        raise RuntimeError("device error in the first step")
+    # graph of one step; warm-up replays
+    stack.capture()
+    h = home
+    for _ in range(args.warmup):
+        h = stack.step(h).clone()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid(dev.index)) as clk:
+        start.record()
+        for _ in range(args.steps):
+            stack._ping[0].copy_(stack._ping[stack.out_slot])
+            stack.graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    if stack.check_error():
+        raise RuntimeError("device error during the timed steps")
+    value = B * args.steps / (ms_max / 1e3)
+
+    # e2e: pinned host rows in, outputs out, every step
+    h_in = torch.empty((T_h, H), dtype=torch.bfloat16, pin_memory=True)
+    h_in.copy_(home)
+    h_out = torch.empty_like(h_in, pin_memory=True)
+    for _ in range(2):
+        stack._ping[0].copy_(h_in, non_blocking=True)
+        stack.graph.replay()
+        h_out.copy_(stack._ping[stack.out_slot], non_blocking=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        stack._ping[0].copy_(h_in, non_blocking=True)
+        stack.graph.replay()
+        h_out.copy_(stack._ping[stack.out_slot], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e = B * args.steps / (float(t2.item()) / 1e3)
+
+    # rooflines of this rank's step: HBM (each local expert record of a layer
+    # once, the dense weights once) and NVLink (rows out, output rows back)
+    rec = [cfg.record_spec(l).record_bytes for l in range(L)]
+    hbm_bytes = sum(n * r for n, r in zip(n_local, rec)) + L * cfg.dense_bytes_per_layer()
+    link_bytes = L * T_h * (H * 2 + K * 4) * (world - 1) + pairs_out * H * 2
+    hbm, src = peaks()
+    step_s = ms_max / args.steps / 1e3
+    achieved = hbm_bytes / step_s / 1e9
+    line = {
+        "metric": EP_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "qwen3_next_80b_a3b_moe_stack48_ep_batch64_decode", "layers": L, "batch": B,
+                   "rows_per_gpu": T_h, "experts_per_gpu": hi - lo, "hidden": H, "experts": cfg.n_experts,
+                   "top_k": K, "expert_bits": "4-bit g64 layers 0-3 and 44-47, 2-bit g64 layers 4-43",
+                   "parallelism": f"ep{world}",
+                   "l2": "no flush: a step reads every local expert record a layer routes to once (~100 of "
+                         "512 per layer, ~4.6 GB per step at one GPU) and all dense weights (>126 MB L2)"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": T_h * H * 2,
+                "d2h_bytes_per_step": T_h * H * 2},
+        "gpu_launches": args.steps * (L * (9 + (T_h - 1) // 8) + 1),
+        "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "whole step (every kernel of yn_ep_layer)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": src, "bytes_per_step": hbm_bytes, "traffic": None,
+                     "local_experts_per_layer_mean": round(float(np.mean(n_local)), 1)},
+        "nvlink": {"bytes_per_step": link_bytes, "achieved_gbs": round(link_bytes / step_s / 1e9, 2),
+                   "peak_gbs": 770.0, "frac": round(link_bytes / step_s / 1e9 / 770.0, 4),
+                   "pairs_sent_back_per_step": pairs_out},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    stack.graph = None
+    barrier()
+    stack.close()
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, rank: int, world: int):
     import numpy as np
@@ -414,8 +552,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
-    ap.add_argument("--workload", choices=["resident", "streaming"], default="resident",
-                    help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier")
+    ap.add_argument("--workload", choices=["resident", "streaming", "ep"], default="resident",
+                    help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier; "
+                         "ep: batch of 64 rows, experts sharded over the GPUs")
+    ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
     args = ap.parse_args()
@@ -435,6 +575,8 @@ def main():
         elif args.workload == "streaming":
             if rank == 0:
                 run_streaming(args, rank, world)
+        elif args.workload == "ep":
+            run_ep(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

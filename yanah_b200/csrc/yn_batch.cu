@@ -32,7 +32,7 @@ struct SymLayout {
   size_t x_all, ids_all, flags, cnt, y, total;
 };
 struct LocalLayout {
-  size_t err, counter, epoch, x_home, logits, ids, w, act_sh, sgate, plan, xf, xg, act, af, ag, sf, sg, ysh, total;
+  size_t err, counter, done, epoch, x_home, logits, ids, w, act_sh, sgate, plan, xf, xg, act, af, ag, sf, sg, ysh, total;
 };
 
 SymLayout sym_layout(const yn_dims& d, const yn_ep_config& c) {
@@ -57,7 +57,8 @@ LocalLayout local_layout(const yn_dims& d, const yn_ep_config& c) {
   const size_t H = d.hidden, E = d.n_experts, K = d.top_k, I = d.moe_inter;
   const size_t Ish = d.shared_inter ? d.shared_inter : 64;
   L.err = take(4);
-  L.counter = take(4);
+  L.counter = take(8 * 4);
+  L.done = take(BT_MAX_RANKS * 4);
   L.epoch = take(8);
   L.x_home = take(T * H * 2);
   L.logits = take(T * E * 4);
@@ -152,6 +153,20 @@ int frags(int bits, int gs, const FragArgs& a, int grid, cudaStream_t st) {
   if (bits == 8 && gs == 64) return launch_frags<8, 64>(a, grid, st);
   if (bits == 8 && gs == 32) return launch_frags<8, 32>(a, grid, st);
   return host_fail(YN_E_UNSUPPORTED, "batch path: " + std::to_string(bits) + "-bit group " + std::to_string(gs));
+}
+
+template <int BITS, int GS>
+int launch_prep(const FragArgs& a, int grid, cudaStream_t st) {
+  k_batch_prep<BITS, GS><<<grid, BT_THREADS, 0, st>>>(a);
+  YN_CUDA_B(cudaGetLastError());
+  return YN_OK;
+}
+
+int prep(int bits, int gs, const FragArgs& a, int grid, cudaStream_t st) {
+  if (bits == 2 && gs == 64) return launch_prep<2, 64>(a, grid, st);
+  if (bits == 4 && gs == 64) return launch_prep<4, 64>(a, grid, st);
+  if (bits == 4 && gs == 32) return launch_prep<4, 32>(a, grid, st);
+  return host_fail(YN_E_UNSUPPORTED, "batch path: routed " + std::to_string(bits) + "-bit group " + std::to_string(gs));
 }
 
 template <int BITS, int GS, int NUT>
@@ -332,9 +347,8 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
   pa.sgate = reinterpret_cast<float*>(lb + L.sgate);
   pa.ids = reinterpret_cast<int32_t*>(lb + L.ids);
   pa.wts = reinterpret_cast<float*>(lb + L.w);
-  pa.counter = reinterpret_cast<int*>(lb + L.counter);
   pa.err = err;
-  if ((rc = host_post_attention_rows(d, Ly, h_in, T_h, pa, st))) return rc;
+  if ((rc = host_batch_dense(d, Ly, h_in, T_h, pa, reinterpret_cast<unsigned*>(lb + L.counter), st))) return rc;
 
   // 2. home rows -> every rank's gather buffer
   {
@@ -343,9 +357,11 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     a.peers = peers;
     a.x_home = pa.x;
     a.ids_home = pa.ids;
+    a.done = reinterpret_cast<unsigned*>(lb + L.done);
     a.H = H;
     a.K = K;
-    k_ep_dispatch<<<G, BT_THREADS, 0, st>>>(a);
+    const int nb = std::max(1, std::min(16, (T_h * H / 8 + BT_THREADS * 4 - 1) / (BT_THREADS * 4)));
+    k_ep_dispatch<<<dim3(G, nb), BT_THREADS, 0, st>>>(a);
     YN_CUDA_B(cudaGetLastError());
   }
 
@@ -361,7 +377,7 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     f.xf = reinterpret_cast<uint32_t*>(lb + L.sf);
     f.xg = reinterpret_cast<float2*>(lb + L.sg);
     f.st = es;
-    if ((rc = frags(8, dgs, f, (T_h + 7) / 8, st))) return rc;
+    if ((rc = frags(8, dgs, f, T_h, st))) return rc;
     BatchDownArgs a{};
     a.shared = 1;
     a.n_shared = T_h;
@@ -377,7 +393,7 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     a.ysh = ysh;
     a.sgate = pa.sgate;
     a.err = err;
-    if ((rc = down(8, dgs, a, d.shared_inter, H / 64, st))) return rc;
+    if ((rc = down(8, dgs, a, d.shared_inter, ((T_h + BT_DN_PASS - 1) / BT_DN_PASS) * (H / 64), st))) return rc;
   }
 
   // 4. wait for every rank's rows, plan the local experts, x fragments
@@ -391,7 +407,6 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     f.Kd = H;
     f.xf = reinterpret_cast<uint32_t*>(lb + L.xf);
     f.xg = reinterpret_cast<float2*>(lb + L.xg);
-    f.wait_and_plan = 1;
     f.st = es;
     f.flags = peers.flag[cfg->rank];
     f.ids = peers.ids_all[cfg->rank];
@@ -400,7 +415,7 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     f.e_lo = cfg->expert_lo;
     f.e_hi = cfg->expert_hi;
     f.plan = plan;
-    if ((rc = frags(bits, gs, f, (R + 7) / 8, st))) return rc;
+    if ((rc = prep(bits, gs, f, 1 + R, st))) return rc;
   }
 
   // 5. gate/up + SwiGLU of the local pairs
@@ -422,7 +437,6 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     a.I = I;
     a.K = K;
     a.act = act;
-    a.gate_err = err;
     a.err = err;
     if ((rc = up(bits, gs, a, st))) return rc;
   }
@@ -438,7 +452,7 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     f.xf = reinterpret_cast<uint32_t*>(lb + L.af);
     f.xg = reinterpret_cast<float2*>(lb + L.ag);
     f.st = es;
-    if ((rc = frags(bits, gs, f, (R * K + 7) / 8, st))) return rc;
+    if ((rc = frags(bits, gs, f, R * K, st))) return rc;
     BatchDownArgs a{};
     a.plan = plan;
     a.af = f.xf;
@@ -457,8 +471,8 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     a.st = es;
     a.peers = peers;
     a.err = err;
-    const int max_items = std::min(cfg->expert_hi - cfg->expert_lo, R * K) * (H / 64);
-    if ((rc = down(bits, gs, a, I, max_items, st))) return rc;
+    const int max_pass = std::min(cfg->expert_hi - cfg->expert_lo, R * K) + (R * K) / BT_DN_PASS;
+    if ((rc = down(bits, gs, a, I, max_pass * (H / 64), st))) return rc;
   }
 
   // 7. combine of the home rows once every unit has landed

@@ -59,11 +59,26 @@ constexpr int BT_MAX_RANKS = 8;
 enum : int { YN_ERR_PEER_TIMEOUT = 6, YN_ERR_BATCH_ID = 7 };
 
 struct BatchPlan {
-  int n_seg, n_pairs, pad0, pad1;
-  int seg_e[BT_MAX_PAIRS];        // expert id of segment s (ascending)
-  int seg_off[BT_MAX_PAIRS + 1];  // pair range of segment s
-  int pair_tj[BT_MAX_PAIRS];      // t * K + j, by (expert, t, j)
+  int n_seg, n_pairs, n_up, n_dn;  // segments, pairs, up passes (8 rows), down passes (32 pairs)
+  int seg_e[BT_MAX_PAIRS];         // expert id of segment s (ascending)
+  int seg_off[BT_MAX_PAIRS + 1];   // pair range of segment s
+  int seg_up0[BT_MAX_PAIRS + 1];   // first up pass of segment s
+  int seg_dn0[BT_MAX_PAIRS + 1];   // first down pass of segment s
+  int pair_tj[BT_MAX_PAIRS];       // t * K + j, by (expert, t, j)
 };
+constexpr int BT_UP_PASS = 8;      // token rows per up work item
+constexpr int BT_DN_PASS = 32;     // pairs per down work item
+
+// Segment of global pass index gp: the last s with first[s] <= gp.
+YN_DEV int seg_of_pass(const int* first, int n_seg, int gp) {
+  int lo = 0, hi = n_seg - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (first[mid] <= gp) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 // ------------------------------------------------------------ code words
 // Per-word unpack of one code word into PPW fp16 pairs; pair p holds word-
@@ -239,6 +254,7 @@ struct DispatchArgs {
   EpPeers peers;
   const uint16_t* x_home;   // (T_h, H)
   const int32_t* ids_home;  // (T_h, K)
+  unsigned* done;           // (G) CTA arrivals per destination (monotonic)
   int H, K;
 };
 
@@ -249,10 +265,9 @@ struct FragArgs {
   const int* n_rows_dev;    // optional device row count (at most n_rows)
   uint32_t* xf;             // (n_rows, frag_stride_words) fp16-pair words
   float2* xg;               // (n_rows, gdata_stride)
-  // optional: wait for every rank's dispatch flag first and build the plan
-  int wait_and_plan;
+  // k_batch_prep only: wait for every rank's rows, then block 0 plans
   EpStep st;
-  const unsigned long long* flags;  // this rank's flags (G)
+  const unsigned long long* flags;  // this rank's arrival flags (G)
   const int32_t* ids;       // (n_rows, K) routed ids of every row
   int K, E, e_lo, e_hi;
   BatchPlan* plan;
@@ -270,13 +285,12 @@ struct BatchUpArgs {
   RecGeom rg;
   int H, I, K;
   uint16_t* act;            // (n_pairs, I) bf16, plan order
-  const int* gate_err;      // skip when set (an earlier wait failed)
   int* err;
 };
 
 struct BatchDownArgs {
-  // routed: segments of `plan`, pairs in plan order; shared: one segment of
-  // n_shared rows (pair p = home row p) with the shared expert's down matrix
+  // routed: the down passes of `plan`, pairs in plan order; shared: n_shared
+  // rows (pair p = home row p) through the shared expert's down matrix
   const BatchPlan* plan;
   int shared, n_shared;
   const uint32_t* af;
@@ -309,114 +323,211 @@ struct CombineArgs {
 };
 
 // ------------------------------------------------------------- dispatch
-// CTA d copies this rank's home rows into rank d's gather buffer, then
-// raises flag[rank] there (release, system scope).
+// Grid (G, NB): the NB CTAs of destination d copy slices of this rank's home
+// rows (and CTA 0 the ids) into rank d's gather buffer; the last of them to
+// finish raises flag[rank] there (release, system scope).
 __global__ void __launch_bounds__(BT_THREADS) k_ep_dispatch(const DispatchArgs a) {
-  const int d = blockIdx.x;
+  __shared__ int last_s;
+  const int d = blockIdx.x, nb = gridDim.y;
   const EpStep& s = a.st;
   const size_t row0 = (size_t)s.rank * s.T_h;
   uint4* xd = reinterpret_cast<uint4*>(a.peers.x_all[d] + row0 * a.H);
   const uint4* xs = reinterpret_cast<const uint4*>(a.x_home);
   const int nx = s.T_h * a.H / 8;
-  for (int i = threadIdx.x; i < nx; i += blockDim.x) xd[i] = xs[i];
-  int32_t* id = a.peers.ids_all[d] + row0 * a.K;
-  for (int i = threadIdx.x; i < s.T_h * a.K; i += blockDim.x) id[i] = a.ids_home[i];
+  constexpr int U = 4;
+  for (int i0 = (blockIdx.y * BT_THREADS + threadIdx.x) * U; i0 < nx; i0 += nb * BT_THREADS * U) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u < nx) v[u] = xs[i0 + u];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u < nx) xd[i0 + u] = v[u];
+  }
+  if (blockIdx.y == 0) {
+    int32_t* id = a.peers.ids_all[d] + row0 * a.K;
+    for (int i = threadIdx.x; i < s.T_h * a.K; i += blockDim.x) id[i] = a.ids_home[i];
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(a.done + d, 1u);
+    last_s = ((prev + 1u) % (unsigned)nb) == 0u;
+  }
+  __syncthreads();
+  if (last_s && threadIdx.x == 0) {
     __threadfence_system();
     st_release_sys_u64(a.peers.flag[d] + s.rank, ep_stamp(s));
   }
 }
 
 // ------------------------------------------------------------ fragments
-// One warp per row: power-of-two scale from max|x|, fragment words and group
-// data (sums in a fixed order). Rows beyond n_rows are skipped. With
-// wait_and_plan, block 0 also builds the segment plan.
+// One row per block: stage the row in shared memory, power-of-two scale from
+// max|x|, fragment words, then per group {-1024 * sum(fragment values),
+// scale * sum(x)} (butterfly over one warp per group) and {1 / scale, 0}.
 template <int BITS, int GS>
-YN_DEV void frag_row(const uint16_t* x, int Kd, uint32_t* xf, float2* xg, int lane) {
+YN_DEV void frag_row_block(const uint16_t* x_g, int Kd, uint32_t* xf, float2* xg, uint16_t* xs, float* red) {
   using F = BFmt<BITS, GS>;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  for (int i = tid; i < Kd / 8; i += blockDim.x)
+    reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(x_g)[i];
+  __syncthreads();
   float mx = 0.0f;
-  for (int k = lane; k < Kd; k += 32) mx = fmaxf(mx, fabsf(bf16_to_f32(x[k])));
+  for (int k = tid; k < Kd; k += blockDim.x) mx = fmaxf(mx, fabsf(bf16_to_f32(xs[k])));
   mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < nw; ++w) mx = fmaxf(mx, red[w]);
   const float scale = fp16_input_scale(mx);
-  for (int w = lane; w < Kd / 2; w += 32) {
+  for (int w = tid; w < Kd / 2; w += blockDim.x) {
     const int p = w % F::PPW, wc = w / F::PPW;  // wc = ch * 4 + c
     const int base = (wc >> 2) * F::CPCH + (wc & 3) * F::WPL;
     const float m = __fmul_rn(scale, BW<BITS>::inv_mult(p));
-    __half2 h = __floats2half2_rn(__fmul_rn(bf16_to_f32(x[base + BW<BITS>::lo(p)]), m),
-                                  __fmul_rn(bf16_to_f32(x[base + BW<BITS>::hi(p)]), m));
+    __half2 h = __floats2half2_rn(__fmul_rn(bf16_to_f32(xs[base + BW<BITS>::lo(p)]), m),
+                                  __fmul_rn(bf16_to_f32(xs[base + BW<BITS>::hi(p)]), m));
     xf[w] = *reinterpret_cast<uint32_t*>(&h);
   }
   const int NG = Kd / GS;
-  for (int g = 0; g < NG; ++g) {
-    float s = 0.0f, o = 0.0f;
+  for (int g = warp; g < NG; g += nw) {
+    float sx = 0.0f, o = 0.0f;
     for (int k = g * GS + lane; k < (g + 1) * GS; k += 32) {
-      const float v = bf16_to_f32(x[k]);
-      s = __fadd_rn(s, v);
-      const int j = k % F::WPL;
-      const float m = __fmul_rn(scale, BW<BITS>::inv_mult(BW<BITS>::pair_of(j)));
+      const float v = bf16_to_f32(xs[k]);
+      sx = __fadd_rn(sx, v);
+      const float m = __fmul_rn(scale, BW<BITS>::inv_mult(BW<BITS>::pair_of(k % F::WPL)));
       o = __fadd_rn(o, __half2float(__float2half_rn(__fmul_rn(v, m))));
     }
-    s = group_sum_bfly(s, 32);
+    sx = group_sum_bfly(sx, 32);
     o = group_sum_bfly(o, 32);
-    if (lane == 0) xg[g] = make_float2(__fmul_rn(-1024.0f, o), __fmul_rn(scale, s));
+    if (lane == 0) xg[g] = make_float2(__fmul_rn(-1024.0f, o), __fmul_rn(scale, sx));
   }
-  if (lane == 0) {
+  if (tid == 0) {
     xg[NG] = make_float2(__fdiv_rn(1.0f, scale), 0.0f);
     xg[NG + 1] = make_float2(0.0f, 0.0f);
   }
+  __syncthreads();
 }
 
+// Block-wide exclusive scan of int4 (256 threads); returns the total.
+YN_DEV int4 block_scan4(int4 v, int4* out_excl) {
+  __shared__ int4 wsum[BT_THREADS / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int4 inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, inc.x, o), y = __shfl_up_sync(0xffffffffu, inc.y, o);
+    const int z = __shfl_up_sync(0xffffffffu, inc.z, o), w = __shfl_up_sync(0xffffffffu, inc.w, o);
+    if (lane >= o) { inc.x += x; inc.y += y; inc.z += z; inc.w += w; }
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  int4 base = make_int4(0, 0, 0, 0), tot = make_int4(0, 0, 0, 0);
+  for (int w = 0; w < BT_THREADS / 32; ++w) {
+    const int4 ws = wsum[w];
+    if (w < warp) { base.x += ws.x; base.y += ws.y; base.z += ws.z; base.w += ws.w; }
+    tot.x += ws.x; tot.y += ws.y; tot.z += ws.z; tot.w += ws.w;
+  }
+  *out_excl = make_int4(base.x + inc.x - v.x, base.y + inc.y - v.y, base.z + inc.z - v.z, base.w + inc.w - v.w);
+  __syncthreads();
+  return tot;
+}
+
+// Segments of the local experts: counting by expert in shared memory, a
+// block scan over experts (ascending id), then each pair's rank among the
+// earlier pairs of its expert (stable: (t, j) order).
 YN_DEV void build_plan(const FragArgs& a) {
+  __shared__ int ids_s[BT_MAX_PAIRS];
   __shared__ int cnt[1024];
   __shared__ int segof[1024];
   const int P = a.n_rows * a.K, El = a.e_hi - a.e_lo;
-  for (int e = threadIdx.x; e < El; e += blockDim.x) cnt[e] = 0;
+  for (int e = threadIdx.x; e < 1024; e += blockDim.x) cnt[e] = 0;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) ids_s[i] = a.ids[i];
   __syncthreads();
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    const int e = a.ids[i];
+    const int e = ids_s[i];
     if (e < 0 || e >= a.E) raise_error(a.st.err, YN_ERR_BATCH_ID);
     else if (e >= a.e_lo && e < a.e_hi) atomicAdd(&cnt[e - a.e_lo], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {  // serial scan over at most 1024 experts
-    int ns = 0, off = 0;
-    for (int e = 0; e < El; ++e) {
-      if (cnt[e]) {
-        a.plan->seg_e[ns] = a.e_lo + e;
-        a.plan->seg_off[ns] = off;
-        segof[e] = ns;
-        off += cnt[e];
-        ++ns;
-      }
+  // thread i owns experts 4i..4i+3
+  int c[4];
+  int4 v = make_int4(0, 0, 0, 0);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int e = 4 * threadIdx.x + k;
+    c[k] = e < El ? cnt[e] : 0;
+    if (c[k]) {
+      v.x += 1;
+      v.y += c[k];
+      v.z += (c[k] + BT_UP_PASS - 1) / BT_UP_PASS;
+      v.w += (c[k] + BT_DN_PASS - 1) / BT_DN_PASS;
     }
-    a.plan->seg_off[ns] = off;
-    a.plan->n_seg = ns;
-    a.plan->n_pairs = off;
+  }
+  int4 ex;
+  const int4 tot = block_scan4(v, &ex);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (!c[k]) continue;
+    const int e = 4 * threadIdx.x + k;
+    a.plan->seg_e[ex.x] = a.e_lo + e;
+    a.plan->seg_off[ex.x] = ex.y;
+    a.plan->seg_up0[ex.x] = ex.z;
+    a.plan->seg_dn0[ex.x] = ex.w;
+    segof[e] = ex.x;
+    ex.x += 1;
+    ex.y += c[k];
+    ex.z += (c[k] + BT_UP_PASS - 1) / BT_UP_PASS;
+    ex.w += (c[k] + BT_DN_PASS - 1) / BT_DN_PASS;
+  }
+  if (threadIdx.x == 0) {
+    a.plan->n_seg = tot.x;
+    a.plan->n_pairs = tot.y;
+    a.plan->n_up = tot.z;
+    a.plan->n_dn = tot.w;
+    a.plan->seg_off[tot.x] = tot.y;
+    a.plan->seg_up0[tot.x] = tot.z;
+    a.plan->seg_dn0[tot.x] = tot.w;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    const int e = a.ids[i];
+    const int e = ids_s[i];
     if (e < a.e_lo || e >= a.e_hi) continue;
     int rank = 0;
-    for (int q = 0; q < i; ++q) rank += (a.ids[q] == e);
+    for (int q = 0; q < i; ++q) rank += (ids_s[q] == e);
     a.plan->pair_tj[a.plan->seg_off[segof[e - a.e_lo]] + rank] = i;
   }
 }
 
+// After every rank's rows have arrived: block 0 builds the plan, block 1 + r
+// the fragments of row r.
+template <int BITS, int GS>
+__global__ void __launch_bounds__(BT_THREADS) k_batch_prep(const FragArgs a) {
+  __shared__ __align__(16) uint16_t xs[8192];
+  __shared__ float red[BT_THREADS / 32];
+  bool ok = true;
+  for (int r = 0; r < a.st.G && ok; ++r) ok = wait_geq_block(a.flags + r, ep_stamp(a.st), a.st.err);
+  if (!ok) return;
+  if (blockIdx.x == 0) {
+    build_plan(a);
+    return;
+  }
+  const int xs_w = frag_stride_words(a.Kd, BITS), gsd = gdata_stride(a.Kd, GS);
+  for (int r = blockIdx.x - 1; r < a.n_rows; r += gridDim.x - 1)
+    frag_row_block<BITS, GS>(a.src + (size_t)r * a.src_stride, a.Kd, a.xf + (size_t)r * xs_w,
+                             a.xg + (size_t)r * gsd, xs, red);
+}
+
+// Fragments of rows without waiting (activations of the pairs, shared rows).
 template <int BITS, int GS>
 __global__ void __launch_bounds__(BT_THREADS) k_batch_frags(const FragArgs a) {
-  if (a.wait_and_plan) {
-    bool ok = true;
-    for (int r = 0; r < a.st.G && ok; ++r) ok = wait_geq_block(a.flags + r, ep_stamp(a.st), a.st.err);
-    if (!ok) return;
-    if (blockIdx.x == 0) build_plan(a);
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int xs = frag_stride_words(a.Kd, BITS), gsd = gdata_stride(a.Kd, GS);
+  __shared__ __align__(16) uint16_t xs[8192];
+  __shared__ float red[BT_THREADS / 32];
+  if (*(volatile const int*)a.st.err) return;
   const int n = a.n_rows_dev ? min(a.n_rows, *a.n_rows_dev) : a.n_rows;
-  for (int r = blockIdx.x * (BT_THREADS / 32) + warp; r < n; r += gridDim.x * (BT_THREADS / 32))
-    frag_row<BITS, GS>(a.src + (size_t)r * a.src_stride, a.Kd, a.xf + (size_t)r * xs, a.xg + (size_t)r * gsd, lane);
+  const int xs_w = frag_stride_words(a.Kd, BITS), gsd = gdata_stride(a.Kd, GS);
+  for (int r = blockIdx.x; r < n; r += gridDim.x)
+    frag_row_block<BITS, GS>(a.src + (size_t)r * a.src_stride, a.Kd, a.xf + (size_t)r * xs_w,
+                             a.xg + (size_t)r * gsd, xs, red);
 }
 
 // ------------------------------------------------------------- MMA core
@@ -508,15 +619,15 @@ YN_DEV void warp_tile(const uint8_t* W, int RB, int r0, const uint16_t* S, const
 YN_DEV size_t al16(size_t v) { return (v + 15) & ~size_t(15); }
 
 // ---------------------------------------------------------- gate / up
-// Work item = (segment, tile of 16*NUT units). Warp w: unit subtile w % NUT,
-// K slice w / NUT of H / (8 / NUT) codes. Token rows of the segment go in
-// passes of 8. Partials of the K slices are summed in slice order.
+// Work item = (up pass, tile of 16*NUT units): the pass's at most 8 token
+// rows of one expert. Warp w: unit subtile w % NUT, K slice w / NUT of
+// H / (8 / NUT) codes; the slices' partials are summed in slice order.
 template <int BITS, int GS, int NUT>
 __global__ void __launch_bounds__(BT_THREADS) k_batch_up(const BatchUpArgs a) {
   using F = BFmt<BITS, GS>;
   constexpr int NKS = 8 / NUT, UR = 16 * NUT;
   extern __shared__ __align__(128) uint8_t smem[];
-  if (*(volatile const int*)a.gate_err) return;
+  if (*(volatile const int*)a.err) return;
   const int H = a.H, RB = H * BITS / 8, NG = H / GS;
   const int srow_b = (int)al16((size_t)NG * 2) + 16, srow_h = srow_b / 2;
   const int xs = a.xf_stride, gsd = a.xg_stride;
@@ -533,84 +644,84 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_up(const BatchUpArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int ut = warp % NUT, ks = warp / NUT;
   const int tiles = a.I / UR;
-  const int n_items = a.plan->n_seg * tiles;
+  const int n_seg = a.plan->n_seg;
+  const int n_items = a.plan->n_up * tiles;
   const int nchunk = H / F::CPCH, cpw = nchunk / NKS;
   for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const int sidx = it / tiles, u0 = (it % tiles) * UR;
+    const int gp = it / tiles, u0 = (it % tiles) * UR;
+    const int sidx = seg_of_pass(a.plan->seg_up0, n_seg, gp);
     const int e = a.plan->seg_e[sidx];
-    const int p_beg = a.plan->seg_off[sidx], p_end = a.plan->seg_off[sidx + 1];
+    const int p0 = a.plan->seg_off[sidx] + (gp - a.plan->seg_up0[sidx]) * BT_UP_PASS;
+    const int ntok = min(BT_UP_PASS, a.plan->seg_off[sidx + 1] - p0);
     const int slot = a.slot_of ? a.slot_of[e] : e - a.e_lo;
     if (slot < 0 || slot >= a.n_slots) {
       if (threadIdx.x == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
       continue;
     }
     const uint8_t* rec = a.base + (size_t)slot * (size_t)a.stride;
-    __syncthreads();  // the previous item's readers are done with the tile
+    __syncthreads();  // the previous item is done with every buffer
+    if (threadIdx.x < 8) tok_s[threadIdx.x] = threadIdx.x < ntok ? a.plan->pair_tj[p0 + threadIdx.x] / a.K : 0;
     cpa_rows_swz(Wt, 0, rec + a.rg.off[0] + (size_t)u0 * RB, UR, RB);
     cpa_rows_swz(Wt, UR, rec + a.rg.off[3] + (size_t)u0 * RB, UR, RB);
     cpa_rows(reinterpret_cast<uint8_t*>(Sg), srow_b, rec + a.rg.off[1] + (size_t)u0 * NG * 2, UR, NG * 2);
     cpa_rows(reinterpret_cast<uint8_t*>(Bg), srow_b, rec + a.rg.off[2] + (size_t)u0 * NG * 2, UR, NG * 2);
     cpa_rows(reinterpret_cast<uint8_t*>(Su), srow_b, rec + a.rg.off[4] + (size_t)u0 * NG * 2, UR, NG * 2);
     cpa_rows(reinterpret_cast<uint8_t*>(Bu), srow_b, rec + a.rg.off[5] + (size_t)u0 * NG * 2, UR, NG * 2);
-    for (int p0 = p_beg; p0 < p_end; p0 += 8) {
-      const int ntok = min(8, p_end - p0);
-      if (p0 != p_beg) __syncthreads();  // previous pass done with XF / RED
-      if (threadIdx.x < 8) tok_s[threadIdx.x] = threadIdx.x < ntok ? a.plan->pair_tj[p0 + threadIdx.x] / a.K : 0;
-      __syncthreads();
-      for (int i = threadIdx.x; i < ntok * (xs / 4); i += blockDim.x) {
-        const int r = i / (xs / 4), q = i % (xs / 4);
-        cpa16(XF + (size_t)r * xs + 4 * q, a.xf + (size_t)tok_s[r] * xs + 4 * q);
-      }
-      for (int i = threadIdx.x; i < ntok * (gsd / 2); i += blockDim.x) {
-        const int r = i / (gsd / 2), q = i % (gsd / 2);
-        cpa16(XG + (size_t)r * gsd + 2 * q, a.xg + (size_t)tok_s[r] * gsd + 2 * q);
-      }
-      cpa_wait_all();
-      __syncthreads();
-      float ag[1][4] = {{0.f, 0.f, 0.f, 0.f}}, au[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-      warp_tile<BITS, GS, 1>(Wt, RB, 16 * ut, Sg, Bg, srow_h, ks * cpw, cpw, XF, xs, XG, gsd, ntok, ag);
-      warp_tile<BITS, GS, 1>(Wt, RB, UR + 16 * ut, Su - (size_t)UR * srow_h, Bu - (size_t)UR * srow_h, srow_h,
-                             ks * cpw, cpw, XF, xs, XG, gsd, ntok, au);
-      // RED[ks][gu][unit][tok]
-      float* rg_ = RED + ((size_t)(ks * 2 + 0) * UR) * 8;
-      float* ru_ = RED + ((size_t)(ks * 2 + 1) * UR) * 8;
-      const int u_a = 16 * ut + g, u_b = u_a + 8;
-      rg_[u_a * 8 + 2 * c] = ag[0][0];
-      rg_[u_a * 8 + 2 * c + 1] = ag[0][1];
-      rg_[u_b * 8 + 2 * c] = ag[0][2];
-      rg_[u_b * 8 + 2 * c + 1] = ag[0][3];
-      ru_[u_a * 8 + 2 * c] = au[0][0];
-      ru_[u_a * 8 + 2 * c + 1] = au[0][1];
-      ru_[u_b * 8 + 2 * c] = au[0][2];
-      ru_[u_b * 8 + 2 * c + 1] = au[0][3];
-      __syncthreads();
-      for (int i = threadIdx.x; i < UR * 8; i += blockDim.x) {
-        const int tok = i / UR, u = i % UR;
-        if (tok >= ntok) continue;
-        float gs_ = 0.0f, us_ = 0.0f;
+    __syncthreads();  // tok_s
+    for (int i = threadIdx.x; i < ntok * (xs / 4); i += blockDim.x) {
+      const int r = i / (xs / 4), q = i % (xs / 4);
+      cpa16(XF + (size_t)r * xs + 4 * q, a.xf + (size_t)tok_s[r] * xs + 4 * q);
+    }
+    for (int i = threadIdx.x; i < ntok * (gsd / 2); i += blockDim.x) {
+      const int r = i / (gsd / 2), q = i % (gsd / 2);
+      cpa16(XG + (size_t)r * gsd + 2 * q, a.xg + (size_t)tok_s[r] * gsd + 2 * q);
+    }
+    cpa_wait_all();
+    __syncthreads();
+    float ag[1][4] = {{0.f, 0.f, 0.f, 0.f}}, au[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    warp_tile<BITS, GS, 1>(Wt, RB, 16 * ut, Sg, Bg, srow_h, ks * cpw, cpw, XF, xs, XG, gsd, ntok, ag);
+    warp_tile<BITS, GS, 1>(Wt, RB, UR + 16 * ut, Su - (size_t)UR * srow_h, Bu - (size_t)UR * srow_h, srow_h,
+                           ks * cpw, cpw, XF, xs, XG, gsd, ntok, au);
+    // RED[ks][gu][unit][tok]
+    float* rg_ = RED + ((size_t)(ks * 2 + 0) * UR) * 8;
+    float* ru_ = RED + ((size_t)(ks * 2 + 1) * UR) * 8;
+    const int u_a = 16 * ut + g, u_b = u_a + 8;
+    rg_[u_a * 8 + 2 * c] = ag[0][0];
+    rg_[u_a * 8 + 2 * c + 1] = ag[0][1];
+    rg_[u_b * 8 + 2 * c] = ag[0][2];
+    rg_[u_b * 8 + 2 * c + 1] = ag[0][3];
+    ru_[u_a * 8 + 2 * c] = au[0][0];
+    ru_[u_a * 8 + 2 * c + 1] = au[0][1];
+    ru_[u_b * 8 + 2 * c] = au[0][2];
+    ru_[u_b * 8 + 2 * c + 1] = au[0][3];
+    __syncthreads();
+    for (int i = threadIdx.x; i < UR * 8; i += blockDim.x) {
+      const int tok = i / UR, u = i % UR;
+      if (tok >= ntok) continue;
+      float gs_ = 0.0f, us_ = 0.0f;
 #pragma unroll
-        for (int k = 0; k < NKS; ++k) {
-          gs_ = __fadd_rn(gs_, RED[((size_t)(k * 2 + 0) * UR + u) * 8 + tok]);
-          us_ = __fadd_rn(us_, RED[((size_t)(k * 2 + 1) * UR + u) * 8 + tok]);
-        }
-        const float inv = XG[(size_t)tok * gsd + NG].x;
-        const float gv = bf16r(__fmul_rn(gs_, inv)), uv = bf16r(__fmul_rn(us_, inv));
-        a.act[(size_t)(p0 + tok) * a.I + u0 + u] = f32_to_bf16(swiglu_bf16(gv, uv));
+      for (int k = 0; k < NKS; ++k) {
+        gs_ = __fadd_rn(gs_, RED[((size_t)(k * 2 + 0) * UR + u) * 8 + tok]);
+        us_ = __fadd_rn(us_, RED[((size_t)(k * 2 + 1) * UR + u) * 8 + tok]);
       }
+      const float inv = XG[(size_t)tok * gsd + NG].x;
+      const float gv = bf16r(__fmul_rn(gs_, inv)), uv = bf16r(__fmul_rn(us_, inv));
+      a.act[(size_t)(p0 + tok) * a.I + u0 + u] = f32_to_bf16(swiglu_bf16(gv, uv));
     }
   }
 }
 
 // --------------------------------------------------------------- down
-// Work item = (segment, tile of 64 output rows). Warp w: row subtile w & 3,
-// K half w >> 2. Pairs in passes of 8 * NCH. Routed outputs go to the home
-// rank's buffer (peer stores), then the home counter is raised by the number
-// of pairs of that rank in the item; shared outputs go to ysh (times the
-// shared gate).
+// Work item = (down pass, tile of 64 output rows): the pass's at most 32
+// pairs of one expert. Warp w: row subtile w & 3, K half w >> 2. Routed
+// outputs go to the home rank's buffer (peer stores), then the home counter
+// is raised by the item's pairs of that rank; shared outputs go to ysh
+// (times the shared gate).
 template <int BITS, int GS, int NCH>
 __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a) {
   using F = BFmt<BITS, GS>;
   constexpr int RT = 64, PP = 8 * NCH;
+  static_assert(PP == BT_DN_PASS, "a down item is one plan pass");
   extern __shared__ __align__(128) uint8_t smem[];
   if (*(volatile const int*)a.st.err) return;
   const int Kd = a.shared ? a.sh_down.cols : a.I;
@@ -628,24 +739,26 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int rs = warp & 3, kh = warp >> 2;
   const int tiles = H / RT;
-  const int n_seg = a.shared ? 1 : a.plan->n_seg;
-  const int n_items = n_seg * tiles;
+  const int n_pass = a.shared ? (a.n_shared + PP - 1) / PP : a.plan->n_dn;
+  const int n_items = n_pass * tiles;
   const int nchunk = Kd / F::CPCH, cpw = nchunk / 2;
   const int T_h = a.st.T_h, K = a.K;
+  if (threadIdx.x < BT_MAX_RANKS) home_cnt[threadIdx.x] = 0;  // units per home rank, over all items
   for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const int sidx = it / tiles, r0 = (it % tiles) * RT;
-    int p_beg, p_end;
+    const int gp = it / tiles, r0 = (it % tiles) * RT;
+    int p0, ntok;
     const uint8_t *wsrc, *ssrc, *bsrc;
     if (a.shared) {
-      p_beg = 0;
-      p_end = a.n_shared;
+      p0 = gp * PP;
+      ntok = min(PP, a.n_shared - p0);
       wsrc = a.sh_down.w + (size_t)r0 * RB;
       ssrc = reinterpret_cast<const uint8_t*>(a.sh_down.s + (size_t)r0 * NG);
       bsrc = reinterpret_cast<const uint8_t*>(a.sh_down.b + (size_t)r0 * NG);
     } else {
+      const int sidx = seg_of_pass(a.plan->seg_dn0, a.plan->n_seg, gp);
       const int e = a.plan->seg_e[sidx];
-      p_beg = a.plan->seg_off[sidx];
-      p_end = a.plan->seg_off[sidx + 1];
+      p0 = a.plan->seg_off[sidx] + (gp - a.plan->seg_dn0[sidx]) * PP;
+      ntok = min(PP, a.plan->seg_off[sidx + 1] - p0);
       const int slot = a.slot_of ? a.slot_of[e] : e - a.e_lo;
       if (slot < 0 || slot >= a.n_slots) {
         if (threadIdx.x == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
@@ -660,63 +773,59 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
     cpa_rows_swz(Wt, 0, wsrc, RT, RB);
     cpa_rows(reinterpret_cast<uint8_t*>(Ss), srow_b, ssrc, RT, NG * 2);
     cpa_rows(reinterpret_cast<uint8_t*>(Bs), srow_b, bsrc, RT, NG * 2);
-    if (threadIdx.x < BT_MAX_RANKS) home_cnt[threadIdx.x] = 0;
-    for (int p0 = p_beg; p0 < p_end; p0 += PP) {
-      const int ntok = min(PP, p_end - p0);
-      if (p0 != p_beg) __syncthreads();
-      cpa_block(XF, a.af + (size_t)p0 * xs, ntok * xs * 4);
-      cpa_block(XG, a.ag + (size_t)p0 * gsd, ntok * gsd * 8);
-      cpa_wait_all();
-      __syncthreads();
-      float acc[NCH][4];
+    cpa_block(XF, a.af + (size_t)p0 * xs, ntok * xs * 4);
+    cpa_block(XG, a.ag + (size_t)p0 * gsd, ntok * gsd * 8);
+    cpa_wait_all();
+    __syncthreads();
+    float acc[NCH][4];
 #pragma unroll
-      for (int t = 0; t < NCH; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-      warp_tile<BITS, GS, NCH>(Wt, RB, 16 * rs, Ss, Bs, srow_h, kh * cpw, cpw, XF, xs, XG, gsd, ntok, acc);
-      float* rd = RED + (size_t)kh * RT * PP;
+    for (int t = 0; t < NCH; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+    warp_tile<BITS, GS, NCH>(Wt, RB, 16 * rs, Ss, Bs, srow_h, kh * cpw, cpw, XF, xs, XG, gsd, ntok, acc);
+    float* rd = RED + (size_t)kh * RT * PP;
 #pragma unroll
-      for (int t = 0; t < NCH; ++t) {
-        const int ra = 16 * rs + g, rb = ra + 8, tk = 8 * t + 2 * c;
-        rd[ra * PP + tk] = acc[t][0];
-        rd[ra * PP + tk + 1] = acc[t][1];
-        rd[rb * PP + tk] = acc[t][2];
-        rd[rb * PP + tk + 1] = acc[t][3];
-      }
-      __syncthreads();
-      // 8 consecutive rows of one pair per thread (one 16-byte store)
-      for (int i = threadIdx.x; i < ntok * (RT / 8); i += blockDim.x) {
-        const int tok = i / (RT / 8), rr = (i % (RT / 8)) * 8;
-        const float inv = XG[(size_t)tok * gsd + NG].x;
-        uint32_t pk[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float v2[2];
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int r = rr + 2 * q + h2;
-            const float v = __fmul_rn(__fadd_rn(RED[(size_t)r * PP + tok], RED[((size_t)RT + r) * PP + tok]), inv);
-            v2[h2] = a.shared ? __fmul_rn(a.sgate[p0 + tok], bf16r(v)) : v;
-          }
-          pk[q] = (uint32_t)f32_to_bf16(v2[0]) | ((uint32_t)f32_to_bf16(v2[1]) << 16);
-        }
-        uint16_t* dst;
-        if (a.shared) {
-          dst = a.ysh + (size_t)(p0 + tok) * H + r0 + rr;
-        } else {
-          const int tj = a.plan->pair_tj[p0 + tok], t = tj / K, j = tj % K;
-          const int home = t / T_h, tl = t % T_h;
-          dst = a.peers.y[home] + ((size_t)tl * K + j) * H + r0 + rr;
-          if (rr == 0) atomicAdd(&home_cnt[home], 1);
-        }
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
+    for (int t = 0; t < NCH; ++t) {
+      const int ra = 16 * rs + g, rb = ra + 8, tk = 8 * t + 2 * c;
+      rd[ra * PP + tk] = acc[t][0];
+      rd[ra * PP + tk + 1] = acc[t][1];
+      rd[rb * PP + tk] = acc[t][2];
+      rd[rb * PP + tk + 1] = acc[t][3];
     }
-    if (!a.shared) {
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence_system();
-        for (int h = 0; h < a.st.G; ++h)
-          if (home_cnt[h]) red_release_sys_add_u64(a.peers.cnt[h], (unsigned long long)home_cnt[h]);
+    __syncthreads();
+    // 8 consecutive rows of one pair per thread (one 16-byte store)
+    for (int i = threadIdx.x; i < ntok * (RT / 8); i += blockDim.x) {
+      const int tok = i / (RT / 8), rr = (i % (RT / 8)) * 8;
+      const float inv = XG[(size_t)tok * gsd + NG].x;
+      uint32_t pk[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v2[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int r = rr + 2 * q + h2;
+          const float v = __fmul_rn(__fadd_rn(RED[(size_t)r * PP + tok], RED[((size_t)RT + r) * PP + tok]), inv);
+          v2[h2] = a.shared ? __fmul_rn(a.sgate[p0 + tok], bf16r(v)) : v;
+        }
+        pk[q] = (uint32_t)f32_to_bf16(v2[0]) | ((uint32_t)f32_to_bf16(v2[1]) << 16);
       }
+      uint16_t* dst;
+      if (a.shared) {
+        dst = a.ysh + (size_t)(p0 + tok) * H + r0 + rr;
+      } else {
+        const int tj = a.plan->pair_tj[p0 + tok], t = tj / K, j = tj % K;
+        const int home = t / T_h, tl = t % T_h;
+        dst = a.peers.y[home] + ((size_t)tl * K + j) * H + r0 + rr;
+        if (rr == 0) atomicAdd(&home_cnt[home], 1);
+      }
+      *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+  // one release per CTA and home rank, after every item's stores
+  if (!a.shared) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int h = 0; h < a.st.G; ++h)
+        if (home_cnt[h]) red_release_sys_add_u64(a.peers.cnt[h], (unsigned long long)home_cnt[h]);
     }
   }
 }

@@ -21,6 +21,7 @@
 #include "yn_qdot.cuh"
 #include "yn_kernels.cuh"
 #include "yn_decode.cuh"
+#include "yn_batch_dense.cuh"
 #include "yn_internal.h"
 
 
@@ -376,6 +377,58 @@ int ynb::host_post_attention_rows(const yn_dims& d, const yn_layer& L, const voi
                                              nullptr, 0, c, st);
     if (rc) return rc;
   }
+  return YN_OK;
+}
+
+int ynb::host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, int T, const PostAttnOut& o,
+                          unsigned* counter, cudaStream_t st) {
+  int rc;
+  const int H = d.hidden, E = d.n_experts;
+  if (!h || !L.post_norm || !counter) return fail(YN_E_INVALID, "batch post-attention: null argument");
+  if (T < 1 || T > 64) return fail(YN_E_UNSUPPORTED, "batch post-attention: rows must be in [1, 64]");
+  if ((rc = check_qmat(L.router, E, H, 8, "router"))) return rc;
+  if (E % BD_ROWS) return fail(YN_E_UNSUPPORTED, "batch post-attention: n_experts must be a multiple of 8");
+  const bool sh = d.shared_inter > 0;
+  if (sh) {
+    if ((rc = check_qmat(L.shared_gate, d.shared_inter, H, 8, "shared_gate"))) return rc;
+    if ((rc = check_qmat(L.shared_up, d.shared_inter, H, 8, "shared_up"))) return rc;
+    if ((rc = check_qmat(L.shared_expert_gate, 1, H, 8, "shared_expert_gate"))) return rc;
+    if (d.shared_inter % BD_ROWS) return fail(YN_E_UNSUPPORTED, "batch post-attention: shared_inter % 8");
+  }
+  BatchDenseArgs a{};
+  a.T = T; a.H = H; a.E = E; a.K = d.top_k; a.Ish = d.shared_inter; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
+  a.h = reinterpret_cast<const uint16_t*>(h);
+  a.norm = reinterpret_cast<const uint16_t*>(L.post_norm);
+  a.router = to_qm(L.router);
+  a.rbias = L.router_bias;
+  a.has_shared = sh;
+  if (sh) {
+    a.sh_gate = to_qm(L.shared_gate);
+    a.sh_up = to_qm(L.shared_up);
+    a.sg = to_qm(L.shared_expert_gate);
+  }
+  a.nt_router = E / BD_ROWS;
+  a.nt_shared = sh ? d.shared_inter / BD_ROWS : 0;
+  a.nt_sg = sh ? 1 : 0;
+  a.x = o.x; a.logits = o.logits; a.act_sh = o.act_sh; a.sgate = o.sgate; a.ids = o.ids; a.wts = o.wts;
+  a.counter = counter;
+  a.err = o.err;
+  auto part = [](size_t R, size_t rb, size_t sb) { return (R * rb + 15) / 16 * 16 + 2 * ((R * sb + 15) / 16 * 16); };
+  size_t tile = part(BD_ROWS, H, (size_t)(H / L.router.group_size) * 2);
+  if (sh) tile = std::max(tile, 2 * part(BD_ROWS, H, (size_t)(H / L.shared_gate.group_size) * 2));
+  const size_t smem = SMEM_HDR + (size_t)BD_TOK * H * 2 + (size_t)H * 2 + tile;
+  dim3 grid(a.nt_router + a.nt_shared + a.nt_sg, (T + BD_TOK - 1) / BD_TOK);
+  switch (H / 512) {
+#define BDK(C)                                                                      \
+  case C:                                                                           \
+    if ((rc = set_smem(k_batch_dense<C>, smem))) return rc;                         \
+    k_batch_dense<C><<<grid, THREADS, smem, st>>>(a);                               \
+    break;
+    BDK(1) BDK(2) BDK(4) BDK(8)
+#undef BDK
+    default: return fail(YN_E_UNSUPPORTED, "batch post-attention: hidden must be 512, 1024, 2048 or 4096");
+  }
+  YN_CUDA(cudaGetLastError());
   return YN_OK;
 }
 

@@ -4,7 +4,7 @@
 // Cody-Waite range reduction plus a degree-7 Taylor polynomial (so the CPU
 // oracle can reproduce it bit for bit), warp butterfly reductions, and thin
 // PTX wrappers for mbarriers and the non-tensor bulk copy engine
-// (cp.async.bulk, no multicast anywhere).
+// (cp.async.bulk, every copy to this CTA alone).
 #pragma once
 
 #include <cuda_runtime.h>

@@ -46,6 +46,21 @@ def home_rows(batch: int, rank: int, world: int) -> Tuple[int, int]:
     return rank * per, (rank + 1) * per
 
 
+def plan_pairs(ids: np.ndarray, e_lo: int, e_hi: int):
+    """The segment plan the device builds per layer (k_batch_frags, block 0):
+    the (row, column) pairs whose expert is in [e_lo, e_hi), grouped by
+    expert in ascending id order, pairs of one expert in (row, column) order.
+    Returns (experts, offsets, pairs) with pairs as row * K + column."""
+    ids = np.asarray(ids)
+    K = ids.shape[1]
+    flat = ids.reshape(-1)
+    sel = np.nonzero((flat >= e_lo) & (flat < e_hi))[0]
+    order = sel[np.argsort(flat[sel], kind="stable")]
+    experts, counts = np.unique(flat[order], return_counts=True)
+    offsets = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    return experts.astype(np.int64), offsets, order.astype(np.int64)
+
+
 def _exchange_handles(handle: bytes, world: int, group=None) -> List[bytes]:
     import torch.distributed as dist
     out: List[Optional[bytes]] = [None] * world
