@@ -303,8 +303,9 @@ def run_ep(args, rank: int, world: int):
     torch.cuda.set_device(dev)
     cfg = qwen3_next_stack(seed=0)
     B = args.batch
-    stack = ExpertParallelStack(cfg, batch=B, rank=rank, world=world, device=dev)
-    H, K, L = cfg.hidden, cfg.top_k, cfg.n_layers
+    layer_ids = list(range(args.first_layer, args.first_layer + (args.layers or cfg.n_layers)))
+    stack = ExpertParallelStack(cfg, batch=B, rank=rank, world=world, device=dev, layers=layer_ids)
+    H, K, L = cfg.hidden, cfg.top_k, len(layer_ids)
     T_h = B // world
     rows = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
     _lib.check(_lib.lib().yn_synth_bf16(rows.data_ptr(), B * H, cfg.seed, hidden_stream_id(500), 1.0, 0.0,
@@ -384,7 +385,7 @@ def run_ep(args, rank: int, world: int):
 
     # rooflines of this rank's step: HBM (each local expert record of a layer
     # once, the dense weights once) and NVLink (rows out, output rows back)
-    rec = [cfg.record_spec(l).record_bytes for l in range(L)]
+    rec = [cfg.record_spec(l).record_bytes for l in layer_ids]
     hbm_bytes = sum(n * r for n, r in zip(n_local, rec)) + L * cfg.dense_bytes_per_layer()
     link_bytes = L * T_h * (H * 2 + K * 4) * (world - 1) + pairs_out * H * 2
     hbm, src = peaks()

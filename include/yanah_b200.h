@@ -267,7 +267,7 @@ typedef struct yn_ep_sym_ptrs {
   void* x_all;        /* (n_ranks * rows_per_rank, H) gathered rows */
   int32_t* ids_all;   /* (n_ranks * rows_per_rank, k) */
   void* y;            /* (rows_per_rank, k, H) routed outputs of the home rows */
-  uint64_t* flags;    /* (8) arrival stamps, slot = writing rank */
+  uint64_t* flags;    /* (8, 16) arrival stamps: [writing rank][dispatch CTA] */
   uint64_t* counter;  /* finished (pair, 64-row tile) units, cumulative */
 } yn_ep_sym_ptrs;
 int yn_ep_view(void* local, const yn_dims* dims, const yn_ep_config* cfg, yn_ep_local_ptrs* out);

@@ -32,7 +32,7 @@ struct SymLayout {
   size_t x_all, ids_all, flags, cnt, y, total;
 };
 struct LocalLayout {
-  size_t err, counter, done, epoch, x_home, logits, ids, w, act_sh, sgate, plan, xf, xg, act, af, ag, sf, sg, ysh, total;
+  size_t err, counter, epoch, x_home, logits, ids, w, act_sh, sgate, plan, xf, xg, act, af, ag, sf, sg, ysh, total;
 };
 
 SymLayout sym_layout(const yn_dims& d, const yn_ep_config& c) {
@@ -42,7 +42,7 @@ SymLayout sym_layout(const yn_dims& d, const yn_ep_config& c) {
   const size_t R = (size_t)c.n_ranks * c.rows_per_rank;
   L.x_all = take(R * d.hidden * 2);
   L.ids_all = take(R * d.top_k * 4);
-  L.flags = take((size_t)BT_MAX_RANKS * 8);
+  L.flags = take((size_t)BT_MAX_RANKS * BT_MAX_DISPATCH * 8);
   L.cnt = take(8);
   L.y = take((size_t)c.rows_per_rank * d.top_k * d.hidden * 2);
   L.total = o;
@@ -58,7 +58,6 @@ LocalLayout local_layout(const yn_dims& d, const yn_ep_config& c) {
   const size_t Ish = d.shared_inter ? d.shared_inter : 64;
   L.err = take(4);
   L.counter = take(8 * 4);
-  L.done = take(BT_MAX_RANKS * 4);
   L.epoch = take(8);
   L.x_home = take(T * H * 2);
   L.logits = take(T * E * 4);
@@ -339,6 +338,9 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     peers.cnt[r] = reinterpret_cast<unsigned long long*>(b + S.cnt);
   }
 
+  // dispatch CTAs per destination (the same on every rank: same T_h and H)
+  const int n_disp = std::max(1, std::min(BT_MAX_DISPATCH, (T_h * H / 8 + BT_THREADS * 4 - 1) / (BT_THREADS * 4)));
+
   // 1. post-attention + routing of the home rows
   PostAttnOut pa{};
   pa.x = reinterpret_cast<uint16_t*>(lb + L.x_home);
@@ -357,11 +359,9 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     a.peers = peers;
     a.x_home = pa.x;
     a.ids_home = pa.ids;
-    a.done = reinterpret_cast<unsigned*>(lb + L.done);
     a.H = H;
     a.K = K;
-    const int nb = std::max(1, std::min(16, (T_h * H / 8 + BT_THREADS * 4 - 1) / (BT_THREADS * 4)));
-    k_ep_dispatch<<<dim3(G, nb), BT_THREADS, 0, st>>>(a);
+    k_ep_dispatch<<<dim3(G, n_disp), BT_THREADS, 0, st>>>(a);
     YN_CUDA_B(cudaGetLastError());
   }
 
@@ -409,6 +409,7 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
     f.xg = reinterpret_cast<float2*>(lb + L.xg);
     f.st = es;
     f.flags = peers.flag[cfg->rank];
+    f.n_dispatch = n_disp;
     f.ids = peers.ids_all[cfg->rank];
     f.K = K;
     f.E = d.n_experts;

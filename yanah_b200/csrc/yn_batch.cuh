@@ -55,6 +55,7 @@ constexpr int BT_MAX_K = 16;
 constexpr int BT_MAX_PAIRS = BT_MAX_TOK * BT_MAX_K;  // 1024
 constexpr int BT_THREADS = 256;
 constexpr int BT_MAX_RANKS = 8;
+constexpr int BT_MAX_DISPATCH = 16;                  // dispatch CTAs per destination
 
 enum : int { YN_ERR_PEER_TIMEOUT = 6, YN_ERR_BATCH_ID = 7 };
 
@@ -69,8 +70,33 @@ struct BatchPlan {
 constexpr int BT_UP_PASS = 8;      // token rows per up work item
 constexpr int BT_DN_PASS = 32;     // pairs per down work item
 
+// The plan's segment tables in shared memory (16-bit: every entry < 2^16),
+// copied once per CTA so that work-item lookups do not chain global loads.
+struct PlanSmem {
+  uint16_t first[BT_MAX_PAIRS + 1];  // first pass of each segment (up or down passes)
+  uint16_t seg_e[BT_MAX_PAIRS];
+  uint16_t off[BT_MAX_PAIRS + 1];
+  uint16_t tj[BT_MAX_PAIRS];
+  int n_seg, n_pass;
+};
+YN_DEV void load_plan(const BatchPlan* p, bool up, PlanSmem* sm) {
+  const int ns = p->n_seg, np = p->n_pairs;
+  const int* first = up ? p->seg_up0 : p->seg_dn0;
+  for (int i = threadIdx.x; i <= ns; i += blockDim.x) {
+    sm->first[i] = (uint16_t)first[i];
+    sm->off[i] = (uint16_t)p->seg_off[i];
+    if (i < ns) sm->seg_e[i] = (uint16_t)p->seg_e[i];
+  }
+  for (int i = threadIdx.x; i < np; i += blockDim.x) sm->tj[i] = (uint16_t)p->pair_tj[i];
+  if (threadIdx.x == 0) {
+    sm->n_seg = ns;
+    sm->n_pass = up ? p->n_up : p->n_dn;
+  }
+  __syncthreads();
+}
+
 // Segment of global pass index gp: the last s with first[s] <= gp.
-YN_DEV int seg_of_pass(const int* first, int n_seg, int gp) {
+YN_DEV int seg_of_pass(const uint16_t* first, int n_seg, int gp) {
   int lo = 0, hi = n_seg - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -173,20 +199,22 @@ YN_DEV void cpa_block(void* dst, const void* src, int bytes) {
 
 // Rows of RB bytes from global into a swizzled shared tile: chunk ch of row r
 // lands at r * RB + ((ch ^ (r & 7)) * 16). RB / 16 must be a multiple of 8.
+// RB / 16 must be a power of two and a multiple of 8.
 YN_DEV void cpa_rows_swz(uint8_t* dst, int row0, const uint8_t* src, int rows, int RB) {
-  const int cpr = RB / 16;
+  const int cpr = RB >> 4, sh = __ffs(cpr) - 1;
   for (int i = threadIdx.x; i < rows * cpr; i += blockDim.x) {
-    const int r = i / cpr, ch = i % cpr, rr = row0 + r;
-    cpa16(dst + (size_t)rr * RB + ((ch ^ (rr & 7)) << 4), src + (size_t)r * RB + 16 * ch);
+    const int r = i >> sh, ch = i & (cpr - 1), rr = row0 + r;
+    cpa16(dst + (size_t)rr * RB + ((ch ^ (rr & 7)) << 4), src + ((size_t)i << 4));
   }
 }
 
-// Rows of `bytes` bytes into rows of `stride` bytes (both multiples of 16).
+// Rows of `bytes` bytes into rows of `stride` bytes (both multiples of 16;
+// bytes / 16 a power of two).
 YN_DEV void cpa_rows(uint8_t* dst, int stride, const uint8_t* src, int rows, int bytes) {
-  const int cpr = bytes / 16;
+  const int cpr = bytes >> 4, sh = __ffs(cpr) - 1;
   for (int i = threadIdx.x; i < rows * cpr; i += blockDim.x) {
-    const int r = i / cpr, ch = i % cpr;
-    cpa16(dst + (size_t)r * stride + 16 * ch, src + (size_t)r * bytes + 16 * ch);
+    const int r = i >> sh, ch = i & (cpr - 1);
+    cpa16(dst + (size_t)r * stride + (ch << 4), src + ((size_t)i << 4));
   }
 }
 
@@ -234,7 +262,7 @@ YN_DEV bool wait_geq_block(const unsigned long long* p, unsigned long long targe
 struct EpPeers {
   uint16_t* x_all[BT_MAX_RANKS];               // (G*T_h, H) gather buffer of rank d
   int32_t* ids_all[BT_MAX_RANKS];              // (G*T_h, K)
-  unsigned long long* flag[BT_MAX_RANKS];      // (G) arrival flags of rank d, slot = writer
+  unsigned long long* flag[BT_MAX_RANKS];      // (G, BT_MAX_DISPATCH) arrival flags of rank d: [writer][cta]
   uint16_t* y[BT_MAX_RANKS];                   // (T_h, K, H) routed outputs of rank d's rows
   unsigned long long* cnt[BT_MAX_RANKS];       // finished-unit counter of rank d
 };
@@ -254,7 +282,6 @@ struct DispatchArgs {
   EpPeers peers;
   const uint16_t* x_home;   // (T_h, H)
   const int32_t* ids_home;  // (T_h, K)
-  unsigned* done;           // (G) CTA arrivals per destination (monotonic)
   int H, K;
 };
 
@@ -267,7 +294,8 @@ struct FragArgs {
   float2* xg;               // (n_rows, gdata_stride)
   // k_batch_prep only: wait for every rank's rows, then block 0 plans
   EpStep st;
-  const unsigned long long* flags;  // this rank's arrival flags (G)
+  const unsigned long long* flags;  // this rank's arrival flags (G, BT_MAX_DISPATCH)
+  int n_dispatch;           // dispatch CTAs per source rank
   const int32_t* ids;       // (n_rows, K) routed ids of every row
   int K, E, e_lo, e_hi;
   BatchPlan* plan;
@@ -324,10 +352,10 @@ struct CombineArgs {
 
 // ------------------------------------------------------------- dispatch
 // Grid (G, NB): the NB CTAs of destination d copy slices of this rank's home
-// rows (and CTA 0 the ids) into rank d's gather buffer; the last of them to
-// finish raises flag[rank] there (release, system scope).
+// rows (and CTA 0 the ids) into rank d's gather buffer; each CTA then raises
+// its own flag there, flag[rank][cta] (a release at system scope, after the
+// block barrier, so it covers every store of the CTA).
 __global__ void __launch_bounds__(BT_THREADS) k_ep_dispatch(const DispatchArgs a) {
-  __shared__ int last_s;
   const int d = blockIdx.x, nb = gridDim.y;
   const EpStep& s = a.st;
   const size_t row0 = (size_t)s.rank * s.T_h;
@@ -348,17 +376,8 @@ __global__ void __launch_bounds__(BT_THREADS) k_ep_dispatch(const DispatchArgs a
     int32_t* id = a.peers.ids_all[d] + row0 * a.K;
     for (int i = threadIdx.x; i < s.T_h * a.K; i += blockDim.x) id[i] = a.ids_home[i];
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned prev = atomicAdd(a.done + d, 1u);
-    last_s = ((prev + 1u) % (unsigned)nb) == 0u;
-  }
-  __syncthreads();
-  if (last_s && threadIdx.x == 0) {
-    __threadfence_system();
-    st_release_sys_u64(a.peers.flag[d] + s.rank, ep_stamp(s));
-  }
+  __syncthreads();  // the CTA's stores, then its flag (a release covers them)
+  if (threadIdx.x == 0) st_release_sys_u64(a.peers.flag[d] + s.rank * BT_MAX_DISPATCH + blockIdx.y, ep_stamp(s));
 }
 
 // ------------------------------------------------------------ fragments
@@ -489,12 +508,27 @@ YN_DEV void build_plan(const FragArgs& a) {
     a.plan->seg_dn0[tot.x] = tot.w;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    const int e = ids_s[i];
-    if (e < a.e_lo || e >= a.e_hi) continue;
-    int rank = 0;
-    for (int q = 0; q < i; ++q) rank += (ids_s[q] == e);
-    a.plan->pair_tj[a.plan->seg_off[segof[e - a.e_lo]] + rank] = i;
+  // warp 0 places the pairs in index order, 32 at a time: a pair's position
+  // is its segment start + the pairs of its expert placed before it
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    for (int e = lane; e < El; e += 32) cnt[e] = 0;
+    __syncwarp();
+    for (int i0 = 0; i0 < P; i0 += 32) {
+      const int i = i0 + lane;
+      const int e = i < P ? ids_s[i] : -1;
+      const bool mine = e >= a.e_lo && e < a.e_hi;
+      const int key = mine ? e : -1 - lane;  // non-local lanes match nobody
+      const unsigned same = __match_any_sync(0xffffffffu, key);
+      if (mine) {
+        const int el = e - a.e_lo;
+        const int before = __popc(same & ((1u << lane) - 1u));
+        a.plan->pair_tj[a.plan->seg_off[segof[el]] + cnt[el] + before] = i;
+      }
+      __syncwarp();
+      if (mine && (same >> lane) == 1u) cnt[e - a.e_lo] += __popc(same);  // highest lane of the group
+      __syncwarp();
+    }
   }
 }
 
@@ -505,7 +539,9 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_prep(const FragArgs a) {
   __shared__ __align__(16) uint16_t xs[8192];
   __shared__ float red[BT_THREADS / 32];
   bool ok = true;
-  for (int r = 0; r < a.st.G && ok; ++r) ok = wait_geq_block(a.flags + r, ep_stamp(a.st), a.st.err);
+  for (int r = 0; r < a.st.G && ok; ++r)
+    for (int q = 0; q < a.n_dispatch && ok; ++q)
+      ok = wait_geq_block(a.flags + r * BT_MAX_DISPATCH + q, ep_stamp(a.st), a.st.err);
   if (!ok) return;
   if (blockIdx.x == 0) {
     build_plan(a);
@@ -640,19 +676,21 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_up(const BatchUpArgs a) {
   float2* XG = reinterpret_cast<float2*>(XF + (size_t)8 * xs);           // 8 rows x gsd
   float* RED = reinterpret_cast<float*>(XG + (size_t)8 * gsd);           // NKS x 2 x UR x 8
   __shared__ int tok_s[8];
+  __shared__ PlanSmem pl;
+  load_plan(a.plan, true, &pl);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int ut = warp % NUT, ks = warp / NUT;
   const int tiles = a.I / UR;
-  const int n_seg = a.plan->n_seg;
-  const int n_items = a.plan->n_up * tiles;
+  const int n_seg = pl.n_seg;
+  const int n_items = pl.n_pass * tiles;
   const int nchunk = H / F::CPCH, cpw = nchunk / NKS;
   for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
     const int gp = it / tiles, u0 = (it % tiles) * UR;
-    const int sidx = seg_of_pass(a.plan->seg_up0, n_seg, gp);
-    const int e = a.plan->seg_e[sidx];
-    const int p0 = a.plan->seg_off[sidx] + (gp - a.plan->seg_up0[sidx]) * BT_UP_PASS;
-    const int ntok = min(BT_UP_PASS, a.plan->seg_off[sidx + 1] - p0);
+    const int sidx = seg_of_pass(pl.first, n_seg, gp);
+    const int e = pl.seg_e[sidx];
+    const int p0 = pl.off[sidx] + (gp - pl.first[sidx]) * BT_UP_PASS;
+    const int ntok = min(BT_UP_PASS, (int)pl.off[sidx + 1] - p0);
     const int slot = a.slot_of ? a.slot_of[e] : e - a.e_lo;
     if (slot < 0 || slot >= a.n_slots) {
       if (threadIdx.x == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
@@ -660,7 +698,7 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_up(const BatchUpArgs a) {
     }
     const uint8_t* rec = a.base + (size_t)slot * (size_t)a.stride;
     __syncthreads();  // the previous item is done with every buffer
-    if (threadIdx.x < 8) tok_s[threadIdx.x] = threadIdx.x < ntok ? a.plan->pair_tj[p0 + threadIdx.x] / a.K : 0;
+    if (threadIdx.x < 8) tok_s[threadIdx.x] = threadIdx.x < ntok ? pl.tj[p0 + threadIdx.x] / a.K : 0;
     cpa_rows_swz(Wt, 0, rec + a.rg.off[0] + (size_t)u0 * RB, UR, RB);
     cpa_rows_swz(Wt, UR, rec + a.rg.off[3] + (size_t)u0 * RB, UR, RB);
     cpa_rows(reinterpret_cast<uint8_t*>(Sg), srow_b, rec + a.rg.off[1] + (size_t)u0 * NG * 2, UR, NG * 2);
@@ -668,13 +706,11 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_up(const BatchUpArgs a) {
     cpa_rows(reinterpret_cast<uint8_t*>(Su), srow_b, rec + a.rg.off[4] + (size_t)u0 * NG * 2, UR, NG * 2);
     cpa_rows(reinterpret_cast<uint8_t*>(Bu), srow_b, rec + a.rg.off[5] + (size_t)u0 * NG * 2, UR, NG * 2);
     __syncthreads();  // tok_s
-    for (int i = threadIdx.x; i < ntok * (xs / 4); i += blockDim.x) {
-      const int r = i / (xs / 4), q = i % (xs / 4);
-      cpa16(XF + (size_t)r * xs + 4 * q, a.xf + (size_t)tok_s[r] * xs + 4 * q);
-    }
-    for (int i = threadIdx.x; i < ntok * (gsd / 2); i += blockDim.x) {
-      const int r = i / (gsd / 2), q = i % (gsd / 2);
-      cpa16(XG + (size_t)r * gsd + 2 * q, a.xg + (size_t)tok_s[r] * gsd + 2 * q);
+    for (int r = 0; r < ntok; ++r) {
+      const uint32_t* xr = a.xf + (size_t)tok_s[r] * xs;
+      for (int q = threadIdx.x; q < xs / 4; q += blockDim.x) cpa16(XF + (size_t)r * xs + 4 * q, xr + 4 * q);
+      const float2* gr = a.xg + (size_t)tok_s[r] * gsd;
+      for (int q = threadIdx.x; q < gsd / 2; q += blockDim.x) cpa16(XG + (size_t)r * gsd + 2 * q, gr + 2 * q);
     }
     cpa_wait_all();
     __syncthreads();
@@ -735,11 +771,13 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
   float2* XG = reinterpret_cast<float2*>(XF + (size_t)PP * xs);
   float* RED = reinterpret_cast<float*>(XG + (size_t)PP * gsd);  // 2 x RT x PP
   __shared__ int home_cnt[BT_MAX_RANKS];
+  __shared__ PlanSmem pl;
+  if (!a.shared) load_plan(a.plan, false, &pl);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int rs = warp & 3, kh = warp >> 2;
   const int tiles = H / RT;
-  const int n_pass = a.shared ? (a.n_shared + PP - 1) / PP : a.plan->n_dn;
+  const int n_pass = a.shared ? (a.n_shared + PP - 1) / PP : pl.n_pass;
   const int n_items = n_pass * tiles;
   const int nchunk = Kd / F::CPCH, cpw = nchunk / 2;
   const int T_h = a.st.T_h, K = a.K;
@@ -755,10 +793,10 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
       ssrc = reinterpret_cast<const uint8_t*>(a.sh_down.s + (size_t)r0 * NG);
       bsrc = reinterpret_cast<const uint8_t*>(a.sh_down.b + (size_t)r0 * NG);
     } else {
-      const int sidx = seg_of_pass(a.plan->seg_dn0, a.plan->n_seg, gp);
-      const int e = a.plan->seg_e[sidx];
-      p0 = a.plan->seg_off[sidx] + (gp - a.plan->seg_dn0[sidx]) * PP;
-      ntok = min(PP, a.plan->seg_off[sidx + 1] - p0);
+      const int sidx = seg_of_pass(pl.first, pl.n_seg, gp);
+      const int e = pl.seg_e[sidx];
+      p0 = pl.off[sidx] + (gp - pl.first[sidx]) * PP;
+      ntok = min(PP, (int)pl.off[sidx + 1] - p0);
       const int slot = a.slot_of ? a.slot_of[e] : e - a.e_lo;
       if (slot < 0 || slot >= a.n_slots) {
         if (threadIdx.x == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
@@ -811,7 +849,7 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
       if (a.shared) {
         dst = a.ysh + (size_t)(p0 + tok) * H + r0 + rr;
       } else {
-        const int tj = a.plan->pair_tj[p0 + tok], t = tj / K, j = tj % K;
+        const int tj = pl.tj[p0 + tok], t = tj / K, j = tj % K;
         const int home = t / T_h, tl = t % T_h;
         dst = a.peers.y[home] + ((size_t)tl * K + j) * H + r0 + rr;
         if (rr == 0) atomicAdd(&home_cnt[home], 1);
@@ -821,12 +859,10 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
   }
   // one release per CTA and home rank, after every item's stores
   if (!a.shared) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
+    __syncthreads();  // every store of the CTA, then the releases (which cover them)
+    if (threadIdx.x == 0)
       for (int h = 0; h < a.st.G; ++h)
         if (home_cnt[h]) red_release_sys_add_u64(a.peers.cnt[h], (unsigned long long)home_cnt[h]);
-    }
   }
 }
 

@@ -18,14 +18,12 @@ constexpr int BD_TOK = 8;    // tokens per CTA
 struct BatchDenseArgs {
   int T, H, E, K, Ish, norm_topk;
   float eps;
-  const uint16_t* h;        // (T, H) input rows
-  const uint16_t* norm;     // (H)
+  const uint16_t* x;        // (T, H) normalised rows (k_rmsnorm_rows)
   QM router;
   const float* rbias;
   QM sh_gate, sh_up, sg;
   int has_shared;
   int nt_router, nt_shared, nt_sg;
-  uint16_t* x;              // (T, H) normalised rows
   float* logits;            // (T, E)
   uint16_t* act_sh;         // (T, Ish)
   float* sgate;             // (T)
@@ -35,19 +33,96 @@ struct BatchDenseArgs {
   int* err;
 };
 
+// RMSNorm of T rows (one 128-thread CTA per row, the canonical order of
+// rmsnorm_row): x = bf16(w * bf16(h * r)).
+__global__ void __launch_bounds__(THREADS) k_rmsnorm_rows(const uint16_t* h, const uint16_t* norm, int H, float eps,
+                                                          uint16_t* x) {
+  extern __shared__ __align__(16) uint16_t rs[];
+  __shared__ float red[32];
+  uint16_t* hs = rs;
+  uint16_t* ws = rs + H;
+  const uint4* hg = reinterpret_cast<const uint4*>(h + (size_t)blockIdx.x * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+    reinterpret_cast<uint4*>(hs)[i] = hg[i];
+    reinterpret_cast<uint4*>(ws)[i] = reinterpret_cast<const uint4*>(norm)[i];
+  }
+  __syncthreads();
+  rmsnorm_row(hs, ws, H, eps, hs, x + (size_t)blockIdx.x * H, red);
+}
+
+// Canonical 8-bit dot products of two rows (codes / scales / biases in
+// shared memory) with the nt token rows of the CTA: lane l owns 16-code
+// chunks ci = l + 32 c (c < CPL); per chunk d = fma chain over the 16 codes in
+// order, acc = fma(s, d, acc), acc = fma(b, sum(x over the chunk), acc); then
+// a butterfly over the 32 lanes -- the exact arithmetic of row_dot_f32 for
+// every (row, token). The codes of a chunk are turned into floats once for
+// all tokens. X: per token, float4 v of lane l's chunk c at
+// ((c * 4 + v) * 32 + l); XS: per token, the chunk sums by chunk index.
+template <int CPL>
+YN_DEV void dense_rows2(const uint8_t* ca, const uint16_t* sa, const uint16_t* ba, const uint8_t* cb,
+                        const uint16_t* sb, const uint16_t* bb, const float4* X, const float* XS, int H, int nt,
+                        int gs, float (&oa)[BD_TOK], float (&ob)[BD_TOK]) {
+  const int l = threadIdx.x & 31;
+  float acca[BD_TOK], accb[BD_TOK];
+#pragma unroll
+  for (int t = 0; t < BD_TOK; ++t) acca[t] = accb[t] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) {
+    const int ci = l + 32 * c;
+    const uint4 wa = *reinterpret_cast<const uint4*>(ca + 16 * ci);
+    const uint4 wb = *reinterpret_cast<const uint4*>(cb + 16 * ci);
+    const uint32_t wva[4] = {wa.x, wa.y, wa.z, wa.w}, wvb[4] = {wb.x, wb.y, wb.z, wb.w};
+    float qa[16], qb[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      qa[k] = __fsub_rn(__uint_as_float(__byte_perm(wva[k >> 2], 0x4B000000u, 0x7540u + (unsigned)(k & 3))),
+                        8388608.0f);
+      qb[k] = __fsub_rn(__uint_as_float(__byte_perm(wvb[k >> 2], 0x4B000000u, 0x7540u + (unsigned)(k & 3))),
+                        8388608.0f);
+    }
+    const int g = ci * 16 / gs;
+    const float s_a = f16_to_f32(sa[g]), b_a = f16_to_f32(ba[g]);
+    const float s_b = f16_to_f32(sb[g]), b_b = f16_to_f32(bb[g]);
+#pragma unroll
+    for (int t = 0; t < BD_TOK; ++t) {
+      if (t < nt) {
+        const float4* xt = X + (size_t)t * (H / 4);
+        float xv[16];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 f = xt[(c * 4 + v) * 32 + l];
+          xv[4 * v] = f.x; xv[4 * v + 1] = f.y; xv[4 * v + 2] = f.z; xv[4 * v + 3] = f.w;
+        }
+        float da = 0.0f, db = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          da = __fmaf_rn(xv[k], qa[k], da);
+          db = __fmaf_rn(xv[k], qb[k], db);
+        }
+        const float xs = XS[(size_t)t * (H / 16) + ci];
+        acca[t] = __fmaf_rn(b_a, xs, __fmaf_rn(s_a, da, acca[t]));
+        accb[t] = __fmaf_rn(b_b, xs, __fmaf_rn(s_b, db, accb[t]));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < BD_TOK; ++t) {
+    oa[t] = group_sum_bfly(acca[t], 32);
+    ob[t] = group_sum_bfly(accb[t], 32);
+  }
+}
+
 template <int CPL>
 __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* bar_a = reinterpret_cast<uint64_t*>(smem + 8);
   int* flag = reinterpret_cast<int*>(smem + 16);
-  float* red = reinterpret_cast<float*>(smem + 32);
   const int H = a.H;
-  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + SMEM_HDR);               // (BD_TOK, H) rows, normalised in place
-  uint16_t* ns = xs + (size_t)BD_TOK * H;                                    // (H) norm weight
-  uint8_t* tile = reinterpret_cast<uint8_t*>(ns + H);
+  float4* X = reinterpret_cast<float4*>(smem + SMEM_HDR);                        // (BD_TOK, H) fp32, lane-interleaved
+  float* XS = reinterpret_cast<float*>(X + (size_t)BD_TOK * (H / 4));            // (BD_TOK, H / 16) chunk sums
+  uint8_t* tile = reinterpret_cast<uint8_t*>(XS + (size_t)BD_TOK * (H / 16));
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int t0 = blockIdx.y * BD_TOK, nt = min(BD_TOK, a.T - t0);
   int t = blockIdx.x, kind, row0, nrows;
   QM m0 = a.router, m1 = a.router;
@@ -71,12 +146,12 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
       pc_b[p] = reinterpret_cast<uint16_t*>(tile + o); o += a16((size_t)nrows * sb);
     }
   }
-  init_bars(bar, bar_a);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   {
-    Piece act[2] = {{reinterpret_cast<uint8_t*>(xs), reinterpret_cast<const uint8_t*>(a.h + (size_t)t0 * H),
-                     (uint32_t)(nt * H * 2)},
-                    {reinterpret_cast<uint8_t*>(ns), reinterpret_cast<const uint8_t*>(a.norm), (uint32_t)(H * 2)}};
-    stage_pieces(act, 2, bar_a);
     Piece pc[6];
     int n = 0;
     for (int p = 0; p < nparts; ++p) {
@@ -89,43 +164,67 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
     }
     stage_pieces(pc, n, bar);
   }
+  // normalised rows -> fp32, lane-interleaved: element 16 ci + 4 v + e of a
+  // token (ci = l + 32 c) at float4 (c * 4 + v) * 32 + l, component e
+  for (int i = tid; i < nt * (H / 8); i += THREADS) {
+    const int tt = i / (H / 8), q = i % (H / 8);       // q: 8 elements 8q..8q+7
+    const uint4 w = reinterpret_cast<const uint4*>(a.x + (size_t)(t0 + tt) * H)[q];
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      const int k = 8 * q + 4 * hlf, ci = k >> 4, v = (k >> 2) & 3, c = ci >> 5, l = ci & 31;
+      float4 f;
+      f.x = bf16_to_f32((uint16_t)(wv[2 * hlf] & 0xFFFFu));
+      f.y = bf16_to_f32((uint16_t)(wv[2 * hlf] >> 16));
+      f.z = bf16_to_f32((uint16_t)(wv[2 * hlf + 1] & 0xFFFFu));
+      f.w = bf16_to_f32((uint16_t)(wv[2 * hlf + 1] >> 16));
+      X[(size_t)tt * (H / 4) + (c * 4 + v) * 32 + l] = f;
+    }
+  }
   __syncthreads();
-  const bool act_ok = mbar_wait_block(bar_a, 0, a.err);
-  if (act_ok)
-    for (int tt = 0; tt < nt; ++tt)
-      rmsnorm_row(xs + (size_t)tt * H, ns, H, a.eps, xs + (size_t)tt * H,
-                  (blockIdx.x == 0) ? a.x + (size_t)(t0 + tt) * H : nullptr, red);
+  for (int i = tid; i < nt * (H / 16); i += THREADS) {  // chunk sums, ascending k (as load_x_f32)
+    const int tt = i / (H / 16), ci = i % (H / 16), c = ci >> 5, l = ci & 31;
+    const float4* xt = X + (size_t)tt * (H / 4);
+    float sum = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float4 f = xt[(c * 4 + v) * 32 + l];
+      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, f.x), f.y), f.z), f.w);
+    }
+    XS[(size_t)tt * (H / 16) + ci] = sum;
+  }
   __syncthreads();
-  const bool ok = mbar_wait_block(bar, 0, a.err) && act_ok;
+  const bool ok = mbar_wait_block(bar, 0, a.err);
   if (ok) {
-    const int lpr = lanes_per_row((int)rb), rpi = 32 / lpr, l = lane % lpr, u = lane / lpr;
-    for (int tt = 0; tt < nt; ++tt) {
-      XF32<8, CPL, 1> X;
-      load_x_f32<8, CPL, 1>(X, xs + (size_t)tt * H, l, lpr);
-      for (int rbase = warp * rpi; rbase < nrows; rbase += 4 * rpi) {
-        const int r = rbase + u;
-        const int rr = (r < nrows) ? r : 0;
-        float v0 = row_dot_f32<8, CPL, 1>(pc_codes[0] + (size_t)rr * rb, pc_s[0] + (size_t)rr * ng,
-                                          pc_b[0] + (size_t)rr * ng, X, l, lpr, m0.gs);
-        v0 = group_sum_bfly(v0, lpr);
-        float v1 = 0.0f;
-        if (kind == 1) {
-          v1 = row_dot_f32<8, CPL, 1>(pc_codes[1] + (size_t)rr * rb, pc_s[1] + (size_t)rr * ng,
-                                      pc_b[1] + (size_t)rr * ng, X, l, lpr, m1.gs);
-          v1 = group_sum_bfly(v1, lpr);
-        }
-        if (l == 0 && r < nrows) {
-          const int row = row0 + r, tg = t0 + tt;
-          if (kind == 0) {
-            const float bias = a.rbias ? a.rbias[row] : 0.0f;
-            a.logits[(size_t)tg * a.E + row] = bf16r(__fadd_rn(v0, bias));
-          } else if (kind == 1) {
-            a.act_sh[(size_t)tg * a.Ish + row] = f32_to_bf16(swiglu_bf16(bf16r(v0), bf16r(v1)));
-          } else {
-            a.sgate[tg] = bf16r(sigmoid_f32(bf16r(v0)));
-          }
+    // router: warp w takes rows w and w + 4; shared: units w and w + 4 (gate
+    // and up rows as the pair); gate row: warp 0
+    float oa[BD_TOK], ob[BD_TOK];
+    if (kind == 0) {
+      const int rA = warp, rB = warp + 4;
+      dense_rows2<CPL>(pc_codes[0] + (size_t)rA * rb, pc_s[0] + (size_t)rA * ng, pc_b[0] + (size_t)rA * ng,
+                       pc_codes[0] + (size_t)rB * rb, pc_s[0] + (size_t)rB * ng, pc_b[0] + (size_t)rB * ng, X, XS,
+                       H, nt, m0.gs, oa, ob);
+      if ((tid & 31) == 0) {
+        const float bA = a.rbias ? a.rbias[row0 + rA] : 0.0f, bB = a.rbias ? a.rbias[row0 + rB] : 0.0f;
+        for (int tt = 0; tt < nt; ++tt) {
+          a.logits[(size_t)(t0 + tt) * a.E + row0 + rA] = bf16r(__fadd_rn(oa[tt], bA));
+          a.logits[(size_t)(t0 + tt) * a.E + row0 + rB] = bf16r(__fadd_rn(ob[tt], bB));
         }
       }
+    } else if (kind == 1) {
+      for (int pass = 0; pass < 2; ++pass) {
+        const int r = warp + 4 * pass;
+        dense_rows2<CPL>(pc_codes[0] + (size_t)r * rb, pc_s[0] + (size_t)r * ng, pc_b[0] + (size_t)r * ng,
+                         pc_codes[1] + (size_t)r * rb, pc_s[1] + (size_t)r * ng, pc_b[1] + (size_t)r * ng, X, XS, H,
+                         nt, m0.gs, oa, ob);
+        if ((tid & 31) == 0)
+          for (int tt = 0; tt < nt; ++tt)
+            a.act_sh[(size_t)(t0 + tt) * a.Ish + row0 + r] = f32_to_bf16(swiglu_bf16(bf16r(oa[tt]), bf16r(ob[tt])));
+      }
+    } else if (warp == 0) {
+      dense_rows2<CPL>(pc_codes[0], pc_s[0], pc_b[0], pc_codes[0], pc_s[0], pc_b[0], X, XS, H, nt, m0.gs, oa, ob);
+      if ((tid & 31) == 0)
+        for (int tt = 0; tt < nt; ++tt) a.sgate[t0 + tt] = bf16r(sigmoid_f32(bf16r(oa[tt])));
     }
   }
   // the last CTA of each token group routes that group's rows

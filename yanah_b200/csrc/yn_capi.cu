@@ -397,8 +397,7 @@ int ynb::host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, in
   }
   BatchDenseArgs a{};
   a.T = T; a.H = H; a.E = E; a.K = d.top_k; a.Ish = d.shared_inter; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
-  a.h = reinterpret_cast<const uint16_t*>(h);
-  a.norm = reinterpret_cast<const uint16_t*>(L.post_norm);
+  a.x = o.x;
   a.router = to_qm(L.router);
   a.rbias = L.router_bias;
   a.has_shared = sh;
@@ -410,14 +409,19 @@ int ynb::host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, in
   a.nt_router = E / BD_ROWS;
   a.nt_shared = sh ? d.shared_inter / BD_ROWS : 0;
   a.nt_sg = sh ? 1 : 0;
-  a.x = o.x; a.logits = o.logits; a.act_sh = o.act_sh; a.sgate = o.sgate; a.ids = o.ids; a.wts = o.wts;
+  a.logits = o.logits; a.act_sh = o.act_sh; a.sgate = o.sgate; a.ids = o.ids; a.wts = o.wts;
   a.counter = counter;
   a.err = o.err;
   auto part = [](size_t R, size_t rb, size_t sb) { return (R * rb + 15) / 16 * 16 + 2 * ((R * sb + 15) / 16 * 16); };
   size_t tile = part(BD_ROWS, H, (size_t)(H / L.router.group_size) * 2);
   if (sh) tile = std::max(tile, 2 * part(BD_ROWS, H, (size_t)(H / L.shared_gate.group_size) * 2));
-  const size_t smem = SMEM_HDR + (size_t)BD_TOK * H * 2 + (size_t)H * 2 + tile;
+  const size_t smem = SMEM_HDR + (size_t)BD_TOK * H * 4 + (size_t)BD_TOK * (H / 16) * 4 + tile;
   dim3 grid(a.nt_router + a.nt_shared + a.nt_sg, (T + BD_TOK - 1) / BD_TOK);
+  // RMSNorm once per row, then the dot products of every tile
+  if ((rc = set_smem(k_rmsnorm_rows, (size_t)H * 4))) return rc;
+  k_rmsnorm_rows<<<T, THREADS, (size_t)H * 4, st>>>(reinterpret_cast<const uint16_t*>(h),
+                                                   reinterpret_cast<const uint16_t*>(L.post_norm), H, d.rms_eps, o.x);
+  YN_CUDA(cudaGetLastError());
   switch (H / 512) {
 #define BDK(C)                                                                      \
   case C:                                                                           \

@@ -91,8 +91,12 @@ YN_DEV float row_dot_f32(const uint8_t* codes_row, const uint16_t* s_row, const 
 #pragma unroll
       for (int e = 0; e < SEG; ++e) {
         const int kk = s * SEG + e;
-        const uint32_t q = (wv[kk / CPW] >> (BITS * (kk % CPW))) & MASK;
-        const float qf = __fsub_rn(__uint_as_float(q | 0x4B000000u), 8388608.0f);
+        uint32_t qb;
+        if constexpr (BITS == 8)  // byte kk % 4 under the exponent of 2^23 in one PRMT
+          qb = __byte_perm(wv[kk / CPW], 0x4B000000u, 0x7540u + (unsigned)(kk % CPW));
+        else
+          qb = ((wv[kk / CPW] >> (BITS * (kk % CPW))) & MASK) | 0x4B000000u;
+        const float qf = __fsub_rn(__uint_as_float(qb), 8388608.0f);
         d = __fmaf_rn(X.v[c][kk], qf, d);
       }
       const int g = (ci * CPC + s * SEG) / gs;
