@@ -32,7 +32,7 @@ struct SymLayout {
   size_t x_all, ids_all, flags, cnt, y, total;
 };
 struct LocalLayout {
-  size_t err, counter, epoch, x_home, logits, ids, w, act_sh, sgate, plan, xf, xg, act, af, ag, sf, sg, ysh, total;
+  size_t err, counter, epoch, xf32, xsum, x_home, logits, ids, w, act_sh, sgate, plan, xf, xg, act, af, ag, sf, sg, ysh, total;
 };
 
 SymLayout sym_layout(const yn_dims& d, const yn_ep_config& c) {
@@ -59,6 +59,8 @@ LocalLayout local_layout(const yn_dims& d, const yn_ep_config& c) {
   L.err = take(4);
   L.counter = take(8 * 4);
   L.epoch = take(8);
+  L.xf32 = take(T * H * 4);
+  L.xsum = take(T * (H / 16) * 4);
   L.x_home = take(T * H * 2);
   L.logits = take(T * E * 4);
   L.ids = take(T * K * 4);
@@ -350,6 +352,8 @@ extern "C" int yn_ep_layer(const yn_dims* dims, const yn_layer* layer, int32_t l
   pa.ids = reinterpret_cast<int32_t*>(lb + L.ids);
   pa.wts = reinterpret_cast<float*>(lb + L.w);
   pa.err = err;
+  pa.xf32 = reinterpret_cast<float*>(lb + L.xf32);
+  pa.xsum = reinterpret_cast<float*>(lb + L.xsum);
   if ((rc = host_batch_dense(d, Ly, h_in, T_h, pa, reinterpret_cast<unsigned*>(lb + L.counter), st))) return rc;
 
   // 2. home rows -> every rank's gather buffer

@@ -5,20 +5,23 @@
 // (row, token) dot product is the canonical fp32 order of k_post_attention
 // (the same lane mapping and reduction tree), so logits, ids and weights are
 // bit-identical to the single-row path; only the work split differs: a CTA
-// takes 8 router rows (or 8 shared units, or the gate row) for a group of at
+// takes 16 router rows (or 8 shared units, or the gate row) for a group of at
 // most 8 tokens, so a batch spreads over hundreds of CTAs.
 #pragma once
 #include "yn_kernels.cuh"
 
 namespace ynb {
 
-constexpr int BD_ROWS = 8;   // router rows / shared units per CTA
-constexpr int BD_TOK = 8;    // tokens per CTA
+constexpr int BD_THREADS = 256;
+constexpr int BD_RROWS = 16;  // router rows per CTA (two per warp)
+constexpr int BD_SUNITS = 8;  // shared-expert units per CTA (gate and up row: one unit per warp)
+constexpr int BD_TOK = 8;     // tokens per CTA
 
 struct BatchDenseArgs {
   int T, H, E, K, Ish, norm_topk;
   float eps;
-  const uint16_t* x;        // (T, H) normalised rows (k_rmsnorm_rows)
+  const float4* xf;         // (T, H / 4) normalised rows, fp32 lane-interleaved (k_rmsnorm_rows)
+  const float* xsum;        // (T, H / 16) chunk sums
   QM router;
   const float* rbias;
   QM sh_gate, sh_up, sg;
@@ -35,8 +38,12 @@ struct BatchDenseArgs {
 
 // RMSNorm of T rows (one 128-thread CTA per row, the canonical order of
 // rmsnorm_row): x = bf16(w * bf16(h * r)).
+// The normalised row is also written in the dot kernel's fp32 layout:
+// element 16 ci + 4 v + e (ci = l + 32 c) at float4 (c * 4 + v) * 32 + l,
+// component e, plus the sum of each 16-element chunk in ascending order (the
+// order of load_x_f32).
 __global__ void __launch_bounds__(THREADS) k_rmsnorm_rows(const uint16_t* h, const uint16_t* norm, int H, float eps,
-                                                          uint16_t* x) {
+                                                          uint16_t* x, float4* xf, float* xsum) {
   extern __shared__ __align__(16) uint16_t rs[];
   __shared__ float red[32];
   uint16_t* hs = rs;
@@ -48,6 +55,23 @@ __global__ void __launch_bounds__(THREADS) k_rmsnorm_rows(const uint16_t* h, con
   }
   __syncthreads();
   rmsnorm_row(hs, ws, H, eps, hs, x + (size_t)blockIdx.x * H, red);
+  __syncthreads();
+  float4* xr = xf + (size_t)blockIdx.x * (H / 4);
+  for (int ci = threadIdx.x; ci < H / 16; ci += blockDim.x) {
+    const int c = ci >> 5, l = ci & 31;
+    float sum = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      float4 f;
+      f.x = bf16_to_f32(hs[16 * ci + 4 * v]);
+      f.y = bf16_to_f32(hs[16 * ci + 4 * v + 1]);
+      f.z = bf16_to_f32(hs[16 * ci + 4 * v + 2]);
+      f.w = bf16_to_f32(hs[16 * ci + 4 * v + 3]);
+      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, f.x), f.y), f.z), f.w);
+      xr[(c * 4 + v) * 32 + l] = f;
+    }
+    xsum[(size_t)blockIdx.x * (H / 16) + ci] = sum;
+  }
 }
 
 // Canonical 8-bit dot products of two rows (codes / scales / biases in
@@ -113,7 +137,7 @@ YN_DEV void dense_rows2(const uint8_t* ca, const uint16_t* sa, const uint16_t* b
 }
 
 template <int CPL>
-__global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a) {
+__global__ void __launch_bounds__(BD_THREADS) k_batch_dense(const BatchDenseArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   int* flag = reinterpret_cast<int*>(smem + 16);
@@ -127,9 +151,9 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
   int t = blockIdx.x, kind, row0, nrows;
   QM m0 = a.router, m1 = a.router;
   if (t < a.nt_router) {
-    kind = 0; row0 = t * BD_ROWS; nrows = BD_ROWS; m0 = a.router;
+    kind = 0; row0 = t * BD_RROWS; nrows = BD_RROWS; m0 = a.router;
   } else if ((t -= a.nt_router) < a.nt_shared) {
-    kind = 1; row0 = t * BD_ROWS; nrows = BD_ROWS; m0 = a.sh_gate; m1 = a.sh_up;
+    kind = 1; row0 = t * BD_SUNITS; nrows = BD_SUNITS; m0 = a.sh_gate; m1 = a.sh_up;
   } else {
     kind = 2; row0 = 0; nrows = 1; m0 = a.sg;
   }
@@ -152,8 +176,12 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
   }
   __syncthreads();
   {
-    Piece pc[6];
+    Piece pc[8];
     int n = 0;
+    pc[n++] = {reinterpret_cast<uint8_t*>(X), reinterpret_cast<const uint8_t*>(a.xf + (size_t)t0 * (H / 4)),
+               (uint32_t)(nt * H * 4)};
+    pc[n++] = {reinterpret_cast<uint8_t*>(XS), reinterpret_cast<const uint8_t*>(a.xsum + (size_t)t0 * (H / 16)),
+               (uint32_t)(nt * (H / 16) * 4)};
     for (int p = 0; p < nparts; ++p) {
       const QM& m = (p == 0) ? m0 : m1;
       pc[n++] = {pc_codes[p], m.w + (size_t)row0 * rb, (uint32_t)(nrows * rb)};
@@ -164,43 +192,14 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
     }
     stage_pieces(pc, n, bar);
   }
-  // normalised rows -> fp32, lane-interleaved: element 16 ci + 4 v + e of a
-  // token (ci = l + 32 c) at float4 (c * 4 + v) * 32 + l, component e
-  for (int i = tid; i < nt * (H / 8); i += THREADS) {
-    const int tt = i / (H / 8), q = i % (H / 8);       // q: 8 elements 8q..8q+7
-    const uint4 w = reinterpret_cast<const uint4*>(a.x + (size_t)(t0 + tt) * H)[q];
-    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int hlf = 0; hlf < 2; ++hlf) {
-      const int k = 8 * q + 4 * hlf, ci = k >> 4, v = (k >> 2) & 3, c = ci >> 5, l = ci & 31;
-      float4 f;
-      f.x = bf16_to_f32((uint16_t)(wv[2 * hlf] & 0xFFFFu));
-      f.y = bf16_to_f32((uint16_t)(wv[2 * hlf] >> 16));
-      f.z = bf16_to_f32((uint16_t)(wv[2 * hlf + 1] & 0xFFFFu));
-      f.w = bf16_to_f32((uint16_t)(wv[2 * hlf + 1] >> 16));
-      X[(size_t)tt * (H / 4) + (c * 4 + v) * 32 + l] = f;
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < nt * (H / 16); i += THREADS) {  // chunk sums, ascending k (as load_x_f32)
-    const int tt = i / (H / 16), ci = i % (H / 16), c = ci >> 5, l = ci & 31;
-    const float4* xt = X + (size_t)tt * (H / 4);
-    float sum = 0.0f;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const float4 f = xt[(c * 4 + v) * 32 + l];
-      sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, f.x), f.y), f.z), f.w);
-    }
-    XS[(size_t)tt * (H / 16) + ci] = sum;
-  }
   __syncthreads();
   const bool ok = mbar_wait_block(bar, 0, a.err);
   if (ok) {
-    // router: warp w takes rows w and w + 4; shared: units w and w + 4 (gate
-    // and up rows as the pair); gate row: warp 0
+    // router: warp w takes rows w and w + 8; shared: unit w (gate and up rows
+    // as the pair); gate row: warp 0
     float oa[BD_TOK], ob[BD_TOK];
     if (kind == 0) {
-      const int rA = warp, rB = warp + 4;
+      const int rA = warp, rB = warp + 8;
       dense_rows2<CPL>(pc_codes[0] + (size_t)rA * rb, pc_s[0] + (size_t)rA * ng, pc_b[0] + (size_t)rA * ng,
                        pc_codes[0] + (size_t)rB * rb, pc_s[0] + (size_t)rB * ng, pc_b[0] + (size_t)rB * ng, X, XS,
                        H, nt, m0.gs, oa, ob);
@@ -212,15 +211,13 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
         }
       }
     } else if (kind == 1) {
-      for (int pass = 0; pass < 2; ++pass) {
-        const int r = warp + 4 * pass;
-        dense_rows2<CPL>(pc_codes[0] + (size_t)r * rb, pc_s[0] + (size_t)r * ng, pc_b[0] + (size_t)r * ng,
-                         pc_codes[1] + (size_t)r * rb, pc_s[1] + (size_t)r * ng, pc_b[1] + (size_t)r * ng, X, XS, H,
-                         nt, m0.gs, oa, ob);
-        if ((tid & 31) == 0)
-          for (int tt = 0; tt < nt; ++tt)
-            a.act_sh[(size_t)(t0 + tt) * a.Ish + row0 + r] = f32_to_bf16(swiglu_bf16(bf16r(oa[tt]), bf16r(ob[tt])));
-      }
+      const int r = warp;
+      dense_rows2<CPL>(pc_codes[0] + (size_t)r * rb, pc_s[0] + (size_t)r * ng, pc_b[0] + (size_t)r * ng,
+                       pc_codes[1] + (size_t)r * rb, pc_s[1] + (size_t)r * ng, pc_b[1] + (size_t)r * ng, X, XS, H,
+                       nt, m0.gs, oa, ob);
+      if ((tid & 31) == 0)
+        for (int tt = 0; tt < nt; ++tt)
+          a.act_sh[(size_t)(t0 + tt) * a.Ish + row0 + r] = f32_to_bf16(swiglu_bf16(bf16r(oa[tt]), bf16r(ob[tt])));
     } else if (warp == 0) {
       dense_rows2<CPL>(pc_codes[0], pc_s[0], pc_b[0], pc_codes[0], pc_s[0], pc_b[0], X, XS, H, nt, m0.gs, oa, ob);
       if ((tid & 31) == 0)
@@ -238,7 +235,7 @@ __global__ void __launch_bounds__(THREADS) k_batch_dense(const BatchDenseArgs a)
   __syncthreads();
   if (*flag) {
     __threadfence();
-    for (int tt = t0 + warp; tt < t0 + nt; tt += 4)
+    for (int tt = t0 + warp; tt < t0 + nt; tt += BD_THREADS / 32)
       route_row(a.logits + (size_t)tt * a.E, a.E, a.K, a.norm_topk, a.ids + (size_t)tt * a.K,
                 a.wts + (size_t)tt * a.K);
   }

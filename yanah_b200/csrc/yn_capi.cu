@@ -348,7 +348,7 @@ static int launch_post_attention_out(const yn_dims& d, const yn_layer& L, const 
 
 static int launch_post_attention(const yn_dims& d, const yn_layer& L, const void* h1, int T, const yn_layer* tg,
                                  int NT, uint8_t* ws, const WsLayout& W, cudaStream_t st) {
-  PostAttnOut o;
+  PostAttnOut o{};
   o.x = reinterpret_cast<uint16_t*>(ws + W.x);
   o.logits = reinterpret_cast<float*>(ws + W.logits);
   o.act_sh = reinterpret_cast<uint16_t*>(ws + W.act_sh);
@@ -387,17 +387,19 @@ int ynb::host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, in
   if (!h || !L.post_norm || !counter) return fail(YN_E_INVALID, "batch post-attention: null argument");
   if (T < 1 || T > 64) return fail(YN_E_UNSUPPORTED, "batch post-attention: rows must be in [1, 64]");
   if ((rc = check_qmat(L.router, E, H, 8, "router"))) return rc;
-  if (E % BD_ROWS) return fail(YN_E_UNSUPPORTED, "batch post-attention: n_experts must be a multiple of 8");
+  if (E % BD_RROWS) return fail(YN_E_UNSUPPORTED, "batch post-attention: n_experts must be a multiple of 16");
+  if (!o.xf32 || !o.xsum) return fail(YN_E_INVALID, "batch post-attention: null fp32 row buffers");
   const bool sh = d.shared_inter > 0;
   if (sh) {
     if ((rc = check_qmat(L.shared_gate, d.shared_inter, H, 8, "shared_gate"))) return rc;
     if ((rc = check_qmat(L.shared_up, d.shared_inter, H, 8, "shared_up"))) return rc;
     if ((rc = check_qmat(L.shared_expert_gate, 1, H, 8, "shared_expert_gate"))) return rc;
-    if (d.shared_inter % BD_ROWS) return fail(YN_E_UNSUPPORTED, "batch post-attention: shared_inter % 8");
+    if (d.shared_inter % BD_SUNITS) return fail(YN_E_UNSUPPORTED, "batch post-attention: shared_inter % 8");
   }
   BatchDenseArgs a{};
   a.T = T; a.H = H; a.E = E; a.K = d.top_k; a.Ish = d.shared_inter; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
-  a.x = o.x;
+  a.xf = reinterpret_cast<const float4*>(o.xf32);
+  a.xsum = o.xsum;
   a.router = to_qm(L.router);
   a.rbias = L.router_bias;
   a.has_shared = sh;
@@ -406,27 +408,28 @@ int ynb::host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, in
     a.sh_up = to_qm(L.shared_up);
     a.sg = to_qm(L.shared_expert_gate);
   }
-  a.nt_router = E / BD_ROWS;
-  a.nt_shared = sh ? d.shared_inter / BD_ROWS : 0;
+  a.nt_router = E / BD_RROWS;
+  a.nt_shared = sh ? d.shared_inter / BD_SUNITS : 0;
   a.nt_sg = sh ? 1 : 0;
   a.logits = o.logits; a.act_sh = o.act_sh; a.sgate = o.sgate; a.ids = o.ids; a.wts = o.wts;
   a.counter = counter;
   a.err = o.err;
   auto part = [](size_t R, size_t rb, size_t sb) { return (R * rb + 15) / 16 * 16 + 2 * ((R * sb + 15) / 16 * 16); };
-  size_t tile = part(BD_ROWS, H, (size_t)(H / L.router.group_size) * 2);
-  if (sh) tile = std::max(tile, 2 * part(BD_ROWS, H, (size_t)(H / L.shared_gate.group_size) * 2));
+  size_t tile = part(BD_RROWS, H, (size_t)(H / L.router.group_size) * 2);
+  if (sh) tile = std::max(tile, 2 * part(BD_SUNITS, H, (size_t)(H / L.shared_gate.group_size) * 2));
   const size_t smem = SMEM_HDR + (size_t)BD_TOK * H * 4 + (size_t)BD_TOK * (H / 16) * 4 + tile;
   dim3 grid(a.nt_router + a.nt_shared + a.nt_sg, (T + BD_TOK - 1) / BD_TOK);
   // RMSNorm once per row, then the dot products of every tile
   if ((rc = set_smem(k_rmsnorm_rows, (size_t)H * 4))) return rc;
   k_rmsnorm_rows<<<T, THREADS, (size_t)H * 4, st>>>(reinterpret_cast<const uint16_t*>(h),
-                                                   reinterpret_cast<const uint16_t*>(L.post_norm), H, d.rms_eps, o.x);
+                                                   reinterpret_cast<const uint16_t*>(L.post_norm), H, d.rms_eps, o.x,
+                                                   reinterpret_cast<float4*>(o.xf32), o.xsum);
   YN_CUDA(cudaGetLastError());
   switch (H / 512) {
 #define BDK(C)                                                                      \
   case C:                                                                           \
     if ((rc = set_smem(k_batch_dense<C>, smem))) return rc;                         \
-    k_batch_dense<C><<<grid, THREADS, smem, st>>>(a);                               \
+    k_batch_dense<C><<<grid, BD_THREADS, smem, st>>>(a);                            \
     break;
     BDK(1) BDK(2) BDK(4) BDK(8)
 #undef BDK

@@ -30,6 +30,8 @@ struct PostAttnOut {
   float* fprobs;
   int* counter;
   int* err;
+  float* xf32;   // batch path only: (T, H) normalised rows in fp32 (dot-kernel layout)
+  float* xsum;   // batch path only: (T, H / 16) chunk sums
 };
 
 // Post-attention + routing for any number of rows, in launches of at most
