@@ -286,6 +286,51 @@ int yn_ipc_close(void* dev_ptr);
  * `stream`: readback for callers that hold raw device pointers. */
 int yn_memcpy(void* dst, const void* src, size_t bytes, void* stream);
 
+/* -------------------------------------------- prefill: tensor-core GEMM */
+
+/* Prompt prefill moves hundreds of rows through each expert (sweep.py:80-138
+ * and the prompt pass of mlx_backend.py:421-433 `moe`), so the routed
+ * experts run as a grouped GEMM on the tcgen05 tensor cores. The grouping
+ * (which rows go to which expert) is planned on the host, as the reference's
+ * prefill sweep plans its staging groups.
+ *
+ * yn_rows_route: post-attention RMSNorm, router logits, top-k ids and
+ * weights of T rows (any T), bit-identical to yn_post_attention row by row;
+ * x_out (T, H) bf16 normalised rows. ws: yn_rows_route_bytes(dims) bytes,
+ * zeroed once before first use; yn_route_error reads and clears its error
+ * word. */
+size_t yn_rows_route_bytes(const yn_dims* dims);
+int yn_rows_route(const yn_dims* dims, const yn_layer* layer, const void* h, int32_t T, void* x_out,
+                  int32_t* ids_out, float* w_out, void* ws, size_t ws_bytes, void* stream);
+int yn_route_error(void* ws, const yn_dims* dims, void* stream, int32_t* code_out);
+
+/* bf16 rows -> fp16 rows in the K-permuted order the tensor-core GEMM reads
+ * (within each block of 8, element p at 2p for p < 4, at 2(p - 4) + 1 else). */
+int yn_to_f16_kperm(const void* x, int64_t rows, int32_t cols, void* out, void* stream);
+
+/* One tile of the grouped GEMM: expert e, pairs [p0, p0 + n) (n <= 256, the
+ * pairs of one expert), first gate/up unit (mode 0, 64 units per tile) or
+ * first output row (mode 1, 128 rows per tile). */
+typedef struct yn_tc_tile {
+  int32_t e, p0, n, u0;
+} yn_tc_tile;
+
+/* mode 0 (mlx_backend.py:447-456 `_switch_glu` up to SwiGLU): for every tile,
+ * act_out[p][kperm(u)] = fp16(swiglu(gate_u . x, up_u . x)) with x =
+ * b_rows[pair_row[p]] (fp16 K-permuted rows of H). mode 1 (the down
+ * projection): y_out[p][h] = bf16(down_h . act_p) with act_p = b_rows[p]
+ * (fp16 K-permuted rows of I). Routed experts 4-bit g64 only. tiles: device
+ * array. err: device error word (bounded waits, bad slots). */
+int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
+                  int32_t n_tiles, const void* b_rows, const int32_t* pair_row, void* act_out, void* y_out,
+                  int32_t* err, void* stream);
+
+/* Combine of T rows (mlx_backend.py:409/:420, :438-440; orchestrator.py:287):
+ * out[t] = h_res[t] + (sum_j bf16(y[pair_of[t][j]] * w[t][j]) in column order
+ * + y_shared[t]); y_shared and h_res may be NULL. */
+int yn_pairs_combine(const yn_dims* dims, const void* y, const int32_t* pair_of, const float* weights,
+                     const void* y_shared, const void* h_res, int32_t T, void* out, void* stream);
+
 /* ---------------------------------------------------------- slot copies */
 
 /* Copy `n` expert records host -> slot arena (io_lanes.py:121-126

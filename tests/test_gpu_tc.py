@@ -1,0 +1,63 @@
+"""GPU parity of the tensor-core (tcgen05) grouped expert GEMM used for
+prompt prefill, against the CPU oracle.
+
+Bit-exact: normalised rows, routed ids and weights (the batch routing path).
+Within REL_L2_TOL (1e-2 relative L2): every sampled pair's SwiGLU activations
+and expert output, and the layer output.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import cpu
+from tests.gpu_helpers import REL_L2_TOL, bf16_dev, bf16_np, hidden_rows, rel_l2, small_config
+from yanah_b200.prefill import PrefillStack, kperm_inverse
+from yanah_b200.synthetic import lfm2_stack
+
+pytestmark = pytest.mark.gpu
+
+
+def _f16_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    return cpu.f32_to_bf16(a.astype(np.float32))
+
+
+def _check(cfg, T, sample_pairs):
+    st = PrefillStack(cfg, max_rows=T, layers=[0])
+    h = hidden_rows(cfg, T, stream=31)
+    hd = bf16_dev(h)
+    out = torch.empty_like(hd)
+    st.layer(0, hd, out)
+    torch.cuda.synchronize()
+    assert st.check_error() == 0
+    orc = cpu.OracleStack(cfg, threads=8)
+    pa = orc.post_attention(0, h)
+    assert np.array_equal(bf16_np(st.x[:T]), pa["x"])
+    assert np.array_equal(st.ids[:T].cpu().numpy(), pa["ids"])
+    assert np.array_equal(st.w[:T].cpu().numpy().view(np.uint32), pa["w"].view(np.uint32))
+    ids, pair_row, pair_of = st.last_plan
+    P = T * cfg.top_k
+    act = kperm_inverse(st.act16[:P].cpu().numpy())
+    y = bf16_np(st.y[:P])
+    rng = np.random.default_rng(0)
+    for p in sorted(set(rng.choice(P, size=min(sample_pairs, P), replace=False).tolist()) | {0, P - 1}):
+        t = int(pair_row[p])
+        j = int(np.nonzero(pair_of[t] == p)[0][0])
+        a_ref, y_ref = orc.expert(0, int(ids[t, j]), pa["x"][t])
+        assert rel_l2(_f16_to_bf16_bits(act[p]), a_ref) < REL_L2_TOL, (p, rel_l2(_f16_to_bf16_bits(act[p]), a_ref))
+        assert rel_l2(y[p], y_ref) < REL_L2_TOL, (p, rel_l2(y[p], y_ref))
+    rows = sorted(set(rng.choice(T, size=min(8, T), replace=False).tolist()))
+    ref = orc.layer(0, h[rows])["out"]
+    assert rel_l2(bf16_np(out)[rows], ref) < REL_L2_TOL
+
+
+def test_tc_small_config():
+    cfg = small_config(bits=(4,), gs=64, hidden=512, n_experts=16, top_k=2, inter=512, shared=0, seed=7)
+    _check(cfg, T=40, sample_pairs=80)
+
+
+def test_tc_lfm2_layer():
+    # a ragged prefill batch: 3 prompts of 37, 300 and 5 rows (342 rows, 1368 pairs)
+    _check(lfm2_stack(n_layers=40), T=342, sample_pairs=48)

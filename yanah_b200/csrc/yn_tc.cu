@@ -1,0 +1,155 @@
+// C ABI of the tensor-core grouped expert GEMM (prefill) and its helpers:
+// routing of many rows, fp16 K-permuted activations, the pair combine.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "yanah_b200.h"
+#include "yn_internal.h"
+#include "yn_tc.cuh"
+
+using namespace ynb;
+
+#define YN_CUDA_T(call)                                                                              \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess) return host_fail(YN_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+namespace {
+cudaStream_t as_st(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+size_t a256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct RouteWs {
+  size_t err, counter, logits, xf32, xsum, act_sh, sgate, total;
+};
+RouteWs route_ws(const yn_dims& d) {
+  RouteWs L{};
+  size_t o = 0;
+  auto take = [&](size_t b) { size_t at = o; o = a256(o + b); return at; };
+  const size_t C = 64;
+  L.err = take(4);
+  L.counter = take(8 * 4);
+  L.logits = take(C * d.n_experts * 4);
+  L.xf32 = take(C * d.hidden * 4);
+  L.xsum = take(C * (d.hidden / 16) * 4);
+  L.act_sh = take(C * (d.shared_inter ? d.shared_inter : 1) * 2);
+  L.sgate = take(C * 4);
+  L.total = o;
+  return L;
+}
+
+size_t tc_smem(int Kd) {
+  return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES + TC_C_BYTES) + 2 * (size_t)TC_M * (Kd / 64) * 2 +
+         TC_S * 8 + 16;
+}
+}  // namespace
+
+extern "C" size_t yn_rows_route_bytes(const yn_dims* dims) {
+  if (!dims) return 0;
+  return route_ws(*dims).total;
+}
+
+extern "C" int yn_rows_route(const yn_dims* dims, const yn_layer* layer, const void* h, int32_t T, void* x_out,
+                             int32_t* ids_out, float* w_out, void* ws, size_t ws_bytes, void* stream) {
+  if (!dims || !layer || !h || !x_out || !ids_out || !w_out || !ws) return host_fail(YN_E_INVALID, "null argument");
+  if (T < 1) return host_fail(YN_E_INVALID, "rows must be positive");
+  const RouteWs L = route_ws(*dims);
+  if (ws_bytes < L.total) return host_fail(YN_E_INVALID, "route workspace too small");
+  uint8_t* b = reinterpret_cast<uint8_t*>(ws);
+  const int H = dims->hidden, K = dims->top_k;
+  for (int t0 = 0; t0 < T; t0 += 64) {
+    const int n = std::min(64, T - t0);
+    PostAttnOut o{};
+    o.x = reinterpret_cast<uint16_t*>(x_out) + (size_t)t0 * H;
+    o.logits = reinterpret_cast<float*>(b + L.logits);
+    o.act_sh = reinterpret_cast<uint16_t*>(b + L.act_sh);
+    o.sgate = reinterpret_cast<float*>(b + L.sgate);
+    o.ids = ids_out + (size_t)t0 * K;
+    o.wts = w_out + (size_t)t0 * K;
+    o.err = reinterpret_cast<int*>(b + L.err);
+    o.xf32 = reinterpret_cast<float*>(b + L.xf32);
+    o.xsum = reinterpret_cast<float*>(b + L.xsum);
+    const int rc = host_batch_dense(*dims, *layer, reinterpret_cast<const uint16_t*>(h) + (size_t)t0 * H, n, o,
+                                    reinterpret_cast<unsigned*>(b + L.counter), as_st(stream));
+    if (rc) return rc;
+  }
+  return YN_OK;
+}
+
+extern "C" int yn_route_error(void* ws, const yn_dims* dims, void* stream, int32_t* code_out) {
+  if (!ws || !dims || !code_out) return host_fail(YN_E_INVALID, "null argument");
+  int32_t* e = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws) + route_ws(*dims).err);
+  YN_CUDA_T(cudaMemcpyAsync(code_out, e, 4, cudaMemcpyDeviceToHost, as_st(stream)));
+  YN_CUDA_T(cudaStreamSynchronize(as_st(stream)));
+  YN_CUDA_T(cudaMemsetAsync(e, 0, 4, as_st(stream)));
+  return YN_OK;
+}
+
+extern "C" int yn_to_f16_kperm(const void* x, int64_t rows, int32_t cols, void* out, void* stream) {
+  if (!x || !out || rows < 1 || cols < 8 || cols % 8) return host_fail(YN_E_INVALID, "bad rows/cols or null");
+  const long long n = rows * (long long)cols;
+  const int grid = (int)std::min<long long>((n + 255) / 256, 4096);
+  k_to_f16_kperm<<<grid, 256, 0, as_st(stream)>>>(reinterpret_cast<const uint16_t*>(x), n, cols,
+                                                  reinterpret_cast<uint16_t*>(out));
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
+                             int32_t n_tiles, const void* b_rows, const int32_t* pair_row, void* act_out, void* y_out,
+                             int32_t* err, void* stream) {
+  if (!dims || !layer || !tiles || !b_rows || !err) return host_fail(YN_E_INVALID, "null argument");
+  if (mode != 0 && mode != 1) return host_fail(YN_E_INVALID, "mode must be 0 (gate/up) or 1 (down)");
+  if (mode == 0 && (!act_out || !pair_row)) return host_fail(YN_E_INVALID, "gate/up needs act_out and pair_row");
+  if (mode == 1 && !y_out) return host_fail(YN_E_INVALID, "down needs y_out");
+  const yn_record& r = layer->record;
+  if (r.bits != 4 || r.group_size != 64)
+    return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: routed experts must be 4-bit g64");
+  const int H = dims->hidden, I = dims->moe_inter;
+  if (H % 512 || I % 512)  // whole 128-row down tiles, 64-unit gate/up tiles, 16-byte scale rows
+    return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: hidden and moe_inter must be multiples of 512");
+  if (!layer->expert_base || reinterpret_cast<uintptr_t>(layer->expert_base) % 16 || layer->slot_stride % 16)
+    return host_fail(YN_E_INVALID, "expert arena and slot stride must be 16-byte aligned");
+  for (int i = 0; i < 9; ++i)
+    if (r.piece_offset[i] % 16) return host_fail(YN_E_INVALID, "record pieces must be 16-byte aligned");
+  if (n_tiles < 1) return YN_OK;
+  TcArgs a{};
+  a.mode = mode;
+  a.tiles = reinterpret_cast<const TcTile*>(tiles);
+  a.n_tiles = n_tiles;
+  a.b_rows = reinterpret_cast<const uint16_t*>(b_rows);
+  a.pair_row = pair_row;
+  a.base = reinterpret_cast<const uint8_t*>(layer->expert_base);
+  a.stride = layer->slot_stride;
+  a.slot_of = layer->expert_slot;
+  a.n_slots = layer->n_slots;
+  for (int i = 0; i < 9; ++i) a.rg.off[i] = r.piece_offset[i];
+  a.rg.bytes = r.record_bytes;
+  a.rg.bits = r.bits;
+  a.rg.gs = r.group_size;
+  a.H = H;
+  a.I = I;
+  a.act_out = reinterpret_cast<uint16_t*>(act_out);
+  a.y_out = reinterpret_cast<uint16_t*>(y_out);
+  a.err = err;
+  const size_t smem = tc_smem(mode == 0 ? H : I);
+  int rc = host_set_smem(reinterpret_cast<const void*>(k_tc_experts), smem);
+  if (rc) return rc;
+  k_tc_experts<<<n_tiles, TC_THREADS, smem, as_st(stream)>>>(a);
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_pairs_combine(const yn_dims* dims, const void* y, const int32_t* pair_of, const float* weights,
+                                const void* y_shared, const void* h_res, int32_t T, void* out, void* stream) {
+  if (!dims || !y || !pair_of || !weights || !out || T < 1) return host_fail(YN_E_INVALID, "null argument or T < 1");
+  const int H = dims->hidden;
+  dim3 grid((H + 255) / 256, T);
+  k_pairs_combine<<<grid, 256, 0, as_st(stream)>>>(
+      reinterpret_cast<const uint16_t*>(y), pair_of, weights, reinterpret_cast<const uint16_t*>(y_shared),
+      reinterpret_cast<const uint16_t*>(h_res), H, dims->top_k, reinterpret_cast<uint16_t*>(out));
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}

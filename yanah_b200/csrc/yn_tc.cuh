@@ -1,0 +1,348 @@
+// Grouped expert GEMM on the 5th-generation tensor cores (tcgen05) for
+// many rows per expert: prompt prefill (sweep.py:80-138, the prompt pass of
+// mlx_backend.py:421-433 `moe` with `_gather_sort`).
+//
+// One CTA computes one tile D[m][n] = sum_k W[m][k] * X[n][k]:
+//  * A = 128 weight rows of one expert, dequantised from MLX 4-bit g64 codes
+//    to fp16 by the CTA's four warps (thread t owns tile row t): for gate/up
+//    the rows interleave gate unit u (row 2i) and up unit u (row 2i + 1) for
+//    64 units, so SwiGLU fuses into the epilogue; for down they are 128
+//    output rows;
+//  * B = up to 256 rows of this expert's tokens (prefill x, or SwiGLU
+//    activations for the down projection), fp16, copied with cp.async;
+//  * both operands are K-major in the 128-byte swizzled layout (row r of an
+//    8-row atom at r * 128 bytes, 16-byte chunk c at (c ^ r) * 16); K moves
+//    in stages of 64 codes = one quantisation group, 4 stages in flight;
+//  * one thread issues tcgen05.mma (M 128, N = tokens rounded up to 16,
+//    K 16 x 4 per stage) into a TMEM accumulator and commits each stage to
+//    its mbarrier, which frees the stage's buffers for the producers;
+//  * the epilogue reads TMEM with tcgen05.ld (warp w: lanes 32w..32w+31).
+//
+// The codes of a word unpack into fp16 pairs (q0,q4), (q1,q5), (q2,q6),
+// (q3,q7) (one LOP3 per pair, yn_mma.cuh), so the K order inside each block of
+// 8 is permuted; the activations are stored in the same permuted order
+// ("K-permuted": element 8j + p at 8j + 2p for p < 4, at 8j + 2(p-4) + 1 for
+// p >= 4), which leaves every dot product unchanged.
+//
+// Every wait is bounded; on timeout the error word is set, the CTA drains
+// its committed MMAs (bounded again), frees its TMEM and returns.
+#pragma once
+#include "yn_common.cuh"
+#include "yn_moe.cuh"
+#include "yn_mma.cuh"
+
+namespace ynb {
+
+constexpr int TC_THREADS = 128;
+constexpr int TC_S = 4;          // pipeline stages
+constexpr int TC_M = 128;        // weight rows per tile
+constexpr int TC_NMAX = 256;     // token rows per tile
+constexpr int TC_A_BYTES = TC_M * 128;       // one stage of A: 128 rows x 64 fp16
+constexpr int TC_B_BYTES = TC_NMAX * 128;    // one stage of B: 256 rows x 64 fp16
+constexpr int TC_C_BYTES = TC_M * 32;        // one stage of staged codes: 128 rows x 32 bytes
+
+struct TcTile {
+  int e;       // expert
+  int p0;      // first pair of the tile (pairs of one expert are contiguous)
+  int n;       // pairs in the tile (1..256)
+  int u0;      // gate/up: first unit (64 per tile); down: first output row (128 per tile)
+};
+
+struct TcArgs {
+  int mode;                    // 0: gate/up + SwiGLU, 1: down
+  const TcTile* tiles;
+  int n_tiles;
+  const uint16_t* b_rows;      // fp16 K-permuted rows: mode 0 x' (rows by token), mode 1 act' (rows by pair)
+  const int32_t* pair_row;     // mode 0: pair -> row of b_rows; mode 1: null (row = pair)
+  const uint8_t* base;         // expert arena
+  long long stride;
+  const int32_t* slot_of;      // expert -> slot or null (slot = expert)
+  int n_slots;
+  RecGeom rg;
+  int H, I;
+  uint16_t* act_out;           // mode 0: (P, I) fp16 K-permuted SwiGLU activations
+  uint16_t* y_out;             // mode 1: (P, H) bf16 expert outputs
+  int* err;
+};
+
+// One 4-bit code word -> fp16 pairs (q0,q4) x1, (q1,q5) x16, (q2,q6) x1,
+// (q3,q7) x16, each value 1024 + mult * q exactly.
+YN_DEV void tc_unpack4(uint32_t w, uint32_t (&pr)[4]) {
+  const uint32_t M = 0x64006400u, a8 = w >> 8;
+  pr[0] = (w & 0x000F000Fu) | M;
+  pr[1] = (w & 0x00F000F0u) | M;
+  pr[2] = (a8 & 0x000F000Fu) | M;
+  pr[3] = (a8 & 0x00F000F0u) | M;
+}
+
+YN_DEV int kperm(int k) { const int p = k & 7; return (k & ~7) | (p < 4 ? 2 * p : 2 * (p - 4) + 1); }
+
+YN_DEV uint64_t tc_desc(uint32_t smem_addr) {
+  // K-major, 128-byte swizzle: start address (>>4), leading offset 1 (unused
+  // for swizzled K-major), stride offset 1024 bytes between 8-row atoms,
+  // version 1, layout type 2 (SWIZZLE_128B)
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+YN_DEV uint32_t tc_idesc(int n) {
+  // f32 accumulate (bits 4-5 = 1), A and B fp16 (formats 0), both K-major,
+  // N >> 3 at bits 17-22, M >> 4 at bits 24-28
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+}
+
+YN_DEV void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+YN_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+YN_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+YN_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+YN_DEV void tc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+YN_DEV void tc_cpa16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+YN_DEV void tc_cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+YN_DEV void tc_cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Bounded wait on an mbarrier phase by every thread; block-uniform result.
+YN_DEV bool tc_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_block(bar, parity, err);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // layout (from a 1024-byte aligned base): [A x S][B x S][codes x S][scales][biases][mbarriers, tmem address]
+  uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
+  uint8_t* Abuf = smem;
+  uint8_t* Bbuf = Abuf + TC_S * TC_A_BYTES;
+  uint8_t* Cbuf = Bbuf + TC_S * TC_B_BYTES;
+  const int Kd = a.mode == 0 ? a.H : a.I;
+  const int NG = Kd / 64, NK = Kd / 64;
+  uint16_t* Ssc = reinterpret_cast<uint16_t*>(Cbuf + TC_S * TC_C_BYTES);  // (128, NG) fp16 scales
+  uint16_t* Sbi = Ssc + TC_M * NG;                                         // (128, NG) fp16 biases
+  uint64_t* bars = reinterpret_cast<uint64_t*>(Sbi + TC_M * NG);           // TC_S mma-done barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TC_S);
+  __shared__ int rows_s[TC_NMAX];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (blockIdx.x >= a.n_tiles) return;
+  const TcTile tl = a.tiles[blockIdx.x];
+  const int n = tl.n, nmma = (n + 15) & ~15;
+  const int slot = a.slot_of ? a.slot_of[tl.e] : tl.e;
+  if (n < 1 || n > TC_NMAX || slot < 0 || slot >= a.n_slots) {
+    if (tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
+    return;
+  }
+  const uint8_t* rec = a.base + (size_t)slot * (size_t)a.stride;
+  const int RB = Kd / 2;  // 4-bit code bytes per row
+
+  // weight row of tile row t in the record, and its piece (weight/scales/biases offsets)
+  const int t = tid;  // this thread's tile row
+  int wrow;
+  long long off_w, off_s, off_b;
+  if (a.mode == 0) {
+    const bool up = t & 1;
+    wrow = tl.u0 + (t >> 1);
+    off_w = a.rg.off[up ? 3 : 0];
+    off_s = a.rg.off[up ? 4 : 1];
+    off_b = a.rg.off[up ? 5 : 2];
+  } else {
+    wrow = tl.u0 + t;
+    off_w = a.rg.off[6];
+    off_s = a.rg.off[7];
+    off_b = a.rg.off[8];
+  }
+  const uint8_t* wsrc = rec + off_w + (size_t)wrow * RB;
+
+  for (int i = tid; i < n; i += TC_THREADS) rows_s[i] = a.pair_row ? a.pair_row[tl.p0 + i] : tl.p0 + i;
+  if (tid == 0) {
+    for (int s = 0; s < TC_S; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  // scales and biases of this thread's row, all groups (NG * 2 bytes each, 16-byte pieces)
+  for (int q = 0; q < NG * 2 / 16; ++q) {
+    tc_cpa16(reinterpret_cast<uint8_t*>(Ssc) + (size_t)t * NG * 2 + 16 * q, rec + off_s + (size_t)wrow * NG * 2 + 16 * q);
+    tc_cpa16(reinterpret_cast<uint8_t*>(Sbi) + (size_t)t * NG * 2 + 16 * q, rec + off_b + (size_t)wrow * NG * 2 + 16 * q);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();  // rows_s, barriers, TMEM address
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // producer: stage kc's codes (this thread's row) and B rows
+  auto issue = [&](int kc) {
+    const int s = kc % TC_S;
+    uint8_t* cd = Cbuf + s * TC_C_BYTES + t * 32;
+    tc_cpa16(cd, wsrc + 32 * kc);
+    tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
+    uint8_t* B = Bbuf + s * TC_B_BYTES;
+    for (int i = tid; i < n * 8; i += TC_THREADS) {
+      const int r = i >> 3, c = i & 7;
+      const uint16_t* src = a.b_rows + (size_t)rows_s[r] * Kd + 64 * kc + 8 * c;
+      tc_cpa16(B + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4), src);
+    }
+  };
+
+  bool ok = true;
+  constexpr int P = 2;  // stages issued ahead
+  for (int kc = 0; kc < P && kc < NK; ++kc) {
+    issue(kc);
+    tc_cpa_commit();
+  }
+  for (int kc = 0; kc < NK && ok; ++kc) {
+    const int s = kc % TC_S;
+    // stage kc + P reuses the buffers of stage kc + P - TC_S: its MMAs must be done
+    const int kn = kc + P;
+    if (kn < NK) {
+      if (kn >= TC_S) ok = tc_wait(&bars[kn % TC_S], ((kn - TC_S) / TC_S) & 1, a.err);
+      if (ok) issue(kn);
+    }
+    tc_cpa_commit();
+    tc_cpa_wait<P>();  // stage kc's copies (this thread's) have landed
+    __syncthreads();   // ... and every thread's
+    if (!ok) break;
+    // dequantise this thread's row of stage kc into A (fp16, K-permuted, swizzled)
+    {
+      const uint4* cw = reinterpret_cast<const uint4*>(Cbuf + s * TC_C_BYTES + t * 32);
+      const uint4 c0 = cw[0], c1 = cw[1];
+      const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const __half sc = __ushort_as_half(Ssc[t * NG + kc]), bi = __ushort_as_half(Sbi[t * NG + kc]);
+      const __half2 s1 = __halves2half2(sc, sc);
+      const __half sc16 = __float2half_rn(__fmul_rn(__half2float(sc), 0.0625f));
+      const __half2 s16 = __halves2half2(sc16, sc16);
+      const __half2 b2 = __halves2half2(bi, bi);
+      const __half2 k1024 = __float2half2_rn(1024.0f);
+      uint8_t* Arow = Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t pr[4];
+        tc_unpack4(words[i], pr);
+        uint32_t o[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
+          h = __hsub2(h, k1024);
+          h = __hfma2(h, (p & 1) ? s16 : s1, b2);
+          o[p] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t abase = smem_u32(Abuf + s * TC_A_BYTES), bbase = smem_u32(Bbuf + s * TC_B_BYTES);
+      const uint32_t idesc = tc_idesc(nmma);
+#pragma unroll
+      for (int k16 = 0; k16 < 4; ++k16)
+        tc_mma(tmem, tc_desc(abase + 32 * k16), tc_desc(bbase + 32 * k16), idesc, (kc > 0 || k16 > 0) ? 1u : 0u);
+      tc_commit(&bars[s]);
+    }
+  }
+  tc_cpa_wait<0>();
+  // the accumulator is complete when the last stage's commit has arrived
+  if (ok) ok = tc_wait(&bars[(NK - 1) % TC_S], ((NK - 1) / TC_S) & 1, a.err);
+  tc_fence_after();
+  if (ok) {
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const int m = 32 * warp + lane;  // tile row of this thread
+    for (int c0 = 0; c0 < nmma; c0 += 32) {
+      float v[32];
+      tc_ld32(lane_base + (uint32_t)c0, v);
+      if (a.mode == 0) {
+        const int unit = tl.u0 + (m >> 1);
+        const int ku = kperm(unit);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+          const int col = c0 + j;
+          if (!(m & 1) && col < n) {
+            const float g = bf16r(v[j]), u = bf16r(other);
+            const float act = swiglu_bf16(g, u);
+            a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = __half_as_ushort(__float2half_rn(act));
+          }
+        }
+      } else {
+        const int row = tl.u0 + m;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int col = c0 + j;
+          if (col < n) a.y_out[(size_t)(tl.p0 + col) * a.H + row] = f32_to_bf16(v[j]);
+        }
+      }
+    }
+  } else {
+    // drain: every committed stage completes before TMEM is released (bounded)
+    for (int s = 0; s < TC_S; ++s) (void)mbar_wait_bounded(&bars[s], 0, a.err);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+}
+
+}  // namespace ynb
+
+namespace ynb {
+
+// bf16 rows -> fp16 rows in the K-permuted order of the tensor-core path.
+__global__ void k_to_f16_kperm(const uint16_t* x, long long n, int cols, uint16_t* out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cols;
+    const int k = (int)(i - r * cols);
+    out[r * cols + kperm(k)] = __half_as_ushort(__float2half_rn(bf16_to_f32(x[i])));
+  }
+}
+
+// out[t] = h_res[t] + (sum_j bf16(y[pair_of[t][j]] * w[t][j]) in column order [+ ysh[t]]),
+// rounded as the single-row combine.
+__global__ void k_pairs_combine(const uint16_t* y, const int32_t* pair_of, const float* w, const uint16_t* ysh,
+                                const uint16_t* h_res, int H, int K, uint16_t* out) {
+  const int t = blockIdx.y, r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= H) return;
+  float acc = 0.0f;
+  for (int j = 0; j < K; ++j) {
+    const float v = bf16_to_f32(y[(size_t)pair_of[(size_t)t * K + j] * H + r]);
+    acc = __fadd_rn(acc, bf16r(__fmul_rn(v, w[(size_t)t * K + j])));
+  }
+  float o = bf16r(acc);
+  if (ysh) o = bf16r(__fadd_rn(o, bf16_to_f32(ysh[(size_t)t * H + r])));
+  if (h_res) o = bf16r(__fadd_rn(bf16_to_f32(h_res[(size_t)t * H + r]), o));
+  out[(size_t)t * H + r] = f32_to_bf16(o);
+}
+
+}  // namespace ynb

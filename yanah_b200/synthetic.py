@@ -100,6 +100,14 @@ def qwen3_next_stack(seed: int = 0, n_layers: int = 48) -> StackConfig:
     return StackConfig("qwen3next_80b_a3b_stack48", n_layers, bits, seed=seed)
 
 
+def lfm2_stack(seed: int = 0, n_layers: int = 40) -> StackConfig:
+    """40-layer LFM2-24B-A2B-shaped MoE stack for the tensor-core prefill path:
+    64 experts, top-4, SwiGLU intermediate 1536, 4-bit g64 experts, 8-bit
+    router, no shared expert."""
+    return StackConfig("lfm2_24b_a2b_stack40", n_layers, (4,) * n_layers, hidden=2048, n_experts=64, top_k=4,
+                       moe_inter=1536, shared_inter=0, seed=seed)
+
+
 # ------------------------------------------------------------ dense weights
 @dataclass
 class DenseLayer:
