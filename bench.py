@@ -420,6 +420,108 @@ def run_ep(args, rank: int, world: int):
     stack.close()
 
 
+# ------------------------------------------------------------- prefill leg
+PREFILL_METRIC = "prefill tok/s, ragged batch of 8 prompts (LFM2-24B-A2B-shaped, 40 layers), tensor-core expert GEMM"
+
+
+def run_prefill(args, rank: int, world: int):
+    """Config 3: a ragged prefill batch of 8 prompts with lengths uniform in
+    1-512 (seeded) through the 40-layer LFM2-shaped stack: routing of every
+    row, the host plan of the expert groups, the tcgen05 grouped gate/up +
+    SwiGLU and down GEMMs, the combine. One step = the whole batch through
+    every layer."""
+    import numpy as np
+    import torch
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.prefill import PrefillStack
+    from yanah_b200.synthetic import hidden_stream_id, lfm2_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = lfm2_stack(seed=0)
+    lens = np.random.default_rng(3).integers(1, 513, size=8)
+    T = int(lens.sum())
+    layer_ids = list(range(args.first_layer, args.first_layer + (args.layers or cfg.n_layers)))
+    stack = PrefillStack(cfg, max_rows=T, device=dev, layers=layer_ids)
+    H, K, I = cfg.hidden, cfg.top_k, cfg.moe_inter
+    h = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(h.data_ptr(), T * H, cfg.seed, hidden_stream_id(600 + rank), 1.0, 0.0,
+                                        stream_ptr()))
+    for _ in range(args.warmup):
+        stack.prefill(h)
+    torch.cuda.synchronize(dev)
+    if stack.check_error():
+        raise RuntimeError("device error in the prefill warm-up")
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid(dev.index)) as clk:
+        start.record()
+        for _ in range(args.steps):
+            stack.prefill(h)
+        end.record()
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end)
+    value = T * args.steps / (ms / 1e3)
+    # grouped GEMM time (untimed pass with events around the two GEMM launches of every layer)
+    ev = []
+    stack.prefill(h, gemm_events=ev)
+    torch.cuda.synchronize(dev)
+    gemm_ms = sum(a.elapsed_time(b) for a, b in ev)
+    L = len(layer_ids)
+    flops = L * T * K * 6.0 * H * I
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    tf_peak = float(peak.get("bf16_tflops", 1590.0))
+    achieved = flops / (gemm_ms / 1e3) / 1e12
+    # e2e: pinned host rows in, outputs back, every step
+    h_in = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    h_in.copy_(h)
+    h_out = torch.empty_like(h_in, pin_memory=True)
+    d_in = torch.empty_like(h)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        d_in.copy_(h_in, non_blocking=True)
+        h_out.copy_(stack.prefill(d_in), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e = T * args.steps / (e0.elapsed_time(e1) / 1e3)
+    if stack.check_error():
+        raise RuntimeError("device error during the timed prefill")
+    line = {
+        "metric": PREFILL_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "lfm2_24b_a2b_moe_stack40_prefill", "layers": L, "prompts": 8,
+                   "prompt_lengths": lens.tolist(), "rows": T, "hidden": H, "experts": cfg.n_experts, "top_k": K,
+                   "moe_inter": I, "expert_bits": "4-bit g64", "router_bits": 8,
+                   "gemm_operands": "gate/up fp16, down bf16 (dequantised weights and activations), fp32 accumulate in TMEM",
+                   "l2": "no flush: a step reads every routed expert of 40 layers (13.6 GB > 126 MB L2)"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": args.steps * L * 5 + args.steps * L * ((T + 63) // 64) * 2,
+        "clocks": clk.summary(),
+        "roofline": {"bound": "tensor", "kernel": "k_tc_experts (gate/up + down, every layer)",
+                     "achieved": round(achieved, 1), "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / tf_peak, 4),
+                     "peak_source": "measured (cuBLAS bf16 burst)" if peak else "fallback",
+                     "flops_per_step": flops, "gemm_ms_per_step": round(gemm_ms, 3), "traffic": None},
+    }
+    if not args.no_cpu:
+        from oracle import cpu
+        threads = len(os.sched_getaffinity(0))
+        o = cpu.OracleStack(cfg, threads=threads)
+        rows = h[:16].view(torch.int16).cpu().numpy().view(np.uint16)
+        o.layer(layer_ids[0], rows)  # record generation (not timed)
+        t0 = time.perf_counter()
+        o.layer(layer_ids[0], rows)
+        secs = (time.perf_counter() - t0) * L
+        line["cpu_baseline"] = {"value": round(16 / secs, 3), "unit": "tok/s", "cores": cpu.lib().yo_num_threads(),
+                                "kind": "port",
+                                "sample": "16 prompt rows through one layer with the C oracle, scaled to 40 layers"}
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, rank: int, world: int):
     import numpy as np
@@ -553,9 +655,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
-    ap.add_argument("--workload", choices=["resident", "streaming", "ep"], default="resident",
+    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill"], default="resident",
                     help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier; "
-                         "ep: batch of 64 rows, experts sharded over the GPUs")
+                         "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill")
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
@@ -578,6 +680,9 @@ def main():
                 run_streaming(args, rank, world)
         elif args.workload == "ep":
             run_ep(args, rank, world)
+        elif args.workload == "prefill":
+            if rank == 0:
+                run_prefill(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

@@ -316,11 +316,12 @@ typedef struct yn_tc_tile {
 } yn_tc_tile;
 
 /* mode 0 (mlx_backend.py:447-456 `_switch_glu` up to SwiGLU): for every tile,
- * act_out[p][kperm(u)] = fp16(swiglu(gate_u . x, up_u . x)) with x =
- * b_rows[pair_row[p]] (fp16 K-permuted rows of H). mode 1 (the down
- * projection): y_out[p][h] = bf16(down_h . act_p) with act_p = b_rows[p]
- * (fp16 K-permuted rows of I). Routed experts 4-bit g64 only. tiles: device
- * array. err: device error word (bounded waits, bad slots). */
+ * act_out[p][kperm(u)] = bf16(swiglu(gate_u . x, up_u . x)) with x =
+ * b_rows[pair_row[p]] (fp16 K-permuted rows of H; weights dequantised to
+ * fp16). mode 1 (the down projection): y_out[p][h] = bf16(down_h . act_p)
+ * with act_p = b_rows[p] (bf16 K-permuted rows of I; weights dequantised to
+ * bf16). Routed experts 4-bit g64 only. tiles: device array. err: device
+ * error word (bounded waits, bad slots). */
 int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
                   int32_t n_tiles, const void* b_rows, const int32_t* pair_row, void* act_out, void* y_out,
                   int32_t* err, void* stream);

@@ -20,10 +20,6 @@ from yanah_b200.synthetic import lfm2_stack
 pytestmark = pytest.mark.gpu
 
 
-def _f16_to_bf16_bits(a: np.ndarray) -> np.ndarray:
-    return cpu.f32_to_bf16(a.astype(np.float32))
-
-
 def _check(cfg, T, sample_pairs):
     st = PrefillStack(cfg, max_rows=T, layers=[0])
     h = hidden_rows(cfg, T, stream=31)
@@ -39,14 +35,14 @@ def _check(cfg, T, sample_pairs):
     assert np.array_equal(st.w[:T].cpu().numpy().view(np.uint32), pa["w"].view(np.uint32))
     ids, pair_row, pair_of = st.last_plan
     P = T * cfg.top_k
-    act = kperm_inverse(st.act16[:P].cpu().numpy())
+    act = kperm_inverse(bf16_np(st.act[:P]))
     y = bf16_np(st.y[:P])
     rng = np.random.default_rng(0)
     for p in sorted(set(rng.choice(P, size=min(sample_pairs, P), replace=False).tolist()) | {0, P - 1}):
         t = int(pair_row[p])
         j = int(np.nonzero(pair_of[t] == p)[0][0])
         a_ref, y_ref = orc.expert(0, int(ids[t, j]), pa["x"][t])
-        assert rel_l2(_f16_to_bf16_bits(act[p]), a_ref) < REL_L2_TOL, (p, rel_l2(_f16_to_bf16_bits(act[p]), a_ref))
+        assert rel_l2(act[p], a_ref) < REL_L2_TOL, (p, rel_l2(act[p], a_ref))
         assert rel_l2(y[p], y_ref) < REL_L2_TOL, (p, rel_l2(y[p], y_ref))
     rows = sorted(set(rng.choice(T, size=min(8, T), replace=False).tolist()))
     ref = orc.layer(0, h[rows])["out"]
@@ -56,6 +52,28 @@ def _check(cfg, T, sample_pairs):
 def test_tc_small_config():
     cfg = small_config(bits=(4,), gs=64, hidden=512, n_experts=16, top_k=2, inter=512, shared=0, seed=7)
     _check(cfg, T=40, sample_pairs=80)
+
+
+def test_tc_lfm2_two_chained_layers():
+    # the residual stream after one layer is large (|h| ~ 6e4): the second
+    # layer's activations exceed the fp16 range, which the down GEMM's bf16
+    # operands must hold
+    cfg = lfm2_stack(n_layers=40)
+    T = 96
+    st = PrefillStack(cfg, max_rows=T, layers=[0, 1])
+    h = bf16_dev(hidden_rows(cfg, T, stream=33))
+    h1, h2 = torch.empty_like(h), torch.empty_like(h)
+    st.layer(0, h, h1)
+    st.layer(1, h1, h2)
+    torch.cuda.synchronize()
+    assert st.check_error() == 0
+    h1n, out = bf16_np(h1), bf16_np(h2)
+    assert np.abs(cpu.bf16_to_f32(h1n)).max() > 6.6e4 / 4  # the large-residual regime this test is about
+    assert np.all(np.isfinite(cpu.bf16_to_f32(out)))
+    orc = cpu.OracleStack(cfg, threads=8)
+    rows = [0, 17, 95]
+    ref = orc.layer(1, h1n[rows])["out"]  # the oracle's second layer on the same input rows
+    assert rel_l2(out[rows], ref) < REL_L2_TOL
 
 
 def test_tc_lfm2_layer():

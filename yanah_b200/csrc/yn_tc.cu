@@ -116,7 +116,6 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
     if (r.piece_offset[i] % 16) return host_fail(YN_E_INVALID, "record pieces must be 16-byte aligned");
   if (n_tiles < 1) return YN_OK;
   TcArgs a{};
-  a.mode = mode;
   a.tiles = reinterpret_cast<const TcTile*>(tiles);
   a.n_tiles = n_tiles;
   a.b_rows = reinterpret_cast<const uint16_t*>(b_rows);
@@ -135,9 +134,12 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   a.y_out = reinterpret_cast<uint16_t*>(y_out);
   a.err = err;
   const size_t smem = tc_smem(mode == 0 ? H : I);
-  int rc = host_set_smem(reinterpret_cast<const void*>(k_tc_experts), smem);
+  const void* kern = mode == 0 ? reinterpret_cast<const void*>(k_tc_experts<0>)
+                               : reinterpret_cast<const void*>(k_tc_experts<1>);
+  int rc = host_set_smem(kern, smem);
   if (rc) return rc;
-  k_tc_experts<<<n_tiles, TC_THREADS, smem, as_st(stream)>>>(a);
+  if (mode == 0) k_tc_experts<0><<<n_tiles, TC_THREADS, smem, as_st(stream)>>>(a);
+  else k_tc_experts<1><<<n_tiles, TC_THREADS, smem, as_st(stream)>>>(a);
   YN_CUDA_T(cudaGetLastError());
   return YN_OK;
 }

@@ -4,12 +4,13 @@
 //
 // One CTA computes one tile D[m][n] = sum_k W[m][k] * X[n][k]:
 //  * A = 128 weight rows of one expert, dequantised from MLX 4-bit g64 codes
-//    to fp16 by the CTA's four warps (thread t owns tile row t): for gate/up
+//    by the CTA's four warps (thread t owns tile row t): for gate/up
 //    the rows interleave gate unit u (row 2i) and up unit u (row 2i + 1) for
 //    64 units, so SwiGLU fuses into the epilogue; for down they are 128
 //    output rows;
-//  * B = up to 256 rows of this expert's tokens (prefill x, or SwiGLU
-//    activations for the down projection), fp16, copied with cp.async;
+//  * B = up to 256 rows of this expert's tokens (prefill x in fp16, or the
+//    SwiGLU activations in bf16 for the down projection, whose weights are
+//    then dequantised to bf16), copied with cp.async;
 //  * both operands are K-major in the 128-byte swizzled layout (row r of an
 //    8-row atom at r * 128 bytes, 16-byte chunk c at (c ^ r) * 16); K moves
 //    in stages of 64 codes = one quantisation group, 4 stages in flight;
@@ -49,10 +50,9 @@ struct TcTile {
 };
 
 struct TcArgs {
-  int mode;                    // 0: gate/up + SwiGLU, 1: down
   const TcTile* tiles;
   int n_tiles;
-  const uint16_t* b_rows;      // fp16 K-permuted rows: mode 0 x' (rows by token), mode 1 act' (rows by pair)
+  const uint16_t* b_rows;      // K-permuted rows: gate/up fp16 x' (rows by token), down bf16 act' (rows by pair)
   const int32_t* pair_row;     // mode 0: pair -> row of b_rows; mode 1: null (row = pair)
   const uint8_t* base;         // expert arena
   long long stride;
@@ -60,7 +60,7 @@ struct TcArgs {
   int n_slots;
   RecGeom rg;
   int H, I;
-  uint16_t* act_out;           // mode 0: (P, I) fp16 K-permuted SwiGLU activations
+  uint16_t* act_out;           // mode 0: (P, I) bf16 K-permuted SwiGLU activations
   uint16_t* y_out;             // mode 1: (P, H) bf16 expert outputs
   int* err;
 };
@@ -90,10 +90,11 @@ YN_DEV uint64_t tc_desc(uint32_t smem_addr) {
   return d;
 }
 
-YN_DEV uint32_t tc_idesc(int n) {
-  // f32 accumulate (bits 4-5 = 1), A and B fp16 (formats 0), both K-major,
-  // N >> 3 at bits 17-22, M >> 4 at bits 24-28
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+YN_DEV uint32_t tc_idesc(int n, bool bf16) {
+  // f32 accumulate (bits 4-5 = 1), A and B fp16 (format 0) or bf16 (format 1),
+  // both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28
+  const uint32_t f = bf16 ? 1u : 0u;
+  return (1u << 4) | (f << 7) | (f << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
 }
 
 YN_DEV void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
@@ -140,6 +141,10 @@ YN_DEV bool tc_wait(uint64_t* bar, uint32_t parity, int* err) {
   return mbar_wait_block(bar, parity, err);
 }
 
+// MODE 0: gate/up + SwiGLU with fp16 operands (normalised rows are small);
+// MODE 1: down with bf16 operands (SwiGLU activations have bf16's range, as
+// the reference's bf16 arrays do; fp16 would overflow on them).
+template <int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // layout (from a 1024-byte aligned base): [A x S][B x S][codes x S][scales][biases][mbarriers, tmem address]
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
   uint8_t* Abuf = smem;
   uint8_t* Bbuf = Abuf + TC_S * TC_A_BYTES;
   uint8_t* Cbuf = Bbuf + TC_S * TC_B_BYTES;
-  const int Kd = a.mode == 0 ? a.H : a.I;
+  const int Kd = MODE == 0 ? a.H : a.I;
   const int NG = Kd / 64, NK = Kd / 64;
   uint16_t* Ssc = reinterpret_cast<uint16_t*>(Cbuf + TC_S * TC_C_BYTES);  // (128, NG) fp16 scales
   uint16_t* Sbi = Ssc + TC_M * NG;                                         // (128, NG) fp16 biases
@@ -171,7 +176,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
   const int t = tid;  // this thread's tile row
   int wrow;
   long long off_w, off_s, off_b;
-  if (a.mode == 0) {
+  if (MODE == 0) {
     const bool up = t & 1;
     wrow = tl.u0 + (t >> 1);
     off_w = a.rg.off[up ? 3 : 0];
@@ -241,25 +246,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
       const uint4 c0 = cw[0], c1 = cw[1];
       const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
       const __half sc = __ushort_as_half(Ssc[t * NG + kc]), bi = __ushort_as_half(Sbi[t * NG + kc]);
-      const __half2 s1 = __halves2half2(sc, sc);
-      const __half sc16 = __float2half_rn(__fmul_rn(__half2float(sc), 0.0625f));
-      const __half2 s16 = __halves2half2(sc16, sc16);
-      const __half2 b2 = __halves2half2(bi, bi);
       const __half2 k1024 = __float2half2_rn(1024.0f);
       uint8_t* Arow = Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+      if constexpr (MODE == 0) {  // w = fp16(s * q + b): one HFMA2 per pair
+        const __half2 s1 = __halves2half2(sc, sc);
+        const __half sc16 = __float2half_rn(__fmul_rn(__half2float(sc), 0.0625f));
+        const __half2 s16 = __halves2half2(sc16, sc16);
+        const __half2 b2 = __halves2half2(bi, bi);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t pr[4];
-        tc_unpack4(words[i], pr);
-        uint32_t o[4];
+        for (int i = 0; i < 8; ++i) {
+          uint32_t pr[4];
+          tc_unpack4(words[i], pr);
+          uint32_t o[4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
-          h = __hsub2(h, k1024);
-          h = __hfma2(h, (p & 1) ? s16 : s1, b2);
-          o[p] = *reinterpret_cast<uint32_t*>(&h);
+          for (int p = 0; p < 4; ++p) {
+            __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
+            h = __hsub2(h, k1024);
+            h = __hfma2(h, (p & 1) ? s16 : s1, b2);
+            o[p] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
-        *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {  // w = bf16(s * q + b) from an fp32 FMA
+        const float s1 = __half2float(sc), s16 = __fmul_rn(s1, 0.0625f), bf = __half2float(bi);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t pr[4];
+          tc_unpack4(words[i], pr);
+          uint32_t o[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
+            h = __hsub2(h, k1024);  // mult * q, exact
+            const float2 q = __half22float2(h);
+            const float m = (p & 1) ? s16 : s1;
+            __nv_bfloat162 w = __floats2bfloat162_rn(__fmaf_rn(q.x, m, bf), __fmaf_rn(q.y, m, bf));
+            o[p] = *reinterpret_cast<uint32_t*>(&w);
+          }
+          *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -267,7 +292,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
     if (tid == 0) {
       tc_fence_after();
       const uint32_t abase = smem_u32(Abuf + s * TC_A_BYTES), bbase = smem_u32(Bbuf + s * TC_B_BYTES);
-      const uint32_t idesc = tc_idesc(nmma);
+      const uint32_t idesc = tc_idesc(nmma, MODE == 1);
 #pragma unroll
       for (int k16 = 0; k16 < 4; ++k16)
         tc_mma(tmem, tc_desc(abase + 32 * k16), tc_desc(bbase + 32 * k16), idesc, (kc > 0 || k16 > 0) ? 1u : 0u);
@@ -284,7 +309,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
     for (int c0 = 0; c0 < nmma; c0 += 32) {
       float v[32];
       tc_ld32(lane_base + (uint32_t)c0, v);
-      if (a.mode == 0) {
+      if (MODE == 0) {
         const int unit = tl.u0 + (m >> 1);
         const int ku = kperm(unit);
 #pragma unroll
@@ -294,7 +319,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
           if (!(m & 1) && col < n) {
             const float g = bf16r(v[j]), u = bf16r(other);
             const float act = swiglu_bf16(g, u);
-            a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = __half_as_ushort(__float2half_rn(act));
+            a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(act);
           }
         }
       } else {

@@ -82,14 +82,16 @@ class PrefillStack:
         self.x16 = torch.empty((T, H), dtype=torch.float16, device=dev)
         self.ids = torch.empty((T, K), dtype=torch.int32, device=dev)
         self.w = torch.empty((T, K), dtype=torch.float32, device=dev)
-        self.act16 = torch.empty((P, I), dtype=torch.float16, device=dev)
+        self.act = torch.empty((P, I), dtype=torch.bfloat16, device=dev)
         self.y = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.ping = torch.empty((2, T, H), dtype=torch.bfloat16, device=dev)
         self.last_plan = None
 
-    def layer(self, i: int, h: torch.Tensor, out: torch.Tensor, stream=None) -> None:
-        """Layer i (index into `layer_ids`) of T = h.shape[0] rows."""
+    def layer(self, i: int, h: torch.Tensor, out: torch.Tensor, stream=None, gemm_events=None) -> None:
+        """Layer i (index into `layer_ids`) of T = h.shape[0] rows. gemm_events:
+        optional list that receives (start, end) CUDA events around the two
+        grouped GEMM launches."""
         lib, cfg = _lib.lib(), self.cfg
         T, H, K = h.shape[0], cfg.hidden, cfg.top_k
         if T > self.max_rows:
@@ -107,20 +109,26 @@ class PrefillStack:
         po = torch.from_numpy(pair_of).to(dev, non_blocking=True)
         tu = torch.from_numpy(up).to(dev, non_blocking=True)
         td = torch.from_numpy(down).to(dev, non_blocking=True)
+        if gemm_events is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
         _lib.check(lib.yn_tc_experts(C.byref(self.dims), L, 0, tu.data_ptr(), len(up), self.x16.data_ptr(),
-                                     pr.data_ptr(), self.act16.data_ptr(), None, self.err.data_ptr(), st))
-        _lib.check(lib.yn_tc_experts(C.byref(self.dims), L, 1, td.data_ptr(), len(down), self.act16.data_ptr(),
+                                     pr.data_ptr(), self.act.data_ptr(), None, self.err.data_ptr(), st))
+        _lib.check(lib.yn_tc_experts(C.byref(self.dims), L, 1, td.data_ptr(), len(down), self.act.data_ptr(),
                                      None, None, self.y.data_ptr(), self.err.data_ptr(), st))
+        if gemm_events is not None:
+            e1.record(stream)
+            gemm_events.append((e0, e1))
         _lib.check(lib.yn_pairs_combine(C.byref(self.dims), self.y.data_ptr(), po.data_ptr(), self.w.data_ptr(),
                                         None, h.data_ptr(), T, out.data_ptr(), st))
         self._keep = (pr, po, tu, td)
 
-    def prefill(self, h: torch.Tensor, stream=None) -> torch.Tensor:
+    def prefill(self, h: torch.Tensor, stream=None, gemm_events=None) -> torch.Tensor:
         """Every layer for the rows h (T, H) bf16; returns the last layer's output."""
         T = h.shape[0]
         self.ping[0, :T].copy_(h)
         for i in range(len(self.layer_ids)):
-            self.layer(i, self.ping[i % 2, :T], self.ping[(i + 1) % 2, :T], stream)
+            self.layer(i, self.ping[i % 2, :T], self.ping[(i + 1) % 2, :T], stream, gemm_events)
         return self.ping[len(self.layer_ids) % 2, :T]
 
     def check_error(self) -> int:
