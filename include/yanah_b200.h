@@ -291,15 +291,15 @@ int yn_memcpy(void* dst, const void* src, size_t bytes, void* stream);
 /* Prompt prefill moves hundreds of rows through each expert (sweep.py:80-138
  * and the prompt pass of mlx_backend.py:421-433 `moe`), so the routed
  * experts run as a grouped GEMM on the tcgen05 tensor cores. The grouping
- * (which rows go to which expert) is planned on the host, as the reference's
- * prefill sweep plans its staging groups.
+ * (which rows go to which expert) is planned by yn_prefill_plan on the
+ * device, or by the caller.
  *
  * yn_rows_route: post-attention RMSNorm, router logits, top-k ids and
- * weights of T rows (any T), bit-identical to yn_post_attention row by row;
- * x_out (T, H) bf16 normalised rows. ws: yn_rows_route_bytes(dims) bytes,
- * zeroed once before first use; yn_route_error reads and clears its error
- * word. */
-size_t yn_rows_route_bytes(const yn_dims* dims);
+ * weights of T rows (T <= 4096), bit-identical to yn_post_attention row by
+ * row; x_out (T, H) bf16 normalised rows. ws: yn_rows_route_bytes(dims,
+ * max_rows) bytes for calls of up to max_rows rows, zeroed once before first
+ * use; yn_route_error reads and clears its error word. */
+size_t yn_rows_route_bytes(const yn_dims* dims, int32_t max_rows);
 int yn_rows_route(const yn_dims* dims, const yn_layer* layer, const void* h, int32_t T, void* x_out,
                   int32_t* ids_out, float* w_out, void* ws, size_t ws_bytes, void* stream);
 int yn_route_error(void* ws, const yn_dims* dims, void* stream, int32_t* code_out);
@@ -323,8 +323,18 @@ typedef struct yn_tc_tile {
  * bf16). Routed experts 4-bit g64 only. tiles: device array. err: device
  * error word (bounded waits, bad slots). */
 int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
-                  int32_t n_tiles, const void* b_rows, const int32_t* pair_row, void* act_out, void* y_out,
-                  int32_t* err, void* stream);
+                  int32_t n_tiles, const int32_t* n_tiles_dev, const void* b_rows, const int32_t* pair_row,
+                  void* act_out, void* y_out, int32_t* err, void* stream);
+
+/* The grouping on the device, so that a prefill layer needs no host
+ * synchronisation: pairs of each expert made contiguous (pair_row: pair ->
+ * row, pair_of: t * k + j -> pair), then the gate/up and down tiles of every
+ * expert (n_tiles[0], n_tiles[1] on the device; pass them to yn_tc_experts
+ * as n_tiles_dev with grids of max_up / max_dn from yn_prefill_max_tiles). */
+int yn_prefill_max_tiles(const yn_dims* dims, int32_t T, int32_t* max_up, int32_t* max_dn);
+int yn_prefill_plan(const yn_dims* dims, const int32_t* ids, int32_t T, int32_t* pair_row, int32_t* pair_of,
+                    yn_tc_tile* tiles_up, int32_t max_up, yn_tc_tile* tiles_dn, int32_t max_dn, int32_t* n_tiles,
+                    int32_t* err, void* stream);
 
 /* Combine of T rows (mlx_backend.py:409/:420, :438-440; orchestrator.py:287):
  * out[t] = h_res[t] + (sum_j bf16(y[pair_of[t][j]] * w[t][j]) in column order

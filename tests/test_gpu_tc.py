@@ -33,7 +33,12 @@ def _check(cfg, T, sample_pairs):
     assert np.array_equal(bf16_np(st.x[:T]), pa["x"])
     assert np.array_equal(st.ids[:T].cpu().numpy(), pa["ids"])
     assert np.array_equal(st.w[:T].cpu().numpy().view(np.uint32), pa["w"].view(np.uint32))
-    ids, pair_row, pair_of = st.last_plan
+    ids, pair_row, pair_of = st.plan(T)
+    # the device plan: every (row, column) pair exactly once, pairs of an expert contiguous
+    assert np.array_equal(np.sort(pair_of.reshape(-1)), np.arange(T * cfg.top_k))
+    assert np.array_equal(pair_row[pair_of.reshape(-1)], np.repeat(np.arange(T), cfg.top_k))
+    e_of_pair = ids.reshape(-1)[np.argsort(pair_of.reshape(-1))]
+    assert np.all(np.diff(e_of_pair) >= 0)
     P = T * cfg.top_k
     act = kperm_inverse(bf16_np(st.act[:P]))
     y = bf16_np(st.y[:P])

@@ -385,7 +385,7 @@ int ynb::host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, in
   int rc;
   const int H = d.hidden, E = d.n_experts;
   if (!h || !L.post_norm || !counter) return fail(YN_E_INVALID, "batch post-attention: null argument");
-  if (T < 1 || T > 64) return fail(YN_E_UNSUPPORTED, "batch post-attention: rows must be in [1, 64]");
+  if (T < 1 || T > 4096) return fail(YN_E_UNSUPPORTED, "batch post-attention: rows must be in [1, 4096]");
   if ((rc = check_qmat(L.router, E, H, 8, "router"))) return rc;
   if (E % BD_RROWS) return fail(YN_E_UNSUPPORTED, "batch post-attention: n_experts must be a multiple of 16");
   if (!o.xf32 || !o.xsum) return fail(YN_E_INVALID, "batch post-attention: null fp32 row buffers");

@@ -39,9 +39,10 @@ struct PostAttnOut {
 int host_post_attention_rows(const yn_dims& d, const yn_layer& L, const void* h1, int T, const PostAttnOut& o,
                              cudaStream_t st);
 
-// Post-attention + routing of up to 64 rows (k_batch_dense): bit-identical to
-// the single-row path, spread over (8 rows x 8 tokens) tiles. `counter` is a
-// device word that only this call sequence uses (monotonic).
+// Post-attention + routing of up to 4096 rows (k_batch_dense): bit-identical
+// to the single-row path, spread over (router rows x 8 tokens) tiles.
+// `counter`: ceil(T / 8) device words that only this call sequence uses
+// (monotonic; zero before the first call).
 int host_batch_dense(const yn_dims& d, const yn_layer& L, const void* h, int T, const PostAttnOut& o,
                      unsigned* counter, cudaStream_t st);
 

@@ -21,16 +21,21 @@ namespace {
 cudaStream_t as_st(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 size_t a256(size_t v) { return (v + 255) / 256 * 256; }
 
+constexpr int ROUTE_MAX_ROWS = 4096;
+
+// Route workspace: error word and the per-group counters first (fixed
+// offsets, so calls with different row counts share them), then the
+// row-sized arrays.
 struct RouteWs {
   size_t err, counter, logits, xf32, xsum, act_sh, sgate, total;
 };
-RouteWs route_ws(const yn_dims& d) {
+RouteWs route_ws(const yn_dims& d, int rows) {
   RouteWs L{};
   size_t o = 0;
   auto take = [&](size_t b) { size_t at = o; o = a256(o + b); return at; };
-  const size_t C = 64;
+  const size_t C = rows;
   L.err = take(4);
-  L.counter = take(8 * 4);
+  L.counter = take((ROUTE_MAX_ROWS / 8) * 4);
   L.logits = take(C * d.n_experts * 4);
   L.xf32 = take(C * d.hidden * 4);
   L.xsum = take(C * (d.hidden / 16) * 4);
@@ -46,41 +51,34 @@ size_t tc_smem(int Kd) {
 }
 }  // namespace
 
-extern "C" size_t yn_rows_route_bytes(const yn_dims* dims) {
-  if (!dims) return 0;
-  return route_ws(*dims).total;
+extern "C" size_t yn_rows_route_bytes(const yn_dims* dims, int32_t max_rows) {
+  if (!dims || max_rows < 1 || max_rows > ROUTE_MAX_ROWS) return 0;
+  return route_ws(*dims, max_rows).total;
 }
 
 extern "C" int yn_rows_route(const yn_dims* dims, const yn_layer* layer, const void* h, int32_t T, void* x_out,
                              int32_t* ids_out, float* w_out, void* ws, size_t ws_bytes, void* stream) {
   if (!dims || !layer || !h || !x_out || !ids_out || !w_out || !ws) return host_fail(YN_E_INVALID, "null argument");
-  if (T < 1) return host_fail(YN_E_INVALID, "rows must be positive");
-  const RouteWs L = route_ws(*dims);
-  if (ws_bytes < L.total) return host_fail(YN_E_INVALID, "route workspace too small");
+  if (T < 1 || T > ROUTE_MAX_ROWS) return host_fail(YN_E_UNSUPPORTED, "rows must be in [1, 4096]");
+  const RouteWs L = route_ws(*dims, T);
+  if (ws_bytes < L.total) return host_fail(YN_E_INVALID, "route workspace too small for this many rows");
   uint8_t* b = reinterpret_cast<uint8_t*>(ws);
-  const int H = dims->hidden, K = dims->top_k;
-  for (int t0 = 0; t0 < T; t0 += 64) {
-    const int n = std::min(64, T - t0);
-    PostAttnOut o{};
-    o.x = reinterpret_cast<uint16_t*>(x_out) + (size_t)t0 * H;
-    o.logits = reinterpret_cast<float*>(b + L.logits);
-    o.act_sh = reinterpret_cast<uint16_t*>(b + L.act_sh);
-    o.sgate = reinterpret_cast<float*>(b + L.sgate);
-    o.ids = ids_out + (size_t)t0 * K;
-    o.wts = w_out + (size_t)t0 * K;
-    o.err = reinterpret_cast<int*>(b + L.err);
-    o.xf32 = reinterpret_cast<float*>(b + L.xf32);
-    o.xsum = reinterpret_cast<float*>(b + L.xsum);
-    const int rc = host_batch_dense(*dims, *layer, reinterpret_cast<const uint16_t*>(h) + (size_t)t0 * H, n, o,
-                                    reinterpret_cast<unsigned*>(b + L.counter), as_st(stream));
-    if (rc) return rc;
-  }
-  return YN_OK;
+  PostAttnOut o{};
+  o.x = reinterpret_cast<uint16_t*>(x_out);
+  o.logits = reinterpret_cast<float*>(b + L.logits);
+  o.act_sh = reinterpret_cast<uint16_t*>(b + L.act_sh);
+  o.sgate = reinterpret_cast<float*>(b + L.sgate);
+  o.ids = ids_out;
+  o.wts = w_out;
+  o.err = reinterpret_cast<int*>(b + L.err);
+  o.xf32 = reinterpret_cast<float*>(b + L.xf32);
+  o.xsum = reinterpret_cast<float*>(b + L.xsum);
+  return host_batch_dense(*dims, *layer, h, T, o, reinterpret_cast<unsigned*>(b + L.counter), as_st(stream));
 }
 
 extern "C" int yn_route_error(void* ws, const yn_dims* dims, void* stream, int32_t* code_out) {
   if (!ws || !dims || !code_out) return host_fail(YN_E_INVALID, "null argument");
-  int32_t* e = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws) + route_ws(*dims).err);
+  int32_t* e = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws) + route_ws(*dims, 1).err);
   YN_CUDA_T(cudaMemcpyAsync(code_out, e, 4, cudaMemcpyDeviceToHost, as_st(stream)));
   YN_CUDA_T(cudaStreamSynchronize(as_st(stream)));
   YN_CUDA_T(cudaMemsetAsync(e, 0, 4, as_st(stream)));
@@ -98,8 +96,8 @@ extern "C" int yn_to_f16_kperm(const void* x, int64_t rows, int32_t cols, void* 
 }
 
 extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
-                             int32_t n_tiles, const void* b_rows, const int32_t* pair_row, void* act_out, void* y_out,
-                             int32_t* err, void* stream) {
+                             int32_t n_tiles, const int32_t* n_tiles_dev, const void* b_rows, const int32_t* pair_row,
+                             void* act_out, void* y_out, int32_t* err, void* stream) {
   if (!dims || !layer || !tiles || !b_rows || !err) return host_fail(YN_E_INVALID, "null argument");
   if (mode != 0 && mode != 1) return host_fail(YN_E_INVALID, "mode must be 0 (gate/up) or 1 (down)");
   if (mode == 0 && (!act_out || !pair_row)) return host_fail(YN_E_INVALID, "gate/up needs act_out and pair_row");
@@ -118,6 +116,7 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   TcArgs a{};
   a.tiles = reinterpret_cast<const TcTile*>(tiles);
   a.n_tiles = n_tiles;
+  a.n_tiles_dev = n_tiles_dev;
   a.b_rows = reinterpret_cast<const uint16_t*>(b_rows);
   a.pair_row = pair_row;
   a.base = reinterpret_cast<const uint8_t*>(layer->expert_base);
@@ -152,6 +151,41 @@ extern "C" int yn_pairs_combine(const yn_dims* dims, const void* y, const int32_
   k_pairs_combine<<<grid, 256, 0, as_st(stream)>>>(
       reinterpret_cast<const uint16_t*>(y), pair_of, weights, reinterpret_cast<const uint16_t*>(y_shared),
       reinterpret_cast<const uint16_t*>(h_res), H, dims->top_k, reinterpret_cast<uint16_t*>(out));
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_prefill_max_tiles(const yn_dims* dims, int32_t T, int32_t* max_up, int32_t* max_dn) {
+  if (!dims || !max_up || !max_dn || T < 1) return host_fail(YN_E_INVALID, "null argument or T < 1");
+  const long long chunks = (long long)dims->n_experts + ((long long)T * dims->top_k + TC_NMAX - 1) / TC_NMAX;
+  *max_up = (int32_t)(chunks * (dims->moe_inter / 64));
+  *max_dn = (int32_t)(chunks * (dims->hidden / 128));
+  return YN_OK;
+}
+
+extern "C" int yn_prefill_plan(const yn_dims* dims, const int32_t* ids, int32_t T, int32_t* pair_row, int32_t* pair_of,
+                               yn_tc_tile* tiles_up, int32_t max_up, yn_tc_tile* tiles_dn, int32_t max_dn,
+                               int32_t* n_tiles, int32_t* err, void* stream) {
+  if (!dims || !ids || !pair_row || !pair_of || !tiles_up || !tiles_dn || !n_tiles || !err)
+    return host_fail(YN_E_INVALID, "null argument");
+  if (T < 1 || (long long)T * dims->top_k > 65536) return host_fail(YN_E_UNSUPPORTED, "T * top_k must be in [1, 65536]");
+  if (dims->n_experts > 1024) return host_fail(YN_E_UNSUPPORTED, "at most 1024 experts");
+  PrefillPlanArgs a{};
+  a.ids = ids;
+  a.T = T;
+  a.K = dims->top_k;
+  a.E = dims->n_experts;
+  a.H = dims->hidden;
+  a.I = dims->moe_inter;
+  a.pair_row = pair_row;
+  a.pair_of = pair_of;
+  a.up = reinterpret_cast<TcTile*>(tiles_up);
+  a.max_up = max_up;
+  a.dn = reinterpret_cast<TcTile*>(tiles_dn);
+  a.max_dn = max_dn;
+  a.n_tiles = n_tiles;
+  a.err = err;
+  k_prefill_plan<<<1, PLAN_THREADS, 0, as_st(stream)>>>(a);
   YN_CUDA_T(cudaGetLastError());
   return YN_OK;
 }

@@ -51,7 +51,8 @@ struct TcTile {
 
 struct TcArgs {
   const TcTile* tiles;
-  int n_tiles;
+  int n_tiles;                 // capacity of `tiles` (grid size)
+  const int* n_tiles_dev;      // tiles actually planned (device), or null for n_tiles
   const uint16_t* b_rows;      // K-permuted rows: gate/up fp16 x' (rows by token), down bf16 act' (rows by pair)
   const int32_t* pair_row;     // mode 0: pair -> row of b_rows; mode 1: null (row = pair)
   const uint8_t* base;         // expert arena
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
   __shared__ int rows_s[TC_NMAX];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (blockIdx.x >= a.n_tiles) return;
+  if (blockIdx.x >= (a.n_tiles_dev ? min(a.n_tiles, *a.n_tiles_dev) : a.n_tiles)) return;
   const TcTile tl = a.tiles[blockIdx.x];
   const int n = tl.n, nmma = (n + 15) & ~15;
   const int slot = a.slot_of ? a.slot_of[tl.e] : tl.e;
@@ -368,6 +369,100 @@ __global__ void k_pairs_combine(const uint16_t* y, const int32_t* pair_of, const
   if (ysh) o = bf16r(__fadd_rn(o, bf16_to_f32(ysh[(size_t)t * H + r])));
   if (h_res) o = bf16r(__fadd_rn(bf16_to_f32(h_res[(size_t)t * H + r]), o));
   out[(size_t)t * H + r] = f32_to_bf16(o);
+}
+
+}  // namespace ynb
+
+namespace ynb {
+
+// Expert groups and GEMM tiles of a prefill batch, on the device (one CTA of
+// 1024 threads): counts per expert, a block scan over experts (ascending id),
+// pair placement (pairs of one expert contiguous; their order inside an
+// expert does not change any pair's result), then per expert ceil(n / 256)
+// row chunks x (I / 64) gate/up tiles and x (H / 128) down tiles.
+// n_tiles[0], n_tiles[1] = gate/up and down tiles written.
+constexpr int PLAN_THREADS = 1024;
+
+struct PrefillPlanArgs {
+  const int32_t* ids;  // (T, K)
+  int T, K, E, H, I;
+  int32_t* pair_row;   // (T * K) pair -> row
+  int32_t* pair_of;    // (T * K) t * K + j -> pair
+  TcTile* up;
+  int max_up;
+  TcTile* dn;
+  int max_dn;
+  int* n_tiles;        // [2]
+  int* err;
+};
+
+YN_DEV int2 block_scan2(int2 v, int2* total) {
+  __shared__ int2 ws[PLAN_THREADS / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int2 inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, inc.x, o), y = __shfl_up_sync(0xffffffffu, inc.y, o);
+    if (lane >= o) { inc.x += x; inc.y += y; }
+  }
+  if (lane == 31) ws[warp] = inc;
+  __syncthreads();
+  int2 base = make_int2(0, 0), tot = make_int2(0, 0);
+  for (int w = 0; w < PLAN_THREADS / 32; ++w) {
+    const int2 q = ws[w];
+    if (w < warp) { base.x += q.x; base.y += q.y; }
+    tot.x += q.x; tot.y += q.y;
+  }
+  *total = tot;
+  __syncthreads();
+  return make_int2(base.x + inc.x - v.x, base.y + inc.y - v.y);
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS) k_prefill_plan(const PrefillPlanArgs a) {
+  __shared__ int cnt[1024], start[1024], cursor[1024], toff[1024];
+  const int P = a.T * a.K, tid = threadIdx.x;
+  for (int e = tid; e < 1024; e += PLAN_THREADS) cnt[e] = cursor[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < P; i += PLAN_THREADS) {
+    const int e = a.ids[i];
+    if (e < 0 || e >= a.E) raise_error(a.err, YN_ERR_BAD_EXPERT);
+    else atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  const int c = tid < a.E ? cnt[tid] : 0;
+  int2 tot;
+  const int2 ex = block_scan2(make_int2(c, (c + TC_NMAX - 1) / TC_NMAX), &tot);
+  if (tid < a.E) {
+    start[tid] = ex.x;
+    toff[tid] = ex.y;
+  }
+  __syncthreads();
+  for (int i = tid; i < P; i += PLAN_THREADS) {
+    const int e = a.ids[i];
+    if (e < 0 || e >= a.E) continue;
+    const int pos = start[e] + atomicAdd(&cursor[e], 1);
+    a.pair_row[pos] = i / a.K;
+    a.pair_of[i] = pos;
+  }
+  const int UT = a.I / 64, DT = a.H / 128;
+  if (tid < a.E && c) {
+    for (int k = 0; k * TC_NMAX < c; ++k) {
+      const int p0 = start[tid] + k * TC_NMAX, n = min(TC_NMAX, c - k * TC_NMAX), chunk = toff[tid] + k;
+      for (int u = 0; u < UT; ++u) {
+        const int q = chunk * UT + u;
+        if (q < a.max_up) a.up[q] = TcTile{tid, p0, n, 64 * u};
+      }
+      for (int r = 0; r < DT; ++r) {
+        const int q = chunk * DT + r;
+        if (q < a.max_dn) a.dn[q] = TcTile{tid, p0, n, 128 * r};
+      }
+    }
+  }
+  if (tid == 0) {
+    a.n_tiles[0] = min(tot.y * UT, a.max_up);
+    a.n_tiles[1] = min(tot.y * DT, a.max_dn);
+    if (tot.y * UT > a.max_up || tot.y * DT > a.max_dn) raise_error(a.err, YN_ERR_BAD_SLOT);
+  }
 }
 
 }  // namespace ynb

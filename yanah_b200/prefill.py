@@ -3,11 +3,11 @@ tensor cores (the LFM2-24B-A2B-shaped configuration).
 
 Per layer: post-attention and routing of every prompt row (`yn_rows_route`,
 bit-identical to the single-row path); the rows' fp16 K-permuted copy
-(`yn_to_f16_kperm`); the grouping of the (row, column) pairs by expert, on
-the host, as the reference's prefill sweep plans its staging groups
-(sweep.py:80-138); the grouped gate/up + SwiGLU and down GEMMs
+(`yn_to_f16_kperm`); the grouping of the (row, column) pairs by expert, as
+the reference's prefill sweep plans its staging groups (sweep.py:80-138); the grouped gate/up + SwiGLU and down GEMMs
 (`yn_tc_experts`, 128 weight rows x up to 256 rows per tile); the combine in
-column order plus the residual (`yn_pairs_combine`).
+column order plus the residual (`yn_pairs_combine`). The grouping runs on the
+device (`yn_prefill_plan`); `plan_prefill` is its host restatement.
 """
 from __future__ import annotations
 
@@ -54,7 +54,9 @@ def plan_prefill(ids: np.ndarray, n_experts: int, inter: int, hidden: int):
 
 class PrefillStack:
     """Resident experts and dense weights of `layers` of `cfg`, and the
-    buffers for prompts of up to `max_rows` rows in total."""
+    buffers for prompts of up to `max_rows` rows in total. A layer runs
+    entirely on the device (routing, grouping, GEMMs, combine): no host
+    synchronisation."""
 
     def __init__(self, cfg: StackConfig, max_rows: int, device: str = "cuda",
                  layers: Optional[Sequence[int]] = None):
@@ -76,8 +78,18 @@ class PrefillStack:
         T, P = max_rows, max_rows * K
         dev = self.device
         self.max_rows = max_rows
-        nb = int(lib.yn_rows_route_bytes(C.byref(self.dims)))
+        nb = int(lib.yn_rows_route_bytes(C.byref(self.dims), max_rows))
+        if not nb:
+            raise ValueError("max_rows outside what the routing workspace supports")
         self.route_ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+        mu, md = C.c_int32(0), C.c_int32(0)
+        _lib.check(lib.yn_prefill_max_tiles(C.byref(self.dims), max_rows, C.byref(mu), C.byref(md)))
+        self.max_up, self.max_dn = mu.value, md.value
+        self.tiles_up = torch.empty((self.max_up, 4), dtype=torch.int32, device=dev)
+        self.tiles_dn = torch.empty((self.max_dn, 4), dtype=torch.int32, device=dev)
+        self.n_tiles = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.pair_row = torch.empty(P, dtype=torch.int32, device=dev)
+        self.pair_of = torch.empty(P, dtype=torch.int32, device=dev)
         self.x = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         self.x16 = torch.empty((T, H), dtype=torch.float16, device=dev)
         self.ids = torch.empty((T, K), dtype=torch.int32, device=dev)
@@ -86,42 +98,42 @@ class PrefillStack:
         self.y = torch.empty((P, H), dtype=torch.bfloat16, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.ping = torch.empty((2, T, H), dtype=torch.bfloat16, device=dev)
-        self.last_plan = None
 
     def layer(self, i: int, h: torch.Tensor, out: torch.Tensor, stream=None, gemm_events=None) -> None:
         """Layer i (index into `layer_ids`) of T = h.shape[0] rows. gemm_events:
         optional list that receives (start, end) CUDA events around the two
         grouped GEMM launches."""
         lib, cfg = _lib.lib(), self.cfg
-        T, H, K = h.shape[0], cfg.hidden, cfg.top_k
+        T, H = h.shape[0], cfg.hidden
         if T > self.max_rows:
             raise ValueError("more rows than the buffers hold")
         st = stream_ptr(stream)
-        L = C.byref(self.structs[i])
-        _lib.check(lib.yn_rows_route(C.byref(self.dims), L, h.data_ptr(), T, self.x.data_ptr(), self.ids.data_ptr(),
-                                     self.w.data_ptr(), self.route_ws.data_ptr(), self.route_ws.numel(), st))
+        D, L = C.byref(self.dims), C.byref(self.structs[i])
+        _lib.check(lib.yn_rows_route(D, L, h.data_ptr(), T, self.x.data_ptr(), self.ids.data_ptr(), self.w.data_ptr(),
+                                     self.route_ws.data_ptr(), self.route_ws.numel(), st))
         _lib.check(lib.yn_to_f16_kperm(self.x.data_ptr(), T, H, self.x16.data_ptr(), st))
-        ids = self.ids[:T].cpu().numpy()  # the host plans the groups (one sync per layer)
-        pair_row, pair_of, up, down = plan_prefill(ids, cfg.n_experts, cfg.moe_inter, H)
-        self.last_plan = (ids, pair_row, pair_of)
-        dev = self.device
-        pr = torch.from_numpy(pair_row).to(dev, non_blocking=True)
-        po = torch.from_numpy(pair_of).to(dev, non_blocking=True)
-        tu = torch.from_numpy(up).to(dev, non_blocking=True)
-        td = torch.from_numpy(down).to(dev, non_blocking=True)
+        _lib.check(lib.yn_prefill_plan(D, self.ids.data_ptr(), T, self.pair_row.data_ptr(), self.pair_of.data_ptr(),
+                                       self.tiles_up.data_ptr(), self.max_up, self.tiles_dn.data_ptr(), self.max_dn,
+                                       self.n_tiles.data_ptr(), self.err.data_ptr(), st))
         if gemm_events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        _lib.check(lib.yn_tc_experts(C.byref(self.dims), L, 0, tu.data_ptr(), len(up), self.x16.data_ptr(),
-                                     pr.data_ptr(), self.act.data_ptr(), None, self.err.data_ptr(), st))
-        _lib.check(lib.yn_tc_experts(C.byref(self.dims), L, 1, td.data_ptr(), len(down), self.act.data_ptr(),
+        nt = self.n_tiles.data_ptr()
+        _lib.check(lib.yn_tc_experts(D, L, 0, self.tiles_up.data_ptr(), self.max_up, nt, self.x16.data_ptr(),
+                                     self.pair_row.data_ptr(), self.act.data_ptr(), None, self.err.data_ptr(), st))
+        _lib.check(lib.yn_tc_experts(D, L, 1, self.tiles_dn.data_ptr(), self.max_dn, nt + 4, self.act.data_ptr(),
                                      None, None, self.y.data_ptr(), self.err.data_ptr(), st))
         if gemm_events is not None:
             e1.record(stream)
             gemm_events.append((e0, e1))
-        _lib.check(lib.yn_pairs_combine(C.byref(self.dims), self.y.data_ptr(), po.data_ptr(), self.w.data_ptr(),
-                                        None, h.data_ptr(), T, out.data_ptr(), st))
-        self._keep = (pr, po, tu, td)
+        _lib.check(lib.yn_pairs_combine(D, self.y.data_ptr(), self.pair_of.data_ptr(), self.w.data_ptr(), None,
+                                        h.data_ptr(), T, out.data_ptr(), st))
+
+    def plan(self, T: int):
+        """Host copies of the last layer's ids, pair -> row and (row, column) -> pair."""
+        K = self.cfg.top_k
+        return (self.ids[:T].cpu().numpy(), self.pair_row[:T * K].cpu().numpy(),
+                self.pair_of[:T * K].cpu().numpy().reshape(T, K))
 
     def prefill(self, h: torch.Tensor, stream=None, gemm_events=None) -> torch.Tensor:
         """Every layer for the rows h (T, H) bf16; returns the last layer's output."""
