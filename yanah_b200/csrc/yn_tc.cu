@@ -47,7 +47,7 @@ RouteWs route_ws(const yn_dims& d, int rows) {
 
 size_t tc_smem(int Kd) {
   return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES + TC_C_BYTES) + 2 * (size_t)TC_M * (Kd / 64) * 2 +
-         TC_S * 8 + 16;
+         (2 * TC_S + 4) * 8 + 16;
 }
 }  // namespace
 
@@ -137,8 +137,12 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
                                : reinterpret_cast<const void*>(k_tc_experts<1>);
   int rc = host_set_smem(kern, smem);
   if (rc) return rc;
-  if (mode == 0) k_tc_experts<0><<<n_tiles, TC_THREADS, smem, as_st(stream)>>>(a);
-  else k_tc_experts<1><<<n_tiles, TC_THREADS, smem, as_st(stream)>>>(a);
+  int dev = 0, sms = 0;
+  YN_CUDA_T(cudaGetDevice(&dev));
+  YN_CUDA_T(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = std::max(1, std::min(n_tiles, sms));  // persistent: one CTA per SM walks the tiles
+  if (mode == 0) k_tc_experts<0><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a);
+  else k_tc_experts<1><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a);
   YN_CUDA_T(cudaGetLastError());
   return YN_OK;
 }

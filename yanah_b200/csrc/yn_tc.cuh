@@ -25,8 +25,11 @@
 // ("K-permuted": element 8j + p at 8j + 2p for p < 4, at 8j + 2(p-4) + 1 for
 // p >= 4), which leaves every dot product unchanged.
 //
-// Every wait is bounded; on timeout the error word is set, the CTA drains
-// its committed MMAs (bounded again), frees its TMEM and returns.
+// Warp-specialised and persistent: producer warps, an MMA warp and epilogue
+// warps hand stages and accumulators to each other through mbarriers (see
+// k_tc_experts). Every wait is bounded; on timeout the error word is set,
+// each role leaves its loop, the MMA warp waits (bounded) for its last
+// commit, and TMEM is released.
 #pragma once
 #include "yn_common.cuh"
 #include "yn_moe.cuh"
@@ -142,203 +145,259 @@ YN_DEV bool tc_wait(uint64_t* bar, uint32_t parity, int* err) {
   return mbar_wait_block(bar, parity, err);
 }
 
-// MODE 0: gate/up + SwiGLU with fp16 operands (normalised rows are small);
-// MODE 1: down with bf16 operands (SwiGLU activations have bf16's range, as
-// the reference's bf16 arrays do; fp16 would overflow on them).
+// Producer-side dequantisation of one 64-code stage of this thread's weight
+// row into the swizzled A tile (fp16 for MODE 0, bf16 for MODE 1).
 template <int MODE>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_tc_experts(const TcArgs a) {
+YN_DEV void tc_dequant_row(const uint8_t* codes32, uint16_t sc_bits, uint16_t bi_bits, uint8_t* Arow, int t) {
+  const uint4* cw = reinterpret_cast<const uint4*>(codes32);
+  const uint4 c0 = cw[0], c1 = cw[1];
+  const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const __half sc = __ushort_as_half(sc_bits), bi = __ushort_as_half(bi_bits);
+  const __half2 k1024 = __float2half2_rn(1024.0f);
+  if constexpr (MODE == 0) {  // w = fp16(s * q + b): one HFMA2 per pair
+    const __half2 s1 = __halves2half2(sc, sc);
+    const __half sc16 = __float2half_rn(__fmul_rn(__half2float(sc), 0.0625f));
+    const __half2 s16 = __halves2half2(sc16, sc16);
+    const __half2 b2 = __halves2half2(bi, bi);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint32_t pr[4];
+      tc_unpack4(words[i], pr);
+      uint32_t o[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
+        h = __hsub2(h, k1024);
+        h = __hfma2(h, (p & 1) ? s16 : s1, b2);
+        o[p] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {  // w = bf16(s * q + b) from an fp32 FMA
+    const float s1 = __half2float(sc), s16 = __fmul_rn(s1, 0.0625f), bf = __half2float(bi);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint32_t pr[4];
+      tc_unpack4(words[i], pr);
+      uint32_t o[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
+        h = __hsub2(h, k1024);  // mult * q, exact
+        const float2 q = __half22float2(h);
+        const float m = (p & 1) ? s16 : s1;
+        __nv_bfloat162 w = __floats2bfloat162_rn(__fmaf_rn(q.x, m, bf), __fmaf_rn(q.y, m, bf));
+        o[p] = *reinterpret_cast<uint32_t*>(&w);
+      }
+      *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+YN_DEV void mbar_arrive1(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Warp-specialised persistent form. 288 threads: warps 0-3 produce (thread t
+// dequantises tile row t; all 128 copy the B rows), warps 4-7 drain the
+// accumulator (warp 4 + q reads TMEM lanes 32q..32q+31), warp 8 issues the
+// MMAs. Stage ring: full[s] (128 producer arrivals), empty[s] (MMA commit);
+// accumulator ring of 2 x 256 TMEM columns: acc_full[b] (MMA commit),
+// acc_empty[b] (128 epilogue arrivals). The CTAs walk the planned tiles with
+// stride gridDim.x, so one tile's epilogue overlaps the next tile's main loop.
+// MODE 0: gate/up + SwiGLU, fp16 operands (normalised rows are small);
+// MODE 1: down, bf16 operands (SwiGLU activations have bf16's range, as the
+// reference's bf16 arrays do; fp16 would overflow on them).
+constexpr int TCW_THREADS = 288;
+
+template <int MODE>
+__global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // layout (from a 1024-byte aligned base): [A x S][B x S][codes x S][scales][biases][mbarriers, tmem address]
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* Abuf = smem;
   uint8_t* Bbuf = Abuf + TC_S * TC_A_BYTES;
   uint8_t* Cbuf = Bbuf + TC_S * TC_B_BYTES;
   const int Kd = MODE == 0 ? a.H : a.I;
   const int NG = Kd / 64, NK = Kd / 64;
-  uint16_t* Ssc = reinterpret_cast<uint16_t*>(Cbuf + TC_S * TC_C_BYTES);  // (128, NG) fp16 scales
-  uint16_t* Sbi = Ssc + TC_M * NG;                                         // (128, NG) fp16 biases
-  uint64_t* bars = reinterpret_cast<uint64_t*>(Sbi + TC_M * NG);           // TC_S mma-done barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TC_S);
+  uint16_t* Ssc = reinterpret_cast<uint16_t*>(Cbuf + TC_S * TC_C_BYTES);  // (128, NG) this tile's scales
+  uint16_t* Sbi = Ssc + TC_M * NG;
+  uint64_t* full = reinterpret_cast<uint64_t*>(Sbi + TC_M * NG);
+  uint64_t* empty = full + TC_S;
+  uint64_t* acc_full = empty + TC_S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   __shared__ int rows_s[TC_NMAX];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (blockIdx.x >= (a.n_tiles_dev ? min(a.n_tiles, *a.n_tiles_dev) : a.n_tiles)) return;
-  const TcTile tl = a.tiles[blockIdx.x];
-  const int n = tl.n, nmma = (n + 15) & ~15;
-  const int slot = a.slot_of ? a.slot_of[tl.e] : tl.e;
-  if (n < 1 || n > TC_NMAX || slot < 0 || slot >= a.n_slots) {
-    if (tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
-    return;
-  }
-  const uint8_t* rec = a.base + (size_t)slot * (size_t)a.stride;
-  const int RB = Kd / 2;  // 4-bit code bytes per row
-
-  // weight row of tile row t in the record, and its piece (weight/scales/biases offsets)
-  const int t = tid;  // this thread's tile row
-  int wrow;
-  long long off_w, off_s, off_b;
-  if (MODE == 0) {
-    const bool up = t & 1;
-    wrow = tl.u0 + (t >> 1);
-    off_w = a.rg.off[up ? 3 : 0];
-    off_s = a.rg.off[up ? 4 : 1];
-    off_b = a.rg.off[up ? 5 : 2];
-  } else {
-    wrow = tl.u0 + t;
-    off_w = a.rg.off[6];
-    off_s = a.rg.off[7];
-    off_b = a.rg.off[8];
-  }
-  const uint8_t* wsrc = rec + off_w + (size_t)wrow * RB;
-
-  for (int i = tid; i < n; i += TC_THREADS) rows_s[i] = a.pair_row ? a.pair_row[tl.p0 + i] : tl.p0 + i;
+  const int n_tiles = a.n_tiles_dev ? min(a.n_tiles, *a.n_tiles_dev) : a.n_tiles;
   if (tid == 0) {
-    for (int s = 0; s < TC_S; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < TC_S; ++s) {
+      mbar_init(&full[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     fence_mbar_init();
   }
-  // scales and biases of this thread's row, all groups (NG * 2 bytes each, 16-byte pieces)
-  for (int q = 0; q < NG * 2 / 16; ++q) {
-    tc_cpa16(reinterpret_cast<uint8_t*>(Ssc) + (size_t)t * NG * 2 + 16 * q, rec + off_s + (size_t)wrow * NG * 2 + 16 * q);
-    tc_cpa16(reinterpret_cast<uint8_t*>(Sbi) + (size_t)t * NG * 2 + 16 * q, rec + off_b + (size_t)wrow * NG * 2 + 16 * q);
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot)));
+  if (warp == 8) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  __syncthreads();  // rows_s, barriers, TMEM address
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  // producer: stage kc's codes (this thread's row) and B rows
-  auto issue = [&](int kc) {
-    const int s = kc % TC_S;
-    uint8_t* cd = Cbuf + s * TC_C_BYTES + t * 32;
-    tc_cpa16(cd, wsrc + 32 * kc);
-    tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
-    uint8_t* B = Bbuf + s * TC_B_BYTES;
-    for (int i = tid; i < n * 8; i += TC_THREADS) {
-      const int r = i >> 3, c = i & 7;
-      const uint16_t* src = a.b_rows + (size_t)rows_s[r] * Kd + 64 * kc + 8 * c;
-      tc_cpa16(B + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4), src);
-    }
-  };
-
   bool ok = true;
-  constexpr int P = 2;  // stages issued ahead
-  for (int kc = 0; kc < P && kc < NK; ++kc) {
-    issue(kc);
-    tc_cpa_commit();
-  }
-  for (int kc = 0; kc < NK && ok; ++kc) {
-    const int s = kc % TC_S;
-    // stage kc + P reuses the buffers of stage kc + P - TC_S: its MMAs must be done
-    const int kn = kc + P;
-    if (kn < NK) {
-      if (kn >= TC_S) ok = tc_wait(&bars[kn % TC_S], ((kn - TC_S) / TC_S) & 1, a.err);
-      if (ok) issue(kn);
-    }
-    tc_cpa_commit();
-    tc_cpa_wait<P>();  // stage kc's copies (this thread's) have landed
-    __syncthreads();   // ... and every thread's
-    if (!ok) break;
-    // dequantise this thread's row of stage kc into A (fp16, K-permuted, swizzled)
-    {
-      const uint4* cw = reinterpret_cast<const uint4*>(Cbuf + s * TC_C_BYTES + t * 32);
-      const uint4 c0 = cw[0], c1 = cw[1];
-      const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      const __half sc = __ushort_as_half(Ssc[t * NG + kc]), bi = __ushort_as_half(Sbi[t * NG + kc]);
-      const __half2 k1024 = __float2half2_rn(1024.0f);
-      uint8_t* Arow = Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
-      if constexpr (MODE == 0) {  // w = fp16(s * q + b): one HFMA2 per pair
-        const __half2 s1 = __halves2half2(sc, sc);
-        const __half sc16 = __float2half_rn(__fmul_rn(__half2float(sc), 0.0625f));
-        const __half2 s16 = __halves2half2(sc16, sc16);
-        const __half2 b2 = __halves2half2(bi, bi);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint32_t pr[4];
-          tc_unpack4(words[i], pr);
-          uint32_t o[4];
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
-            h = __hsub2(h, k1024);
-            h = __hfma2(h, (p & 1) ? s16 : s1, b2);
-            o[p] = *reinterpret_cast<uint32_t*>(&h);
-          }
-          *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-      } else {  // w = bf16(s * q + b) from an fp32 FMA
-        const float s1 = __half2float(sc), s16 = __fmul_rn(s1, 0.0625f), bf = __half2float(bi);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint32_t pr[4];
-          tc_unpack4(words[i], pr);
-          uint32_t o[4];
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
-            h = __hsub2(h, k1024);  // mult * q, exact
-            const float2 q = __half22float2(h);
-            const float m = (p & 1) ? s16 : s1;
-            __nv_bfloat162 w = __floats2bfloat162_rn(__fmaf_rn(q.x, m, bf), __fmaf_rn(q.y, m, bf));
-            o[p] = *reinterpret_cast<uint32_t*>(&w);
-          }
-          *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t abase = smem_u32(Abuf + s * TC_A_BYTES), bbase = smem_u32(Bbuf + s * TC_B_BYTES);
-      const uint32_t idesc = tc_idesc(nmma, MODE == 1);
-#pragma unroll
-      for (int k16 = 0; k16 < 4; ++k16)
-        tc_mma(tmem, tc_desc(abase + 32 * k16), tc_desc(bbase + 32 * k16), idesc, (kc > 0 || k16 > 0) ? 1u : 0u);
-      tc_commit(&bars[s]);
-    }
-  }
-  tc_cpa_wait<0>();
-  // the accumulator is complete when the last stage's commit has arrived
-  if (ok) ok = tc_wait(&bars[(NK - 1) % TC_S], ((NK - 1) / TC_S) & 1, a.err);
-  tc_fence_after();
-  if (ok) {
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
-    const int m = 32 * warp + lane;  // tile row of this thread
-    for (int c0 = 0; c0 < nmma; c0 += 32) {
-      float v[32];
-      tc_ld32(lane_base + (uint32_t)c0, v);
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ producers
+    const int t = tid;
+    int g = 0;  // stages produced by this CTA so far
+    for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x) {
+      const TcTile tl = a.tiles[ti];
+      const int n = tl.n;
+      const int slot = a.slot_of ? a.slot_of[tl.e] : tl.e;
+      const bool good = n >= 1 && n <= TC_NMAX && slot >= 0 && slot < a.n_slots;
+      if (!good && t == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
+      const uint8_t* rec = a.base + (size_t)(good ? slot : 0) * (size_t)a.stride;
+      int wrow;
+      long long off_w, off_s, off_b;
       if (MODE == 0) {
-        const int unit = tl.u0 + (m >> 1);
-        const int ku = kperm(unit);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
-          const int col = c0 + j;
-          if (!(m & 1) && col < n) {
-            const float g = bf16r(v[j]), u = bf16r(other);
-            const float act = swiglu_bf16(g, u);
-            a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(act);
+        const bool up = t & 1;
+        wrow = tl.u0 + (t >> 1);
+        off_w = a.rg.off[up ? 3 : 0];
+        off_s = a.rg.off[up ? 4 : 1];
+        off_b = a.rg.off[up ? 5 : 2];
+      } else {
+        wrow = tl.u0 + t;
+        off_w = a.rg.off[6];
+        off_s = a.rg.off[7];
+        off_b = a.rg.off[8];
+      }
+      const uint8_t* wsrc = rec + off_w + (size_t)wrow * (Kd / 2);
+      const int nn = good ? n : 0;  // a bad tile still walks its stages (no copies) so every role stays in step
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // every producer is done with the previous rows_s
+      for (int i = t; i < nn; i += 128) rows_s[i] = a.pair_row ? a.pair_row[tl.p0 + i] : tl.p0 + i;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // this thread's scale / bias row (read back only by this thread)
+      if (good)
+        for (int q = 0; q < NG * 2 / 16; ++q) {
+          tc_cpa16(reinterpret_cast<uint8_t*>(Ssc) + (size_t)t * NG * 2 + 16 * q, rec + off_s + (size_t)wrow * NG * 2 + 16 * q);
+          tc_cpa16(reinterpret_cast<uint8_t*>(Sbi) + (size_t)t * NG * 2 + 16 * q, rec + off_b + (size_t)wrow * NG * 2 + 16 * q);
+        }
+      auto issue = [&](int kc) -> bool {
+        const int gg = g + kc, s = gg % TC_S;
+        if (gg >= TC_S && !mbar_wait_bounded(&empty[s], ((gg / TC_S) - 1) & 1, a.err)) return false;
+        if (good) {
+          uint8_t* cd = Cbuf + s * TC_C_BYTES + t * 32;
+          tc_cpa16(cd, wsrc + 32 * kc);
+          tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
+          uint8_t* B = Bbuf + s * TC_B_BYTES;
+          for (int i = t; i < nn * 8; i += 128) {
+            const int r = i >> 3, c = i & 7;
+            tc_cpa16(B + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4),
+                     a.b_rows + (size_t)rows_s[r] * Kd + 64 * kc + 8 * c);
           }
         }
-      } else {
-        const int row = tl.u0 + m;
+        return true;
+      };
+      constexpr int P = 2;
+      for (int kc = 0; kc < P && kc < NK && ok; ++kc) {
+        ok = issue(kc);
+        tc_cpa_commit();
+      }
+      for (int kc = 0; kc < NK && ok; ++kc) {
+        const int s = (g + kc) % TC_S;
+        if (kc + P < NK) ok = issue(kc + P);
+        tc_cpa_commit();
+        tc_cpa_wait<P>();
+        if (!ok) break;
+        if (good)
+          tc_dequant_row<MODE>(Cbuf + s * TC_C_BYTES + t * 32, Ssc[t * NG + kc], Sbi[t * NG + kc],
+                               Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive1(&full[s]);
+      }
+      tc_cpa_wait<0>();
+      g += NK;
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp - 4, m = 32 * q + lane;  // tile row of this thread
+    int j = 0;
+    for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x, ++j) {
+      const TcTile tl = a.tiles[ti];
+      const int n = tl.n, nmma = (n + 15) & ~15, b = j & 1;
+      ok = mbar_wait_bounded(&acc_full[b], (j >> 1) & 1, a.err);
+      ok = __all_sync(0xffffffffu, ok) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t base = tmem + (uint32_t)(b * 256) + ((uint32_t)(32 * q) << 16);
+      const bool good = n >= 1 && n <= TC_NMAX;
+      for (int c0 = 0; c0 < nmma; c0 += 32) {
+        float v[32];
+        tc_ld32(base + (uint32_t)c0, v);
+        if (!good) continue;
+        if (MODE == 0) {
+          // lanes 2i (gate of unit u) and 2i+1 (up of unit u) split the columns
+          const int ku = kperm(tl.u0 + (m >> 1));
+          const bool is_up = m & 1;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int col = c0 + j;
-          if (col < n) a.y_out[(size_t)(tl.p0 + col) * a.H + row] = f32_to_bf16(v[j]);
+          for (int jj = 0; jj < 32; ++jj) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[jj], 1);
+            const int col = c0 + jj;
+            if ((jj & 1) == (int)is_up && col < n) {
+              const float gv = bf16r(is_up ? other : v[jj]), uv = bf16r(is_up ? v[jj] : other);
+              a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(swiglu_bf16(gv, uv));
+            }
+          }
+        } else {
+          const int row = tl.u0 + m;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj)
+            if (c0 + jj < n) a.y_out[(size_t)(tl.p0 + c0 + jj) * a.H + row] = f32_to_bf16(v[jj]);
         }
       }
+      tc_fence_before();
+      mbar_arrive1(&acc_empty[b]);
     }
   } else {
-    // drain: every committed stage completes before TMEM is released (bounded)
-    for (int s = 0; s < TC_S; ++s) (void)mbar_wait_bounded(&bars[s], 0, a.err);
+    // ------------------------------------------------------------------ MMA
+    int g = 0, j = 0;
+    for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x, ++j) {
+      const TcTile tl = a.tiles[ti];
+      const int nmma = ((tl.n >= 1 && tl.n <= TC_NMAX ? tl.n : 16) + 15) & ~15, b = j & 1;
+      if (j >= 2) ok = mbar_wait_bounded(&acc_empty[b], ((j >> 1) - 1) & 1, a.err);
+      ok = __all_sync(0xffffffffu, ok) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t idesc = tc_idesc(nmma, MODE == 1), dcol = tmem + (uint32_t)(b * 256);
+      for (int kc = 0; kc < NK && ok; ++kc, ++g) {
+        const int s = g % TC_S;
+        ok = mbar_wait_bounded(&full[s], (g / TC_S) & 1, a.err);
+        ok = __all_sync(0xffffffffu, ok) != 0;
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t abase = smem_u32(Abuf + s * TC_A_BYTES), bbase = smem_u32(Bbuf + s * TC_B_BYTES);
+#pragma unroll
+          for (int k16 = 0; k16 < 4; ++k16)
+            tc_mma(dcol, tc_desc(abase + 32 * k16), tc_desc(bbase + 32 * k16), idesc, (kc > 0 || k16 > 0) ? 1u : 0u);
+          tc_commit(&empty[s]);
+          if (kc == NK - 1) tc_commit(&acc_full[b]);
+        }
+        __syncwarp();
+      }
+    }
+    // the last commits must land before TMEM is released (bounded)
+    if (lane == 0 && j > 0) (void)mbar_wait_bounded(&acc_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err);
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  tc_fence_after();
+  if (warp == 8) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
 
 }  // namespace ynb
