@@ -106,7 +106,7 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   if (r.bits != 4 || r.group_size != 64)
     return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: routed experts must be 4-bit g64");
   const int H = dims->hidden, I = dims->moe_inter;
-  if (H % 512 || I % 512)  // whole 128-row down tiles, 64-unit gate/up tiles, 16-byte scale rows
+  if (H % 512 || I % 512)  // whole 128-row down tiles, 64-unit gate/up tiles, scale rows in 8-group blocks
     return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: hidden and moe_inter must be multiples of 512");
   if (!layer->expert_base || reinterpret_cast<uintptr_t>(layer->expert_base) % 16 || layer->slot_stride % 16)
     return host_fail(YN_E_INVALID, "expert arena and slot stride must be 16-byte aligned");

@@ -194,6 +194,15 @@ YN_DEV void tc_dequant_row(const uint8_t* codes32, uint16_t sc_bits, uint16_t bi
   }
 }
 
+// SwiGLU with the same bf16 rounding points as swiglu_bf16, but the sigmoid
+// from the hardware exponential and an approximate divide: these outputs are
+// held to the bf16 output tolerance, not to bit equality, and the epilogue
+// evaluates one per (row, unit).
+YN_DEV float swiglu_bf16_fast(float g, float u) {
+  const float sg = bf16r(__fdividef(1.0f, 1.0f + __expf(-g)));
+  return bf16r(__fmul_rn(bf16r(__fmul_rn(g, sg)), u));
+}
+
 YN_DEV void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -307,17 +316,32 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
         ok = issue(kc);
         tc_cpa_commit();
       }
-      for (int kc = 0; kc < NK && ok; ++kc) {
-        const int s = (g + kc) % TC_S;
-        if (kc + P < NK) ok = issue(kc + P);
-        tc_cpa_commit();
-        tc_cpa_wait<P>();
-        if (!ok) break;
-        if (good)
-          tc_dequant_row<MODE>(Cbuf + s * TC_C_BYTES + t * 32, Ssc[t * NG + kc], Sbi[t * NG + kc],
-                               Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive1(&full[s]);
+      // stages in blocks of 8 (NK is a multiple of 8): the block's 8 scales and
+      // biases of this row come from shared memory as two 16-byte loads
+      uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8;
+      for (int kc0 = 0; kc0 < NK && ok; kc0 += 8) {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int kc = kc0 + jj;
+          const int s = (g + kc) % TC_S;
+          if (kc + P < NK) ok = issue(kc + P);
+          tc_cpa_commit();
+          tc_cpa_wait<P>();
+          if (!ok) break;
+          if (good) {
+            if (jj == 0) {
+              s8 = *reinterpret_cast<const uint4*>(Ssc + t * NG + kc0);
+              b8 = *reinterpret_cast<const uint4*>(Sbi + t * NG + kc0);
+            }
+            const uint32_t sw = jj < 2 ? s8.x : jj < 4 ? s8.y : jj < 6 ? s8.z : s8.w;
+            const uint32_t bw = jj < 2 ? b8.x : jj < 4 ? b8.y : jj < 6 ? b8.z : b8.w;
+            tc_dequant_row<MODE>(Cbuf + s * TC_C_BYTES + t * 32, (uint16_t)(sw >> (16 * (jj & 1))),
+                                 (uint16_t)(bw >> (16 * (jj & 1))),
+                                 Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive1(&full[s]);
+        }
       }
       tc_cpa_wait<0>();
       g += NK;
@@ -349,7 +373,7 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
             const int col = c0 + jj;
             if ((jj & 1) == (int)is_up && col < n) {
               const float gv = bf16r(is_up ? other : v[jj]), uv = bf16r(is_up ? v[jj] : other);
-              a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(swiglu_bf16(gv, uv));
+              a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(swiglu_bf16_fast(gv, uv));
             }
           }
         } else {
