@@ -316,15 +316,19 @@ typedef struct yn_tc_tile {
 } yn_tc_tile;
 
 /* mode 0 (mlx_backend.py:447-456 `_switch_glu` up to SwiGLU): for every tile,
- * act_out[p][kperm(u)] = bf16(swiglu(gate_u . x, up_u . x)) with x =
- * b_rows[pair_row[p]] (fp16 K-permuted rows of H; weights dequantised to
- * fp16). mode 1 (the down projection): y_out[p][h] = bf16(down_h . act_p)
- * with act_p = b_rows[p] (bf16 K-permuted rows of I; weights dequantised to
- * bf16). Routed experts 4-bit g64 only. tiles: device array. err: device
- * error word (bounded waits, bad slots). */
+ * act_out[p][kperm(u)] = bf16(swiglu(gate_u . x_p, up_u . x_p)) with x_p =
+ * b_rows[p] (fp16 K-permuted rows of H in pair order, yn_gather_f16_kperm;
+ * weights dequantised to fp16). mode 1 (the down projection): y_out[p][h] =
+ * bf16(down_h . act_p) with act_p = b_rows[p] (bf16 K-permuted rows of I;
+ * weights dequantised to bf16). b_rows holds n_rows rows (read through TMA
+ * tensor maps; 16-byte aligned). Routed experts 4-bit g64 only. tiles:
+ * device array. err: device error word (bounded waits, bad slots). */
 int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
-                  int32_t n_tiles, const int32_t* n_tiles_dev, const void* b_rows, const int32_t* pair_row,
+                  int32_t n_tiles, const int32_t* n_tiles_dev, const void* b_rows, int64_t n_rows,
                   void* act_out, void* y_out, int32_t* err, void* stream);
+/* The gate/up GEMM's rows in pair order: out[p] = fp16 K-permuted copy of
+ * x[row_of[p]] (bf16 rows of `cols`). */
+int yn_gather_f16_kperm(const void* x, const int32_t* row_of, int64_t rows, int32_t cols, void* out, void* stream);
 
 /* The grouping on the device, so that a prefill layer needs no host
  * synchronisation: pairs of each expert made contiguous (pair_row: pair ->

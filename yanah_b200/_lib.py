@@ -117,7 +117,8 @@ _SIGS = {
     "yn_rows_route": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _I, _P, _P, _P, _P, C.c_size_t, _P]),
     "yn_route_error": (C.c_int, [_P, C.POINTER(Dims), _P, C.POINTER(C.c_int32)]),
     "yn_to_f16_kperm": (C.c_int, [_P, C.c_int64, _I, _P, _P]),
-    "yn_tc_experts": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _I, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "yn_tc_experts": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _I, _P, _I, _P, _P, C.c_int64, _P, _P, _P, _P]),
+    "yn_gather_f16_kperm": (C.c_int, [_P, _P, C.c_int64, _I, _P, _P]),
     "yn_prefill_max_tiles": (C.c_int, [C.POINTER(Dims), _I, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "yn_prefill_plan": (C.c_int, [C.POINTER(Dims), _P, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P]),
     "yn_pairs_combine": (C.c_int, [C.POINTER(Dims), _P, _P, _P, _P, _P, _I, _P, _P]),

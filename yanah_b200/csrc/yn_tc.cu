@@ -1,8 +1,10 @@
 // C ABI of the tensor-core grouped expert GEMM (prefill) and its helpers:
 // routing of many rows, fp16 K-permuted activations, the pair combine.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "yanah_b200.h"
@@ -45,6 +47,50 @@ RouteWs route_ws(const yn_dims& d, int rows) {
   return L;
 }
 
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+int encode_fn(EncodeTiled* out) {
+  static std::mutex mu;
+  static EncodeTiled fn = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    YN_CUDA_T(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (!p || q != cudaDriverEntryPointSuccess)
+      return host_fail(YN_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  *out = fn;
+  return YN_OK;
+}
+
+// Row maps over `rows` rows of `cols` 16-bit elements: boxes of 64 elements x
+// 16 << i rows, 128-byte swizzle (the UMMA K-major layout), zero fill.
+int make_row_maps(const void* base, long long rows, int cols, bool bf16, TcMaps* maps) {
+  EncodeTiled fn;
+  int rc = encode_fn(&fn);
+  if (rc) return rc;
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (cols * 2) % 16)
+    return host_fail(YN_E_INVALID, "tensor-map rows must be 16-byte aligned");
+  for (int i = 0; i < TC_NMAPS; ++i) {
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)(16 << i)};
+    const cuuint32_t elem[2] = {1u, 1u};
+    const CUresult r = fn(&maps->m[i], bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                          const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return host_fail(YN_E_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  }
+  return YN_OK;
+}
+
 size_t tc_smem(int Kd) {
   return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES + TC_C_BYTES) + 2 * (size_t)TC_M * (Kd / 64) * 2 +
          (2 * TC_S + 4) * 8 + 16;
@@ -85,6 +131,17 @@ extern "C" int yn_route_error(void* ws, const yn_dims* dims, void* stream, int32
   return YN_OK;
 }
 
+extern "C" int yn_gather_f16_kperm(const void* x, const int32_t* row_of, int64_t rows, int32_t cols, void* out,
+                                   void* stream) {
+  if (!x || !row_of || !out || rows < 1 || cols < 8 || cols % 8) return host_fail(YN_E_INVALID, "bad rows/cols or null");
+  const long long n = rows * (long long)cols;
+  const int grid = (int)std::min<long long>((n / 8 + 255) / 256, 8192);
+  k_gather_f16_kperm<<<grid, 256, 0, as_st(stream)>>>(reinterpret_cast<const uint16_t*>(x), row_of, rows, cols,
+                                                      reinterpret_cast<uint16_t*>(out));
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}
+
 extern "C" int yn_to_f16_kperm(const void* x, int64_t rows, int32_t cols, void* out, void* stream) {
   if (!x || !out || rows < 1 || cols < 8 || cols % 8) return host_fail(YN_E_INVALID, "bad rows/cols or null");
   const long long n = rows * (long long)cols;
@@ -96,11 +153,12 @@ extern "C" int yn_to_f16_kperm(const void* x, int64_t rows, int32_t cols, void* 
 }
 
 extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t mode, const yn_tc_tile* tiles,
-                             int32_t n_tiles, const int32_t* n_tiles_dev, const void* b_rows, const int32_t* pair_row,
+                             int32_t n_tiles, const int32_t* n_tiles_dev, const void* b_rows, int64_t n_rows,
                              void* act_out, void* y_out, int32_t* err, void* stream) {
   if (!dims || !layer || !tiles || !b_rows || !err) return host_fail(YN_E_INVALID, "null argument");
+  if (n_rows < 1) return host_fail(YN_E_INVALID, "n_rows must be positive");
   if (mode != 0 && mode != 1) return host_fail(YN_E_INVALID, "mode must be 0 (gate/up) or 1 (down)");
-  if (mode == 0 && (!act_out || !pair_row)) return host_fail(YN_E_INVALID, "gate/up needs act_out and pair_row");
+  if (mode == 0 && !act_out) return host_fail(YN_E_INVALID, "gate/up needs act_out");
   if (mode == 1 && !y_out) return host_fail(YN_E_INVALID, "down needs y_out");
   const yn_record& r = layer->record;
   if (r.bits != 4 || r.group_size != 64)
@@ -117,8 +175,6 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   a.tiles = reinterpret_cast<const TcTile*>(tiles);
   a.n_tiles = n_tiles;
   a.n_tiles_dev = n_tiles_dev;
-  a.b_rows = reinterpret_cast<const uint16_t*>(b_rows);
-  a.pair_row = pair_row;
   a.base = reinterpret_cast<const uint8_t*>(layer->expert_base);
   a.stride = layer->slot_stride;
   a.slot_of = layer->expert_slot;
@@ -141,8 +197,10 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   YN_CUDA_T(cudaGetDevice(&dev));
   YN_CUDA_T(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::max(1, std::min(n_tiles, sms));  // persistent: one CTA per SM walks the tiles
-  if (mode == 0) k_tc_experts<0><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a);
-  else k_tc_experts<1><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a);
+  TcMaps maps;
+  if ((rc = make_row_maps(b_rows, n_rows, mode == 0 ? H : I, mode == 1, &maps))) return rc;
+  if (mode == 0) k_tc_experts<0><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a, maps);
+  else k_tc_experts<1><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a, maps);
   YN_CUDA_T(cudaGetLastError());
   return YN_OK;
 }

@@ -31,6 +31,8 @@
 // each role leaves its loop, the MMA warp waits (bounded) for its last
 // commit, and TMEM is released.
 #pragma once
+#include <cuda.h>
+
 #include "yn_common.cuh"
 #include "yn_moe.cuh"
 #include "yn_mma.cuh"
@@ -52,12 +54,18 @@ struct TcTile {
   int u0;      // gate/up: first unit (64 per tile); down: first output row (128 per tile)
 };
 
+// Tensor maps of the B rows (rows of the batch in pair order, 64-element x
+// box-row boxes, 128-byte swizzle): box heights 16, 32, 64, 128, 256.
+constexpr int TC_NMAPS = 5;
+struct TcMaps {
+  CUtensorMap m[TC_NMAPS];
+};
+
 struct TcArgs {
   const TcTile* tiles;
   int n_tiles;                 // capacity of `tiles` (grid size)
   const int* n_tiles_dev;      // tiles actually planned (device), or null for n_tiles
-  const uint16_t* b_rows;      // K-permuted rows: gate/up fp16 x' (rows by token), down bf16 act' (rows by pair)
-  const int32_t* pair_row;     // mode 0: pair -> row of b_rows; mode 1: null (row = pair)
+  // B rows (K-permuted, by pair: gate/up fp16 x, down bf16 SwiGLU activations) come through the tensor maps
   const uint8_t* base;         // expert arena
   long long stride;
   const int32_t* slot_of;      // expert -> slot or null (slot = expert)
@@ -203,6 +211,13 @@ YN_DEV float swiglu_bf16_fast(float g, float u) {
   return bf16r(__fmul_rn(bf16r(__fmul_rn(g, sg)), u));
 }
 
+YN_DEV void tc_tma_rows(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 YN_DEV void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -220,7 +235,7 @@ YN_DEV void mbar_arrive1(uint64_t* bar) {
 constexpr int TCW_THREADS = 288;
 
 template <int MODE>
-__global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
+__global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, const __grid_constant__ TcMaps maps) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* Abuf = smem;
@@ -235,13 +250,12 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
   uint64_t* acc_full = empty + TC_S;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  __shared__ int rows_s[TC_NMAX];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tiles = a.n_tiles_dev ? min(a.n_tiles, *a.n_tiles_dev) : a.n_tiles;
   if (tid == 0) {
     for (int s = 0; s < TC_S; ++s) {
-      mbar_init(&full[s], 128);
+      mbar_init(&full[s], 129);  // 128 dequantising threads + the TMA transaction's expect_tx
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -285,10 +299,10 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
         off_b = a.rg.off[8];
       }
       const uint8_t* wsrc = rec + off_w + (size_t)wrow * (Kd / 2);
-      const int nn = good ? n : 0;  // a bad tile still walks its stages (no copies) so every role stays in step
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // every producer is done with the previous rows_s
-      for (int i = t; i < nn; i += 128) rows_s[i] = a.pair_row ? a.pair_row[tl.p0 + i] : tl.p0 + i;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // B box: the smallest map whose height covers the tile's MMA width
+      const int nmma = ((good ? n : 16) + 15) & ~15;
+      const int mi = nmma <= 16 ? 0 : nmma <= 32 ? 1 : nmma <= 64 ? 2 : nmma <= 128 ? 3 : 4;
+      const uint32_t box_bytes = (16u << mi) * 128u;
       // this thread's scale / bias row (read back only by this thread)
       if (good)
         for (int q = 0; q < NG * 2 / 16; ++q) {
@@ -302,12 +316,10 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a) {
           uint8_t* cd = Cbuf + s * TC_C_BYTES + t * 32;
           tc_cpa16(cd, wsrc + 32 * kc);
           tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
-          uint8_t* B = Bbuf + s * TC_B_BYTES;
-          for (int i = t; i < nn * 8; i += 128) {
-            const int r = i >> 3, c = i & 7;
-            tc_cpa16(B + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4),
-                     a.b_rows + (size_t)rows_s[r] * Kd + 64 * kc + 8 * c);
-          }
+        }
+        if (t == 0) {  // the stage's B rows: one TMA copy (rows past the batch read as zeros)
+          mbar_arrive_expect_tx(&full[s], good ? box_bytes : 0u);
+          if (good) tc_tma_rows(Bbuf + s * TC_B_BYTES, &maps.m[mi], 64 * kc, tl.p0, &full[s]);
         }
         return true;
       };
@@ -434,6 +446,31 @@ __global__ void k_to_f16_kperm(const uint16_t* x, long long n, int cols, uint16_
     const long long r = i / cols;
     const int k = (int)(i - r * cols);
     out[r * cols + kperm(k)] = __half_as_ushort(__float2half_rn(bf16_to_f32(x[i])));
+  }
+}
+
+// out[p] = fp16 K-permuted copy of row row_of[p] of x (bf16): one 8-element
+// block (16-byte load, 16-byte store) per thread step.
+__global__ void k_gather_f16_kperm(const uint16_t* x, const int32_t* row_of, long long rows, int cols, uint16_t* out) {
+  const long long nb = rows * (cols / 8);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nb; i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i / (cols / 8);
+    const int blk = (int)(i - p * (cols / 8));
+    const uint4 v = reinterpret_cast<const uint4*>(x + (size_t)row_of[p] * cols)[blk];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      f[2 * e] = bf16_to_f32((uint16_t)(w[e] & 0xFFFFu));
+      f[2 * e + 1] = bf16_to_f32((uint16_t)(w[e] >> 16));
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // positions 2q, 2q+1 hold elements q, q+4
+      __half2 h = __floats2half2_rn(f[q], f[q + 4]);
+      o[q] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    reinterpret_cast<uint4*>(out + (size_t)p * cols)[blk] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 

@@ -3,7 +3,7 @@ tensor cores (the LFM2-24B-A2B-shaped configuration).
 
 Per layer: post-attention and routing of every prompt row (`yn_rows_route`,
 bit-identical to the single-row path); the rows' fp16 K-permuted copy
-(`yn_to_f16_kperm`); the grouping of the (row, column) pairs by expert, as
+(`yn_gather_f16_kperm`, in pair order); the grouping of the (row, column) pairs by expert, as
 the reference's prefill sweep plans its staging groups (sweep.py:80-138); the grouped gate/up + SwiGLU and down GEMMs
 (`yn_tc_experts`, 128 weight rows x up to 256 rows per tile); the combine in
 column order plus the residual (`yn_pairs_combine`). The grouping runs on the
@@ -91,7 +91,7 @@ class PrefillStack:
         self.pair_row = torch.empty(P, dtype=torch.int32, device=dev)
         self.pair_of = torch.empty(P, dtype=torch.int32, device=dev)
         self.x = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-        self.x16 = torch.empty((T, H), dtype=torch.float16, device=dev)
+        self.x16 = torch.empty((P, H), dtype=torch.float16, device=dev)  # rows in pair order
         self.ids = torch.empty((T, K), dtype=torch.int32, device=dev)
         self.w = torch.empty((T, K), dtype=torch.float32, device=dev)
         self.act = torch.empty((P, I), dtype=torch.bfloat16, device=dev)
@@ -111,18 +111,19 @@ class PrefillStack:
         D, L = C.byref(self.dims), C.byref(self.structs[i])
         _lib.check(lib.yn_rows_route(D, L, h.data_ptr(), T, self.x.data_ptr(), self.ids.data_ptr(), self.w.data_ptr(),
                                      self.route_ws.data_ptr(), self.route_ws.numel(), st))
-        _lib.check(lib.yn_to_f16_kperm(self.x.data_ptr(), T, H, self.x16.data_ptr(), st))
         _lib.check(lib.yn_prefill_plan(D, self.ids.data_ptr(), T, self.pair_row.data_ptr(), self.pair_of.data_ptr(),
                                        self.tiles_up.data_ptr(), self.max_up, self.tiles_dn.data_ptr(), self.max_dn,
                                        self.n_tiles.data_ptr(), self.err.data_ptr(), st))
+        P = T * cfg.top_k
+        _lib.check(lib.yn_gather_f16_kperm(self.x.data_ptr(), self.pair_row.data_ptr(), P, H, self.x16.data_ptr(), st))
         if gemm_events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
         nt = self.n_tiles.data_ptr()
-        _lib.check(lib.yn_tc_experts(D, L, 0, self.tiles_up.data_ptr(), self.max_up, nt, self.x16.data_ptr(),
-                                     self.pair_row.data_ptr(), self.act.data_ptr(), None, self.err.data_ptr(), st))
-        _lib.check(lib.yn_tc_experts(D, L, 1, self.tiles_dn.data_ptr(), self.max_dn, nt + 4, self.act.data_ptr(),
-                                     None, None, self.y.data_ptr(), self.err.data_ptr(), st))
+        _lib.check(lib.yn_tc_experts(D, L, 0, self.tiles_up.data_ptr(), self.max_up, nt, self.x16.data_ptr(), P,
+                                     self.act.data_ptr(), None, self.err.data_ptr(), st))
+        _lib.check(lib.yn_tc_experts(D, L, 1, self.tiles_dn.data_ptr(), self.max_dn, nt + 4, self.act.data_ptr(), P,
+                                     None, self.y.data_ptr(), self.err.data_ptr(), st))
         if gemm_events is not None:
             e1.record(stream)
             gemm_events.append((e0, e1))
