@@ -522,6 +522,100 @@ def run_prefill(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# -------------------------------------------------------------- verify leg
+VERIFY_METRIC = "speculative-verify tok/s, 1+4 rows per step (LFM2-24B-A2B-shaped, 40 layers), union-of-experts batch"
+
+
+def run_verify(args, rank: int, world: int):
+    """Config 3, verify batches: 1 + 4 draft rows per step through the 40
+    LFM2-shaped layers on the batch path (each routed expert record read
+    once per layer however many of the 5 rows chose it). HBM-bound: the
+    roofline counts each distinct expert record a layer routes to once."""
+    import numpy as np
+    import torch
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.ep import ExpertParallelStack
+    from yanah_b200.synthetic import hidden_stream_id, lfm2_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = lfm2_stack(seed=0)
+    B = 5
+    layer_ids = list(range(args.first_layer, args.first_layer + (args.layers or cfg.n_layers)))
+    stack = ExpertParallelStack(cfg, batch=B, device=dev, layers=layer_ids)
+    H, K, L = cfg.hidden, cfg.top_k, len(layer_ids)
+    rows = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(rows.data_ptr(), B * H, cfg.seed, hidden_stream_id(700), 1.0, 0.0,
+                                        stream_ptr()))
+    # untimed pass: distinct experts per layer (the algorithmic bytes)
+    n_distinct = []
+    ids = torch.empty((B, K), dtype=torch.int32)
+    ping = [rows.clone(), torch.empty_like(rows)]
+    for i in range(L):
+        stack.layer(i, ping[i % 2], ping[(i + 1) % 2])
+        torch.cuda.synchronize(dev)
+        _lib.check(_lib.lib().yn_memcpy(ids.data_ptr(), stack.sview.ids_all, B * K * 4, None))
+        n_distinct.append(len(np.unique(ids.numpy())))
+    stack.step_end()
+    torch.cuda.synchronize(dev)
+    if stack.check_error():
+        raise RuntimeError("device error in the first verify step")
+    stack.capture()
+    for _ in range(args.warmup):
+        stack.step(rows)
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid(dev.index)) as clk:
+        start.record()
+        for _ in range(args.steps):
+            stack._ping[0].copy_(rows)
+            stack.graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end)
+    if stack.check_error():
+        raise RuntimeError("device error during the timed verify steps")
+    value = B * args.steps / (ms / 1e3)
+    h_in = torch.empty((B, H), dtype=torch.bfloat16, pin_memory=True)
+    h_in.copy_(rows)
+    h_out = torch.empty_like(h_in, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        stack._ping[0].copy_(h_in, non_blocking=True)
+        stack.graph.replay()
+        h_out.copy_(stack._ping[stack.out_slot], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e = B * args.steps / (e0.elapsed_time(e1) / 1e3)
+    rec = [cfg.record_spec(l).record_bytes for l in layer_ids]
+    hbm_bytes = sum(n * r for n, r in zip(n_distinct, rec)) + L * cfg.dense_bytes_per_layer()
+    hbm, src = peaks()
+    step_s = ms / args.steps / 1e3
+    achieved = hbm_bytes / step_s / 1e9
+    line = {
+        "metric": VERIFY_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "lfm2_24b_a2b_moe_stack40_verify_1p4", "layers": L, "rows_per_step": B,
+                   "hidden": H, "experts": cfg.n_experts, "top_k": K, "moe_inter": cfg.moe_inter,
+                   "expert_bits": "4-bit g64",
+                   "l2": "no flush: a step reads the routed records of 40 layers (~1 GB > 126 MB L2)"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+        "gpu_launches": args.steps * (L * 9 + 1),
+        "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "whole step (every kernel of yn_ep_layer)", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
+                     "bytes_per_step": hbm_bytes, "distinct_experts_per_layer_mean": round(float(np.mean(n_distinct)), 2),
+                     "traffic": None},
+    }
+    print(json.dumps(line), flush=True)
+    stack.graph = None
+    stack.close()
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, rank: int, world: int):
     import numpy as np
@@ -655,9 +749,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
-    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill"], default="resident",
+    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill", "verify"], default="resident",
                     help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier; "
-                         "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill")
+                         "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill; "
+                         "verify: 1+4-row speculative-verify batches")
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
@@ -683,6 +778,9 @@ def main():
         elif args.workload == "prefill":
             if rank == 0:
                 run_prefill(args, rank, world)
+        elif args.workload == "verify":
+            if rank == 0:
+                run_verify(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

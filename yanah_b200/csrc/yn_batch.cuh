@@ -199,21 +199,25 @@ YN_DEV void cpa_block(void* dst, const void* src, int bytes) {
 
 // Rows of RB bytes from global into a swizzled shared tile: chunk ch of row r
 // lands at r * RB + ((ch ^ (r & 7)) * 16). RB / 16 must be a multiple of 8.
-// RB / 16 must be a power of two and a multiple of 8.
+// Row index of piece i for cpr pieces per row: a shift when cpr is a power
+// of two, a division otherwise.
+YN_DEV int piece_row(int i, int cpr, int sh) { return sh >= 0 ? i >> sh : i / cpr; }
+YN_DEV int pow2_shift(int cpr) { return (cpr & (cpr - 1)) == 0 ? __ffs(cpr) - 1 : -1; }
+
+// RB / 16 must be a multiple of 8 (the XOR stays inside the row).
 YN_DEV void cpa_rows_swz(uint8_t* dst, int row0, const uint8_t* src, int rows, int RB) {
-  const int cpr = RB >> 4, sh = __ffs(cpr) - 1;
+  const int cpr = RB >> 4, sh = pow2_shift(cpr);
   for (int i = threadIdx.x; i < rows * cpr; i += blockDim.x) {
-    const int r = i >> sh, ch = i & (cpr - 1), rr = row0 + r;
+    const int r = piece_row(i, cpr, sh), ch = i - r * cpr, rr = row0 + r;
     cpa16(dst + (size_t)rr * RB + ((ch ^ (rr & 7)) << 4), src + ((size_t)i << 4));
   }
 }
 
-// Rows of `bytes` bytes into rows of `stride` bytes (both multiples of 16;
-// bytes / 16 a power of two).
+// Rows of `bytes` bytes into rows of `stride` bytes (both multiples of 16).
 YN_DEV void cpa_rows(uint8_t* dst, int stride, const uint8_t* src, int rows, int bytes) {
-  const int cpr = bytes >> 4, sh = __ffs(cpr) - 1;
+  const int cpr = bytes >> 4, sh = pow2_shift(cpr);
   for (int i = threadIdx.x; i < rows * cpr; i += blockDim.x) {
-    const int r = i >> sh, ch = i & (cpr - 1);
+    const int r = piece_row(i, cpr, sh), ch = i - r * cpr;
     cpa16(dst + (size_t)r * stride + (ch << 4), src + ((size_t)i << 4));
   }
 }
