@@ -21,6 +21,15 @@ resident stack does not shard), and the slowest rank's time is reported.
 --impl reference: the reference's MLX path is unavailable on this box (MLX is
 not installed), so this times the CPU restatement of that path (oracle/, a C
 port using every host core) on one token per step.
+
+Other workloads (--workload), each printing one JSON line of its own metric:
+  streaming  the same stack with the HBM slot pool at 20% of the experts and a
+             pinned host tier (hit rate, host-link GB/s, hidden copy fraction);
+  ep         a batch of 64 rows, experts sharded over the torchrun ranks with
+             dispatch/combine over NVLink peer memory (HBM and NVLink rooflines);
+  prefill    8 ragged prompts through 40 LFM2-24B-A2B-shaped layers on the
+             tcgen05 grouped expert GEMM (tensor-pipe roofline);
+  verify     1 + 4-row speculative-verify batches through the same 40 layers.
 """
 from __future__ import annotations
 
@@ -209,7 +218,7 @@ def host_link_gbs(dev, nbytes: int = 1 << 30) -> float:
 
 
 def run_streaming(args, rank: int, world: int):
-    """Config 2: the 48-layer stack with the slot pool at 20% of the experts;
+    """Streaming decode: the 48-layer stack with the slot pool at 20% of the experts;
     the rest in pinned host memory; lookahead-2 forecasts (threshold 0.062,
     at most 32 per target, top 24) copy on a side stream. Input rows follow
     an AR(1) process (rho = args.rho) so consecutive tokens route alike."""
@@ -286,7 +295,7 @@ EP_METRIC = "decode tok/s, batch of 64 rows, experts sharded over GPUs (Qwen3-Ne
 
 
 def run_ep(args, rank: int, world: int):
-    """Config 4: a decode batch of 64 rows (one token each per step) through
+    """Expert-parallel batch decode: 64 rows (one token each per step) through
     the 48-layer stack, experts sharded 512/world per GPU, per-layer dispatch
     and combine over peer memory (yn_ep_layer). One step = one CUDA graph
     replay. Inputs differ every step (the previous step's outputs)."""
@@ -425,7 +434,7 @@ PREFILL_METRIC = "prefill tok/s, ragged batch of 8 prompts (LFM2-24B-A2B-shaped,
 
 
 def run_prefill(args, rank: int, world: int):
-    """Config 3: a ragged prefill batch of 8 prompts with lengths uniform in
+    """Tensor-core prefill: a ragged batch of 8 prompts with lengths uniform in
     1-512 (seeded) through the 40-layer LFM2-shaped stack: routing of every
     row, the host plan of the expert groups, the tcgen05 grouped gate/up +
     SwiGLU and down GEMMs, the combine. One step = the whole batch through
@@ -527,7 +536,7 @@ VERIFY_METRIC = "speculative-verify tok/s, 1+4 rows per step (LFM2-24B-A2B-shape
 
 
 def run_verify(args, rank: int, world: int):
-    """Config 3, verify batches: 1 + 4 draft rows per step through the 40
+    """Speculative verify: 1 + 4 draft rows per step through the 40
     LFM2-shaped layers on the batch path (each routed expert record read
     once per layer however many of the 5 rows chose it). HBM-bound: the
     roofline counts each distinct expert record a layer routes to once."""
