@@ -92,8 +92,8 @@ int make_row_maps(const void* base, long long rows, int cols, bool bf16, TcMaps*
 }
 
 size_t tc_smem(int Kd) {
-  return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES + TC_C_BYTES) + 2 * (size_t)TC_M * (Kd / 64) * 2 +
-         (2 * TC_S + 4) * 8 + 16;
+  (void)Kd;
+  return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES) + (size_t)TC_CR * TC_C_BYTES + (2 * TC_S + 4) * 8 + 16;
 }
 }  // namespace
 

@@ -46,6 +46,9 @@ constexpr int TC_NMAX = 256;     // token rows per tile
 constexpr int TC_A_BYTES = TC_M * 128;       // one stage of A: 128 rows x 64 fp16
 constexpr int TC_B_BYTES = TC_NMAX * 128;    // one stage of B: 256 rows x 64 fp16
 constexpr int TC_C_BYTES = TC_M * 32;        // one stage of staged codes: 128 rows x 32 bytes
+constexpr int TC_CR = 8;                     // code ring slots
+constexpr int TC_PC = 6;                     // stages whose code words are in flight ahead of the dequantiser
+constexpr int TC_PB = 2;                     // stages whose B rows are requested ahead
 
 struct TcTile {
   int e;       // expert
@@ -243,9 +246,7 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
   uint8_t* Cbuf = Bbuf + TC_S * TC_B_BYTES;
   const int Kd = MODE == 0 ? a.H : a.I;
   const int NG = Kd / 64, NK = Kd / 64;
-  uint16_t* Ssc = reinterpret_cast<uint16_t*>(Cbuf + TC_S * TC_C_BYTES);  // (128, NG) this tile's scales
-  uint16_t* Sbi = Ssc + TC_M * NG;
-  uint64_t* full = reinterpret_cast<uint64_t*>(Sbi + TC_M * NG);
+  uint64_t* full = reinterpret_cast<uint64_t*>(Cbuf + TC_CR * TC_C_BYTES);
   uint64_t* empty = full + TC_S;
   uint64_t* acc_full = empty + TC_S;
   uint64_t* acc_empty = acc_full + 2;
@@ -303,51 +304,57 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
       const int nmma = ((good ? n : 16) + 15) & ~15;
       const int mi = nmma <= 16 ? 0 : nmma <= 32 ? 1 : nmma <= 64 ? 2 : nmma <= 128 ? 3 : 4;
       const uint32_t box_bytes = (16u << mi) * 128u;
-      // this thread's scale / bias row (read back only by this thread)
-      if (good)
-        for (int q = 0; q < NG * 2 / 16; ++q) {
-          tc_cpa16(reinterpret_cast<uint8_t*>(Ssc) + (size_t)t * NG * 2 + 16 * q, rec + off_s + (size_t)wrow * NG * 2 + 16 * q);
-          tc_cpa16(reinterpret_cast<uint8_t*>(Sbi) + (size_t)t * NG * 2 + 16 * q, rec + off_b + (size_t)wrow * NG * 2 + 16 * q);
-        }
-      auto issue = [&](int kc) -> bool {
+      // B rows of stage kc: one TMA copy (rows past the batch read as zeros);
+      // the stage's buffers are reused only after the MMA of 4 stages back
+      auto issue_b = [&](int kc) -> bool {
         const int gg = g + kc, s = gg % TC_S;
         if (gg >= TC_S && !mbar_wait_bounded(&empty[s], ((gg / TC_S) - 1) & 1, a.err)) return false;
-        if (good) {
-          uint8_t* cd = Cbuf + s * TC_C_BYTES + t * 32;
-          tc_cpa16(cd, wsrc + 32 * kc);
-          tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
-        }
-        if (t == 0) {  // the stage's B rows: one TMA copy (rows past the batch read as zeros)
+        if (t == 0) {
           mbar_arrive_expect_tx(&full[s], good ? box_bytes : 0u);
           if (good) tc_tma_rows(Bbuf + s * TC_B_BYTES, &maps.m[mi], 64 * kc, tl.p0, &full[s]);
         }
         return true;
       };
-      constexpr int P = 2;
-      for (int kc = 0; kc < P && kc < NK && ok; ++kc) {
-        ok = issue(kc);
+      // this thread's code words of stage kc into its slot of the code ring
+      // (TC_CR slots, read back only by this thread)
+      auto issue_codes = [&](int kc) {
+        if (good) {
+          uint8_t* cd = Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32;
+          tc_cpa16(cd, wsrc + 32 * kc);
+          tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
+        }
         tc_cpa_commit();
+      };
+      // scales and biases of this row in blocks of 8 groups (16-byte loads, one block ahead)
+      const uint4* srow = reinterpret_cast<const uint4*>(rec + off_s + (size_t)wrow * NG * 2);
+      const uint4* brow = reinterpret_cast<const uint4*>(rec + off_b + (size_t)wrow * NG * 2);
+      uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8, s8n = s8, b8n = s8;
+      if (good) {
+        s8n = srow[0];
+        b8n = brow[0];
       }
-      // stages in blocks of 8 (NK is a multiple of 8): the block's 8 scales and
-      // biases of this row come from shared memory as two 16-byte loads
-      uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8;
+      for (int kc = 0; kc < TC_PC && kc < NK; ++kc) issue_codes(kc);
+      for (int kc = 0; kc < TC_PB && kc < NK && ok; ++kc) ok = issue_b(kc);
       for (int kc0 = 0; kc0 < NK && ok; kc0 += 8) {
+        s8 = s8n;
+        b8 = b8n;
+        if (good && kc0 + 8 < NK) {
+          s8n = srow[(kc0 + 8) / 8];
+          b8n = brow[(kc0 + 8) / 8];
+        }
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
           const int kc = kc0 + jj;
           const int s = (g + kc) % TC_S;
-          if (kc + P < NK) ok = issue(kc + P);
-          tc_cpa_commit();
-          tc_cpa_wait<P>();
+          if (kc + TC_PC < NK) issue_codes(kc + TC_PC);
+          else tc_cpa_commit();  // keep one group per stage
+          if (kc + TC_PB < NK) ok = issue_b(kc + TC_PB);
+          tc_cpa_wait<TC_PC>();  // this stage's code words have landed
           if (!ok) break;
           if (good) {
-            if (jj == 0) {
-              s8 = *reinterpret_cast<const uint4*>(Ssc + t * NG + kc0);
-              b8 = *reinterpret_cast<const uint4*>(Sbi + t * NG + kc0);
-            }
             const uint32_t sw = jj < 2 ? s8.x : jj < 4 ? s8.y : jj < 6 ? s8.z : s8.w;
             const uint32_t bw = jj < 2 ? b8.x : jj < 4 ? b8.y : jj < 6 ? b8.z : b8.w;
-            tc_dequant_row<MODE>(Cbuf + s * TC_C_BYTES + t * 32, (uint16_t)(sw >> (16 * (jj & 1))),
+            tc_dequant_row<MODE>(Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32, (uint16_t)(sw >> (16 * (jj & 1))),
                                  (uint16_t)(bw >> (16 * (jj & 1))),
                                  Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t);
           }
