@@ -342,7 +342,9 @@ int yn_prefill_plan(const yn_dims* dims, const int32_t* ids, int32_t T, int32_t*
 
 /* Combine of T rows (mlx_backend.py:409/:420, :438-440; orchestrator.py:287):
  * out[t] = h_res[t] + (sum_j bf16(y[pair_of[t][j]] * w[t][j]) in column order
- * + y_shared[t]); y_shared and h_res may be NULL. */
+ * + y_shared[t]); y_shared and h_res may be NULL. Columns whose pair_of entry
+ * is negative are skipped (a staging group of the prefill sweep computes only
+ * the pairs of its experts, mlx_backend.py:421-433). */
 int yn_pairs_combine(const yn_dims* dims, const void* y, const int32_t* pair_of, const float* weights,
                      const void* y_shared, const void* h_res, int32_t T, void* out, void* stream);
 

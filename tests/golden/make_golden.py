@@ -27,6 +27,11 @@ What each fixture pins (the reference function that produced it):
   + ``ForecastPolicy`` replaying the same seeded routing trace in
   ``simulate``'s order (:296-323), with per-(step, layer) counters, the
   final dictionary and the demand-miss log.
+* ``sweep.json`` — ``moe_prefetch/sweep.py:80-138`` ``PrefillSweep`` over the
+  reference ``SlotPool``, driven by ``tests/sweep_driver.drive_sweep``: staging
+  groups, resident copies and host reads per group, the rows given to each
+  grouped ``moe`` call, the outputs, the pool after every layer (the final
+  pass admits each layer's fair share) and the statistics.
 * ``expert_mlp.npz`` — ``moe_prefetch/test_synthetic.py:46-51``
   ``expert_mlp`` (fp16 weights, fp32 SwiGLU MLP) on weights that are exactly
   representable as 4-bit affine codes, so the quantised CUDA/oracle path and
@@ -213,12 +218,42 @@ def make_pool(rng, S: int, L: int, E: int, k: int, n_cand: int, spec: int):
             "miss_layer": ml_layer, "miss_expert": ml_expert, "miss_len": ml_len, **fc_to_arrays(fc)}
 
 
+def make_sweep(seed: int = 20261202) -> dict:
+    """Reference PrefillSweep + SlotPool on two seeded prompt sets: a warm pool
+    with staging groups of 8 (several groups per layer, CLOCK evictions on
+    admission) and a cold pool with the default group of 32."""
+    sys.path.insert(0, str(REPO))
+    from tests.sweep_driver import TagMemory, drive_sweep, make_prompts, warm_pool
+    from moe_prefetch.layout import ModelGeometry
+    from moe_prefetch.pool import SlotPool
+    from moe_prefetch.sweep import PrefillSweep
+
+    rng = np.random.default_rng(seed)
+    cases = []
+    for (L, E, k, T, passes, slots, spec, group, n_warm) in [(4, 64, 4, 48, 3, 40, 8, 8, 30),
+                                                              (3, 128, 8, 40, 2, 48, 8, 32, 0)]:
+        ids, w = make_prompts(rng, passes, L, T, E, k)
+        warm = [(int(rng.integers(L)), int(rng.integers(E))) for _ in range(n_warm)]
+        g = ModelGeometry(n_layers=L, n_mtp_layers=0, n_experts=E, top_k=k, hidden=64, moe_inter=32, bits=4,
+                          group_size=32)
+        pool = SlotPool(g, slots, spec_slot_cap=spec, memory=TagMemory(slots))
+        warm_pool(pool, warm)
+        res = drive_sweep(PrefillSweep, pool, ids, w, group)
+        cases.append({"L": L, "E": E, "k": k, "slots": slots, "spec": spec, "group": group, "warm": warm,
+                      "ids": ids.tolist(), "w": w.tolist(), **res})
+    return {"cases": cases}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["sweep"], help="write only this fixture")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
+    if args.only == "sweep":
+        (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
+        return
     rng = np.random.default_rng(20260101)
     (HERE / "layout.json").write_text(json.dumps(make_layout(ref), indent=1) + "\n")
     np.savez_compressed(HERE / "route.npz", **make_route(rng))
@@ -228,6 +263,7 @@ def main():
     np.savez_compressed(HERE / "expert_mlp.npz", **make_expert_mlp(rng))
     np.savez_compressed(HERE / "pool_small.npz", **make_pool(rng, S=40, L=12, E=128, k=8, n_cand=16, spec=32))
     np.savez_compressed(HERE / "pool_wide.npz", **make_pool(rng, S=12, L=24, E=512, k=10, n_cand=12, spec=64))
+    (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 

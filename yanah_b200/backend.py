@@ -22,8 +22,14 @@ Differences from the MLX backend, all outside the MoE path:
 * the shared expert is added in the same kernel as the weighted sum over the
   k columns (same bf16 rounding order as `routed + shared`), so
   `moe_finalize` returns its input;
-* `moe` with experts missing from `rows` (the prefill sweep's staging groups,
-  mlx_backend.py:421-433) is not built yet and raises.
+* prompt passes of more than 8 rows route with `yn_rows_route` (bit-identical
+  to the single-row routing, row by row; no lookahead routers) and run their
+  routed experts as grouped GEMMs on the tensor cores (`yn_tc_experts`), as
+  does `moe` with experts missing from `rows` (the prefill sweep's staging
+  groups, mlx_backend.py:421-433): the group's (row, column) pairs sorted by
+  slot, the contribution of those pairs only. The grouped path needs 4-bit g64
+  routed experts and a stack without a shared expert (the LFM2 shape); other
+  stacks raise NotImplementedError there.
 
 Every call is asynchronous on the backend's stream; `fence()` blocks until the
 work that reads pool slots has finished.
@@ -108,6 +114,9 @@ class CudaMoEBackend:
         self._lut_i = 0
         self._pre: Dict[int, dict] = {}
         self._unfenced: Optional[torch.cuda.Event] = None
+        self._route_ws: Optional[torch.Tensor] = None     # yn_rows_route workspace (prompt passes)
+        self._route_rows = 0
+        self._tc_err = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     # -------------------------------------------------------------- helpers
     def _st(self) -> int:
@@ -154,6 +163,8 @@ class CudaMoEBackend:
         x = RMSNorm(h1), shared-expert activations and gate, router logits,
         and the lookahead probabilities of the next `lookahead` layers."""
         T = h1.shape[0]
+        if T > _lib.YN_MAX_ROWS:
+            return self._pre_rows(layer, h1)
         targets = self._targets(layer)
         tg = (_lib.Layer * max(len(targets), 1))(*[self.layers[t].struct() for t in targets]) if targets else None
         _lib.check(_lib.lib().yn_post_attention(C.byref(self.dims), C.byref(self.layers[layer].struct()),
@@ -163,8 +174,46 @@ class CudaMoEBackend:
         self._pre = {"layer": layer, "T": T, "targets": targets}
         return h1, x, logits
 
+    def _grouped_supported(self, layer: int) -> Optional[str]:
+        spec = self.cfg.record_spec(layer)
+        if self.cfg.shared_inter:
+            return "the grouped expert path is built for stacks without a shared expert"
+        if spec.bits != 4 or spec.group_size != 64:
+            return "the grouped expert path needs 4-bit g64 routed experts"
+        return None
+
+    def _pre_rows(self, layer: int, h1: torch.Tensor):
+        """Prompt pass of T > 8 rows: RMSNorm, router logits, top-k ids and
+        weights of every row (`yn_rows_route`). The logits stay in the routing
+        workspace (None is returned in their place)."""
+        why = self._grouped_supported(layer)
+        if why:
+            raise NotImplementedError(f"prompt pass of {h1.shape[0]} rows: {why}")
+        lib, cfg = _lib.lib(), self.cfg
+        T, H, K = h1.shape[0], cfg.hidden, cfg.top_k
+        with torch.cuda.stream(self.stream):
+            if self._route_ws is None or T > self._route_rows:
+                nb = int(lib.yn_rows_route_bytes(C.byref(self.dims), T))
+                if not nb:
+                    raise ValueError(f"{T} rows: more than the routing workspace supports")
+                self._route_ws = torch.zeros(nb, dtype=torch.uint8, device=self.device)
+                self._route_rows = T
+            x = torch.empty((T, H), dtype=torch.bfloat16, device=self.device)
+            ids = torch.empty((T, K), dtype=torch.int32, device=self.device)
+            w = torch.empty((T, K), dtype=torch.float32, device=self.device)
+        _lib.check(lib.yn_rows_route(C.byref(self.dims), C.byref(self.layers[layer].struct()), h1.data_ptr(), T,
+                                     x.data_ptr(), ids.data_ptr(), w.data_ptr(), self._route_ws.data_ptr(),
+                                     self._route_ws.numel(), self._st()))
+        self._pre = {"layer": layer, "T": T, "targets": [], "rows": (ids, w)}
+        return h1, x, None
+
     def _ids_w(self):
         T, K = self._pre["T"], self.cfg.top_k
+        if "rows" in self._pre:
+            ids, w = self._pre["rows"]
+            with torch.cuda.stream(self.stream):
+                ids_np = ids.cpu().numpy().astype(np.int64)      # the routing sync
+            return ids_np, w
         ids = self.ws.tensor("ids", (T, K), torch.int32)
         with torch.cuda.stream(self.stream):
             ids_np = ids.cpu().numpy().astype(np.int64)          # the routing sync
@@ -177,6 +226,8 @@ class CudaMoEBackend:
     def route_and_forecast(self, logits, h_res, targets: Sequence[int]):
         ids, w = self._ids_w()
         have = self._pre["targets"]
+        if not have:
+            return ids, w, {}
         fp = self.ws.tensor("fprobs", (max(len(have), 1), self.cfg.n_experts), torch.float32)
         with torch.cuda.stream(self.stream):
             fp_np = fp.cpu().numpy()
@@ -208,14 +259,78 @@ class CudaMoEBackend:
 
     def moe(self, layer: int, x, ids: np.ndarray, w, memory: CudaExpertMemory, rows: Dict[int, int],
             sync: bool = True) -> torch.Tensor:
-        if not np.isin(ids, np.fromiter(rows.keys(), dtype=np.int64)).all():
-            raise NotImplementedError("moe over a partial staging group (prefill sweep) is not built yet")
+        if ids.shape[0] > _lib.YN_MAX_ROWS or not np.isin(ids, np.fromiter(rows.keys(), dtype=np.int64)).all():
+            out = self._moe_grouped(layer, x, ids, w, memory, rows)
+            if sync:
+                self.stream.synchronize()
+            return out
         L = self._layer_struct(layer, memory, rows)
         _lib.check(_lib.lib().yn_moe_up(C.byref(self.dims), C.byref(L), None, None, ids.shape[0], None, 0,
                                         self.ws.ptr, self._st()))
         out = self._down(L, ids.shape[0])
         if sync:
             self.stream.synchronize()   # slots may be overwritten once this returns
+        return out
+
+    def _moe_grouped(self, layer: int, x, ids: np.ndarray, w, memory: CudaExpertMemory,
+                     rows: Dict[int, int]) -> torch.Tensor:
+        """Sum over the (row, column) pairs whose expert is in `rows` of
+        w * expert(x_row), as one grouped GEMM (mlx_backend.py:421-433): the
+        pairs sorted by slot (stable in row-major order), gate/up + SwiGLU and
+        down on the tensor cores, then per row the sum over its present
+        columns in column order (fp32, one bf16 rounding). Rows without a
+        present pair are zero."""
+        why = self._grouped_supported(layer)
+        if why:
+            raise NotImplementedError(why)
+        lib, cfg = _lib.lib(), self.cfg
+        T, K = ids.shape
+        H, I = cfg.hidden, cfg.moe_inter
+        keys = np.fromiter(rows.keys(), dtype=np.int64, count=len(rows))
+        lut = np.full(cfg.n_experts, -1, np.int64)
+        lut[keys] = np.fromiter(rows.values(), dtype=np.int64, count=len(rows))
+        t_idx, j_idx = np.nonzero(np.isin(ids, keys))
+        with torch.cuda.stream(self.stream):
+            out = torch.zeros((T, H), dtype=torch.bfloat16, device=self.device)
+        n = len(t_idx)
+        if n == 0:
+            return out
+        order = np.argsort(lut[ids[t_idx, j_idx]], kind="stable")
+        t_idx, j_idx = t_idx[order], j_idx[order]
+        e_of = ids[t_idx, j_idx]
+        pair_of = np.full((T, K), -1, np.int64)
+        pair_of[t_idx, j_idx] = np.arange(n)
+        starts = np.flatnonzero(np.r_[True, e_of[1:] != e_of[:-1]])
+        ends = np.r_[starts[1:], n]
+        up, dn = [], []
+        from .prefill import DOWN_ROWS, TILE_ROWS, UP_UNITS
+        for a, b in zip(starts.tolist(), ends.tolist()):
+            e = int(e_of[a])
+            for c0 in range(a, b, TILE_ROWS):
+                m = min(TILE_ROWS, b - c0)
+                up += [(e, c0, m, u) for u in range(0, I, UP_UNITS)]
+                dn += [(e, c0, m, r) for r in range(0, H, DOWN_ROWS)]
+        pad4 = lambda a: np.r_[a, np.zeros(-len(a) % 4, np.int64)]     # 16-byte aligned sections
+        sec = [pad4(t_idx), pad4(pair_of.reshape(-1)), np.asarray(up).reshape(-1), np.asarray(dn).reshape(-1)]
+        plan = np.concatenate(sec).astype(np.int32)
+        L = self._layer_struct(layer, memory, rows)
+        D, st = C.byref(self.dims), self._st()
+        with torch.cuda.stream(self.stream):
+            dev = torch.from_numpy(plan).pin_memory().to(self.device, non_blocking=True)
+            x16 = torch.empty((n, H), dtype=torch.float16, device=self.device)
+            act = torch.empty((n, I), dtype=torch.bfloat16, device=self.device)
+            y = torch.empty((n, H), dtype=torch.bfloat16, device=self.device)
+        p_row = dev.data_ptr()
+        p_of = p_row + 4 * len(sec[0])
+        p_up = p_of + 4 * len(sec[1])
+        p_dn = p_up + 4 * len(sec[2])
+        err = self._tc_err.data_ptr()
+        _lib.check(lib.yn_gather_f16_kperm(x.data_ptr(), p_row, n, H, x16.data_ptr(), st))
+        _lib.check(lib.yn_tc_experts(D, C.byref(L), 0, p_up, len(up), None, x16.data_ptr(), n, act.data_ptr(), None,
+                                     err, st))
+        _lib.check(lib.yn_tc_experts(D, C.byref(L), 1, p_dn, len(dn), None, act.data_ptr(), n, None, y.data_ptr(),
+                                     err, st))
+        _lib.check(lib.yn_pairs_combine(D, y.data_ptr(), p_of, w.data_ptr(), None, None, T, out.data_ptr(), st))
         return out
 
     def _down(self, L, T: int) -> torch.Tensor:
@@ -242,8 +357,18 @@ class CudaMoEBackend:
             self._unfenced = None
 
     def check_error(self) -> int:
-        """Read and clear the device error word (synchronises the stream)."""
-        return self.ws.check_error(self.stream)
+        """Read and clear the device error words (synchronises the stream)."""
+        code = self.ws.check_error(self.stream)
+        self.stream.synchronize()
+        tc = int(self._tc_err.item())
+        self._tc_err.zero_()
+        rc = 0
+        if self._route_ws is not None:
+            v = C.c_int32(0)
+            _lib.check(_lib.lib().yn_route_error(self._route_ws.data_ptr(), C.byref(self.dims), self._st(),
+                                                 C.byref(v)))
+            rc = v.value
+        return code or tc or rc
 
     def reset(self) -> None:
         self._pre = {}

@@ -489,7 +489,9 @@ __global__ void k_pairs_combine(const uint16_t* y, const int32_t* pair_of, const
   if (r >= H) return;
   float acc = 0.0f;
   for (int j = 0; j < K; ++j) {
-    const float v = bf16_to_f32(y[(size_t)pair_of[(size_t)t * K + j] * H + r]);
+    const int p = pair_of[(size_t)t * K + j];
+    if (p < 0) continue;  // column outside the computed pairs (a staging group)
+    const float v = bf16_to_f32(y[(size_t)p * H + r]);
     acc = __fadd_rn(acc, bf16r(__fmul_rn(v, w[(size_t)t * K + j])));
   }
   float o = bf16r(acc);

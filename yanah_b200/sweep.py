@@ -1,0 +1,280 @@
+"""Scan-resistant prefill sweep over the HBM slot pool (moe_prefetch/sweep.py:80-138).
+
+A prompt pass of `min_tokens` rows or more does not go through the pool's
+demand path (orchestrator.py:322-337). Per MoE layer:
+
+1. the layer's routed experts, sorted by id, are cut into staging groups of
+   `group` (32);
+2. for each group, the experts resident in the pool are copied out of it
+   (reference bits untouched: a prompt says nothing about decode locality) and
+   the rest are read from the host tier, one read per run of consecutive ids;
+3. the group runs as one grouped GEMM over its (row, column) pairs sorted by
+   expert (`CudaMoEBackend.moe` with a partial `rows`: the tensor-core kernel);
+4. the reads of group g+1 overlap the GEMM of group g: two staging buffers.
+
+The sweep never writes the pool except on the final prompt pass, which admits
+each layer's fair share (slots // layers) of its most frequently routed
+experts from staging (`SlotPool.admit`). Group composition depends on routing
+alone, never on residency, so the arithmetic is identical on a cold and a warm
+pool.
+
+On the device (`streams` given) every copy runs on a copy stream and the GEMMs
+on the compute stream, ordered by events instead of host waits:
+
+* at the start of a layer the copy stream waits for the compute stream (the
+  pool slots and the layer's rows are final; an admitted record may replace a
+  slot an earlier layer read);
+* a group's `futures` are events on the copy stream; `result()` makes the
+  compute stream wait for them on the device;
+* before a staging buffer is refilled (group g+2) the copy stream waits for the
+  GEMM of group g, which read it;
+* admitted records are copied staging -> pool slot on the copy stream, and the
+  compute stream waits for the copy stream at the end of the layer.
+
+Without `streams` (host memory, the reference's arrangement) copies are
+synchronous and futures are whatever the reader returns.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+from typing import Callable, Dict, List, Optional, Sequence
+
+import numpy as np
+
+GROUP = 32
+
+
+@dataclass
+class SweepStats:
+    passes: int = 0
+    layers: int = 0
+    resident_copies: int = 0
+    disk_records: int = 0
+    admitted: int = 0
+    read_wait_s: float = 0.0
+
+
+def _is_torch(v) -> bool:
+    return hasattr(v, "data_ptr") and hasattr(v, "copy_")
+
+
+def copy_record(dst: Sequence, src: Sequence) -> None:
+    """Copy one record given as lists of piece buffers (pool.py:85-87).
+    Device tensors (uint8 views of one slot, in record order): one
+    asynchronous copy on the current stream of the span from the first piece's
+    start to the end of the last (a slot holds the record's bytes in their
+    on-disk layout, padding included); a record of a smaller layer format
+    (mixed-bit stacks) fills the front of a larger slot. Host buffers: slice
+    assignment."""
+    if dst and _is_torch(dst[0]):
+        def flat(parts):
+            p0 = parts[0].data_ptr()
+            span = max(t.data_ptr() + t.numel() * t.element_size() for t in parts) - p0
+            return parts[0].as_strided((span,), (1,))
+        d, s = flat(dst), flat(src)
+        m = min(d.numel(), s.numel())
+        d[:m].copy_(s[:m], non_blocking=True)
+        return
+    for a, b in zip(dst, src):
+        a[:] = b
+
+
+class DeviceFuture:
+    """Completion of copies enqueued on a copy stream. `result()` makes the
+    compute stream wait for them on the device (no host wait); `done()`
+    polls."""
+
+    def __init__(self, event, compute_stream):
+        self.event, self.compute = event, compute_stream
+
+    def result(self, timeout=None):
+        self.compute.wait_event(self.event)
+
+    def done(self) -> bool:
+        return self.event.query()
+
+
+class SweepStreams:
+    """Copy and compute streams of a device sweep."""
+
+    def __init__(self, compute=None, copy=None, device="cuda"):
+        import torch
+        self.compute = compute or torch.cuda.current_stream(device)
+        self.copy = copy or torch.cuda.Stream(device)
+
+    def event(self, stream):
+        import torch
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        return ev
+
+
+class HostSlabMemory:
+    """n host slots of `slot_bytes` holding one record each (pool.py:66-82)."""
+
+    def __init__(self, n: int, record_bytes: int, slot_bytes: int):
+        self.n, self.record_bytes, self.slot_bytes = n, record_bytes, slot_bytes
+        self._buf = bytearray(max(1, n * slot_bytes))
+        self._view = memoryview(self._buf)
+
+    def views(self, i: int) -> List[memoryview]:
+        s = i * self.slot_bytes
+        return [self._view[s:s + self.record_bytes]]
+
+    def close(self) -> None:
+        self._view.release()
+
+
+class _Staging:
+    """One staging group. `memory` has the layout of pool memory, so the
+    backend computes on it exactly as on the pool (rows = staging index)."""
+
+    def __init__(self, memory):
+        self.memory = memory
+        self.index: Dict[int, int] = {}
+        self.futures: List = []
+        self.read_done = None   # event after the GEMM that last read this buffer
+
+    def views(self, e: int):
+        return self.memory.views(self.index[e])
+
+
+class HostTierReader:
+    """Reads routed records from the pinned host tier into staging slots on
+    the copy stream (the sweep half of io_lanes.py:145-173 `runs` /
+    `submit_runs`): runs of consecutive expert ids, one asynchronous copy per
+    record, one future per run."""
+
+    def __init__(self, tier, streams: SweepStreams):
+        self.tier, self.streams = tier, streams
+        self.sweep_runs = 0
+        self.sweep_records = 0
+
+    @staticmethod
+    def runs(experts: Sequence[int]) -> List[List[int]]:
+        """Sorted ids split into runs of consecutive ids (records contiguous in the tier)."""
+        out: List[List[int]] = []
+        for e in experts:
+            if out and e == out[-1][-1] + 1:
+                out[-1].append(e)
+            else:
+                out.append([e])
+        return out
+
+    def submit_runs(self, layer: int, experts: Sequence[int], dst_for: Callable[[int], List]) -> List[DeviceFuture]:
+        import torch
+        futs = []
+        rb = self.tier.rec[layer]
+        host = self.tier.buf[layer]
+        with torch.cuda.stream(self.streams.copy):
+            for run in self.runs(list(experts)):
+                for e in run:
+                    copy_record(dst_for(e), [host[e * rb:(e + 1) * rb]])
+                futs.append(DeviceFuture(self.streams.event(self.streams.copy), self.streams.compute))
+                self.sweep_runs += 1
+                self.sweep_records += len(run)
+        return futs
+
+
+class PrefillSweep:
+    """pool: `SlotPool`; reader: `submit_runs(layer, experts, dst_for)`;
+    make_memory(n): staging memory of n slots with the pool memory's layout
+    (default host slabs); streams: `SweepStreams` for device memory, None for host memory."""
+
+    def __init__(self, pool, reader, min_tokens: int = 16, group: int = GROUP,
+                 make_memory: Optional[Callable[[int], object]] = None, streams: Optional[SweepStreams] = None):
+        self.pool, self.reader = pool, reader
+        self.min_tokens, self.group = min_tokens, group
+        if make_memory is None:
+            g = pool.g
+            make_memory = lambda n: HostSlabMemory(n, g.expert_nbytes, g.slot_nbytes)
+        self.streams = streams
+        self._staging = [_Staging(make_memory(group)) for _ in range(2)]
+        self.stats = SweepStats()
+
+    def fair_share(self) -> int:
+        return self.pool.slots // self.pool.g.total_moe_layers
+
+    def _on_copy_stream(self):
+        import contextlib
+        if self.streams is None:
+            return contextlib.nullcontext()
+        import torch
+        return torch.cuda.stream(self.streams.copy)
+
+    def _load(self, st: _Staging, layer: int, experts: List[int]) -> None:
+        """Copy residents out of the pool, start host-tier reads for the rest."""
+        s_ = self.streams
+        if s_ is not None and st.read_done is not None:
+            s_.copy.wait_event(st.read_done)          # the GEMM that read this buffer has run
+        st.index = {e: i for i, e in enumerate(experts)}      # sorted id order
+        missing = []
+        with self._on_copy_stream():
+            for e in experts:
+                s = self.pool.lookup((layer, e))
+                if s is not None:
+                    copy_record(st.views(e), self.pool.views(s))   # no reference-bit change
+                    self.stats.resident_copies += 1
+                else:
+                    missing.append(e)
+        self.stats.disk_records += len(missing)
+        st.futures = list(self.reader.submit_runs(layer, missing, st.views))
+        if s_ is not None:
+            st.futures.append(DeviceFuture(s_.event(s_.copy), s_.compute))
+
+    def run_layer(self, layer: int, x, ids: np.ndarray, w, moe: Callable, admit: bool):
+        """moe(layer, x, ids, w, memory, rows) -> the contribution of `rows`' experts only."""
+        s_ = self.streams
+        if s_ is not None:
+            s_.copy.wait_stream(s_.compute)
+        experts, counts = np.unique(ids, return_counts=True)
+        experts = [int(e) for e in experts]
+        groups = [experts[i:i + self.group] for i in range(0, len(experts), self.group)]
+        admit_set = set()
+        if admit:
+            order = np.argsort(-counts, kind="stable")
+            admit_set = {experts[i] for i in order[: self.fair_share()]}
+
+        out = None
+        self._load(self._staging[0], layer, groups[0])
+        for gi, grp in enumerate(groups):
+            st = self._staging[gi % 2]
+            if gi + 1 < len(groups):                              # read ahead one group
+                self._load(self._staging[(gi + 1) % 2], layer, groups[gi + 1])
+            t0 = time.perf_counter()
+            for f in st.futures:
+                f.result()
+            self.stats.read_wait_s += time.perf_counter() - t0
+            part = moe(layer, x, ids, w, st.memory, dict(st.index))
+            if s_ is not None:
+                st.read_done = s_.event(s_.compute)
+            out = part if out is None else out + part
+            if admit_set:
+                members = [e for e in grp if e in admit_set]
+                with self._on_copy_stream():
+                    self.stats.admitted += self.pool.admit(
+                        layer, members, len(members), lambda e, dst: copy_record(dst, st.views(e)))
+        if s_ is not None:
+            s_.compute.wait_stream(s_.copy)
+        self.stats.layers += 1
+        return out
+
+    def close(self):
+        for st in self._staging:
+            st.memory.close()
+
+
+def prompt_pass(backend, sweep: PrefillSweep, h, admit: bool = True, layers: Optional[Sequence[int]] = None):
+    """The sweep branch of the orchestrator's forward (orchestrator.py:322-337)
+    over the MoE half of each layer: `pre_moe`, routing (one host sync for the
+    ids), the sweep, `moe_finalize`, residual. Staging reuse is ordered on the
+    device, so the backend's `moe` runs without its host synchronisation."""
+    import functools
+    moe = functools.partial(backend.moe, sync=False)
+    for layer in (range(backend.cfg.n_layers) if layers is None else layers):
+        h_res, x, logits = backend.pre_moe(layer, h)
+        ids, w = backend.route(logits)
+        h = h_res + backend.moe_finalize(layer, sweep.run_layer(layer, x, ids, w, moe, admit))
+    sweep.stats.passes += 1
+    return h
