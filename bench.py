@@ -29,7 +29,10 @@ Other workloads (--workload), each printing one JSON line of its own metric:
              dispatch/combine over NVLink peer memory (HBM and NVLink rooflines);
   prefill    8 ragged prompts through 40 LFM2-24B-A2B-shaped layers on the
              tcgen05 grouped expert GEMM (tensor-pipe roofline);
-  verify     1 + 4-row speculative-verify batches through the same 40 layers.
+  verify     1 + 4-row speculative-verify batches through the same 40 layers;
+  sweep      the same 8 prompts through the prefill sweep: staging groups of 32
+             over an HBM slot pool at 20% of the experts, the rest read from
+             the pinned host tier (host-link roofline).
 """
 from __future__ import annotations
 
@@ -531,6 +534,111 @@ def run_prefill(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------- sweep leg
+SWEEP_METRIC = ("prefill tok/s through the prefill sweep, 8 prompts (LFM2-24B-A2B-shaped, 40 layers), "
+                "20% HBM slot pool + pinned host tier")
+
+
+def run_sweep(args, rank: int, world: int):
+    """Prefill sweep: the prefill workload's 8 ragged prompts through the
+    40-layer LFM2-shaped stack, every routed record held in pinned host
+    memory and an HBM slot pool at 20% of the experts (512 slots). Per layer:
+    routing of every row, then the routed experts in staging groups of 32
+    (residents copied out of the pool, the rest read from the host tier on a
+    copy stream, two staging buffers), each group one grouped tcgen05 GEMM.
+    A warm-up pass admits each layer's fair share into the pool; the timed
+    passes do not admit, so every step sees the same pool."""
+    import numpy as np
+    import torch
+
+    from yanah_b200 import _lib
+    from yanah_b200.backend import CudaMoEBackend
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.pool import SlotPool
+    from yanah_b200.streaming import HostTier
+    from yanah_b200.sweep import HostTierReader, PrefillSweep, SweepStreams, prompt_pass
+    from yanah_b200.synthetic import hidden_stream_id, lfm2_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = lfm2_stack(seed=0)
+    lens = np.random.default_rng(3).integers(1, 513, size=8)
+    T = int(lens.sum())
+    link = host_link_gbs(dev)
+    tier = HostTier(cfg, dev)
+    be = CudaMoEBackend(cfg, device=dev)
+    slots = int(0.2 * cfg.n_experts * cfg.n_layers)
+    pool = SlotPool(be.geometry, slots, spec_slot_cap=0, memory=be.make_expert_memory(slots))
+    streams = SweepStreams(device=dev)
+    reader = HostTierReader(tier, streams)
+    sweep = PrefillSweep(pool, reader, group=32, make_memory=be.make_expert_memory, streams=streams)
+    H = cfg.hidden
+    h = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(h.data_ptr(), T * H, cfg.seed, hidden_stream_id(600 + rank), 1.0, 0.0,
+                                        stream_ptr()))
+    for w in range(args.warmup):
+        prompt_pass(be, sweep, h, admit=(w == 0))
+    torch.cuda.synchronize(dev)
+    if be.check_error():
+        raise RuntimeError("device error in the sweep warm-up")
+    st0 = (sweep.stats.resident_copies, sweep.stats.disk_records, reader.sweep_runs)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid(dev.index)) as clk:
+        start.record()
+        for _ in range(args.steps):
+            prompt_pass(be, sweep, h, admit=False)
+        end.record()
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end)
+    value = T * args.steps / (ms / 1e3)
+    res = (sweep.stats.resident_copies - st0[0]) / args.steps
+    disk = (sweep.stats.disk_records - st0[1]) / args.steps
+    runs = (reader.sweep_runs - st0[2]) / args.steps
+    rec = cfg.record_spec(0).record_bytes
+    h2d = disk * rec / (ms / args.steps / 1e3) / 1e9
+    # e2e: pinned host rows in, outputs back, every step
+    h_in = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    h_in.copy_(h)
+    h_out = torch.empty_like(h_in, pin_memory=True)
+    d_in = torch.empty_like(h)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        d_in.copy_(h_in, non_blocking=True)
+        h_out.copy_(prompt_pass(be, sweep, d_in, admit=False), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e = T * args.steps / (e0.elapsed_time(e1) / 1e3)
+    if be.check_error():
+        raise RuntimeError("device error during the timed sweep")
+    per_layer = (res + disk) / cfg.n_layers
+    n_groups = int(np.ceil(per_layer / 32)) * cfg.n_layers
+    line = {
+        "metric": SWEEP_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "lfm2_24b_a2b_moe_stack40_prefill_sweep", "layers": cfg.n_layers, "prompts": 8,
+                   "prompt_lengths": lens.tolist(), "rows": T, "pool_slots": slots, "pool_fraction": 0.2,
+                   "staging_group": 32, "host_tier_gb": round(tier.nbytes / 1e9, 2),
+                   "admission": "warm-up pass admits each layer's fair share; timed passes do not admit",
+                   "l2": "no flush: a step moves 13.6 GB of expert records (> 126 MB L2)"},
+        "sweep": {"resident_copies_per_step": res, "host_records_per_step": disk, "host_runs_per_step": runs,
+                  "distinct_experts_per_layer": round(per_layer, 2), "h2d_gbs": round(h2d, 2)},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        # per layer: row norm + router/routing; per staging group: row gather, two grouped GEMMs, combine
+        "gpu_launches": args.steps * (cfg.n_layers * 2 + n_groups * 4),
+        "clocks": clk.summary(),
+        "roofline": {"bound": "host-link", "kernel": "host tier -> staging copies (cudaMemcpyAsync per record)",
+                     "achieved": round(h2d, 2), "peak": round(link, 2), "unit": "GB/s",
+                     "frac": round(h2d / link, 4),
+                     "peak_source": "pinned host->device cudaMemcpyAsync of 1 GiB, measured in this run",
+                     "traffic": None},
+    }
+    sweep.close()
+    print(json.dumps(line), flush=True)
+
+
 # -------------------------------------------------------------- verify leg
 VERIFY_METRIC = "speculative-verify tok/s, 1+4 rows per step (LFM2-24B-A2B-shaped, 40 layers), union-of-experts batch"
 
@@ -758,10 +866,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
-    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill", "verify"], default="resident",
+    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill", "verify", "sweep"],
+                    default="resident",
                     help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier; "
                          "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill; "
-                         "verify: 1+4-row speculative-verify batches")
+                         "verify: 1+4-row speculative-verify batches; sweep: prefill through the prefill sweep")
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
@@ -790,6 +899,9 @@ def main():
         elif args.workload == "verify":
             if rank == 0:
                 run_verify(args, rank, world)
+        elif args.workload == "sweep":
+            if rank == 0:
+                run_sweep(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:
