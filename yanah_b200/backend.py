@@ -300,18 +300,22 @@ class CudaMoEBackend:
         e_of = ids[t_idx, j_idx]
         pair_of = np.full((T, K), -1, np.int64)
         pair_of[t_idx, j_idx] = np.arange(n)
+        from .prefill import DOWN_ROWS, TILE_ROWS, UP_UNITS
+        # chunks of at most TILE_ROWS pairs of one expert, then per chunk the gate/up and down tiles
         starts = np.flatnonzero(np.r_[True, e_of[1:] != e_of[:-1]])
         ends = np.r_[starts[1:], n]
-        up, dn = [], []
-        from .prefill import DOWN_ROWS, TILE_ROWS, UP_UNITS
-        for a, b in zip(starts.tolist(), ends.tolist()):
-            e = int(e_of[a])
-            for c0 in range(a, b, TILE_ROWS):
-                m = min(TILE_ROWS, b - c0)
-                up += [(e, c0, m, u) for u in range(0, I, UP_UNITS)]
-                dn += [(e, c0, m, r) for r in range(0, H, DOWN_ROWS)]
+        nch = (ends - starts + TILE_ROWS - 1) // TILE_ROWS
+        run = np.repeat(np.arange(len(starts)), nch)
+        p0 = starts[run] + (np.arange(len(run)) - np.repeat(np.cumsum(nch) - nch, nch)) * TILE_ROWS
+        chunk = np.stack([e_of[starts][run], p0, np.minimum(TILE_ROWS, ends[run] - p0)], axis=1)
+
+        def tiles(step_units, total):
+            offs = np.arange(0, total, step_units)
+            return np.concatenate([np.repeat(chunk, len(offs), axis=0),
+                                   np.tile(offs, len(chunk))[:, None]], axis=1)
+        up, dn = tiles(UP_UNITS, I), tiles(DOWN_ROWS, H)
         pad4 = lambda a: np.r_[a, np.zeros(-len(a) % 4, np.int64)]     # 16-byte aligned sections
-        sec = [pad4(t_idx), pad4(pair_of.reshape(-1)), np.asarray(up).reshape(-1), np.asarray(dn).reshape(-1)]
+        sec = [pad4(t_idx), pad4(pair_of.reshape(-1)), up.reshape(-1), dn.reshape(-1)]
         plan = np.concatenate(sec).astype(np.int32)
         L = self._layer_struct(layer, memory, rows)
         D, st = C.byref(self.dims), self._st()

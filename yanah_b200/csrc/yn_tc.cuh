@@ -4,20 +4,20 @@
 //
 // One CTA computes one tile D[m][n] = sum_k W[m][k] * X[n][k]:
 //  * A = 128 weight rows of one expert, dequantised from MLX 4-bit g64 codes
-//    by the CTA's four warps (thread t owns tile row t): for gate/up
+//    by the CTA's producer warps (TC_PW / 4 threads per tile row): for gate/up
 //    the rows interleave gate unit u (row 2i) and up unit u (row 2i + 1) for
 //    64 units, so SwiGLU fuses into the epilogue; for down they are 128
 //    output rows;
 //  * B = up to 256 rows of this expert's tokens (prefill x in fp16, or the
 //    SwiGLU activations in bf16 for the down projection, whose weights are
-//    then dequantised to bf16), copied with cp.async;
+//    then dequantised to bf16), copied by TMA;
 //  * both operands are K-major in the 128-byte swizzled layout (row r of an
 //    8-row atom at r * 128 bytes, 16-byte chunk c at (c ^ r) * 16); K moves
 //    in stages of 64 codes = one quantisation group, 4 stages in flight;
 //  * one thread issues tcgen05.mma (M 128, N = tokens rounded up to 16,
 //    K 16 x 4 per stage) into a TMEM accumulator and commits each stage to
 //    its mbarrier, which frees the stage's buffers for the producers;
-//  * the epilogue reads TMEM with tcgen05.ld (warp w: lanes 32w..32w+31).
+//  * the epilogue reads TMEM with tcgen05.ld (warp w: lanes 32(w % 4)..+31).
 //
 // The codes of a word unpack into fp16 pairs (q0,q4), (q1,q5), (q2,q6),
 // (q3,q7) (one LOP3 per pair, yn_mma.cuh), so the K order inside each block of
@@ -48,7 +48,6 @@ constexpr int TC_B_BYTES = TC_NMAX * 128;    // one stage of B: 256 rows x 64 fp
 constexpr int TC_C_BYTES = TC_M * 32;        // one stage of staged codes: 128 rows x 32 bytes
 constexpr int TC_CR = 8;                     // code ring slots
 constexpr int TC_PC = 6;                     // stages whose code words are in flight ahead of the dequantiser
-constexpr int TC_PB = 2;                     // stages whose B rows are requested ahead
 
 struct TcTile {
   int e;       // expert
@@ -156,13 +155,21 @@ YN_DEV bool tc_wait(uint64_t* bar, uint32_t parity, int* err) {
   return mbar_wait_block(bar, parity, err);
 }
 
-// Producer-side dequantisation of one 64-code stage of this thread's weight
-// row into the swizzled A tile (fp16 for MODE 0, bf16 for MODE 1).
-template <int MODE>
-YN_DEV void tc_dequant_row(const uint8_t* codes32, uint16_t sc_bits, uint16_t bi_bits, uint8_t* Arow, int t) {
-  const uint4* cw = reinterpret_cast<const uint4*>(codes32);
-  const uint4 c0 = cw[0], c1 = cw[1];
-  const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+// Producer-side dequantisation of NW code words (8 codes each) of one 64-code
+// stage of a weight row, words i0 .. i0+NW-1 of the stage, into the swizzled
+// A tile (fp16 for MODE 0, bf16 for MODE 1). t: the tile row (swizzle phase).
+template <int MODE, int NW>
+YN_DEV void tc_dequant_row(const uint8_t* codes, uint16_t sc_bits, uint16_t bi_bits, uint8_t* Arow, int t, int i0) {
+  const uint4* cw = reinterpret_cast<const uint4*>(codes);
+  uint32_t words[NW];
+#pragma unroll
+  for (int v = 0; v < NW / 4; ++v) {
+    const uint4 c = cw[v];
+    words[4 * v] = c.x;
+    words[4 * v + 1] = c.y;
+    words[4 * v + 2] = c.z;
+    words[4 * v + 3] = c.w;
+  }
   const __half sc = __ushort_as_half(sc_bits), bi = __ushort_as_half(bi_bits);
   const __half2 k1024 = __float2half2_rn(1024.0f);
   if constexpr (MODE == 0) {  // w = fp16(s * q + b): one HFMA2 per pair
@@ -171,7 +178,7 @@ YN_DEV void tc_dequant_row(const uint8_t* codes32, uint16_t sc_bits, uint16_t bi
     const __half2 s16 = __halves2half2(sc16, sc16);
     const __half2 b2 = __halves2half2(bi, bi);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < NW; ++i) {
       uint32_t pr[4];
       tc_unpack4(words[i], pr);
       uint32_t o[4];
@@ -182,12 +189,12 @@ YN_DEV void tc_dequant_row(const uint8_t* codes32, uint16_t sc_bits, uint16_t bi
         h = __hfma2(h, (p & 1) ? s16 : s1, b2);
         o[p] = *reinterpret_cast<uint32_t*>(&h);
       }
-      *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(Arow + (((i0 + i) ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   } else {  // w = bf16(s * q + b) from an fp32 FMA
     const float s1 = __half2float(sc), s16 = __fmul_rn(s1, 0.0625f), bf = __half2float(bi);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < NW; ++i) {
       uint32_t pr[4];
       tc_unpack4(words[i], pr);
       uint32_t o[4];
@@ -200,7 +207,7 @@ YN_DEV void tc_dequant_row(const uint8_t* codes32, uint16_t sc_bits, uint16_t bi
         __nv_bfloat162 w = __floats2bfloat162_rn(__fmaf_rn(q.x, m, bf), __fmaf_rn(q.y, m, bf));
         o[p] = *reinterpret_cast<uint32_t*>(&w);
       }
-      *reinterpret_cast<uint4*>(Arow + ((i ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(Arow + (((i0 + i) ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
@@ -225,17 +232,36 @@ YN_DEV void mbar_arrive1(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Warp-specialised persistent form. 288 threads: warps 0-3 produce (thread t
-// dequantises tile row t; all 128 copy the B rows), warps 4-7 drain the
-// accumulator (warp 4 + q reads TMEM lanes 32q..32q+31), warp 8 issues the
-// MMAs. Stage ring: full[s] (128 producer arrivals), empty[s] (MMA commit);
+// Warp-specialised persistent form. 32 * (TC_PW + TC_EPW + 2) threads: warps
+// 0..TC_PW-1 produce A (TC_PW / 4 threads per tile row, each dequantising
+// 8 / (TC_PW / 4) code words of the row's stage), the next TC_EPW warps drain
+// the accumulator (epilogue warp e reads TMEM lanes 32(e % 4)..+31, 32-column
+// chunks e / 4, e / 4 + TC_EPW / 4, ...), then the MMA warp and the loader
+// warp (one TMA copy of the B rows per stage). A stage's
+// A and B are both written as soon as the MMA that last read the stage has
+// committed, so the whole ring is in flight. Stage ring: full[s]
+// (32 * TC_PW producer arrivals + the loader's expect_tx), empty[s] (MMA commit);
 // accumulator ring of 2 x 256 TMEM columns: acc_full[b] (MMA commit),
-// acc_empty[b] (128 epilogue arrivals). The CTAs walk the planned tiles with
+// acc_empty[b] (one arrival per epilogue thread). The CTAs walk the planned tiles with
 // stride gridDim.x, so one tile's epilogue overlaps the next tile's main loop.
 // MODE 0: gate/up + SwiGLU, fp16 operands (normalised rows are small);
 // MODE 1: down, bf16 operands (SwiGLU activations have bf16's range, as the
 // reference's bf16 arrays do; fp16 would overflow on them).
-constexpr int TCW_THREADS = 288;
+#ifndef TC_PW
+#define TC_PW 8
+#endif
+static_assert(TC_PW == 4 || TC_PW == 8, "producer warps: 4 or 8");
+constexpr int TC_PT = 32 * TC_PW;            // producer threads
+constexpr int TC_NH = TC_PW / 4;             // producer threads per tile row
+constexpr int TC_NW = 8 / TC_NH;             // code words per producer thread and stage
+#ifndef TC_EPW
+#define TC_EPW 8
+#endif
+static_assert(TC_EPW == 4 || TC_EPW == 8, "epilogue warps: 4 or 8");
+constexpr int TC_EW = TC_PW;                 // first epilogue warp (a multiple of 4: warp % 4 = TMEM lane quadrant)
+constexpr int TC_MW = TC_PW + TC_EPW;        // the MMA warp
+constexpr int TC_LW = TC_MW + 1;             // the B-row loader warp
+constexpr int TCW_THREADS = 32 * (TC_MW + 2);
 
 template <int MODE>
 __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, const __grid_constant__ TcMaps maps) {
@@ -256,16 +282,16 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
   const int n_tiles = a.n_tiles_dev ? min(a.n_tiles, *a.n_tiles_dev) : a.n_tiles;
   if (tid == 0) {
     for (int s = 0; s < TC_S; ++s) {
-      mbar_init(&full[s], 129);  // 128 dequantising threads + the TMA transaction's expect_tx
+      mbar_init(&full[s], TC_PT + 1);  // dequantising threads + the TMA transaction's expect_tx
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 32 * TC_EPW);
     }
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == TC_MW) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
@@ -274,9 +300,9 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
 
-  if (warp < 4) {
+  if (warp < TC_PW) {
     // ------------------------------------------------------------ producers
-    const int t = tid;
+    const int t = tid & (TC_M - 1), h = tid / TC_M;  // tile row, part of the row's stage
     int g = 0;  // stages produced by this CTA so far
     for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x) {
       const TcTile tl = a.tiles[ti];
@@ -300,28 +326,13 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
         off_b = a.rg.off[8];
       }
       const uint8_t* wsrc = rec + off_w + (size_t)wrow * (Kd / 2);
-      // B box: the smallest map whose height covers the tile's MMA width
-      const int nmma = ((good ? n : 16) + 15) & ~15;
-      const int mi = nmma <= 16 ? 0 : nmma <= 32 ? 1 : nmma <= 64 ? 2 : nmma <= 128 ? 3 : 4;
-      const uint32_t box_bytes = (16u << mi) * 128u;
-      // B rows of stage kc: one TMA copy (rows past the batch read as zeros);
-      // the stage's buffers are reused only after the MMA of 4 stages back
-      auto issue_b = [&](int kc) -> bool {
-        const int gg = g + kc, s = gg % TC_S;
-        if (gg >= TC_S && !mbar_wait_bounded(&empty[s], ((gg / TC_S) - 1) & 1, a.err)) return false;
-        if (t == 0) {
-          mbar_arrive_expect_tx(&full[s], good ? box_bytes : 0u);
-          if (good) tc_tma_rows(Bbuf + s * TC_B_BYTES, &maps.m[mi], 64 * kc, tl.p0, &full[s]);
-        }
-        return true;
-      };
       // this thread's code words of stage kc into its slot of the code ring
       // (TC_CR slots, read back only by this thread)
       auto issue_codes = [&](int kc) {
         if (good) {
-          uint8_t* cd = Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32;
-          tc_cpa16(cd, wsrc + 32 * kc);
-          tc_cpa16(cd + 16, wsrc + 32 * kc + 16);
+          uint8_t* cd = Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32 + h * 4 * TC_NW;
+#pragma unroll
+          for (int v = 0; v < TC_NW / 4; ++v) tc_cpa16(cd + 16 * v, wsrc + 32 * kc + h * 4 * TC_NW + 16 * v);
         }
         tc_cpa_commit();
       };
@@ -334,7 +345,6 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
         b8n = brow[0];
       }
       for (int kc = 0; kc < TC_PC && kc < NK; ++kc) issue_codes(kc);
-      for (int kc = 0; kc < TC_PB && kc < NK && ok; ++kc) ok = issue_b(kc);
       for (int kc0 = 0; kc0 < NK && ok; kc0 += 8) {
         s8 = s8n;
         b8 = b8n;
@@ -348,15 +358,16 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
           const int s = (g + kc) % TC_S;
           if (kc + TC_PC < NK) issue_codes(kc + TC_PC);
           else tc_cpa_commit();  // keep one group per stage
-          if (kc + TC_PB < NK) ok = issue_b(kc + TC_PB);
+          // the stage's A buffer is free once the MMA of TC_S stages back has committed
+          if (g + kc >= TC_S) ok = mbar_wait_bounded(&empty[s], (((g + kc) / TC_S) - 1) & 1, a.err);
           tc_cpa_wait<TC_PC>();  // this stage's code words have landed
           if (!ok) break;
           if (good) {
             const uint32_t sw = jj < 2 ? s8.x : jj < 4 ? s8.y : jj < 6 ? s8.z : s8.w;
             const uint32_t bw = jj < 2 ? b8.x : jj < 4 ? b8.y : jj < 6 ? b8.z : b8.w;
-            tc_dequant_row<MODE>(Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32, (uint16_t)(sw >> (16 * (jj & 1))),
-                                 (uint16_t)(bw >> (16 * (jj & 1))),
-                                 Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t);
+            tc_dequant_row<MODE, TC_NW>(Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32 + h * 4 * TC_NW,
+                                        (uint16_t)(sw >> (16 * (jj & 1))), (uint16_t)(bw >> (16 * (jj & 1))),
+                                        Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t, h * TC_NW);
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           mbar_arrive1(&full[s]);
@@ -365,9 +376,10 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
       tc_cpa_wait<0>();
       g += NK;
     }
-  } else if (warp < 8) {
+  } else if (warp < TC_MW) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp - 4, m = 32 * q + lane;  // tile row of this thread
+    const int q = (warp - TC_EW) & 3, m = 32 * q + lane;  // tile row of this thread
+    const int hc = (warp - TC_EW) >> 2;                    // first 32-column chunk of this warp
     int j = 0;
     for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x, ++j) {
       const TcTile tl = a.tiles[ti];
@@ -378,22 +390,22 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
       tc_fence_after();
       const uint32_t base = tmem + (uint32_t)(b * 256) + ((uint32_t)(32 * q) << 16);
       const bool good = n >= 1 && n <= TC_NMAX;
-      for (int c0 = 0; c0 < nmma; c0 += 32) {
+      for (int c0 = 32 * hc; c0 < nmma; c0 += 32 * (TC_EPW / 4)) {
         float v[32];
         tc_ld32(base + (uint32_t)c0, v);
         if (!good) continue;
         if (MODE == 0) {
-          // lanes 2i (gate of unit u) and 2i+1 (up of unit u) split the columns
+          // lanes 2i (gate of unit u) and 2i+1 (up of unit u) share the columns:
+          // of each column pair the gate lane takes the even column, the up lane
+          // the odd one, after one exchange
           const int ku = kperm(tl.u0 + (m >> 1));
           const bool is_up = m & 1;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const float other = __shfl_xor_sync(0xffffffffu, v[jj], 1);
-            const int col = c0 + jj;
-            if ((jj & 1) == (int)is_up && col < n) {
-              const float gv = bf16r(is_up ? other : v[jj]), uv = bf16r(is_up ? v[jj] : other);
-              a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(swiglu_bf16_fast(gv, uv));
-            }
+          for (int k = 0; k < 16; ++k) {
+            const float recv = __shfl_xor_sync(0xffffffffu, is_up ? v[2 * k] : v[2 * k + 1], 1);
+            const int col = c0 + 2 * k + (is_up ? 1 : 0);
+            const float gv = bf16r(is_up ? recv : v[2 * k]), uv = bf16r(is_up ? v[2 * k + 1] : recv);
+            if (col < n) a.act_out[(size_t)(tl.p0 + col) * a.I + ku] = f32_to_bf16(swiglu_bf16_fast(gv, uv));
           }
         } else {
           const int row = tl.u0 + m;
@@ -405,7 +417,7 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
       tc_fence_before();
       mbar_arrive1(&acc_empty[b]);
     }
-  } else {
+  } else if (warp == TC_MW) {
     // ------------------------------------------------------------------ MMA
     int g = 0, j = 0;
     for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x, ++j) {
@@ -436,11 +448,38 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
     // the last commits must land before TMEM is released (bounded)
     if (lane == 0 && j > 0) (void)mbar_wait_bounded(&acc_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err);
     __syncwarp();
+  } else if (warp == TC_LW) {
+    // ------------------------------------------------------- B-row loader
+    // one TMA copy per stage (rows past the batch read as zeros), as soon as
+    // the stage's buffers are free
+    int g = 0;
+    for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x) {
+      const TcTile tl = a.tiles[ti];
+      const int n = tl.n;
+      const int slot = a.slot_of ? a.slot_of[tl.e] : tl.e;
+      const bool good = n >= 1 && n <= TC_NMAX && slot >= 0 && slot < a.n_slots;
+      // B box: the smallest map whose height covers the tile's MMA width
+      const int nmma = ((good ? n : 16) + 15) & ~15;
+      const int mi = nmma <= 16 ? 0 : nmma <= 32 ? 1 : nmma <= 64 ? 2 : nmma <= 128 ? 3 : 4;
+      const uint32_t box_bytes = (16u << mi) * 128u;
+      for (int kc = 0; kc < NK && ok; ++kc) {
+        const int gg = g + kc, s = gg % TC_S;
+        if (gg >= TC_S) ok = mbar_wait_bounded(&empty[s], ((gg / TC_S) - 1) & 1, a.err);
+        ok = __all_sync(0xffffffffu, ok) != 0;
+        if (!ok) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], good ? box_bytes : 0u);
+          if (good) tc_tma_rows(Bbuf + s * TC_B_BYTES, &maps.m[mi], 64 * kc, tl.p0, &full[s]);
+        }
+        __syncwarp();
+      }
+      g += NK;
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  if (warp == TC_MW) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
 
 }  // namespace ynb

@@ -18,18 +18,23 @@ experts from staging (`SlotPool.admit`). Group composition depends on routing
 alone, never on residency, so the arithmetic is identical on a cold and a warm
 pool.
 
-On the device (`streams` given) every copy runs on a copy stream and the GEMMs
-on the compute stream, ordered by events instead of host waits:
+On the device (`streams` given) host-tier reads and admissions run on a copy
+stream, pool -> staging copies and the GEMMs on the compute stream, ordered by
+events instead of host waits:
 
 * at the start of a layer the copy stream waits for the compute stream (the
   pool slots and the layer's rows are final; an admitted record may replace a
   slot an earlier layer read);
-* a group's `futures` are events on the copy stream; `result()` makes the
-  compute stream wait for them on the device;
+* a group's reads are issued before its pool copies, so the host link starts
+  at once; the group's `futures` are events on the copy stream, and `result()`
+  makes the compute stream wait for them on the device;
 * before a staging buffer is refilled (group g+2) the copy stream waits for the
-  GEMM of group g, which read it;
-* admitted records are copied staging -> pool slot on the copy stream, and the
-  compute stream waits for the copy stream at the end of the layer.
+  GEMM of group g, which read it (the compute stream's own copies follow it
+  in stream order);
+* admitted records are copied staging -> pool slot on the copy stream after it
+  has waited for the compute stream (pool copies queued there read their slots
+  first), and the compute stream waits for the copy stream at the end of the
+  layer.
 
 Without `streams` (host memory, the reference's arrangement) copies are
 synchronous and futures are whatever the reader returns.
@@ -204,24 +209,24 @@ class PrefillSweep:
         return torch.cuda.stream(self.streams.copy)
 
     def _load(self, st: _Staging, layer: int, experts: List[int]) -> None:
-        """Copy residents out of the pool, start host-tier reads for the rest."""
+        """Start the host-tier reads of the group's missing experts, then copy
+        its residents out of the pool (no reference-bit change). On the device
+        the reads go first, on the copy stream, and the pool copies run on the
+        current (compute) stream alongside them."""
         s_ = self.streams
         if s_ is not None and st.read_done is not None:
             s_.copy.wait_event(st.read_done)          # the GEMM that read this buffer has run
         st.index = {e: i for i, e in enumerate(experts)}      # sorted id order
-        missing = []
-        with self._on_copy_stream():
-            for e in experts:
-                s = self.pool.lookup((layer, e))
-                if s is not None:
-                    copy_record(st.views(e), self.pool.views(s))   # no reference-bit change
-                    self.stats.resident_copies += 1
-                else:
-                    missing.append(e)
+        slots = {e: self.pool.lookup((layer, e)) for e in experts}
+        missing = [e for e in experts if slots[e] is None]
         self.stats.disk_records += len(missing)
         st.futures = list(self.reader.submit_runs(layer, missing, st.views))
         if s_ is not None:
             st.futures.append(DeviceFuture(s_.event(s_.copy), s_.compute))
+        for e in experts:
+            if slots[e] is not None:
+                copy_record(st.views(e), self.pool.views(slots[e]))
+                self.stats.resident_copies += 1
 
     def run_layer(self, layer: int, x, ids: np.ndarray, w, moe: Callable, admit: bool):
         """moe(layer, x, ids, w, memory, rows) -> the contribution of `rows`' experts only."""
@@ -252,6 +257,8 @@ class PrefillSweep:
             out = part if out is None else out + part
             if admit_set:
                 members = [e for e in grp if e in admit_set]
+                if s_ is not None:
+                    s_.copy.wait_stream(s_.compute)   # pool copies already queued there read their slots first
                 with self._on_copy_stream():
                     self.stats.admitted += self.pool.admit(
                         layer, members, len(members), lambda e, dst: copy_record(dst, st.views(e)))
