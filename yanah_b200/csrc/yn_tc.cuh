@@ -303,60 +303,81 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
   if (warp < TC_PW) {
     // ------------------------------------------------------------ producers
     const int t = tid & (TC_M - 1), h = tid / TC_M;  // tile row, part of the row's stage
-    int g = 0;  // stages produced by this CTA so far
-    for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x) {
-      const TcTile tl = a.tiles[ti];
-      const int n = tl.n;
-      const int slot = a.slot_of ? a.slot_of[tl.e] : tl.e;
-      const bool good = n >= 1 && n <= TC_NMAX && slot >= 0 && slot < a.n_slots;
-      if (!good && t == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
+    // Where this thread's row of a tile lives: its code words and its scale / bias blocks.
+    struct RowSrc {
+      const uint8_t* w;
+      const uint4* s;
+      const uint4* b;
+      bool good;
+    };
+    auto row_src = [&](const TcTile& tl, int slot) -> RowSrc {
+      const bool good = tl.n >= 1 && tl.n <= TC_NMAX && slot >= 0 && slot < a.n_slots;
       const uint8_t* rec = a.base + (size_t)(good ? slot : 0) * (size_t)a.stride;
-      int wrow;
-      long long off_w, off_s, off_b;
-      if (MODE == 0) {
-        const bool up = t & 1;
-        wrow = tl.u0 + (t >> 1);
-        off_w = a.rg.off[up ? 3 : 0];
-        off_s = a.rg.off[up ? 4 : 1];
-        off_b = a.rg.off[up ? 5 : 2];
-      } else {
-        wrow = tl.u0 + t;
-        off_w = a.rg.off[6];
-        off_s = a.rg.off[7];
-        off_b = a.rg.off[8];
-      }
-      const uint8_t* wsrc = rec + off_w + (size_t)wrow * (Kd / 2);
-      // this thread's code words of stage kc into its slot of the code ring
-      // (TC_CR slots, read back only by this thread)
-      auto issue_codes = [&](int kc) {
-        if (good) {
-          uint8_t* cd = Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32 + h * 4 * TC_NW;
+      const bool up = (MODE == 0) && (t & 1);
+      const int wrow = MODE == 0 ? tl.u0 + (t >> 1) : tl.u0 + t;
+      const int pw = MODE == 0 ? (up ? 3 : 0) : 6;
+      return {rec + a.rg.off[pw] + (size_t)wrow * (Kd / 2),
+              reinterpret_cast<const uint4*>(rec + a.rg.off[pw + 1] + (size_t)wrow * NG * 2),
+              reinterpret_cast<const uint4*>(rec + a.rg.off[pw + 2] + (size_t)wrow * NG * 2), good};
+    };
+    // The next tile is prepared while the current one runs: its descriptor at
+    // the start, its slot one block later, its first scale block and its first
+    // TC_PC stages of code words in the last stages, so a tile starts without
+    // a chain of dependent global loads.
+    int g = 0;  // stages produced by this CTA so far
+    TcTile ntl = {0, 0, 0, 0};
+    int nslot = -1;
+    if ((int)blockIdx.x < n_tiles) {
+      ntl = a.tiles[blockIdx.x];
+      nslot = a.slot_of ? a.slot_of[ntl.e] : ntl.e;
+    }
+    RowSrc nsrc = row_src(ntl, nslot);
+    uint4 ns8 = make_uint4(0, 0, 0, 0), nb8 = ns8;
+    if (nsrc.good) {
+      ns8 = nsrc.s[0];
+      nb8 = nsrc.b[0];
+    }
+    // this thread's code words of stage kc of a tile into its slot of the code
+    // ring (TC_CR slots, read back only by this thread); one group per stage
+    auto issue_codes = [&](const RowSrc& r, int ring, int kc) {
+      if (r.good) {
+        uint8_t* cd = Cbuf + (ring % TC_CR) * TC_C_BYTES + t * 32 + h * 4 * TC_NW;
 #pragma unroll
-          for (int v = 0; v < TC_NW / 4; ++v) tc_cpa16(cd + 16 * v, wsrc + 32 * kc + h * 4 * TC_NW + 16 * v);
-        }
-        tc_cpa_commit();
-      };
-      // scales and biases of this row in blocks of 8 groups (16-byte loads, one block ahead)
-      const uint4* srow = reinterpret_cast<const uint4*>(rec + off_s + (size_t)wrow * NG * 2);
-      const uint4* brow = reinterpret_cast<const uint4*>(rec + off_b + (size_t)wrow * NG * 2);
-      uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8, s8n = s8, b8n = s8;
-      if (good) {
-        s8n = srow[0];
-        b8n = brow[0];
+        for (int v = 0; v < TC_NW / 4; ++v) tc_cpa16(cd + 16 * v, r.w + 32 * kc + h * 4 * TC_NW + 16 * v);
       }
-      for (int kc = 0; kc < TC_PC && kc < NK; ++kc) issue_codes(kc);
+      tc_cpa_commit();
+    };
+    for (int kc = 0; kc < TC_PC; ++kc) issue_codes(nsrc, kc, kc);  // NK >= 8 > TC_PC
+    for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x) {
+      const RowSrc src = nsrc;
+      const bool good = src.good;
+      if (!good && t == 0) raise_error(a.err, YN_ERR_BAD_SLOT);
+      const int tn = ti + gridDim.x;
+      const bool more = tn < n_tiles;
+      if (more) ntl = a.tiles[tn];
+      // scales and biases of this row in blocks of 8 groups (16-byte loads, one block ahead)
+      uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8, s8n = ns8, b8n = nb8;
       for (int kc0 = 0; kc0 < NK && ok; kc0 += 8) {
         s8 = s8n;
         b8 = b8n;
         if (good && kc0 + 8 < NK) {
-          s8n = srow[(kc0 + 8) / 8];
-          b8n = brow[(kc0 + 8) / 8];
+          s8n = src.s[(kc0 + 8) / 8];
+          b8n = src.b[(kc0 + 8) / 8];
+        }
+        if (more && kc0 == (NK > 8 ? 8 : 0)) nslot = a.slot_of ? a.slot_of[ntl.e] : ntl.e;
+        if (more && kc0 + 8 >= NK) {  // last block: the next tile's sources and first scale block
+          nsrc = row_src(ntl, nslot);
+          if (nsrc.good) {
+            ns8 = nsrc.s[0];
+            nb8 = nsrc.b[0];
+          }
         }
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
           const int kc = kc0 + jj;
           const int s = (g + kc) % TC_S;
-          if (kc + TC_PC < NK) issue_codes(kc + TC_PC);
+          if (kc + TC_PC < NK) issue_codes(src, g + kc + TC_PC, kc + TC_PC);
+          else if (more) issue_codes(nsrc, g + kc + TC_PC, kc + TC_PC - NK);
           else tc_cpa_commit();  // keep one group per stage
           // the stage's A buffer is free once the MMA of TC_S stages back has committed
           if (g + kc >= TC_S) ok = mbar_wait_bounded(&empty[s], (((g + kc) / TC_S) - 1) & 1, a.err);
@@ -373,9 +394,9 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
           mbar_arrive1(&full[s]);
         }
       }
-      tc_cpa_wait<0>();
       g += NK;
     }
+    tc_cpa_wait<0>();
   } else if (warp < TC_MW) {
     // ------------------------------------------------------------ epilogue
     const int q = (warp - TC_EW) & 3, m = 32 * q + lane;  // tile row of this thread
