@@ -616,7 +616,10 @@ YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, c
   }
 }
 
-constexpr int DEC_CW = 1;  // warps that issue the C-tile copies
+#ifndef YN_DEC_CW
+#define YN_DEC_CW 1
+#endif
+constexpr int DEC_CW = YN_DEC_CW;  // warps that issue the C-tile copies (tile t by warp t % DEC_CW)
 
 
 // D tile (down rows [d0, d0+nd) of every routed column and of the shared
@@ -903,7 +906,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
 
   if (tid == 0) {
     mbar_init(barA, DEC_THREADS);
-    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1 + 32 * DEC_CW);
+    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1 + 32);  // one issuing warp per tile
     mbar_init(barD, DEC_THREADS);
     fence_mbar_init();
   }
