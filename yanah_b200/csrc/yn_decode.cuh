@@ -950,16 +950,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     if (a_ok) {
       phA ^= 1;
       pendA = false;
-      // power-of-two scale of the normed row, fragments and group sums for P2
+      // power-of-two scale of the normed row; the router logits go out first,
+      // then the fragments and group sums for P2 are built while the other
+      // CTAs' logits arrive (routing's block syncs order them before P2)
       xscale2 = fp16_input_scale(rmsnorm_smem(hs, t1.norm, a.eps, xs, red));
+      stamp(a, tok, layer, 3);
+      p1_compute(a, r1, t1, xs, rbias_s, gu, par, ep);
       switch (fmt) {
         case 0: p2_frags<2, 64>(xs, xscale2, xf2, xsum2); break;
         case 1: p2_frags<2, 32>(xs, xscale2, xf2, xsum2); break;
         case 2: p2_frags<4, 64>(xs, xscale2, xf2, xsum2); break;
         default: p2_frags<4, 32>(xs, xscale2, xf2, xsum2); break;
       }
-      stamp(a, tok, layer, 3);
-      p1_compute(a, r1, t1, xs, rbias_s, gu, par, ep);
     }
     stamp(a, tok, layer, 4);
     if (!a_ok) { drain(); return; }
