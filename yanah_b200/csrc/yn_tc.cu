@@ -209,6 +209,15 @@ extern "C" int yn_pairs_combine(const yn_dims* dims, const void* y, const int32_
                                 const void* y_shared, const void* h_res, int32_t T, void* out, void* stream) {
   if (!dims || !y || !pair_of || !weights || !out || T < 1) return host_fail(YN_E_INVALID, "null argument or T < 1");
   const int H = dims->hidden;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (H % 8 == 0 && a16(y) && a16(out) && (!y_shared || a16(y_shared)) && (!h_res || a16(h_res))) {
+    dim3 grid((H / 8 + 255) / 256, T);
+    k_pairs_combine8<<<grid, 256, 0, as_st(stream)>>>(
+        reinterpret_cast<const uint16_t*>(y), pair_of, weights, reinterpret_cast<const uint16_t*>(y_shared),
+        reinterpret_cast<const uint16_t*>(h_res), H, dims->top_k, reinterpret_cast<uint16_t*>(out));
+    YN_CUDA_T(cudaGetLastError());
+    return YN_OK;
+  }
   dim3 grid((H + 255) / 256, T);
   k_pairs_combine<<<grid, 256, 0, as_st(stream)>>>(
       reinterpret_cast<const uint16_t*>(y), pair_of, weights, reinterpret_cast<const uint16_t*>(y_shared),

@@ -543,6 +543,53 @@ __global__ void k_gather_f16_kperm(const uint16_t* x, const int32_t* row_of, lon
 
 // out[t] = h_res[t] + (sum_j bf16(y[pair_of[t][j]] * w[t][j]) in column order [+ ysh[t]]),
 // rounded as the single-row combine.
+// The same combine with 8 columns per thread (16-byte loads and stores);
+// every element's arithmetic is that of k_pairs_combine. H % 8 == 0 and
+// 16-byte aligned rows.
+__global__ void k_pairs_combine8(const uint16_t* y, const int32_t* pair_of, const float* w, const uint16_t* ysh,
+                                 const uint16_t* h_res, int H, int K, uint16_t* out) {
+  const int t = blockIdx.y, r0 = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (r0 >= H) return;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int j = 0; j < K; ++j) {
+    const int p = pair_of[(size_t)t * K + j];
+    if (p < 0) continue;  // column outside the computed pairs (a staging group)
+    const float wj = w[(size_t)t * K + j];
+    const uint4 q = *reinterpret_cast<const uint4*>(y + (size_t)p * H + r0);
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float v = bf16_to_f32((uint16_t)(u[i >> 1] >> (16 * (i & 1))));
+      acc[i] = __fadd_rn(acc[i], bf16r(__fmul_rn(v, wj)));
+    }
+  }
+  uint32_t sh[4] = {0, 0, 0, 0}, hr[4] = {0, 0, 0, 0};
+  if (ysh) {
+    const uint4 q = *reinterpret_cast<const uint4*>(ysh + (size_t)t * H + r0);
+    sh[0] = q.x; sh[1] = q.y; sh[2] = q.z; sh[3] = q.w;
+  }
+  if (h_res) {
+    const uint4 q = *reinterpret_cast<const uint4*>(h_res + (size_t)t * H + r0);
+    hr[0] = q.x; hr[1] = q.y; hr[2] = q.z; hr[3] = q.w;
+  }
+  uint32_t o4[4];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    uint32_t pk = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float o = bf16r(acc[i + k]);
+      if (ysh) o = bf16r(__fadd_rn(o, bf16_to_f32((uint16_t)(sh[i >> 1] >> (16 * k)))));
+      if (h_res) o = bf16r(__fadd_rn(bf16_to_f32((uint16_t)(hr[i >> 1] >> (16 * k))), o));
+      pk |= (uint32_t)f32_to_bf16(o) << (16 * k);
+    }
+    o4[i >> 1] = pk;
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * H + r0) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+}
+
 __global__ void k_pairs_combine(const uint16_t* y, const int32_t* pair_of, const float* w, const uint16_t* ysh,
                                 const uint16_t* h_res, int H, int K, uint16_t* out) {
   const int t = blockIdx.y, r = blockIdx.x * blockDim.x + threadIdx.x;
