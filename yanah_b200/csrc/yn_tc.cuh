@@ -654,15 +654,35 @@ YN_DEV int2 block_scan2(int2 v, int2* total) {
   return make_int2(base.x + inc.x - v.x, base.y + inc.y - v.y);
 }
 
+// Warp-aggregated increment of ctr[e]: lanes with the same e take
+// consecutive values from one atomicAdd (popular experts would otherwise
+// serialise one shared-memory atomic per pair). Returns this lane's value.
+YN_DEV int agg_atomic_add(int* ctr, int e, bool active) {
+  const unsigned act = __ballot_sync(0xffffffffu, active);
+  if (!active) return 0;
+  const unsigned peers = __match_any_sync(act, e);
+  const int lane = threadIdx.x & 31, leader = __ffs(peers) - 1;
+  int base = 0;
+  if (lane == leader) base = atomicAdd(&ctr[e], __popc(peers));
+  base = __shfl_sync(peers, base, leader);
+  return base + __popc(peers & ((1u << lane) - 1u));
+}
+
+constexpr int PLAN_MAX_CHUNKS = 1024 + 65536 / TC_NMAX;  // experts + pairs / rows per tile
+
 __global__ void __launch_bounds__(PLAN_THREADS) k_prefill_plan(const PrefillPlanArgs a) {
   __shared__ int cnt[1024], start[1024], cursor[1024], toff[1024];
+  __shared__ int chunk_e[PLAN_MAX_CHUNKS], chunk_p0[PLAN_MAX_CHUNKS], chunk_n[PLAN_MAX_CHUNKS];
   const int P = a.T * a.K, tid = threadIdx.x;
   for (int e = tid; e < 1024; e += PLAN_THREADS) cnt[e] = cursor[e] = 0;
   __syncthreads();
-  for (int i = tid; i < P; i += PLAN_THREADS) {
-    const int e = a.ids[i];
-    if (e < 0 || e >= a.E) raise_error(a.err, YN_ERR_BAD_EXPERT);
-    else atomicAdd(&cnt[e], 1);
+  // loop bounds rounded up to whole warps: the aggregated atomics are warp-collective
+  const int Pw = (P + 31) & ~31;
+  for (int i = tid; i < Pw; i += PLAN_THREADS) {
+    const int e = i < P ? a.ids[i] : -1;
+    const bool valid = e >= 0 && e < a.E;
+    if (i < P && !valid) raise_error(a.err, YN_ERR_BAD_EXPERT);
+    agg_atomic_add(cnt, valid ? e : 0, valid);
   }
   __syncthreads();
   const int c = tid < a.E ? cnt[tid] : 0;
@@ -673,31 +693,40 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_prefill_plan(const PrefillPlan
     toff[tid] = ex.y;
   }
   __syncthreads();
-  for (int i = tid; i < P; i += PLAN_THREADS) {
-    const int e = a.ids[i];
-    if (e < 0 || e >= a.E) continue;
-    const int pos = start[e] + atomicAdd(&cursor[e], 1);
-    a.pair_row[pos] = i / a.K;
-    a.pair_of[i] = pos;
+  for (int i = tid; i < Pw; i += PLAN_THREADS) {
+    const int e = i < P ? a.ids[i] : -1;
+    const bool valid = e >= 0 && e < a.E;
+    const int pos = agg_atomic_add(cursor, valid ? e : 0, valid);
+    if (valid) {
+      a.pair_row[start[e] + pos] = i / a.K;
+      a.pair_of[i] = start[e] + pos;
+    }
   }
-  const int UT = a.I / 64, DT = a.H / 128;
+  // chunks of at most TC_NMAX pairs per expert, then every tile in parallel
   if (tid < a.E && c) {
     for (int k = 0; k * TC_NMAX < c; ++k) {
-      const int p0 = start[tid] + k * TC_NMAX, n = min(TC_NMAX, c - k * TC_NMAX), chunk = toff[tid] + k;
-      for (int u = 0; u < UT; ++u) {
-        const int q = chunk * UT + u;
-        if (q < a.max_up) a.up[q] = TcTile{tid, p0, n, 64 * u};
-      }
-      for (int r = 0; r < DT; ++r) {
-        const int q = chunk * DT + r;
-        if (q < a.max_dn) a.dn[q] = TcTile{tid, p0, n, 128 * r};
+      const int chunk = toff[tid] + k;
+      if (chunk < PLAN_MAX_CHUNKS) {
+        chunk_e[chunk] = tid;
+        chunk_p0[chunk] = start[tid] + k * TC_NMAX;
+        chunk_n[chunk] = min(TC_NMAX, c - k * TC_NMAX);
       }
     }
   }
+  __syncthreads();
+  const int UT = a.I / 64, DT = a.H / 128, nch = min(tot.y, PLAN_MAX_CHUNKS);
+  for (int q = tid; q < nch * UT && q < a.max_up; q += PLAN_THREADS) {
+    const int ch = q / UT;
+    a.up[q] = TcTile{chunk_e[ch], chunk_p0[ch], chunk_n[ch], 64 * (q % UT)};
+  }
+  for (int q = tid; q < nch * DT && q < a.max_dn; q += PLAN_THREADS) {
+    const int ch = q / DT;
+    a.dn[q] = TcTile{chunk_e[ch], chunk_p0[ch], chunk_n[ch], 128 * (q % DT)};
+  }
   if (tid == 0) {
-    a.n_tiles[0] = min(tot.y * UT, a.max_up);
-    a.n_tiles[1] = min(tot.y * DT, a.max_dn);
-    if (tot.y * UT > a.max_up || tot.y * DT > a.max_dn) raise_error(a.err, YN_ERR_BAD_SLOT);
+    a.n_tiles[0] = min(nch * UT, a.max_up);
+    a.n_tiles[1] = min(nch * DT, a.max_dn);
+    if (tot.y * UT > a.max_up || tot.y * DT > a.max_dn || tot.y > PLAN_MAX_CHUNKS) raise_error(a.err, YN_ERR_BAD_SLOT);
   }
 }
 
