@@ -32,6 +32,10 @@ What each fixture pins (the reference function that produced it):
   groups, resident copies and host reads per group, the rows given to each
   grouped ``moe`` call, the outputs, the pool after every layer (the final
   pass admits each layer's fair share) and the statistics.
+* ``repack.json`` — ``moe_prefetch/repack.py:66-126`` ``repack`` on the tiny
+  seeded checkpoints of ``tests/repack_driver.py``: the SHA-256 and size of
+  each experts.bin, the text of each experts.json, and, for the mixed-bit
+  checkpoint, the error it raises.
 * ``expert_mlp.npz`` — ``moe_prefetch/test_synthetic.py:46-51``
   ``expert_mlp`` (fp16 weights, fp32 SwiGLU MLP) on weights that are exactly
   representable as 4-bit affine codes, so the quantised CUDA/oracle path and
@@ -41,6 +45,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -244,15 +249,44 @@ def make_sweep(seed: int = 20261202) -> dict:
     return {"cases": cases}
 
 
+def make_repack() -> dict:
+    """Reference repack on every checkpoint of tests/repack_driver.CASES."""
+    import hashlib
+    import tempfile
+    sys.path.insert(0, str(REPO))
+    from tests.repack_driver import CASES, write_checkpoint
+    from moe_prefetch.repack import repack
+
+    out = {}
+    for case in CASES:
+        with tempfile.TemporaryDirectory() as tmp:
+            model, dst = os.path.join(tmp, "model"), os.path.join(tmp, "out")
+            write_checkpoint(model, case)
+            try:
+                repack(model, dst)
+            except ValueError as exc:
+                out[case] = {"error": type(exc).__name__, "message": str(exc)}
+                continue
+            with open(os.path.join(dst, "experts.bin"), "rb") as fh:
+                data = fh.read()
+            with open(os.path.join(dst, "experts.json")) as fh:
+                text = fh.read()
+            out[case] = {"sha256": hashlib.sha256(data).hexdigest(), "bytes": len(data), "json": text}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["sweep"], help="write only this fixture")
+    ap.add_argument("--only", choices=["sweep", "repack"], help="write only this fixture")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
     if args.only == "sweep":
         (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
+        return
+    if args.only == "repack":
+        (HERE / "repack.json").write_text(json.dumps(make_repack(), indent=1) + "\n")
         return
     rng = np.random.default_rng(20260101)
     (HERE / "layout.json").write_text(json.dumps(make_layout(ref), indent=1) + "\n")
@@ -264,6 +298,7 @@ def main():
     np.savez_compressed(HERE / "pool_small.npz", **make_pool(rng, S=40, L=12, E=128, k=8, n_cand=16, spec=32))
     np.savez_compressed(HERE / "pool_wide.npz", **make_pool(rng, S=12, L=24, E=512, k=10, n_cand=12, spec=64))
     (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
+    (HERE / "repack.json").write_text(json.dumps(make_repack(), indent=1) + "\n")
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 

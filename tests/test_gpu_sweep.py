@@ -159,3 +159,26 @@ def test_sweep_lfm2_layer():
     assert ps.check_error() == 0
     assert rel_l2(bf16_np(out), bf16_np(y0)) < REL_L2_TOL
     sw.close()
+
+
+def test_sweep_from_repacked_file_tier(tmp_path):
+    # the host tier read from an experts.bin written by the record writer gives
+    # the same prompt pass, bit for bit, as the tier generated in memory
+    from tests.repack_driver import write_checkpoint_from_tier
+    from yanah_b200.repack import FileHostTier, repack
+
+    cfg = small_config(bits=(4, 4), gs=64, hidden=512, n_experts=16, top_k=2, inter=512, shared=0, seed=9)
+    be = CudaMoEBackend(cfg)
+    tier = HostTier(cfg, be.device)
+    write_checkpoint_from_tier(str(tmp_path / "model"), cfg, tier, [0, 1])
+    repack(str(tmp_path / "model"), str(tmp_path / "out"))
+    ftier = FileHostTier(str(tmp_path / "out"))
+    assert ftier.slot == cfg.record_spec(0).slot_bytes
+    hd = bf16_dev(hidden_rows(cfg, 24, stream=47))
+    outs = []
+    for t in (tier, ftier):
+        sw = _sweep(be, t, _pool(be, t, 12, 2, [(0, 3), (1, 7)]), 4)
+        outs.append(_pass_by_layer(be, sw, hd, [0, 1], admit=True))
+        sw.close()
+    for a, b in zip(*outs):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
