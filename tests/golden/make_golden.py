@@ -36,6 +36,10 @@ What each fixture pins (the reference function that produced it):
   seeded checkpoints of ``tests/repack_driver.py``: the SHA-256 and size of
   each experts.bin, the text of each experts.json, and, for the mixed-bit
   checkpoint, the error it raises.
+* ``speculation.json`` — ``moe_prefetch/speculative.py:39-77``
+  ``AdaptiveSpeculationPolicy`` driven by ``tests/speculation_driver.py``
+  through seeded decode sessions: every action, step time, emitted count,
+  depth and stop flag.
 * ``expert_mlp.npz`` — ``moe_prefetch/test_synthetic.py:46-51``
   ``expert_mlp`` (fp16 weights, fp32 SwiGLU MLP) on weights that are exactly
   representable as 4-bit affine codes, so the quantised CUDA/oracle path and
@@ -275,15 +279,32 @@ def make_repack() -> dict:
     return out
 
 
+SPEC_SESSIONS = [(1, 3, 0.8, 0.2), (2, 4, 0.3, 0.35), (3, 8, 0.6, 0.3), (4, 16, 0.9, 0.1), (5, 2, 0.1, 0.4),
+                 (6, 4, 0.95, 0.05)]
+
+
+def make_speculation() -> dict:
+    """Reference AdaptiveSpeculationPolicy through the seeded sessions of SPEC_SESSIONS."""
+    sys.path.insert(0, str(REPO))
+    from tests.speculation_driver import drive_policy
+    from moe_prefetch.speculative import AdaptiveSpeculationPolicy
+
+    return {"sessions": [{"args": list(a), "log": drive_policy(AdaptiveSpeculationPolicy, *a)}
+                         for a in SPEC_SESSIONS]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["sweep", "repack"], help="write only this fixture")
+    ap.add_argument("--only", choices=["sweep", "repack", "speculation"], help="write only this fixture")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
     if args.only == "sweep":
         (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
+        return
+    if args.only == "speculation":
+        (HERE / "speculation.json").write_text(json.dumps(make_speculation()) + "\n")
         return
     if args.only == "repack":
         (HERE / "repack.json").write_text(json.dumps(make_repack(), indent=1) + "\n")
@@ -299,6 +320,7 @@ def main():
     np.savez_compressed(HERE / "pool_wide.npz", **make_pool(rng, S=12, L=24, E=512, k=10, n_cand=12, spec=64))
     (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
     (HERE / "repack.json").write_text(json.dumps(make_repack(), indent=1) + "\n")
+    (HERE / "speculation.json").write_text(json.dumps(make_speculation()) + "\n")
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 
