@@ -672,7 +672,7 @@ constexpr int PLAN_MAX_CHUNKS = 1024 + 65536 / TC_NMAX;  // experts + pairs / ro
 
 __global__ void __launch_bounds__(PLAN_THREADS) k_prefill_plan(const PrefillPlanArgs a) {
   __shared__ int cnt[1024], start[1024], cursor[1024], toff[1024];
-  __shared__ int chunk_e[PLAN_MAX_CHUNKS], chunk_p0[PLAN_MAX_CHUNKS], chunk_n[PLAN_MAX_CHUNKS];
+  __shared__ int chunk_e[PLAN_MAX_CHUNKS], chunk_p0[PLAN_MAX_CHUNKS], chunk_n[PLAN_MAX_CHUNKS], order[PLAN_MAX_CHUNKS];
   const int P = a.T * a.K, tid = threadIdx.x;
   for (int e = tid; e < 1024; e += PLAN_THREADS) cnt[e] = cursor[e] = 0;
   __syncthreads();
@@ -715,12 +715,28 @@ __global__ void __launch_bounds__(PLAN_THREADS) k_prefill_plan(const PrefillPlan
   }
   __syncthreads();
   const int UT = a.I / 64, DT = a.H / 128, nch = min(tot.y, PLAN_MAX_CHUNKS);
+  // Tiles of the largest chunks first: the persistent GEMM CTAs take the
+  // tiles round-robin, so descending rows per tile evens out their work. A
+  // counting sort on TC_NMAX - rows (cnt / cursor / start are free again).
+  for (int k = tid; k <= TC_NMAX; k += PLAN_THREADS) cnt[k] = cursor[k] = 0;
+  __syncthreads();
+  for (int ch = tid; ch < nch; ch += PLAN_THREADS) atomicAdd(&cnt[TC_NMAX - chunk_n[ch]], 1);
+  __syncthreads();
+  int2 btot;
+  const int2 bex = block_scan2(make_int2(tid <= TC_NMAX ? cnt[tid] : 0, 0), &btot);
+  if (tid <= TC_NMAX) start[tid] = bex.x;
+  __syncthreads();
+  for (int ch = tid; ch < nch; ch += PLAN_THREADS) {
+    const int key = TC_NMAX - chunk_n[ch];
+    order[start[key] + atomicAdd(&cursor[key], 1)] = ch;
+  }
+  __syncthreads();
   for (int q = tid; q < nch * UT && q < a.max_up; q += PLAN_THREADS) {
-    const int ch = q / UT;
+    const int ch = order[q / UT];
     a.up[q] = TcTile{chunk_e[ch], chunk_p0[ch], chunk_n[ch], 64 * (q % UT)};
   }
   for (int q = tid; q < nch * DT && q < a.max_dn; q += PLAN_THREADS) {
-    const int ch = q / DT;
+    const int ch = order[q / DT];
     a.dn[q] = TcTile{chunk_e[ch], chunk_p0[ch], chunk_n[ch], 128 * (q % DT)};
   }
   if (tid == 0) {
