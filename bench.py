@@ -61,6 +61,15 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def sub_label(name: str, args, n_total: int) -> str:
+    """Workload name of a run over a layer sub-range (--layers/--first-layer):
+    the full stack's name only when every layer runs."""
+    n = args.layers or n_total
+    if n == n_total and args.first_layer == 0:
+        return name
+    return f"{name}_sub{n}_from{args.first_layer}"
+
+
 def workload_config(cfg, tokens):
     return {
         "workload": "qwen3_next_80b_a3b_moe_stack48_bs1_decode",
@@ -266,7 +275,7 @@ def run_streaming(args, rank: int, world: int):
     r = dec.report(secs)
     if dec.be.check_error():
         raise RuntimeError("device error in the streaming decode")
-    tr = np.array(dec.trace).reshape(-1, cfg.n_layers, cfg.top_k)
+    tr = np.array([ids for _, _, ids, _ in dec.trace]).reshape(-1, cfg.n_layers, cfg.top_k)
     rep = float(np.mean([len(set(tr[t, l]) & set(tr[t - 1, l])) / cfg.top_k
                          for t in range(1, tr.shape[0]) for l in range(cfg.n_layers)])) if tr.shape[0] > 1 else 0.0
     tokens = N * args.steps
@@ -407,7 +416,7 @@ def run_ep(args, rank: int, world: int):
         "metric": EP_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "qwen3_next_80b_a3b_moe_stack48_ep_batch64_decode", "layers": L, "batch": B,
+        "config": {"workload": sub_label("qwen3_next_80b_a3b_moe_stack48_ep_batch64_decode", args, cfg.n_layers), "layers": L, "batch": B,
                    "rows_per_gpu": T_h, "experts_per_gpu": hi - lo, "hidden": H, "experts": cfg.n_experts,
                    "top_k": K, "expert_bits": "4-bit g64 layers 0-3 and 44-47, 2-bit g64 layers 4-43",
                    "parallelism": f"ep{world}",
@@ -504,7 +513,7 @@ def run_prefill(args, rank: int, world: int):
         "metric": PREFILL_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "lfm2_24b_a2b_moe_stack40_prefill", "layers": L, "prompts": 8,
+        "config": {"workload": sub_label("lfm2_24b_a2b_moe_stack40_prefill", args, cfg.n_layers), "layers": L, "prompts": 8,
                    "prompt_lengths": lens.tolist(), "rows": T, "hidden": H, "experts": cfg.n_experts, "top_k": K,
                    "moe_inter": I, "expert_bits": "4-bit g64", "router_bits": 8,
                    "gemm_operands": "gate/up fp16, down bf16 (dequantised weights and activations), fp32 accumulate in TMEM",
@@ -716,7 +725,7 @@ def run_verify(args, rank: int, world: int):
         "metric": VERIFY_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "lfm2_24b_a2b_moe_stack40_verify_1p4", "layers": L, "rows_per_step": B,
+        "config": {"workload": sub_label("lfm2_24b_a2b_moe_stack40_verify_1p4", args, cfg.n_layers), "layers": L, "rows_per_step": B,
                    "hidden": H, "experts": cfg.n_experts, "top_k": K, "moe_inter": cfg.moe_inter,
                    "expert_bits": "4-bit g64",
                    "l2": "no flush: a step reads the routed records of 40 layers (~1 GB > 126 MB L2)"},
@@ -841,7 +850,8 @@ def run_ours(args, rank: int, world: int):
                      "traffic": traffic},
         "phases": phases,
     }
-    if args.layers:
+    if args.layers or args.first_layer:
+        line["config"]["workload"] = sub_label(line["config"]["workload"], args, cfg.n_layers)
         line["config"]["layers"] = len(layers)
         line["config"]["bytes_per_token"] = bytes_tok
     if rank == 0 and world == 1 and not args.no_cpu and not args.layers:

@@ -194,15 +194,21 @@ int yn_moe_layer_noalloc(const yn_dims* dims, const yn_layer* layer, const void*
  * Prepare once: yn_stack_prepare copies the layer descriptors into a device
  * table of yn_stack_table_bytes(n_layers) bytes; `layers` is the same host
  * array (used for sizing). inputs/outputs: (n_tokens, H) bf16.
- * trace_ids: (n_tokens, n_layers, k) routed ids or NULL. timing: (n_layers,
- * 16, n_SMs) int64 global-timer stamps (ns) of the last token's phases on
- * every CTA, or NULL (diagnostics: adds a block sync per stamp). */
+ * Per-layer traces, each optional (NULL: not written): trace_ids (n_tokens,
+ * n_layers, k) routed ids; trace_hidden (n_tokens, n_layers, H) bf16, the
+ * input row of every layer (16-byte aligned); trace_weights (n_tokens,
+ * n_layers, k) fp32 routed weights. With them a caller can check every
+ * layer of the decode against its own reference on the kernel's own layer
+ * inputs. timing: (n_layers, 16, n_SMs) int64 global-timer stamps (ns) of the
+ * last token's phases on every CTA, or NULL (diagnostics: adds a block sync
+ * per stamp). */
 size_t yn_stack_table_bytes(int32_t n_layers);
 size_t yn_stack_scratch_bytes(const yn_dims* dims);
 int yn_stack_prepare(const yn_dims* dims, const yn_layer* layers, int32_t n_layers, void* table, size_t table_bytes);
 int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
                     const void* inputs, int32_t n_tokens, void* outputs, void* scratch, size_t scratch_bytes,
-                    int32_t* trace_ids, int64_t* timing, void* stream);
+                    int32_t* trace_ids, void* trace_hidden, float* trace_weights, int64_t* timing,
+                    void* stream);
 /* Read and clear the stack decode error word (synchronises the stream). */
 int yn_stack_error(void* scratch, const yn_dims* dims, void* stream, int32_t* code_out);
 

@@ -1,10 +1,10 @@
 """Generate the golden fixtures in this directory from the reference's own code.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference``; the fixtures it writes are committed, so nothing that
-runs on a GPU machine needs the reference:
+Run where a checkout of the reference is readable, giving its path (or
+setting YANAH_REFERENCE); the fixtures it writes are committed, so nothing
+that runs on a GPU machine needs the reference:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 What each fixture pins (the reference function that produced it):
 
@@ -36,6 +36,15 @@ What each fixture pins (the reference function that produced it):
   seeded checkpoints of ``tests/repack_driver.py``: the SHA-256 and size of
   each experts.bin, the text of each experts.json, and, for the mixed-bit
   checkpoint, the error it raises.
+* ``orchestrator.json.gz`` — ``moe_prefetch/orchestrator.py:158-343``
+  ``MoEOrchestrator`` (pool path, lazy, resident-first overlap) over the
+  reference ``SlotPool``, ``RouterForecast`` and ``SpeculativeScheduler``,
+  driven by ``tests/orch_driver.py`` over the C oracle on an eight-layer
+  Qwen3-Next-shaped stack: every backend hook call with its arguments, every
+  record read with its slot, the pool statistics after every layer, the
+  routing trace, the reference ``cache_sim.save_trace`` arrays (digests) and
+  the ``cache_sim`` replay of that trace (per-layer counters, final
+  dictionary, miss log).
 * ``speculation.json`` — ``moe_prefetch/speculative.py:39-77``
   ``AdaptiveSpeculationPolicy`` driven by ``tests/speculation_driver.py``
   through seeded decode sessions: every action, step time, emitted count,
@@ -293,10 +302,31 @@ def make_speculation() -> dict:
                          for a in SPEC_SESSIONS]}
 
 
+def make_orchestrator() -> dict:
+    """The reference's MoEOrchestrator, SlotPool, RouterForecast and
+    SpeculativeScheduler driven over the C oracle on an eight-layer
+    Qwen3-Next-shaped stack (tests/orch_driver.py): hook calls, record reads,
+    pool statistics per layer, the routing trace and its cache_sim replay."""
+    sys.path.insert(0, str(REPO))
+    from moe_prefetch import cache_sim, io_lanes, layout, orchestrator, pool, predictor
+    from tests import orch_driver as od
+    cfg = od.orch_config()
+    return od.run_reference((orchestrator, pool, io_lanes, predictor, layout, cache_sim), cfg, od.token_inputs(cfg))
+
+
+def write_orchestrator() -> None:
+    import gzip
+    with gzip.open(HERE / "orchestrator.json.gz", "wt") as f:
+        json.dump(make_orchestrator(), f, separators=(",", ":"))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["sweep", "repack", "speculation"], help="write only this fixture")
+    ap.add_argument("--reference", default=os.environ.get("YANAH_REFERENCE"),
+                    required="YANAH_REFERENCE" not in os.environ,
+                    help="path of the reference checkout (default: $YANAH_REFERENCE)")
+    ap.add_argument("--only", choices=["sweep", "repack", "speculation", "orchestrator"],
+                    help="write only this fixture")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
@@ -305,6 +335,9 @@ def main():
         return
     if args.only == "speculation":
         (HERE / "speculation.json").write_text(json.dumps(make_speculation()) + "\n")
+        return
+    if args.only == "orchestrator":
+        write_orchestrator()
         return
     if args.only == "repack":
         (HERE / "repack.json").write_text(json.dumps(make_repack(), indent=1) + "\n")
@@ -321,6 +354,7 @@ def main():
     (HERE / "sweep.json").write_text(json.dumps(make_sweep()) + "\n")
     (HERE / "repack.json").write_text(json.dumps(make_repack(), indent=1) + "\n")
     (HERE / "speculation.json").write_text(json.dumps(make_speculation()) + "\n")
+    write_orchestrator()
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 

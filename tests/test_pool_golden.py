@@ -2,11 +2,11 @@
 
 Fixtures (tests/golden/pool_*.npz, written by tests/golden/make_golden.py):
 the reference SlotPool (moe_prefetch/pool.py) driven by the orchestrator-like
-sequence of tests/pool_driver.py, and the reference cache_sim replay
-(PoolSim + ForecastPolicy in simulate's loop order) on the same seeded
-Zipf(1.1) / repeat-0.6 routing trace. Everything is compared exactly: every
-slot decision, the pool statistics, the per-(step, layer) counters, the final
-dictionary and the demand-miss log.
+sequence of tests/pool_driver.py on a seeded Zipf(1.1) / repeat-0.6 routing
+trace. Every slot decision and the pool statistics are compared exactly.
+(The fixtures also hold the reference cache_sim's replay of those traces; the
+streaming path's trace is pinned against cache_sim in
+tests/test_orchestrator_golden.py and tests/test_gpu_orchestrator.py.)
 """
 from __future__ import annotations
 
@@ -17,7 +17,7 @@ import pytest
 
 from tests.pool_driver import NullMemory, drive_slot_pool, fc_from_arrays, stats_tuple
 from yanah_b200.formats import ModelGeometry
-from yanah_b200.pool import ForecastPolicy, PoolSim, SlotPool, simulate
+from yanah_b200.pool import SlotPool
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 CASES = ["pool_small.npz", "pool_wide.npz"]
@@ -48,22 +48,3 @@ def test_slot_pool_decisions_match_reference(name):
     st = pool.stats
     assert st.hits and st.misses and st.adopted and st.adopt_evictions and st.spec_discarded
     assert st.evictions or "wide" in name
-
-
-@pytest.mark.parametrize("name", CASES)
-def test_cache_sim_replay_matches_reference(name):
-    z, routed, fc, S, L, k = _load(name)
-    snaps = []
-    miss_log = []
-    final = simulate(routed, fc, z["test"], int(z["slots"]), int(z["spec"]), forecast=ForecastPolicy(fc, 0.062, 32),
-                     miss_log=miss_log, on_layer=lambda s, l, sim: snaps.append([sim.c[n] for n in PoolSim.COUNTERS]))
-    assert np.array_equal(np.array(snaps).reshape(S, L, -1), z["snaps"])
-    ref = dict(zip(z["final_keys"].tolist(), z["final_vals"].tolist()))
-    assert set(ref) == set(final)
-    for key, v in ref.items():
-        assert final[key] == v, key
-    lens = z["miss_len"].tolist()
-    assert [len(m) for _, m in miss_log] == lens
-    assert [l for l, m in miss_log for _ in m] == z["miss_layer"].tolist()
-    assert [e for _, m in miss_log for e in m] == z["miss_expert"].tolist()
-    assert final["adopted"] > 0 and final["demand"] > 0 and final["wasted"] > 0

@@ -1,7 +1,7 @@
 """CUDA backend for the MoE part of the reference's ModelBackend interface.
 
 Mirrors the hooks `moe_prefetch/orchestrator.py` calls on
-`moe_prefetch/mlx_backend.py` (see INTEGRATION.md for the table):
+`moe_prefetch/mlx_backend.py`:
 
     pre_moe(layer, h1) -> (h_res, x, logits)          mlx_backend.py:290-306
     route(logits) -> (ids np (T,k), w)                :308-316

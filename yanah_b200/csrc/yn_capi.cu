@@ -808,7 +808,8 @@ static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) 
 
 extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
                                const void* inputs, int32_t n_tokens, void* outputs, void* scratch,
-                               size_t scratch_bytes, int32_t* trace_ids, int64_t* timing, void* stream) {
+                               size_t scratch_bytes, int32_t* trace_ids, void* trace_hidden, float* trace_weights,
+                               int64_t* timing, void* stream) {
   int rc = check_dims(dims, 1);
   if (rc) return rc;
   const yn_dims& d = *dims;
@@ -907,6 +908,9 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   a.act_sh = reinterpret_cast<uint16_t*>(sc + S.act_sh);
   a.sgate = reinterpret_cast<float*>(sc + S.sgate);
   a.trace_ids = trace_ids;
+  a.trace_h = reinterpret_cast<uint16_t*>(trace_hidden);
+  a.trace_w = trace_weights;
+  if (trace_hidden && !al16(trace_hidden)) return fail(YN_E_INVALID, "stack decode: trace_hidden must be 16-byte aligned");
   a.bar = reinterpret_cast<unsigned*>(sc + S.bar);
   a.err = reinterpret_cast<int*>(sc + S.err);
   a.timing = reinterpret_cast<long long*>(timing);

@@ -86,6 +86,8 @@ struct DecodeArgs {
   uint16_t* act_sh;    // (Ish) shared-expert SwiGLU activations
   float* sgate;        // (1) shared-expert gate
   int32_t* trace_ids;  // (n_tokens, n_layers, K) or null
+  uint16_t* trace_h;   // (n_tokens, n_layers, H) each layer's input row, or null
+  float* trace_w;      // (n_tokens, n_layers, K) routed weights, or null
   unsigned* bar;       // grid barrier counter (zeroed before every launch)
   int* err;
   long long* timing;   // (n_layers, DEC_STAMPS, grid) for the last token, or null
@@ -939,7 +941,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     {
       const uint16_t* hin = (layer == 0) ? a.inputs + (size_t)tok * DEC_H : a.hbuf + (size_t)par * DEC_H;
       const float bv = (tid < nr1 && L.rbias) ? __ldcg(L.rbias + r1.r0 + tid) : 0.0f;
-      if (tid < DEC_H / 8) reinterpret_cast<uint4*>(hs)[tid] = __ldcg(reinterpret_cast<const uint4*>(hin) + tid);
+      if (tid < DEC_H / 8) {
+        const uint4 hv = __ldcg(reinterpret_cast<const uint4*>(hin) + tid);
+        reinterpret_cast<uint4*>(hs)[tid] = hv;
+        if (a.trace_h && b == 0)
+          reinterpret_cast<uint4*>(a.trace_h + ((size_t)tok * a.n_layers + layer) * DEC_H)[tid] = hv;
+      }
       if (tid < 64) rbias_s[tid] = bv;
     }
     const P1Tile t1 = p1_tile(Abuf, r1);
@@ -971,7 +978,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
       drain();
       return;
     }
-    if (a.trace_ids && b == 0 && tid < K) a.trace_ids[((size_t)tok * a.n_layers + layer) * K + tid] = ids[tid];
+    if (b == 0 && tid < K) {
+      if (a.trace_ids) a.trace_ids[((size_t)tok * a.n_layers + layer) * K + tid] = ids[tid];
+      if (a.trace_w) a.trace_w[((size_t)tok * a.n_layers + layer) * K + tid] = wts[tid];
+    }
     stamp(a, tok, layer, 6);
     const bool ids_ok = *ids_ok_s != 0;   // block-uniform (set before routing's last sync)
     if (!ids_ok && tid == 0) raise_error(a.err, YN_ERR_BAD_SLOT);

@@ -46,6 +46,9 @@ inline WsLayout ws_layout(const yn_dims& d) {
   const size_t T = YN_MAX_ROWS, NT = YN_MAX_TARGETS;
   const size_t H = d.hidden, E = d.n_experts, K = d.top_k, I = d.moe_inter, Ish = d.shared_inter;
   L.n_cb = (int)((H + CB_ROWS - 1) / CB_ROWS);
+  // The error word and the combine counters come first, in this order, for
+  // every dims: yn_moe_layer_noalloc keeps them zero across calls of
+  // different shapes by zeroing only [counters, counters + size) growth.
   L.err = take(4);
   L.counters = take((1 + T * L.n_cb) * 4);
   L.x = take(T * H * 2);

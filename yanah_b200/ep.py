@@ -82,6 +82,9 @@ class ExpertParallelStack:
         if not 1 <= batch <= MAX_BATCH_ROWS:
             raise ValueError("batch must be in [1, 64]")
         self.cfg, self.rank, self.world, self.batch = cfg, rank, world, batch
+        self.group = group
+        self.sym = None
+        self._imported: List[int] = []
         self.device = torch.device(device)
         self.rows = home_rows(batch, rank, world)
         self.rows_per_rank = batch // world
@@ -113,7 +116,6 @@ class ExpertParallelStack:
         _lib.check(lib.yn_ep_init(self.sym, self.local.data_ptr(), C.byref(self.dims), C.byref(self.ep),
                                   stream_ptr()))
         torch.cuda.synchronize(self.device)
-        self._imported: List[int] = []
         if world > 1:
             h = (C.c_uint8 * _lib.YN_IPC_HANDLE_BYTES)()
             _lib.check(lib.yn_ipc_export(self.sym, h))
@@ -214,8 +216,24 @@ class ExpertParallelStack:
         return out
 
     def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's peer-visible one.
+
+        With world > 1 this is collective: every rank calls it after its
+        last step. Peers store into this rank's buffer during a step, so it
+        is freed only after a barrier over the group has shown that every
+        rank has finished (its own steps synchronised first). If the process
+        group is already gone the peers cannot be waited for, and the buffer
+        is left mapped until the process exits rather than freed under them."""
+        if self.sym is None and not self._imported:
+            return
         lib = _lib.lib()
         torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            import torch.distributed as dist
+            if not (dist.is_available() and dist.is_initialized()):
+                self._imported, self.sym = [], None
+                return
+            dist.barrier(group=self.group)
         for p in self._imported:
             lib.yn_ipc_close(p)
         self._imported = []
@@ -224,6 +242,11 @@ class ExpertParallelStack:
             self.sym = None
 
     def __del__(self):
+        # A collective cannot run from the garbage collector (ranks collect at
+        # different times), so a multi-rank stack that was not closed keeps its
+        # buffer until the process exits.
+        if self.world > 1:
+            return
         try:
             self.close()
         except Exception:

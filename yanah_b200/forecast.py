@@ -7,9 +7,11 @@ into the candidate list the prefetcher issues, and keeps recall statistics,
 as ``RouterForecast`` in backend mode does in moe_prefetch/predictor.py:49-125
 (``select`` :100-111, ``observe`` :113-118, stats :37-47).
 
-Selection order: descending probability; equal probabilities go to the lower
-expert id (the reference sorts a partition with an unstable sort, so its tie
-order is unspecified; on tie-free inputs both give the same list).
+Selection order: the `top` largest probabilities by numpy's introselect
+(`argpartition`), then ordered by descending probability with numpy's
+default sort. Equal probabilities are common (router logits are bf16 before
+the softmax), and these two calls fix their order exactly as the reference's
+selection does, so the candidate lists match element for element.
 """
 from __future__ import annotations
 
@@ -46,8 +48,9 @@ class RouterForecast:
         k = min(int(top), score.shape[0])
         if k <= 0:
             return []
-        ids = np.arange(score.shape[0])
-        order = np.lexsort((ids, -score.astype(np.float64)))[:k]
+        neg = -score
+        part = np.argpartition(neg, k - 1)[:k]          # the k most probable, in no particular order
+        order = part[np.argsort(neg[part])]             # most probable first; ties as numpy's sort leaves them
         out = [(int(e), float(score[e])) for e in order]
         self._pending.setdefault(target_layer, set()).update(e for e, _ in out)
         self.stats.forecasts += 1

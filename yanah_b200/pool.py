@@ -16,11 +16,10 @@ identically on top of HBM slots (`backend.CudaExpertMemory`):
   to stay full; an unused forecast goes back to the partition.
 * Pins protect the slots of the layer being computed.
 
-`PoolSim` / `ForecastPolicy` / `simulate` replay a routing trace with the
-same CLOCK + partition model as moe_prefetch/cache_sim.py:88-195, :296-323
-(per layer: use the routed experts, issue forecasts, expire forecasts that
-target this layer or earlier), so hit / adopted / demand / prefetch / wasted
-counts can be compared per (step, layer).
+The reference's offline cache simulator (moe_prefetch/cache_sim.py) is not
+part of this package: the streaming decoder writes its routing trace in that
+tool's format (yanah_b200/trace.py), so the reference's own simulator can
+replay it.
 """
 from __future__ import annotations
 
@@ -53,9 +52,11 @@ class SlotPool:
                  memory=None):
         k = geometry.top_k
         if slots < 3 * k:
-            raise ValueError(f"{slots} slots cannot hold a layer's routing plus margin")
+            raise ValueError(f"pool of {slots} slots: at least 3 x top_k = {3 * k} are needed "
+                             f"(one layer's experts pinned, with room to evict)")
         if slots - spec_slot_cap < 3 * k:
-            raise ValueError(f"spec_slot_cap {spec_slot_cap} leaves too few demand slots in {slots}")
+            raise ValueError(f"pool of {slots} slots with a speculative partition of {spec_slot_cap}: "
+                             f"{slots - spec_slot_cap} demand slots left, at least {3 * k} are needed")
         self.g, self.slots, self.memory = geometry, slots, memory
         self.slot_bytes = geometry.slot_nbytes
         self.spec_slot_cap = spec_slot_cap
@@ -110,7 +111,8 @@ class SlotPool:
                 self.key_of[s] = None
                 self.stats.evictions += 1
             return s
-        raise MemoryError(f"slot pool exhausted: all {self.slots} slots pinned or reserved")
+        raise MemoryError(f"no evictable slot among {self.slots}: every slot is pinned, reserved for a "
+                          f"forecast read or in the speculative partition")
 
     # ----------------------------------------------------------------- memory
     def views(self, slot: int):
@@ -235,146 +237,3 @@ class SlotPool:
     def close(self) -> None:
         if self.memory is not None:
             self.memory.close()
-
-
-# --------------------------------------------------------------- offline replay
-class PoolSim:
-    """CLOCK over `slots - spec_slots` demand slots plus a partition of
-    `spec_slots` for forecasts not yet used (cache_sim.py:88-178)."""
-
-    COUNTERS = ("uses", "hits", "adopted", "demand", "prefetch", "wasted", "refused", "tokens")
-
-    def __init__(self, slots: int, spec_slots: int):
-        self.n = slots - spec_slots
-        self.spec = spec_slots
-        self.key_of: List[Optional[Key]] = [None] * self.n
-        self.ref = [False] * self.n
-        self.map: Dict[Key, int] = {}
-        self._fresh = 0
-        self.hand = 0
-        self.staged: Dict[Key, int] = {}     # forecast read, not yet used -> target layer
-        self.measure = False
-        self.c = {name: 0 for name in self.COUNTERS}
-        self.miss_log: Optional[list] = None
-
-    def _add(self, name: str, n: int = 1) -> None:
-        if self.measure:
-            self.c[name] += n
-
-    def _victim(self, pinned) -> int:
-        if self._fresh < self.n:
-            s = self._fresh
-            self._fresh += 1
-            return s
-        while True:
-            s = self.hand
-            self.hand = s + 1 if s + 1 < self.n else 0
-            k = self.key_of[s]
-            if k in pinned:
-                continue
-            if self.ref[s]:
-                self.ref[s] = False
-                continue
-            del self.map[k]
-            self.key_of[s] = None
-            return s
-
-    def _place(self, key: Key, pinned) -> None:
-        s = self._victim(pinned)
-        self.key_of[s] = key
-        self.map[key] = s
-        self.ref[s] = True
-
-    def layer(self, l: int, experts: Sequence[int]) -> None:
-        # distinct experts in the iteration order of a Python set built from
-        # the routed ids (the order decides CLOCK insertions)
-        keys = [(l, int(e)) for e in set(experts)]
-        pinned = set(keys)
-        missed = []
-        for key in keys:
-            self._add("uses")
-            s = self.map.get(key)
-            if s is not None:
-                self.ref[s] = True
-                self._add("hits")
-            elif key in self.staged:
-                del self.staged[key]
-                self._place(key, pinned)
-                self._add("adopted")
-            else:
-                self._place(key, pinned)
-                self._add("demand")
-                missed.append(key[1])
-        if missed and self.measure and self.miss_log is not None:
-            self.miss_log.append((l, missed))
-
-    def stage(self, key: Key) -> Optional[bool]:
-        """True staged, False already there, None partition full."""
-        if key in self.map or key in self.staged:
-            return False
-        if len(self.staged) >= self.spec:
-            self._add("refused")
-            return None
-        self.staged[key] = key[0]
-        self._add("prefetch")
-        return True
-
-    def expire(self, upto_layer: int) -> None:
-        dead = [k for k, t in self.staged.items() if t <= upto_layer]
-        for k in dead:
-            del self.staged[k]
-        self._add("wasted", len(dead))
-
-    def end_token(self) -> None:
-        self.expire(1 << 30)
-        self._add("tokens")
-
-
-class ForecastPolicy:
-    """Issue rule of the engine's router forecast (cache_sim.py:181-200):
-    per target layer, candidates by descending probability, those with
-    p >= threshold, at most `issue_cap`, stop when the partition is full."""
-
-    def __init__(self, fc, threshold: float = 0.062, issue_cap: int = 32):
-        self.fc, self.thr, self.cap = fc, threshold, issue_cap
-
-    def issue(self, sim: PoolSim, s: int, l: int) -> None:
-        for target, cands in self.fc[s][l].items():
-            issued = 0
-            for e, p in sorted(cands, key=lambda c: -c[1]):
-                if p < self.thr:
-                    continue
-                if issued >= self.cap:
-                    break
-                r = sim.stage((target, e))
-                if r is None:
-                    return
-                issued += int(r)
-
-
-def simulate(routed, fc, test, slots: int, spec_slots: int, forecast: Optional[ForecastPolicy] = None,
-             miss_log: Optional[list] = None, on_layer: Optional[Callable[[int, int, PoolSim], None]] = None) -> dict:
-    """Replay steps in order, counting only on `test` steps; per layer: use,
-    issue forecasts, expire those targeting this layer or earlier."""
-    sim = PoolSim(slots, spec_slots)
-    sim.miss_log = miss_log
-    S, L = routed.shape[0], routed.shape[1]
-    for s in range(S):
-        sim.measure = bool(test[s])
-        for l in range(L):
-            sim.layer(l, routed[s, l])
-            if forecast is not None:
-                forecast.issue(sim, s, l)
-            sim.expire(l)
-            if on_layer is not None:
-                on_layer(s, l, sim)
-        sim.end_token()
-    c = dict(sim.c)
-    n = max(1, c["tokens"])
-    c["hit_rate"] = (c["hits"] + c["adopted"]) / max(1, c["uses"])
-    c["demand_per_tok"] = c["demand"] / n
-    c["prefetch_per_tok"] = c["prefetch"] / n
-    c["useful_per_tok"] = c["adopted"] / n
-    c["wasted_per_tok"] = c["wasted"] / n
-    c["reads_per_tok"] = (c["demand"] + c["prefetch"]) / n
-    return c

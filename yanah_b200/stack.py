@@ -121,17 +121,20 @@ class ResidentStack:
 
     # ------------------------------------------------- persistent decode
     def decode(self, inputs: torch.Tensor, outputs: torch.Tensor, trace: Optional[torch.Tensor] = None,
-               timing: Optional[torch.Tensor] = None, stream=None) -> None:
+               timing: Optional[torch.Tensor] = None, stream=None, trace_hidden: Optional[torch.Tensor] = None,
+               trace_weights: Optional[torch.Tensor] = None) -> None:
         """Sequential bs1 decode of inputs (N,H) -> outputs (N,H) in ONE
         persistent cooperative launch. trace: (N, L, k) int32 routed ids;
-        timing: (L, 16, n_SM) int64 global-timer stamps (ns) of every CTA
-        for the last token."""
+        trace_hidden: (N, L, H) bf16 input row of every layer; trace_weights:
+        (N, L, k) fp32 routed weights; timing: (L, 16, n_SM) int64
+        global-timer stamps (ns) of every CTA for the last token."""
         lib = _lib.lib()
         n = len(self.structs)
+        ptr = lambda t: t.data_ptr() if t is not None else None
         _lib.check(lib.yn_stack_decode(C.byref(self.dims), self.table.data_ptr(), self.layer_array, n,
                                        inputs.data_ptr(), inputs.shape[0], outputs.data_ptr(), self.scratch.data_ptr(),
-                                       self.scratch.numel(), trace.data_ptr() if trace is not None else None,
-                                       timing.data_ptr() if timing is not None else None, stream_ptr(stream)))
+                                       self.scratch.numel(), ptr(trace), ptr(trace_hidden), ptr(trace_weights),
+                                       ptr(timing), stream_ptr(stream)))
 
     def decode_error(self, stream=None) -> int:
         code = C.c_int32(0)

@@ -80,27 +80,132 @@ class StreamStats:
     _pending: list = field(default_factory=list)
 
 
+class PoolPolicy:
+    """Host bookkeeping of one pool-path layer, in the order of the reference's
+    engine (orchestrator.py:158-214 `_submit_demand` / `_finish_demand`,
+    :226-300 `_pool_layer`; io_lanes.py:271-362 `SpeculativeScheduler`), so that
+    every slot decision equals the reference's on the same routing:
+
+    1. `classify`: returned forecasts drained; the layer's distinct experts in
+       ascending id order are hits (pinned) or forecasts taken into the cache
+       (`adopt`); only then are the misses claimed (CLOCK victims, pinned), in
+       the same order;
+    2. `issue`: per target layer, the selected candidates in descending
+       probability: below `threshold` skipped, at most `issue_cap` reserved,
+       candidates already forecast or resident skipped, the first refusal of
+       the partition ends that target; made while this layer's slots are
+       still pinned;
+    3. `publish` the misses; 4. `expire` forecasts whose target layer has
+       passed (they go back to the partition); 5. `release` (unpin).
+
+    Speculative reads are logically complete when their layer classifies
+    (the device waits for a copy still in flight), which is the deterministic
+    reading of the reference's engine that cache_sim also assumes."""
+
+    def __init__(self, pool: SlotPool, forecast: RouterForecast, threshold: float = 0.062, issue_cap: int = 32,
+                 top: int = 24):
+        self.pool, self.fc = pool, forecast
+        self.threshold, self.cap, self.top = threshold, issue_cap, top
+        self.tickets: Dict[Tuple[int, int], int] = {}   # (target layer, expert) -> partition slot, in issue order
+
+    def classify(self, l: int, ids: np.ndarray):
+        """-> (out {expert: slot}, ready {expert: slot} (hits + adopted),
+        misses [expert], adopted [expert]). Every slot in `out` is pinned."""
+        pool = self.pool
+        pool.drain_returned()
+        out: Dict[int, int] = {}
+        ready: Dict[int, int] = {}
+        misses: List[int] = []
+        adopted: List[int] = []
+        for e in sorted({int(v) for v in np.asarray(ids).reshape(-1)}):
+            key = (l, e)
+            s = pool.hit(key)
+            if s is None:
+                s = self.tickets.pop(key, None)
+                if s is None:
+                    misses.append(e)
+                    continue
+                pool.adopt(s, key)
+                adopted.append(e)
+            out[e] = ready[e] = s
+        for e in misses:
+            out[e] = pool.claim_for_demand((l, e))
+        return out, ready, misses, adopted
+
+    def issue(self, targets: List[int], probs: Dict[int, np.ndarray]):
+        """-> ({target: [(expert, slot)] reserved}, {target: candidates})."""
+        pool = self.pool
+        reserved: Dict[int, List[Tuple[int, int]]] = {}
+        cands_of: Dict[int, list] = {}
+        for t in targets:
+            if t not in probs:
+                continue
+            cands = self.fc.select(t, probs[t], self.top)
+            cands_of[t] = cands
+            n, pairs = 0, []
+            for e, p in cands[:self.top]:
+                if p < self.threshold:
+                    continue
+                if n >= self.cap:
+                    break
+                key = (t, e)
+                if key in self.tickets or pool.is_resident(key):
+                    continue
+                s = pool.reserve_speculative(key)
+                if s is None:
+                    break
+                self.tickets[key] = s
+                pairs.append((e, s))
+                n += 1
+            reserved[t] = pairs
+        return reserved, cands_of
+
+    def publish(self, l: int, misses: List[int], out: Dict[int, int]) -> None:
+        for e in misses:
+            self.pool.publish(out[e], (l, e))
+
+    def expire(self, l: int) -> List[Tuple[int, int]]:
+        """Forecasts for layers <= l go back unused (in issue order)."""
+        dead = [k for k in self.tickets if k[0] <= l]
+        for k in dead:
+            self.pool.return_speculative(self.tickets.pop(k))
+        return dead
+
+    def release(self, out: Dict[int, int]) -> None:
+        for s in out.values():
+            self.pool.unpin(s)
+
+    def end_token(self) -> None:
+        """A new token starts: every outstanding forecast goes back."""
+        for k in list(self.tickets):
+            self.pool.return_speculative(self.tickets.pop(k))
+
+
 class StreamingDecoder:
     def __init__(self, cfg: StackConfig, slot_fraction: float = 0.2, spec_slot_cap: int = 64, lookahead: int = 2,
                  threshold: float = 0.062, issue_cap: int = 32, top: int = 24, device="cuda",
-                 host: Optional[HostTier] = None, measure: bool = True):
+                 host: Optional[HostTier] = None, measure: bool = True, slots: Optional[int] = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.compute = torch.cuda.Stream(self.device)
         self.copy = torch.cuda.Stream(self.device)
         self.spec = torch.cuda.Stream(self.device)
         self.be = CudaMoEBackend(cfg, self.device, lookahead=lookahead, stream=self.compute)
-        slots = max(int(round(slot_fraction * cfg.n_experts * cfg.n_layers)), 3 * cfg.top_k + spec_slot_cap)
+        if slots is None:
+            slots = max(int(round(slot_fraction * cfg.n_experts * cfg.n_layers)), 3 * cfg.top_k + spec_slot_cap)
         self.pool = SlotPool(self.be.geometry, slots, spec_slot_cap=spec_slot_cap,
                              memory=self.be.make_expert_memory(slots))
         self.fc = RouterForecast(self.be.geometry)
+        self.policy = PoolPolicy(self.pool, self.fc, threshold, issue_cap, top)
         self.host = host if host is not None else HostTier(cfg, self.device)
-        self.threshold, self.cap, self.top = threshold, issue_cap, top
-        self.tickets: Dict[Tuple[int, int], Tuple[int, torch.cuda.Event]] = {}
+        self.events: Dict[Tuple[int, int], torch.cuda.Event] = {}   # forecast copies in flight
         self.ev_compute: Optional[torch.cuda.Event] = None
         self.stats = StreamStats()
         self.measure = measure
-        self.trace: Optional[List[np.ndarray]] = None   # routed ids per layer, when set to a list
+        self.generation = 0
+        # routing trace in the reference's format (orchestrator.py:268-270), when set to a list:
+        # (generation, layer, routed experts, {target layer: [(expert, p)]})
+        self.trace: Optional[list] = None
 
     # ------------------------------------------------------------- copies
     def _copy(self, stream, pairs: List[Tuple[int, int]], layer: int) -> Optional[torch.cuda.Event]:
@@ -127,40 +232,33 @@ class StreamingDecoder:
 
     # -------------------------------------------------------------- layers
     def layer(self, l: int, h: torch.Tensor) -> torch.Tensor:
-        be, pool = self.be, self.pool
+        be, pool, pol = self.be, self.pool, self.policy
         h_res, x, logits = be.pre_moe(l, h)
         targets = [t for t in (l + 1, l + 2) if t < self.cfg.n_layers]
         ids, w, probs = be.route_and_forecast(logits, h_res, targets)
-        if self.trace is not None:
-            self.trace.append(ids[0].copy())
         self.fc.observe(l, ids)
-        pool.drain_returned()
-        out: Dict[int, int] = {}
-        ready: Dict[int, int] = {}
-        misses: List[Tuple[int, int]] = []
+        out, ready, misses, adopted = pol.classify(l, ids)
         waits: List[torch.cuda.Event] = []
-        for e in sorted({int(v) for v in ids.reshape(-1)}):
-            key = (l, e)
-            s = pool.hit(key)
-            if s is not None:
-                out[e] = ready[e] = s
-                continue
-            t = self.tickets.pop(key, None)
-            if t is not None:
-                s, ev = t
-                pool.adopt(s, key)
-                out[e] = s
-                if ev.query():
-                    ready[e] = s
-                else:
-                    waits.append(ev)
-                continue
-            s = pool.claim_for_demand(key)
-            out[e] = s
-            misses.append((e, s))
-        ev_demand = self._copy(self.copy, misses, l)
+        for e in adopted:
+            ev = self.events.pop((l, e), None)
+            if ev is not None and not ev.query():
+                waits.append(ev)
+                del ready[e]
+        ev_demand = self._copy(self.copy, [(e, out[e]) for e in misses], l)
         self.stats.demand_records += len(misses)
         handle = be.moe_ready(l, x, ids, pool.memory, ready)
+        # forecasts for the next layers, copied while this layer computes
+        reserved, cands = pol.issue(targets, probs)
+        for t, pairs in reserved.items():
+            ev = self._copy(self.spec, pairs, t)
+            for e, _ in pairs:
+                self.events[(t, e)] = ev
+            self.stats.spec_records += len(pairs)
+        if self.trace is not None and ids.shape[0] == 1:
+            self.trace.append((self.generation, l, [int(e) for e in ids[0]], cands))
+        pol.publish(l, misses, out)
+        for k in pol.expire(l):
+            self.events.pop(k, None)
         ev_ready = None
         if ev_demand is not None or waits:
             if self.measure and ev_demand is not None:
@@ -177,40 +275,21 @@ class StreamingDecoder:
             self.stats._pending.append(("stall", ev_ready, ev_demand))
         self.ev_compute = torch.cuda.Event()
         self.ev_compute.record(self.compute)
-        for e, s in misses:
-            pool.publish(s, (l, e))
-        for s in out.values():
-            pool.unpin(s)
-        # forecasts for the next layers, copied while this layer computes
-        for t in targets:
-            if t not in probs:
-                continue
-            cands = self.fc.select(t, probs[t], self.top)
-            issued, pairs = 0, []
-            for e, p in cands:
-                if p < self.threshold or (t, e) in self.tickets or pool.is_resident((t, e)):
-                    continue
-                if issued >= self.cap:
-                    break
-                s = pool.reserve_speculative((t, e))
-                if s is None:
-                    break
-                pairs.append((e, s))
-                issued += 1
-            ev = self._copy(self.spec, pairs, t)
-            for e, s in pairs:
-                self.tickets[(t, e)] = (s, ev)
-            self.stats.spec_records += len(pairs)
-        for key in [k for k in self.tickets if k[0] <= l]:
-            pool.return_speculative(self.tickets.pop(key)[0])
+        pol.release(out)
         self.stats.layers += 1
         return h_next
 
+    def begin_token(self) -> None:
+        """Start of a token (a forward pass): forecasts left from the last
+        token go back to the partition."""
+        self.generation += 1
+        self.policy.end_token()
+        self.events.clear()
+
     def token(self, h: torch.Tensor) -> torch.Tensor:
+        self.begin_token()
         for l in range(self.cfg.n_layers):
             h = self.layer(l, h)
-        for key in list(self.tickets):
-            self.pool.return_speculative(self.tickets.pop(key)[0])
         self.stats.tokens += 1
         return h
 
