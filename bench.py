@@ -652,6 +652,100 @@ def run_sweep(args, rank: int, world: int):
 VERIFY_METRIC = "speculative-verify tok/s, 1+4 rows per step (LFM2-24B-A2B-shaped, 40 layers), union-of-experts batch"
 
 
+def run_verify_tc(args, rank: int, world: int):
+    """Speculative verify: 1 + 4 draft rows per step through the 40
+    LFM2-shaped layers on the tcgen05 grouped expert GEMM (the prefill path:
+    routing, device-side grouping by expert, gate/up + SwiGLU and down GEMMs
+    that read each routed expert record once for all the rows that chose it,
+    combine), one CUDA graph per step. HBM-bound: the roofline counts each
+    distinct expert record a layer routes to once."""
+    import numpy as np
+    import torch
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.prefill import PrefillStack
+    from yanah_b200.synthetic import hidden_stream_id, lfm2_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = lfm2_stack(seed=0)
+    B = 5
+    layer_ids = list(range(args.first_layer, args.first_layer + (args.layers or cfg.n_layers)))
+    stack = PrefillStack(cfg, max_rows=B, device=dev, layers=layer_ids)
+    H, K, L = cfg.hidden, cfg.top_k, len(layer_ids)
+    rows = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(rows.data_ptr(), B * H, cfg.seed, hidden_stream_id(700), 1.0, 0.0,
+                                        stream_ptr()))
+    # untimed pass: distinct experts per layer (the algorithmic bytes)
+    n_distinct = []
+    ping = [rows.clone(), torch.empty_like(rows)]
+    for i in range(L):
+        stack.layer(i, ping[i % 2], ping[(i + 1) % 2])
+        n_distinct.append(len(np.unique(stack.ids[:B].cpu().numpy())))
+    if stack.check_error():
+        raise RuntimeError("device error in the first verify step")
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        stack.prefill(rows, stream=s)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            out = stack.prefill(rows, stream=s)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid(dev.index)) as clk:
+        start.record()
+        for _ in range(args.steps):
+            g.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+    ms = start.elapsed_time(end)
+    if stack.check_error():
+        raise RuntimeError("device error during the timed verify steps")
+    value = B * args.steps / (ms / 1e3)
+    h_in = torch.empty((B, H), dtype=torch.bfloat16, pin_memory=True)
+    h_in.copy_(rows)
+    h_out = torch.empty_like(h_in, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        rows.copy_(h_in, non_blocking=True)
+        g.replay()
+        h_out.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e = B * args.steps / (e0.elapsed_time(e1) / 1e3)
+    rec = [cfg.record_spec(l).record_bytes for l in layer_ids]
+    hbm_bytes = sum(n * r for n, r in zip(n_distinct, rec)) + L * cfg.dense_bytes_per_layer()
+    hbm, src = peaks()
+    step_s = ms / args.steps / 1e3
+    achieved = hbm_bytes / step_s / 1e9
+    line = {
+        "metric": VERIFY_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": sub_label("lfm2_24b_a2b_moe_stack40_verify_1p4", args, cfg.n_layers), "layers": L,
+                   "rows_per_step": B, "hidden": H, "experts": cfg.n_experts, "top_k": K, "moe_inter": cfg.moe_inter,
+                   "expert_bits": "4-bit g64", "path": "tcgen05 grouped GEMM (yn_tc_experts)",
+                   "l2": "no flush: a step reads the routed records of 40 layers (~1 GB > 126 MB L2)"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+        "gpu_launches": args.steps * L * 7,
+        "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "whole step (7 kernels per layer)", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
+                     "bytes_per_step": hbm_bytes, "distinct_experts_per_layer_mean": round(float(np.mean(n_distinct)), 2),
+                     "traffic": None},
+    }
+    print(json.dumps(line), flush=True)
+    del g
+
+
 def run_verify(args, rank: int, world: int):
     """Speculative verify: 1 + 4 draft rows per step through the 40
     LFM2-shaped layers on the batch path (each routed expert record read
@@ -882,6 +976,8 @@ def main():
                          "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill; "
                          "verify: 1+4-row speculative-verify batches; sweep: prefill through the prefill sweep")
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
+    ap.add_argument("--verify-path", choices=["tc", "batch"], default="tc",
+                    help="verify workload: tcgen05 grouped GEMM (default) or the union-of-experts batch path")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
     args = ap.parse_args()
@@ -908,7 +1004,7 @@ def main():
                 run_prefill(args, rank, world)
         elif args.workload == "verify":
             if rank == 0:
-                run_verify(args, rank, world)
+                (run_verify if args.verify_path == "batch" else run_verify_tc)(args, rank, world)
         elif args.workload == "sweep":
             if rank == 0:
                 run_sweep(args, rank, world)

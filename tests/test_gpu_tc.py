@@ -84,3 +84,9 @@ def test_tc_lfm2_two_chained_layers():
 def test_tc_lfm2_layer():
     # a ragged prefill batch: 3 prompts of 37, 300 and 5 rows (342 rows, 1368 pairs)
     _check(lfm2_stack(n_layers=40), T=342, sample_pairs=48)
+
+
+def test_tc_lfm2_verify_rows():
+    # a speculative-verify batch (1 + 4 draft rows) on the same grouped GEMM:
+    # few rows per expert, every pair checked
+    _check(lfm2_stack(n_layers=40), T=5, sample_pairs=20)
