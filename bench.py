@@ -70,6 +70,10 @@ def sub_label(name: str, args, n_total: int) -> str:
     return f"{name}_sub{n}_from{args.first_layer}"
 
 
+def line_kernel(kern: str) -> str:
+    return "k_stack_flow" if kern == "flow" else "k_stack_decode"
+
+
 def workload_config(cfg, tokens):
     return {
         "workload": "qwen3_next_80b_a3b_moe_stack48_bs1_decode",
@@ -590,7 +594,7 @@ def run_sweep(args, rank: int, world: int):
     torch.cuda.synchronize(dev)
     if be.check_error():
         raise RuntimeError("device error in the sweep warm-up")
-    st0 = (sweep.stats.resident_copies, sweep.stats.disk_records, reader.sweep_runs)
+    st0 = (sweep.stats.pool_copies, sweep.stats.host_records, reader.sweep_runs)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_uuid(dev.index)) as clk:
         start.record()
@@ -600,8 +604,8 @@ def run_sweep(args, rank: int, world: int):
         torch.cuda.synchronize(dev)
     ms = start.elapsed_time(end)
     value = T * args.steps / (ms / 1e3)
-    res = (sweep.stats.resident_copies - st0[0]) / args.steps
-    disk = (sweep.stats.disk_records - st0[1]) / args.steps
+    res = (sweep.stats.pool_copies - st0[0]) / args.steps
+    disk = (sweep.stats.host_records - st0[1]) / args.steps
     runs = (reader.sweep_runs - st0[2]) / args.steps
     rec = cfg.record_spec(0).record_bytes
     h2d = disk * rec / (ms / args.steps / 1e3) / 1e9
@@ -844,7 +848,7 @@ def run_ours(args, rank: int, world: int):
 
     from yanah_b200 import _lib
     from yanah_b200.device import stream_ptr
-    from yanah_b200.stack import DECODE_STAMPS, ResidentStack, decode_phase_report
+    from yanah_b200.stack import DECODE_STAMPS, ResidentStack, decode_phase_report, flow_phase_report
     from yanah_b200.synthetic import hidden_stream_id, qwen3_next_stack
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -858,7 +862,8 @@ def run_ours(args, rank: int, world: int):
     _lib.check(lib.yn_synth_bf16(inputs.data_ptr(), N * H, cfg.seed, hidden_stream_id(rank), 1.0, 0.0,
                                  stream_ptr()))
     outputs = torch.empty_like(inputs)
-    stack.decode(inputs[:2], outputs[:2])
+    kern = args.decode_kernel
+    stack.decode(inputs[:2], outputs[:2], kernel=kern)
     torch.cuda.synchronize(dev)
     if stack.decode_error():
         raise RuntimeError("device error in the first decode")
@@ -866,9 +871,9 @@ def run_ours(args, rank: int, world: int):
     # extra untimed launch)
     n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
     timing = torch.zeros((len(layers), DECODE_STAMPS, n_sm), dtype=torch.int64, device=dev)
-    stack.decode(inputs[:2], outputs[:2], timing=timing)
+    stack.decode(inputs[:2], outputs[:2], timing=timing, kernel=kern)
     torch.cuda.synchronize(dev)
-    phases = decode_phase_report(timing.cpu().numpy())
+    phases = (flow_phase_report if kern == "flow" else decode_phase_report)(timing.cpu().numpy())
 
     def barrier():
         if world > 1:
@@ -876,13 +881,13 @@ def run_ours(args, rank: int, world: int):
         torch.cuda.synchronize(dev)
 
     for _ in range(args.warmup):
-        stack.decode(inputs, outputs)
+        stack.decode(inputs, outputs, kernel=kern)
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_uuid(dev.index)) as clk:
         start.record()
         for _ in range(args.steps):
-            stack.decode(inputs, outputs)
+            stack.decode(inputs, outputs, kernel=kern)
         end.record()
         torch.cuda.synchronize(dev)
     barrier()
@@ -901,12 +906,12 @@ def run_ours(args, rank: int, world: int):
     h_out = torch.empty_like(h_in, pin_memory=True)
     d_in, d_out = torch.empty_like(inputs), torch.empty_like(outputs)
     for _ in range(2):
-        stack.decode_host(h_in, h_out, d_in, d_out)
+        stack.decode_host(h_in, h_out, d_in, d_out, kernel=kern)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        stack.decode_host(h_in, h_out, d_in, d_out)
+        stack.decode_host(h_in, h_out, d_in, d_out, kernel=kern)
     e1.record()
     torch.cuda.synchronize(dev)
     barrier()
@@ -925,7 +930,7 @@ def run_ours(args, rank: int, world: int):
     tf = ROOT / "profiles" / "kernel_traffic.json"
     if tf.exists() and not args.layers:
         try:
-            per_tok = json.loads(tf.read_text()).get("k_stack_decode_bytes_per_token")
+            per_tok = json.loads(tf.read_text()).get(f"{line_kernel(kern)}_bytes_per_token")
             traffic = int(per_tok * N) if per_tok else None
         except (ValueError, AttributeError, TypeError):
             traffic = None
@@ -938,7 +943,8 @@ def run_ours(args, rank: int, world: int):
                 "d2h_bytes_per_step": N * H * 2},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
-        "roofline": {"bound": "hbm", "kernel": "k_stack_decode", "achieved": round(achieved, 1), "peak": hbm,
+        "roofline": {"bound": "hbm", "kernel": "k_stack_flow" if kern == "flow" else "k_stack_decode",
+                     "achieved": round(achieved, 1), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
                      "bytes_per_launch": bytes_tok * N, "avg_launch_us": round(launch_ms * 1e3, 1),
                      "traffic": traffic},
@@ -976,6 +982,8 @@ def main():
                          "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill; "
                          "verify: 1+4-row speculative-verify batches; sweep: prefill through the prefill sweep")
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
+    ap.add_argument("--decode-kernel", choices=["flow", "barrier"], default="flow",
+                    help="resident workload: the data-flow persistent decode (default) or the grid-barrier form")
     ap.add_argument("--verify-path", choices=["tc", "batch"], default="tc",
                     help="verify workload: tcgen05 grouped GEMM (default) or the union-of-experts batch path")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")

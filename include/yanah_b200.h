@@ -209,7 +209,22 @@ int yn_stack_decode(const yn_dims* dims, const void* table, const yn_layer* laye
                     const void* inputs, int32_t n_tokens, void* outputs, void* scratch, size_t scratch_bytes,
                     int32_t* trace_ids, void* trace_hidden, float* trace_weights, int64_t* timing,
                     void* stream);
-/* Read and clear the stack decode error word (synchronises the stream). */
+/* The same decode (same arguments, same results bit for bit) in data-flow
+ * form: no grid barriers. The layer's work is split by routed column (groups
+ * of CTAs that each compute gate/up and then down for one routed expert,
+ * exchanging only that expert's activations) and every exchange between CTAs
+ * is a set of flagged words read directly by its consumers: router logits,
+ * the expert's activations, the shared expert's activations, the expert
+ * outputs of a block of rows, the layer output. No counterpart in the
+ * reference (a persistent-kernel schedule of orchestrator.py:308-343 with
+ * every expert resident). scratch: yn_stack_flow_scratch_bytes(dims). */
+size_t yn_stack_flow_scratch_bytes(const yn_dims* dims);
+int yn_stack_flow_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
+                         const void* inputs, int32_t n_tokens, void* outputs, void* scratch, size_t scratch_bytes,
+                         int32_t* trace_ids, void* trace_hidden, float* trace_weights, int64_t* timing,
+                         void* stream);
+/* Read and clear the stack decode error word (synchronises the stream);
+ * either form's scratch. */
 int yn_stack_error(void* scratch, const yn_dims* dims, void* stream, int32_t* code_out);
 
 /* ------------------------------------- batch decode, expert parallelism */

@@ -111,7 +111,7 @@ def drive_sweep(sweep_cls, pool, ids: np.ndarray, w: np.ndarray, group: int) -> 
     ps = pool.stats
     return {
         "reader": reader.log, "moe": moe_log, "outs": outs, "maps": maps,
-        "sweep_stats": [st.passes, st.layers, st.resident_copies, st.disk_records, st.admitted],
+        "sweep_stats": [st.passes, st.layers, st.pool_copies, st.host_records, st.admitted],
         "pool_stats": [ps.hits, ps.misses, ps.evictions, ps.admitted],
         "fair_share": sweep.fair_share(),
     }

@@ -172,14 +172,14 @@ def test_persistent_decode_single_layers_vs_oracle():
     """The persistent whole-stack kernel on one-layer stacks (4-bit g64, 2-bit
     g64, 2-bit g32): routing ids bit-exact, outputs within tolerance of the oracle."""
     from yanah_b200.stack import ResidentStack
-    for bits, gs in ((4, 64), (2, 64), (2, 32)):
+    for (bits, gs), kernel in [((b_, g_), k_) for b_, g_ in ((4, 64), (2, 64), (2, 32)) for k_ in ("flow", "barrier")]:
         cfg = small_config(bits=(bits,), gs=gs, hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=4)
         st = ResidentStack(cfg, "cuda")
         N = 3
         x = bf16_dev(hidden_rows(cfg, N, stream=2))
         got = torch.empty_like(x)
         trace = torch.full((N, 1, cfg.top_k), -1, dtype=torch.int32, device="cuda")
-        st.decode(x, got, trace=trace)
+        st.decode(x, got, trace=trace, kernel=kernel)
         torch.cuda.synchronize()
         assert st.decode_error() == 0
         o = cpu.OracleStack(cfg)
@@ -203,9 +203,12 @@ def test_persistent_decode_stack_vs_layer_kernels():
     got = torch.empty_like(x)
     trace = torch.full((N, cfg.n_layers, cfg.top_k), -1, dtype=torch.int32, device="cuda")
     st.decode(x, got, trace=trace)
+    got_b = torch.empty_like(x)
+    st.decode(x, got_b, kernel="barrier")
     torch.cuda.synchronize()
     assert st.decode_error() == 0
     assert (trace >= 0).all()
+    assert torch.equal(got.view(torch.int16), got_b.view(torch.int16))
     o = cpu.OracleStack(cfg)
     for t in range(N):
         r = o.post_attention(0, bf16_np(x[t:t + 1]))
@@ -218,11 +221,12 @@ def test_persistent_decode_full_stack_every_layer_vs_oracle(gs):
     """The benchmarked configuration: the 48-layer Qwen3-Next-shaped stack
     (experts 4-bit in layers 0-3 and 44-47, 2-bit elsewhere; Zipf(1.1)
     router popularity; seed 0), three bs1 tokens through the persistent
-    kernel. At EVERY layer, on the kernel's own input row of that layer: the
-    routed ids and weights equal the oracle's bit for bit, and the layer
-    output (the next layer's input) is within REL_L2_TOL of the oracle's.
-    Group size 64 is the benchmarked stack; 32 is the reference's 2-bit
-    default. The traced launch gives the same outputs as an untraced one."""
+    kernel (data-flow form). At EVERY layer, on the kernel's own input row of
+    that layer: the routed ids and weights equal the oracle's bit for bit, and
+    the layer output (the next layer's input) is within REL_L2_TOL of the
+    oracle's. Group size 64 is the benchmarked stack; 32 is the reference's
+    2-bit default. The traced launch, an untraced one and the barrier form of
+    the kernel give the same outputs bit for bit."""
     import dataclasses
     from yanah_b200.stack import ResidentStack
     cfg = qwen3_next_stack(seed=0)
@@ -238,9 +242,13 @@ def test_persistent_decode_full_stack_every_layer_vs_oracle(gs):
     st.decode(x, got, trace=ids, trace_hidden=hin, trace_weights=wts)
     plain = torch.empty_like(x)
     st.decode(x, plain)
+    barrier = torch.empty_like(x)
+    st.decode(x, barrier, kernel="barrier")
     torch.cuda.synchronize()
     assert st.decode_error() == 0
+    # untraced launch and the barrier form of the kernel: the same outputs, bit for bit
     assert torch.equal(got.view(torch.int16), plain.view(torch.int16))
+    assert torch.equal(got.view(torch.int16), barrier.view(torch.int16))
     ids, wts, hin, got = ids.cpu().numpy(), wts.cpu().numpy(), bf16_np(hin), bf16_np(got)
     del st
     torch.cuda.empty_cache()

@@ -73,7 +73,7 @@ def test_sweep_small_stack_cold_warm_oracle():
 
     cold = _sweep(be, tier, _pool(be, tier, 12, 2, []), group)
     out_cold = _pass_by_layer(be, cold, hd, [0, 1], admit=False)
-    assert cold.pool.resident_count() == 0 and cold.stats.resident_copies == 0
+    assert cold.pool.resident_count() == 0 and cold.stats.pool_copies == 0
 
     warm_keys = [(0, 1), (0, 5), (0, 9), (1, 2), (1, 3), (1, 14)]
     warm = _sweep(be, tier, _pool(be, tier, 12, 2, warm_keys), group)
@@ -82,8 +82,8 @@ def test_sweep_small_stack_cold_warm_oracle():
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
     st = warm.stats
     distinct = len(np.unique(_routed(be, hd, 0))) + len(np.unique(_routed(be, out_warm[0], 1)))
-    assert st.resident_copies + st.disk_records == distinct
-    assert st.resident_copies > 0 and st.layers == 2 and st.passes == 2
+    assert st.pool_copies + st.host_records == distinct
+    assert st.pool_copies > 0 and st.layers == 2 and st.passes == 2
 
     # admission wrote records from staging into the pool (CLOCK may evict an earlier admission): every
     # resident record equals the host tier's bytes
@@ -148,7 +148,7 @@ def test_sweep_lfm2_layer():
     h = hidden_rows(cfg, T, stream=45)
     hd = bf16_dev(h)
     out = _pass_by_layer(be, sw, hd, [0], admit=True)[0]
-    assert sw.stats.resident_copies > 0 and sw.stats.disk_records > 0
+    assert sw.stats.pool_copies > 0 and sw.stats.host_records > 0
     orc = cpu.OracleStack(cfg, threads=8)
     rows = [0, 150, T - 1]
     assert rel_l2(bf16_np(out)[rows], orc.layer(0, h[rows])["out"]) < REL_L2_TOL

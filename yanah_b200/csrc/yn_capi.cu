@@ -20,7 +20,7 @@
 #include "yn_moe.cuh"
 #include "yn_qdot.cuh"
 #include "yn_kernels.cuh"
-#include "yn_decode.cuh"
+#include "yn_flow.cuh"
 #include "yn_batch_dense.cuh"
 #include "yn_internal.h"
 
@@ -925,6 +925,148 @@ extern "C" int yn_stack_decode(const yn_dims* dims, const void* table, const yn_
   int per_sm = 0;
   YN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, DEC_THREADS, smem));
   if (per_sm < 1) return fail(YN_E_UNSUPPORTED, "stack decode kernel does not fit on an SM");
+  void* args[] = {&a};
+  YN_CUDA(cudaLaunchCooperativeKernel(kernel, dim3(G), dim3(DEC_THREADS), args, smem, st));
+  return YN_OK;
+}
+
+// ------------------------------------------ persistent decode, data-flow form
+struct FlowScratch {
+  size_t err, f_logits, f_act, f_ash, f_y, f_h, total;
+};
+// Error word first (as in the barrier form, so yn_stack_error reads both),
+// then the flagged-word buffers, zeroed before every launch.
+static FlowScratch flow_scratch(const yn_dims& d) {
+  FlowScratch S{};
+  size_t o = 0;
+  auto take = [&](size_t b) { size_t at = o; o = (o + b + 255) / 256 * 256; return at; };
+  S.err = take(4);
+  S.f_logits = take(2 * (size_t)d.n_experts * 8);
+  S.f_act = take(2 * (size_t)d.top_k * (d.moe_inter / 2) * 8);
+  S.f_ash = take(2 * ((size_t)d.shared_inter + 1) * 8);
+  S.f_y = take(2 * ((size_t)d.top_k + 1) * (d.hidden / 2) * 8);
+  S.f_h = take(2 * (size_t)(d.hidden / 2) * 8);
+  S.total = o;
+  return S;
+}
+extern "C" size_t yn_stack_flow_scratch_bytes(const yn_dims* dims) { return dims ? flow_scratch(*dims).total : 0; }
+
+extern "C" int yn_stack_flow_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
+                                    const void* inputs, int32_t n_tokens, void* outputs, void* scratch,
+                                    size_t scratch_bytes, int32_t* trace_ids, void* trace_hidden,
+                                    float* trace_weights, int64_t* timing, void* stream) {
+  int rc = check_dims(dims, 1);
+  if (rc) return rc;
+  const yn_dims& d = *dims;
+  if (!table || !inputs || !outputs || !scratch || !layers) return fail(YN_E_INVALID, "null argument");
+  if (n_layers < 1 || n_tokens < 1) return fail(YN_E_INVALID, "n_layers and n_tokens must be >= 1");
+  const FlowScratch S = flow_scratch(d);
+  if (scratch_bytes < S.total) return fail(YN_E_INVALID, "scratch too small");
+  const int K = d.top_k, Ish = d.shared_inter;
+  if (d.hidden != DEC_H || d.n_experts != DEC_E || d.moe_inter != DEC_I || (Ish != 0 && Ish != DEC_I) ||
+      K > DEC_MAX_K)
+    return fail(YN_E_UNSUPPORTED, "stack decode is compiled for hidden 2048, 512 experts, intermediate 512 "
+                                  "(shared 0 or 512), top_k <= 16");
+  int rb_max = 0, sb_max = 0, rbi_max = 0, sbi_max = 0;
+  for (int l = 0; l < n_layers; ++l) {
+    const yn_layer& L = layers[l];
+    const int bits = L.record.bits, gs = L.record.group_size;
+    if ((bits != 2 && bits != 4) || (gs != 32 && gs != 64))
+      return fail(YN_E_UNSUPPORTED, "stack decode: routed experts must be 2- or 4-bit with groups of 32 or 64");
+    if (L.router.group_size != DEC_DGS ||
+        (Ish && (L.shared_gate.group_size != DEC_DGS || L.shared_up.group_size != DEC_DGS ||
+                 L.shared_down.group_size != DEC_DGS || L.shared_expert_gate.group_size != DEC_DGS)))
+      return fail(YN_E_UNSUPPORTED, "stack decode: dense 8-bit matrices must use groups of 64");
+    for (int i = 0; i < 9; ++i)
+      if (L.record.piece_offset[i] % 16) return fail(YN_E_UNSUPPORTED, "stack decode: record pieces must be 16-byte aligned");
+    if (!al16(L.expert_base) || L.slot_stride % 16)
+      return fail(YN_E_UNSUPPORTED, "stack decode: slot arena and stride must be 16-byte aligned");
+    if (!al16(L.router.weight) || !al16(L.router.scales) || !al16(L.router.biases) || !al16(L.post_norm))
+      return fail(YN_E_UNSUPPORTED, "stack decode: router pieces must be 16-byte aligned");
+    if (Ish && (!al16(L.shared_gate.weight) || !al16(L.shared_gate.scales) || !al16(L.shared_gate.biases) ||
+                !al16(L.shared_up.weight) || !al16(L.shared_up.scales) || !al16(L.shared_up.biases) ||
+                !al16(L.shared_down.weight) || !al16(L.shared_down.scales) || !al16(L.shared_down.biases) ||
+                !al16(L.shared_expert_gate.weight) || !al16(L.shared_expert_gate.scales) ||
+                !al16(L.shared_expert_gate.biases)))
+      return fail(YN_E_UNSUPPORTED, "stack decode: shared-expert pieces must be 16-byte aligned");
+    rb_max = std::max(rb_max, DEC_H * bits / 8);
+    sb_max = std::max(sb_max, DEC_H / gs * 2);
+    rbi_max = std::max(rbi_max, DEC_I * bits / 8);
+    sbi_max = std::max(sbi_max, DEC_I / gs * 2);
+  }
+  int dev = 0, sms = 0;
+  YN_CUDA(cudaGetDevice(&dev));
+  YN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int G = sms;
+  // K groups of nr CTAs (routed columns), the rest (ns >= 8) for the shared expert's down rows
+  const int nr = (G - 8) / K, ns = G - K * nr;
+  const int oct_max = (DEC_I / 8 + nr - 1) / std::max(nr, 1), dt_max = (DEC_H / 16 + nr - 1) / std::max(nr, 1);
+  const int dts_max = (DEC_H / 16 + ns - 1) / ns;
+  if (nr < 1 || oct_max > DEC_MAX_OCT || dt_max > FL_MAX_DT || dts_max > FL_MAX_DT ||
+      (FL_HW + G - 1) / G > FL_MAX_CW)
+    return fail(YN_E_UNSUPPORTED, "data-flow decode: " + std::to_string(G) + " SMs cannot hold " +
+                                      std::to_string(K) + " routed columns of at least 8 CTAs plus 8 shared CTAs");
+  FlowArgs a{};
+  size_t o = 256;
+  auto put = [&](int& off, size_t bytes) { off = (int)o; o += (bytes + 127) / 128 * 128; };
+  put(a.off_hs, (size_t)DEC_H * 2);
+  put(a.off_xs, (size_t)DEC_H * 2);
+  put(a.off_route, 4 * (size_t)DEC_E + 4 * DEC_WARPS * DEC_MAX_K + 4 * DEC_MAX_K + 4 * DEC_MAX_K + 4 * (DEC_MAX_K + 4) +
+                       4 * 64 + 4 * 256 + 3 * sizeof(DecLayer));
+  put(a.off_xf2, (size_t)DEC_H / 2 * 4 + 2 * (size_t)DEC_H / 32 * 4);
+  put(a.off_xf3, (size_t)DEC_I / 2 * 4 + 2 * 16 * 4);
+  const size_t part_up = (size_t)oct_max * 8 * 2 * (DEC_H * 4 / 8 / 64) * 4;
+  const size_t part_dn = (size_t)16 * std::max(dt_max, dts_max) * (DEC_I / 64) * 4;
+  put(a.off_part, std::max(part_up, part_dn));
+  put(a.off_stage, (size_t)DEC_I * 2 + (size_t)(K + 1) * FL_MAX_CW * 4);
+  put(a.off_A, p1_tile_bytes_max(Ish, G));
+  a.c_rows = 8 * oct_max;
+  a.c_rb = rb_max;
+  a.c_sb = sb_max;
+  a.d_rows = 16 * dt_max;
+  a.d_rb = rbi_max;
+  a.d_sb = sbi_max;
+  const size_t c_bytes = (size_t)2 * a.c_rows * a.c_rb + (size_t)4 * a.c_rows * a.c_sb;
+  const size_t d_bytes = (size_t)a.d_rows * (a.d_rb + 2 * a.d_sb);
+  const size_t sd_bytes = Ish ? (size_t)16 * dts_max * (DEC_I + 2 * DEC_DSBI) : 0;
+  a.off_C = (int)o;
+  a.off_D = (int)(o + (c_bytes + 127) / 128 * 128);
+  o += std::max((c_bytes + 127) / 128 * 128 + d_bytes, sd_bytes);
+  const size_t smem = (o + 127) / 128 * 128;
+  int optin = 0;
+  YN_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (smem > (size_t)optin)
+    return fail(YN_E_UNSUPPORTED, "data-flow decode needs " + std::to_string(smem) + " B of shared memory (" +
+                                      std::to_string(optin) + " available)");
+  uint8_t* sc = reinterpret_cast<uint8_t*>(scratch);
+  a.K = K; a.Ish = Ish; a.norm_topk = d.norm_topk; a.eps = d.rms_eps;
+  a.layers = reinterpret_cast<const DecLayer*>(table);
+  a.n_layers = n_layers;
+  a.inputs = reinterpret_cast<const uint16_t*>(inputs);
+  a.n_tokens = n_tokens;
+  a.outputs = reinterpret_cast<uint16_t*>(outputs);
+  a.f_logits = reinterpret_cast<unsigned long long*>(sc + S.f_logits);
+  a.f_act = reinterpret_cast<unsigned long long*>(sc + S.f_act);
+  a.f_ash = reinterpret_cast<unsigned long long*>(sc + S.f_ash);
+  a.f_y = reinterpret_cast<unsigned long long*>(sc + S.f_y);
+  a.f_h = reinterpret_cast<unsigned long long*>(sc + S.f_h);
+  a.trace_ids = trace_ids;
+  a.trace_h = reinterpret_cast<uint16_t*>(trace_hidden);
+  a.trace_w = trace_weights;
+  a.err = reinterpret_cast<int*>(sc + S.err);
+  a.timing = reinterpret_cast<long long*>(timing);
+  a.nr = nr;
+  a.ns = ns;
+  if (!al16(inputs) || !al16(outputs) || !al16(scratch) || (trace_hidden && !al16(trace_hidden)))
+    return fail(YN_E_INVALID, "stack decode: inputs, outputs, scratch and trace_hidden must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  // stale epochs of an earlier launch must not match this launch's steps
+  YN_CUDA(cudaMemsetAsync(sc + S.f_logits, 0, S.total - S.f_logits, st));
+  const void* kernel = reinterpret_cast<const void*>(&k_stack_flow);
+  if ((rc = set_smem_ptr(kernel, smem))) return rc;
+  int per_sm = 0;
+  YN_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, DEC_THREADS, smem));
+  if (per_sm < 1) return fail(YN_E_UNSUPPORTED, "data-flow decode kernel does not fit on an SM");
   void* args[] = {&a};
   YN_CUDA(cudaLaunchCooperativeKernel(kernel, dim3(G), dim3(DEC_THREADS), args, smem, st));
   return YN_OK;

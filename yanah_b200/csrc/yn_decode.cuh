@@ -590,8 +590,8 @@ YN_DEV const uint8_t* expert_record(const DecLayer& L, int e) {
 // byte count); the four small scale/bias pieces go as 16-byte cp.async over
 // the 32 lanes, which then arrive on the barrier when their copies land. A
 // tile (8 units) never crosses an expert boundary.
-template <int BITS, int GS>
-YN_DEV void copy_c(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, int ntile, uint8_t* C,
+template <int BITS, int GS, class Args>
+YN_DEV void copy_c(const Args& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, int ntile, uint8_t* C,
                    uint64_t* barT, int t0, int tstep) {
   constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, CS = SBH / 16;
   const int lane = threadIdx.x & 31;
@@ -665,8 +665,8 @@ YN_DEV void copy_d(const DecodeArgs& a, const DecLayer& L, const int32_t* ids, i
 // P2: gate/up dots of this CTA's tiles. Items (tile t, super-block sb) go
 // round-robin over the warps; partial sums land in
 // part[((t * 8 + row) * 2 + up) * NSB + sb].
-template <int BITS, int GS>
-YN_DEV void p2_tiles(const DecodeArgs& a, int ntile, const uint8_t* C, const uint32_t* xf, const float* xsum,
+template <int BITS, int GS, class Args>
+YN_DEV void p2_tiles(const Args& a, int ntile, const uint8_t* C, const uint32_t* xf, const float* xsum,
                      float inv, float* part, uint64_t* barT, uint32_t phT) {
   using S = Sb<BITS>;
   constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, NSB = RB / 64;

@@ -27,6 +27,22 @@ from .synthetic import StackConfig, dense_layer
 DECODE_STAMPS = 16
 DECODE_PHASES = ["loads", "wait_p1_tile", "norm_frags", "p1_rows", "bar1", "route", "issue_c", "p2_tiles",
                  "swiglu_issue_d", "bar2", "p3_frags", "wait_d", "p3_tiles", "combine", "end"]
+# Data-flow form (yn_stack_flow_decode): the same 16 stamps per layer; phases 12-14 are empty.
+FLOW_PHASES = ["h_in", "wait_p1_tile", "norm", "p1_rows_frags", "route", "issue", "gate_up_act_out", "act_in",
+               "frags_down", "y_out", "y_in", "combine_h_out", "-", "-", "-"]
+
+
+def flow_phase_report(timing: np.ndarray) -> dict:
+    """Per-phase means (over layers of the mean and of the max over CTAs, us)
+    of the data-flow decode's stamps; `layer_us` as in decode_phase_report."""
+    t = np.asarray(timing, dtype=np.float64) / 1e3
+    d = np.diff(t, axis=1)
+    out = {"phases_mean_us": {n: round(float(d[:, i].mean()), 3) for i, n in enumerate(FLOW_PHASES) if n != "-"},
+           "phases_max_us": {n: round(float(d[:, i].max(axis=1).mean()), 3) for i, n in enumerate(FLOW_PHASES)
+                             if n != "-"}}
+    if t.shape[0] > 1:
+        out["layer_us"] = round(float(np.diff(t[:, 0].min(1)).mean()), 3)
+    return out
 
 
 def decode_phase_report(timing: np.ndarray) -> dict:
@@ -80,7 +96,8 @@ class ResidentStack:
         self.table = torch.empty(tb, dtype=torch.uint8, device=self.device)
         arr = (_lib.Layer * n)(*self.structs)
         _lib.check(lib.yn_stack_prepare(C.byref(self.dims), arr, n, self.table.data_ptr(), tb))
-        sb = int(lib.yn_stack_scratch_bytes(C.byref(self.dims)))
+        sb = max(int(lib.yn_stack_scratch_bytes(C.byref(self.dims))),
+                 int(lib.yn_stack_flow_scratch_bytes(C.byref(self.dims))))
         self.scratch = torch.zeros(sb, dtype=torch.uint8, device=self.device)
         self.layer_array = arr
         torch.cuda.synchronize(self.device)
@@ -122,16 +139,19 @@ class ResidentStack:
     # ------------------------------------------------- persistent decode
     def decode(self, inputs: torch.Tensor, outputs: torch.Tensor, trace: Optional[torch.Tensor] = None,
                timing: Optional[torch.Tensor] = None, stream=None, trace_hidden: Optional[torch.Tensor] = None,
-               trace_weights: Optional[torch.Tensor] = None) -> None:
+               trace_weights: Optional[torch.Tensor] = None, kernel: str = "flow") -> None:
         """Sequential bs1 decode of inputs (N,H) -> outputs (N,H) in ONE
         persistent cooperative launch. trace: (N, L, k) int32 routed ids;
         trace_hidden: (N, L, H) bf16 input row of every layer; trace_weights:
         (N, L, k) fp32 routed weights; timing: (L, 16, n_SM) int64
-        global-timer stamps (ns) of every CTA for the last token."""
+        global-timer stamps (ns) of every CTA for the last token. kernel:
+        "flow" (data-flow form, yn_stack_flow_decode) or "barrier"
+        (yn_stack_decode); both give the same outputs bit for bit."""
         lib = _lib.lib()
         n = len(self.structs)
         ptr = lambda t: t.data_ptr() if t is not None else None
-        _lib.check(lib.yn_stack_decode(C.byref(self.dims), self.table.data_ptr(), self.layer_array, n,
+        fn = {"flow": lib.yn_stack_flow_decode, "barrier": lib.yn_stack_decode}[kernel]
+        _lib.check(fn(C.byref(self.dims), self.table.data_ptr(), self.layer_array, n,
                                        inputs.data_ptr(), inputs.shape[0], outputs.data_ptr(), self.scratch.data_ptr(),
                                        self.scratch.numel(), ptr(trace), ptr(trace_hidden), ptr(trace_weights),
                                        ptr(timing), stream_ptr(stream)))
@@ -144,13 +164,13 @@ class ResidentStack:
         return code.value
 
     def decode_host(self, host_inputs: torch.Tensor, host_outputs: torch.Tensor, dev_in: torch.Tensor,
-                    dev_out: torch.Tensor, stream=None) -> None:
+                    dev_out: torch.Tensor, stream=None, kernel: str = "flow") -> None:
         """End-to-end call with host buffers: copy pinned inputs in, decode,
         copy outputs back (all on `stream`, asynchronous)."""
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         with torch.cuda.stream(s):
             dev_in.copy_(host_inputs, non_blocking=True)
-            self.decode(dev_in, dev_out, stream=s)
+            self.decode(dev_in, dev_out, stream=s, kernel=kernel)
             host_outputs.copy_(dev_out, non_blocking=True)
 
     # ------------------------------------------------------ kernel timing

@@ -41,6 +41,7 @@ synchronous and futures are whatever the reader returns.
 """
 from __future__ import annotations
 
+import contextlib
 import time
 from dataclasses import dataclass
 from typing import Callable, Dict, List, Optional, Sequence
@@ -52,12 +53,35 @@ GROUP = 32
 
 @dataclass
 class SweepStats:
+    """Counters of the sweeps run so far. `passes` is advanced by the caller
+    after a whole prompt pass (the reference's orchestrator does the same)."""
     passes: int = 0
     layers: int = 0
-    resident_copies: int = 0
-    disk_records: int = 0
-    admitted: int = 0
-    read_wait_s: float = 0.0
+    pool_copies: int = 0        # staged records copied out of the pool
+    host_records: int = 0       # staged records read from the host tier
+    admitted: int = 0           # records written into the pool by final passes
+    read_wait_s: float = 0.0    # host time spent waiting for staged records
+
+
+@dataclass
+class SweepPlan:
+    """What the sweep does for one layer, decided from its routing alone:
+    `experts`, the distinct routed experts in ascending id order, cut into
+    consecutive `groups` of at most the staging size; `admit`, the experts a
+    final pass writes into the pool: the layer's fair share of its most used
+    experts (routing count descending, lower id first on equal counts)."""
+    layer: int
+    experts: List[int]
+    groups: List[List[int]]
+    admit: frozenset
+
+    @classmethod
+    def build(cls, layer: int, ids: np.ndarray, group: int, share: int, admit: bool) -> "SweepPlan":
+        experts, counts = np.unique(np.asarray(ids), return_counts=True)
+        chosen = experts[np.argsort(-counts, kind="stable")[:share]] if admit else experts[:0]
+        ex = experts.tolist()
+        return cls(layer, ex, [ex[i:i + group] for i in range(0, len(ex), group)],
+                   frozenset(int(e) for e in chosen))
 
 
 def _is_torch(v) -> bool:
@@ -131,18 +155,22 @@ class HostSlabMemory:
         self._view.release()
 
 
-class _Staging:
-    """One staging group. `memory` has the layout of pool memory, so the
-    backend computes on it exactly as on the pool (rows = staging index)."""
+class StagingBuffer:
+    """One of the two staging buffers: `memory` is laid out like pool memory,
+    so the backend's `moe` runs on it as on the pool, with staging slot i
+    holding `experts[i]` of the group it was filled with."""
 
     def __init__(self, memory):
         self.memory = memory
-        self.index: Dict[int, int] = {}
-        self.futures: List = []
-        self.read_done = None   # event after the GEMM that last read this buffer
+        self.slot_of: Dict[int, int] = {}
+        self.pending: List = []          # futures of the records still arriving
+        self.gemm_done = None            # device event after the GEMM that last read it
+
+    def fill_order(self, experts: List[int]) -> None:
+        self.slot_of = {e: i for i, e in enumerate(experts)}
 
     def views(self, e: int):
-        return self.memory.views(self.index[e])
+        return self.memory.views(self.slot_of[e])
 
 
 class HostTierReader:
@@ -183,9 +211,12 @@ class HostTierReader:
 
 
 class PrefillSweep:
-    """pool: `SlotPool`; reader: `submit_runs(layer, experts, dst_for)`;
-    make_memory(n): staging memory of n slots with the pool memory's layout
-    (default host slabs); streams: `SweepStreams` for device memory, None for host memory."""
+    """Prompt-pass sweep of `pool` (a `SlotPool`). reader: `submit_runs(layer,
+    experts, dst_for)` -> futures; make_memory(n): staging memory of n slots
+    laid out like the pool's (default: host slabs); streams: `SweepStreams`
+    for device memory, None for host memory. The constructor and `run_layer`
+    are the surface the reference's orchestrator calls
+    (orchestrator.py:322-337)."""
 
     def __init__(self, pool, reader, min_tokens: int = 16, group: int = GROUP,
                  make_memory: Optional[Callable[[int], object]] = None, streams: Optional[SweepStreams] = None):
@@ -195,81 +226,88 @@ class PrefillSweep:
             g = pool.g
             make_memory = lambda n: HostSlabMemory(n, g.expert_nbytes, g.slot_nbytes)
         self.streams = streams
-        self._staging = [_Staging(make_memory(group)) for _ in range(2)]
+        self.ring = [StagingBuffer(make_memory(group)) for _ in range(2)]
         self.stats = SweepStats()
 
     def fair_share(self) -> int:
+        """Pool slots a final pass may fill per layer."""
         return self.pool.slots // self.pool.g.total_moe_layers
 
-    def _on_copy_stream(self):
-        import contextlib
-        if self.streams is None:
-            return contextlib.nullcontext()
-        import torch
-        return torch.cuda.stream(self.streams.copy)
+    def plan(self, layer: int, ids: np.ndarray, admit: bool) -> SweepPlan:
+        return SweepPlan.build(layer, ids, self.group, self.fair_share(), admit)
 
-    def _load(self, st: _Staging, layer: int, experts: List[int]) -> None:
-        """Start the host-tier reads of the group's missing experts, then copy
-        its residents out of the pool (no reference-bit change). On the device
-        the reads go first, on the copy stream, and the pool copies run on the
-        current (compute) stream alongside them."""
-        s_ = self.streams
-        if s_ is not None and st.read_done is not None:
-            s_.copy.wait_event(st.read_done)          # the GEMM that read this buffer has run
-        st.index = {e: i for i, e in enumerate(experts)}      # sorted id order
-        slots = {e: self.pool.lookup((layer, e)) for e in experts}
-        missing = [e for e in experts if slots[e] is None]
-        self.stats.disk_records += len(missing)
-        st.futures = list(self.reader.submit_runs(layer, missing, st.views))
-        if s_ is not None:
-            st.futures.append(DeviceFuture(s_.event(s_.copy), s_.compute))
-        for e in experts:
-            if slots[e] is not None:
-                copy_record(st.views(e), self.pool.views(slots[e]))
-                self.stats.resident_copies += 1
+    # ----------------------------------------------------------- staging
+    def stage(self, buf: StagingBuffer, layer: int, experts: List[int]) -> None:
+        """Fill `buf` with `experts`: the host-tier reads of those not in the
+        pool are started first, then the resident ones are copied out of the
+        pool (their reference bits are left alone: a prompt says nothing
+        about what decode will reuse). On the device the reads go on the copy
+        stream after the GEMM that last read this buffer, the pool copies on
+        the compute stream."""
+        dev = self.streams
+        if dev is not None and buf.gemm_done is not None:
+            dev.copy.wait_event(buf.gemm_done)
+        buf.fill_order(experts)
+        resident = [(e, self.pool.lookup((layer, e))) for e in experts]
+        from_host = [e for e, s in resident if s is None]
+        buf.pending = list(self.reader.submit_runs(layer, from_host, buf.views))
+        if dev is not None:
+            buf.pending.append(DeviceFuture(dev.event(dev.copy), dev.compute))
+        self.stats.host_records += len(from_host)
+        for e, s in resident:
+            if s is not None:
+                copy_record(buf.views(e), self.pool.views(s))
+                self.stats.pool_copies += 1
 
+    def _admit(self, buf: StagingBuffer, layer: int, members: List[int]) -> None:
+        """Write `members` from staging into the pool (CLOCK victims). On the
+        device: on the copy stream, after the compute stream (whose queued
+        pool copies read the victims' old records first)."""
+        dev = self.streams
+        if dev is not None:
+            dev.copy.wait_stream(dev.compute)
+        ctx = contextlib.nullcontext()
+        if dev is not None:
+            import torch
+            ctx = torch.cuda.stream(dev.copy)
+        with ctx:
+            self.stats.admitted += self.pool.admit(layer, members, len(members),
+                                                   lambda e, dst: copy_record(dst, buf.views(e)))
+
+    # ----------------------------------------------------------- execution
     def run_layer(self, layer: int, x, ids: np.ndarray, w, moe: Callable, admit: bool):
-        """moe(layer, x, ids, w, memory, rows) -> the contribution of `rows`' experts only."""
-        s_ = self.streams
-        if s_ is not None:
-            s_.copy.wait_stream(s_.compute)
-        experts, counts = np.unique(ids, return_counts=True)
-        experts = [int(e) for e in experts]
-        groups = [experts[i:i + self.group] for i in range(0, len(experts), self.group)]
-        admit_set = set()
-        if admit:
-            order = np.argsort(-counts, kind="stable")
-            admit_set = {experts[i] for i in order[: self.fair_share()]}
-
-        out = None
-        self._load(self._staging[0], layer, groups[0])
-        for gi, grp in enumerate(groups):
-            st = self._staging[gi % 2]
-            if gi + 1 < len(groups):                              # read ahead one group
-                self._load(self._staging[(gi + 1) % 2], layer, groups[gi + 1])
+        """The routed contribution of every (row, column) of `ids`, one grouped
+        `moe(layer, x, ids, w, staging_memory, {expert: staging slot})` per
+        staging group, group g+1 staged while group g computes; a final pass
+        (`admit`) also writes the plan's admitted experts into the pool."""
+        dev = self.streams
+        if dev is not None:
+            dev.copy.wait_stream(dev.compute)     # pool contents and this layer's rows are final
+        plan = self.plan(layer, ids, admit)
+        self.stage(self.ring[0], layer, plan.groups[0])
+        total = None
+        for gi, experts in enumerate(plan.groups):
+            buf = self.ring[gi % 2]
+            if gi + 1 < len(plan.groups):
+                self.stage(self.ring[(gi + 1) % 2], layer, plan.groups[gi + 1])
             t0 = time.perf_counter()
-            for f in st.futures:
+            for f in buf.pending:
                 f.result()
             self.stats.read_wait_s += time.perf_counter() - t0
-            part = moe(layer, x, ids, w, st.memory, dict(st.index))
-            if s_ is not None:
-                st.read_done = s_.event(s_.compute)
-            out = part if out is None else out + part
-            if admit_set:
-                members = [e for e in grp if e in admit_set]
-                if s_ is not None:
-                    s_.copy.wait_stream(s_.compute)   # pool copies already queued there read their slots first
-                with self._on_copy_stream():
-                    self.stats.admitted += self.pool.admit(
-                        layer, members, len(members), lambda e, dst: copy_record(dst, st.views(e)))
-        if s_ is not None:
-            s_.compute.wait_stream(s_.copy)
+            part = moe(layer, x, ids, w, buf.memory, dict(buf.slot_of))
+            if dev is not None:
+                buf.gemm_done = dev.event(dev.compute)
+            total = part if total is None else total + part
+            if plan.admit:
+                self._admit(buf, layer, [e for e in experts if e in plan.admit])
+        if dev is not None:
+            dev.compute.wait_stream(dev.copy)
         self.stats.layers += 1
-        return out
+        return total
 
     def close(self):
-        for st in self._staging:
-            st.memory.close()
+        for buf in self.ring:
+            buf.memory.close()
 
 
 def prompt_pass(backend, sweep: PrefillSweep, h, admit: bool = True, layers: Optional[Sequence[int]] = None):
