@@ -16,7 +16,9 @@ and outputs copied out inside the timed region); `roofline` = the dominant
 kernel's algorithmic bytes per launch over its live CUDA-event duration;
 `cpu_baseline` = the C oracle timed on the host cores on a bounded sample.
 For N > 1 (torchrun) every rank decodes its own sequences (replicas: the
-resident stack does not shard), and the slowest rank's time is reported.
+resident stack does not shard), and the slowest rank's time is reported; the
+line also carries an `ep` object, the sharded path at the same N: the 64-row
+batch decode with the experts split over the ranks (as --workload ep).
 
 --impl reference: the reference's MLX path is unavailable on this box (MLX is
 not installed), so this times the CPU restatement of that path (oracle/, a C
@@ -310,7 +312,7 @@ def run_streaming(args, rank: int, world: int):
 EP_METRIC = "decode tok/s, batch of 64 rows, experts sharded over GPUs (Qwen3-Next-80B-A3B-shaped, 48 layers)"
 
 
-def run_ep(args, rank: int, world: int):
+def run_ep(args, rank: int, world: int, emit: bool = True):
     """Expert-parallel batch decode: 64 rows (one token each per step) through
     the 48-layer stack, experts sharded 512/world per GPU, per-layer dispatch
     and combine over peer memory (yn_ep_layer). One step = one CUDA graph
@@ -438,11 +440,12 @@ def run_ep(args, rank: int, world: int):
                    "peak_gbs": 770.0, "frac": round(link_bytes / step_s / 1e9 / 770.0, 4),
                    "pairs_sent_back_per_step": pairs_out},
     }
-    if rank == 0:
+    if rank == 0 and emit:
         print(json.dumps(line), flush=True)
     stack.graph = None
     barrier()
     stack.close()
+    return line
 
 
 # ------------------------------------------------------------- prefill leg
@@ -840,6 +843,51 @@ def run_verify(args, rank: int, world: int):
     stack.close()
 
 
+def hooks_sample(cfg, dev, inputs, n_tok: int) -> dict:
+    """The same decode through the per-layer hook sequence the reference's
+    orchestrator calls on a backend (orchestrator.py:226-300, every routed
+    expert a pool hit): pre_moe -> route (the routed ids come to the host: the
+    reference's routing sync) -> moe_ready -> moe_rest -> h_res +
+    moe_finalize, on CudaMoEBackend with every expert of every layer resident
+    in one CudaExpertMemory (slot = layer * E + expert)."""
+    import numpy as np
+    import torch
+
+    from yanah_b200.backend import CudaMoEBackend
+    from yanah_b200.device import fill_synthetic_experts
+
+    E = cfg.n_experts
+    be = CudaMoEBackend(cfg, dev, lookahead=0)
+    mem = be.make_expert_memory(cfg.n_layers * E)
+    for l in range(cfg.n_layers):
+        fill_synthetic_experts(mem.arena, cfg, l, first_slot=l * E)
+    torch.cuda.synchronize(dev)
+
+    def token(h):
+        for l in range(cfg.n_layers):
+            h_res, x, logits = be.pre_moe(l, h)
+            ids, w = be.route(logits)
+            rows = {int(e): l * E + int(e) for e in np.unique(ids)}
+            handle = be.moe_ready(l, x, ids, mem, rows)
+            out = be.moe_rest(l, x, ids, w, mem, rows, handle)
+            h = h_res + be.moe_finalize(l, out)
+        return h
+
+    token(inputs[0:1])
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for t in range(n_tok):
+        token(inputs[t:t + 1])
+    torch.cuda.synchronize(dev)
+    secs = time.perf_counter() - t0
+    if be.check_error():
+        raise RuntimeError("device error in the hook-sequence decode")
+    del mem
+    return {"value": round(n_tok / secs, 2), "unit": "tok/s", "tokens": n_tok,
+            "path": "CudaMoEBackend hooks per layer: pre_moe, route (host routing sync), moe_ready, moe_rest, "
+                    "moe_finalize; every expert resident"}
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args, rank: int, world: int):
     import numpy as np
@@ -961,6 +1009,14 @@ def run_ours(args, rank: int, world: int):
                                 "kind": "port",
                                 "sample": f"{args.cpu_tokens} sequential bs1 token(s) through all 48 layers, "
                                           f"C oracle, {used} OpenMP threads"}
+    if world == 1 and not args.no_hooks and not args.layers:
+        line["e2e_hooks"] = hooks_sample(cfg, dev, inputs, 16)
+    if world > 1 and not args.no_ep:
+        # the sharded path at the same GPU count: config 4's 64-row batch decode with the experts split
+        # over the ranks (its own line from `--workload ep`, reported here beside the replicas)
+        ep = run_ep(args, rank, world, emit=False)
+        line["ep"] = {k: ep[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling", "config", "e2e",
+                                         "gpu_launches", "clocks", "roofline", "nvlink")}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -974,6 +1030,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--cpu-tokens", type=int, default=12)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ep", action="store_true", help="with --gpus N > 1: skip the expert-parallel leg")
+    ap.add_argument("--no-hooks", action="store_true", help="skip the per-layer hook-sequence (e2e_hooks) sample")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
     ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill", "verify", "sweep"],

@@ -998,11 +998,12 @@ extern "C" int yn_stack_flow_decode(const yn_dims* dims, const void* table, cons
   YN_CUDA(cudaGetDevice(&dev));
   YN_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int G = sms;
-  // K groups of nr CTAs (routed columns), the rest (ns >= 8) for the shared expert's down rows
-  const int nr = (G - 8) / K, ns = G - K * nr;
+  // K groups of nr CTAs (routed columns), the rest (ns >= 18 where the SMs allow, else >= 8) for the shared
+  // expert's down rows: 8-bit rows cost ~4x a 2-bit routed row, so the shared blocks are spread wider
+  const int nr = std::max((G - 18) / K, std::min(8, (G - 8) / K)), ns = G - K * nr;
   const int oct_max = (DEC_I / 8 + nr - 1) / std::max(nr, 1), dt_max = (DEC_H / 16 + nr - 1) / std::max(nr, 1);
   const int dts_max = (DEC_H / 16 + ns - 1) / ns;
-  if (nr < 1 || oct_max > DEC_MAX_OCT || dt_max > FL_MAX_DT || dts_max > FL_MAX_DT ||
+  if (nr < 1 || ns < 8 || oct_max > DEC_MAX_OCT || dt_max > FL_MAX_DT || dts_max > FL_MAX_DT ||
       (FL_HW + G - 1) / G > FL_MAX_CW)
     return fail(YN_E_UNSUPPORTED, "data-flow decode: " + std::to_string(G) + " SMs cannot hold " +
                                       std::to_string(K) + " routed columns of at least 8 CTAs plus 8 shared CTAs");

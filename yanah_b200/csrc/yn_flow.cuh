@@ -341,14 +341,16 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_flow(const FlowArgs a)
     if (routed) {
       // -------- P2r: gate/up rows (tile by tile) and this CTA's down rows, issued together
       const int RBI = DEC_I * L.rg.bits / 8, SBI = DEC_I / L.rg.gs * 2;
-      if (warp == DEC_WARPS - 1) {
+      // one warp per tile (warp DEC_WARPS - 1 - t issues tile t), so the issue is not one warp's serial chain
+      if (warp >= DEC_WARPS - DEC_MAX_OCT) {
+        const int tw = DEC_WARPS - 1 - warp;
         switch (fmt) {
-          case 0: copy_c<2, 64>(a, L, ids, sg, ntile, C, barT, 0, 1); break;
-          case 1: copy_c<2, 32>(a, L, ids, sg, ntile, C, barT, 0, 1); break;
-          case 2: copy_c<4, 64>(a, L, ids, sg, ntile, C, barT, 0, 1); break;
-          default: copy_c<4, 32>(a, L, ids, sg, ntile, C, barT, 0, 1); break;
+          case 0: copy_c<2, 64>(a, L, ids, sg, ntile, C, barT, tw, DEC_MAX_OCT); break;
+          case 1: copy_c<2, 32>(a, L, ids, sg, ntile, C, barT, tw, DEC_MAX_OCT); break;
+          case 2: copy_c<4, 64>(a, L, ids, sg, ntile, C, barT, tw, DEC_MAX_OCT); break;
+          default: copy_c<4, 32>(a, L, ids, sg, ntile, C, barT, tw, DEC_MAX_OCT); break;
         }
-      } else if (tid == 32 * (DEC_WARPS - 2)) {
+      } else if (tid == 32 * (DEC_WARPS - DEC_MAX_OCT - 1)) {
         const uint8_t* rec = expert_record(L, ids[col]);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         issue_down(rec + L.rg.off[6], rec + L.rg.off[7], rec + L.rg.off[8], 16 * q0, 16 * ndt, RBI, SBI, Dw, Dsc, Dbi,
@@ -368,27 +370,25 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_flow(const FlowArgs a)
       phT ^= 1;
       pendT = false;
       __syncthreads();
-      // SwiGLU of this CTA's units (thread v: units 2v, 2v+1), published two per word
-      if (tid < ntile * 4) {
-        const int NSB = DEC_H * L.rg.bits / 8 / 64;
-        uint32_t pk = 0;
-        for (int h = 0; h < 2; ++h) {
-          const int u = 2 * tid + h;
+      // SwiGLU of this CTA's units, one unit per thread (gate/up sums over the super-blocks in
+      // order), published two units per word by the even thread
+      if (warp < DEC_MAX_OCT * 8 / 32) {
+        const int NSB = DEC_H * L.rg.bits / 8 / 64, u = tid;
+        uint32_t v = 0;
+        if (u < 8 * ntile) {
           float gsum = 0.0f, usum = 0.0f;
           for (int q = 0; q < NSB; ++q) {
             gsum = __fadd_rn(gsum, part[(u * 2 + 0) * NSB + q]);
             usum = __fadd_rn(usum, part[(u * 2 + 1) * NSB + q]);
           }
-          pk |= (uint32_t)f32_to_bf16(swiglu_bf16(bf16r(gsum), bf16r(usum))) << (16 * h);
+          v = (uint32_t)f32_to_bf16(swiglu_bf16(bf16r(gsum), bf16r(usum)));
         }
-        put_flag(a.f_act + ((size_t)par * K + col) * FL_AW + 4 * t0 + tid, pk, ep);
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, v, 1);
+        if (u < 8 * ntile && !(u & 1))
+          put_flag(a.f_act + ((size_t)par * K + col) * FL_AW + 4 * t0 + (u >> 1), v | (hi << 16), ep);
       }
     }
     stamp(a, tok, layer, 7);
-    // next layer's P1 tile (and the descriptor of layer step + 2) while the exchanges run
-    if (step + 2 < total_steps) load_layer_async(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
-    if (more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA, 0);
-    pendA = more;
     float gate = 0.0f;
     if (routed) {
       // -------- P2r: the expert's 512 activations back, down rows
@@ -447,6 +447,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_flow(const FlowArgs a)
         pendS = true;
       }
     }
+    // next layer's P1 tile (and the descriptor of layer step + 2) while the row exchange runs
+    if (step + 2 < total_steps) load_layer_async(&lay[(step + 2) % 3], a.layers, (step + 2) % a.n_layers);
+    if (more) issue_p1(Ln, r1, p1_tile(Abuf, r1), barA, 0);
+    pendA = more;
     stamp(a, tok, layer, 9);
     // -------- P3: this CTA's output rows: routed y, shared term, combine, residual
     for (int i = tid; i < nsrc * ncw; i += DEC_THREADS) {
