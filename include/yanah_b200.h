@@ -369,6 +369,20 @@ int yn_prefill_plan(const yn_dims* dims, const int32_t* ids, int32_t T, int32_t*
 int yn_pairs_combine(const yn_dims* dims, const void* y, const int32_t* pair_of, const float* weights,
                      const void* y_shared, const void* h_res, int32_t T, void* out, void* stream);
 
+/* Rows (row_of[p], or p when row_of is NULL) of x (bf16, cols % 16 == 0) in the
+ * K order the tensor-core GEMM uses for `bits`-bit codes (2, 4 or 8), as fp16
+ * (f16 != 0, gate/up operands) or bf16 (down operands). The 4-bit order is
+ * yn_gather_f16_kperm's. Part of the prompt pass of sweep.py:80-138 /
+ * mlx_backend.py:421-433 for every record format. */
+int yn_gather_kperm(const void* x, const int32_t* row_of, int64_t rows, int32_t cols, int32_t bits, int32_t f16,
+                    void* out, void* stream);
+/* out[t][c] = bf16(scale[t] * y[t][c]) for bf16 y: the gated shared-expert term
+ * sigmoid(g) * shared(x) of many rows (mlx_backend.py:302-306 with :438-440). */
+int yn_scale_rows(const void* y, const float* scale, int64_t rows, int32_t cols, void* out, void* stream);
+/* Where yn_rows_route of T rows left the shared expert's SwiGLU activations
+ * (T, shared_inter) bf16 and its gates sigmoid(g) (T) fp32 in `ws`. */
+int yn_rows_route_shared(const yn_dims* dims, int32_t T, void* ws, void** act_sh, float** sgate);
+
 /* ---------------------------------------------------------- slot copies */
 
 /* Copy `n` expert records host -> slot arena (io_lanes.py:121-126

@@ -182,3 +182,35 @@ def test_sweep_from_repacked_file_tier(tmp_path):
         sw.close()
     for a, b in zip(*outs):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_sweep_qwen3_shape_two_bit_and_shared_expert():
+    """A Qwen3-Next-shaped prompt pass (512 experts, top-10, 2-bit g64 and
+    g32 routed records, 8-bit shared expert) through the sweep over a pool
+    holding part of the stack: cold and warm pools give bit-identical layer
+    outputs, each within REL_L2_TOL of the oracle's layer on the same rows."""
+    cfg = small_config(bits=(2, 2), gs=64, hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=13)
+    for gs in (64, 32):
+        cfg.group_size = gs
+        T, group = 96, 32
+        be = CudaMoEBackend(cfg)
+        tier = HostTier(cfg, be.device)
+        h = hidden_rows(cfg, T, stream=43)
+        hd = bf16_dev(h)
+        cold = _sweep(be, tier, _pool(be, tier, 300, 8, []), group)
+        out_cold = _pass_by_layer(be, cold, hd, [0, 1], admit=False)
+        warm_keys = [(l, int(e)) for l in (0, 1) for e in np.unique(_routed(be, hd, l))[:40]]
+        warm = _sweep(be, tier, _pool(be, tier, 300, 8, warm_keys), group)
+        out_warm = _pass_by_layer(be, warm, hd, [0, 1], admit=True)
+        for a, b in zip(out_cold, out_warm):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+        assert cold.stats.host_records > 0 and warm.stats.pool_copies > 0
+        orc = cpu.OracleStack(cfg, threads=8)
+        rows = [0, 31, 95]
+        inp = [h, bf16_np(out_cold[0])]
+        for l in (0, 1):
+            ref = orc.layer(l, inp[l][rows])["out"]
+            err = rel_l2(bf16_np(out_cold[l])[rows], ref)
+            assert err < REL_L2_TOL, (gs, l, err)
+        cold.close()
+        warm.close()

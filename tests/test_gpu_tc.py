@@ -90,3 +90,36 @@ def test_tc_lfm2_verify_rows():
     # a speculative-verify batch (1 + 4 draft rows) on the same grouped GEMM:
     # few rows per expert, every pair checked
     _check(lfm2_stack(n_layers=40), T=5, sample_pairs=20)
+
+
+@pytest.mark.parametrize("bits,gs", [(2, 64), (2, 32), (4, 64)])
+def test_grouped_prompt_pass_qwen3_shape(bits, gs):
+    """A Qwen3-Next-shaped prompt pass of 300 rows (512 experts, top-10, an
+    8-bit shared expert behind its gate) through the backend hooks the
+    orchestrator calls (pre_moe, route, moe, moe_finalize) on the grouped
+    tensor-core path, for each routed record format: routed ids bit-exact,
+    layer outputs within REL_L2_TOL of the oracle."""
+    from yanah_b200.backend import CudaMoEBackend
+    from yanah_b200.device import fill_synthetic_experts
+    cfg = small_config(bits=(bits,), gs=gs, hidden=2048, n_experts=512, top_k=10, inter=512, shared=512, seed=12)
+    be = CudaMoEBackend(cfg, "cuda", lookahead=0)
+    mem = be.make_expert_memory(cfg.n_experts)
+    fill_synthetic_experts(mem.arena, cfg, 0)
+    T = 300
+    h = hidden_rows(cfg, T, stream=41)
+    hd = bf16_dev(h)
+    h_res, x, logits = be.pre_moe(0, hd)
+    ids, w = be.route(logits)
+    rows = {int(e): int(e) for e in np.unique(ids)}
+    routed = be.moe(0, x, ids, w, mem, rows)
+    with torch.cuda.stream(be.stream):
+        out = h_res + be.moe_finalize(0, routed)
+    torch.cuda.synchronize()
+    assert be.check_error() == 0
+    orc = cpu.OracleStack(cfg, threads=8)
+    pa = orc.post_attention(0, h)
+    assert np.array_equal(ids, pa["ids"])
+    sample = [0, 1, 57, 150, 298, 299]
+    ref = orc.layer(0, h[sample])["out"]
+    err = rel_l2(bf16_np(out)[sample], ref)
+    assert err < REL_L2_TOL, err

@@ -126,6 +126,9 @@ _SIGS = {
     "yn_prefill_max_tiles": (C.c_int, [C.POINTER(Dims), _I, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "yn_prefill_plan": (C.c_int, [C.POINTER(Dims), _P, _I, _P, _P, _P, _I, _P, _I, _P, _P, _P]),
     "yn_pairs_combine": (C.c_int, [C.POINTER(Dims), _P, _P, _P, _P, _P, _I, _P, _P]),
+    "yn_gather_kperm": (C.c_int, [_P, _P, C.c_int64, _I, _I, _I, _P, _P]),
+    "yn_scale_rows": (C.c_int, [_P, _P, C.c_int64, _I, _P, _P]),
+    "yn_rows_route_shared": (C.c_int, [C.POINTER(Dims), _I, _P, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
 }
 
 _lib = None

@@ -27,9 +27,10 @@ Differences from the MLX backend, all outside the MoE path:
   routed experts as grouped GEMMs on the tensor cores (`yn_tc_experts`), as
   does `moe` with experts missing from `rows` (the prefill sweep's staging
   groups, mlx_backend.py:421-433): the group's (row, column) pairs sorted by
-  slot, the contribution of those pairs only. The grouped path needs 4-bit g64
-  routed experts and a stack without a shared expert (the LFM2 shape); other
-  stacks raise NotImplementedError there.
+  slot, the contribution of those pairs only. The grouped path takes 4-bit g64
+  and 2-bit g64 / g32 routed records; the shared expert of such a pass (its
+  activations and gates come from the row routing) runs as one more grouped
+  GEMM over every row in `moe_finalize`.
 
 Every call is asynchronous on the backend's stream; `fence()` blocks until the
 work that reads pool slots has finished.
@@ -176,10 +177,10 @@ class CudaMoEBackend:
 
     def _grouped_supported(self, layer: int) -> Optional[str]:
         spec = self.cfg.record_spec(layer)
-        if self.cfg.shared_inter:
-            return "the grouped expert path is built for stacks without a shared expert"
-        if spec.bits != 4 or spec.group_size != 64:
-            return "the grouped expert path needs 4-bit g64 routed experts"
+        if (spec.bits, spec.group_size) not in ((4, 64), (2, 64), (2, 32)):
+            return "the grouped expert path needs 4-bit g64 or 2-bit g64 / g32 routed experts"
+        if self.cfg.shared_inter and self.cfg.shared_inter != self.cfg.moe_inter:
+            return "the grouped path runs the shared expert with shared_inter == moe_inter"
         return None
 
     def _pre_rows(self, layer: int, h1: torch.Tensor):
@@ -329,7 +330,8 @@ class CudaMoEBackend:
         p_up = p_of + 4 * len(sec[1])
         p_dn = p_up + 4 * len(sec[2])
         err = self._tc_err.data_ptr()
-        _lib.check(lib.yn_gather_f16_kperm(x.data_ptr(), p_row, n, H, x16.data_ptr(), st))
+        bits = cfg.record_spec(layer).bits
+        _lib.check(lib.yn_gather_kperm(x.data_ptr(), p_row, n, H, bits, 1, x16.data_ptr(), st))
         _lib.check(lib.yn_tc_experts(D, C.byref(L), 0, p_up, len(up), None, x16.data_ptr(), n, act.data_ptr(), None,
                                      err, st))
         _lib.check(lib.yn_tc_experts(D, C.byref(L), 1, p_dn, len(dn), None, act.data_ptr(), n, None, y.data_ptr(),
@@ -345,8 +347,56 @@ class CudaMoEBackend:
         return out
 
     def moe_finalize(self, layer: int, routed: torch.Tensor) -> torch.Tensor:
-        """routed + shared: the shared expert was added with the weighted sum."""
-        return routed
+        """routed + shared. Passes of at most 8 rows added the shared expert
+        with the weighted sum (yn_moe_down); a prompt pass of more rows adds it
+        here: bf16(routed + bf16(sigmoid(g) * shared(x)))."""
+        if "rows" not in self._pre or not self.cfg.shared_inter:
+            return routed
+        return self._shared_rows(self._pre["layer"], routed)
+
+    def _shared_layer(self, layer: int) -> _lib.Layer:
+        """The shared expert's down matrix as a one-slot 'expert' of 8-bit
+        records for the grouped down GEMM (pieces at their own addresses)."""
+        L = self.layers[layer].struct()
+        m = self.layers[layer].shared[2]
+        L.expert_base = m.w.data_ptr()
+        L.slot_stride = 16
+        L.n_slots = 1
+        L.expert_slot = None
+        r = _lib.Record()
+        r.bits, r.group_size = 8, self.cfg.dense_group
+        r.piece_offset[6] = 0
+        r.piece_offset[7] = m.s.data_ptr() - m.w.data_ptr()
+        r.piece_offset[8] = m.b.data_ptr() - m.w.data_ptr()
+        r.record_bytes = m.w.numel() * 4
+        L.record = r
+        return L
+
+    def _shared_rows(self, layer: int, routed: torch.Tensor) -> torch.Tensor:
+        lib, cfg = _lib.lib(), self.cfg
+        T, H, K, I = routed.shape[0], cfg.hidden, cfg.top_k, cfg.shared_inter
+        D, st = C.byref(self.dims), self._st()
+        act_p, sg_p = C.c_void_p(), C.c_void_p()
+        _lib.check(lib.yn_rows_route_shared(D, T, self._route_ws.data_ptr(), C.byref(act_p), C.byref(sg_p)))
+        from .prefill import DOWN_ROWS, TILE_ROWS
+        tiles = np.array([(0, p0, min(TILE_ROWS, T - p0), u0) for p0 in range(0, T, TILE_ROWS)
+                          for u0 in range(0, H, DOWN_ROWS)], np.int32)
+        with torch.cuda.stream(self.stream):
+            dev_tiles = torch.from_numpy(tiles).pin_memory().to(self.device, non_blocking=True)
+            act = torch.empty((T, I), dtype=torch.bfloat16, device=self.device)
+            y = torch.empty((T, H), dtype=torch.bfloat16, device=self.device)
+            term = torch.empty_like(y)
+            out = torch.empty_like(routed)
+            none = torch.full((T, K), -1, dtype=torch.int32, device=self.device)
+        _lib.check(lib.yn_gather_kperm(act_p.value, None, T, I, 8, 0, act.data_ptr(), st))
+        L = self._shared_layer(layer)
+        _lib.check(lib.yn_tc_experts(D, C.byref(L), 1, dev_tiles.data_ptr(), len(tiles), None, act.data_ptr(), T, None,
+                                     y.data_ptr(), self._tc_err.data_ptr(), st))
+        _lib.check(lib.yn_scale_rows(y.data_ptr(), sg_p.value, T, H, term.data_ptr(), st))
+        _ids, w = self._pre["rows"]
+        _lib.check(lib.yn_pairs_combine(D, y.data_ptr(), none.data_ptr(), w.data_ptr(), term.data_ptr(),
+                                        routed.data_ptr(), T, out.data_ptr(), st))
+        return out
 
     # ------------------------------------------------------ lazy + write fence
     def launch(self, h) -> None:

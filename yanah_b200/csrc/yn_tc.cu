@@ -91,9 +91,11 @@ int make_row_maps(const void* base, long long rows, int cols, bool bf16, TcMaps*
   return YN_OK;
 }
 
-size_t tc_smem(int Kd) {
+size_t tc_smem(int Kd, int bits) {
   (void)Kd;
-  return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES) + (size_t)TC_CR * TC_C_BYTES + (2 * TC_S + 4) * 8 + 16;
+  const size_t ring = bits == 2 ? (size_t)TcFmt<2>::CR * TcFmt<2>::SLOT
+                     : bits == 8 ? (size_t)TcFmt<8>::CR * TcFmt<8>::SLOT : (size_t)TcFmt<4>::CR * TcFmt<4>::SLOT;
+  return 1024 + (size_t)TC_S * (TC_A_BYTES + TC_B_BYTES) + ring + (2 * TC_S + 4) * 8 + 16;
 }
 }  // namespace
 
@@ -142,6 +144,51 @@ extern "C" int yn_gather_f16_kperm(const void* x, const int32_t* row_of, int64_t
   return YN_OK;
 }
 
+extern "C" int yn_gather_kperm(const void* x, const int32_t* row_of, int64_t rows, int32_t cols, int32_t bits,
+                               int32_t f16, void* out, void* stream) {
+  if (!x || !out || rows < 1 || cols < 16 || cols % 16) return host_fail(YN_E_INVALID, "bad rows/cols or null");
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(x) || !a16(out)) return host_fail(YN_E_INVALID, "rows must be 16-byte aligned");
+  const long long nu = rows * (long long)(cols / 16);
+  const int grid = (int)std::min<long long>((nu + 255) / 256, 8192);
+  auto xx = reinterpret_cast<const uint16_t*>(x);
+  auto oo = reinterpret_cast<uint16_t*>(out);
+  cudaStream_t st = as_st(stream);
+  if (bits == 2) {
+    if (f16) k_perm_rows<2, true><<<grid, 256, 0, st>>>(xx, row_of, rows, cols, oo);
+    else k_perm_rows<2, false><<<grid, 256, 0, st>>>(xx, row_of, rows, cols, oo);
+  } else if (bits == 4) {
+    if (f16) k_perm_rows<4, true><<<grid, 256, 0, st>>>(xx, row_of, rows, cols, oo);
+    else k_perm_rows<4, false><<<grid, 256, 0, st>>>(xx, row_of, rows, cols, oo);
+  } else if (bits == 8) {
+    if (f16) k_perm_rows<8, true><<<grid, 256, 0, st>>>(xx, row_of, rows, cols, oo);
+    else k_perm_rows<8, false><<<grid, 256, 0, st>>>(xx, row_of, rows, cols, oo);
+  } else {
+    return host_fail(YN_E_UNSUPPORTED, "bits must be 2, 4 or 8");
+  }
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_scale_rows(const void* y, const float* scale, int64_t rows, int32_t cols, void* out, void* stream) {
+  if (!y || !scale || !out || rows < 1 || cols < 1) return host_fail(YN_E_INVALID, "bad rows/cols or null");
+  const long long n = rows * (long long)cols;
+  const int grid = (int)std::min<long long>((n + 255) / 256, 8192);
+  k_scale_rows<<<grid, 256, 0, as_st(stream)>>>(reinterpret_cast<const uint16_t*>(y), scale, rows, cols,
+                                                reinterpret_cast<uint16_t*>(out));
+  YN_CUDA_T(cudaGetLastError());
+  return YN_OK;
+}
+
+extern "C" int yn_rows_route_shared(const yn_dims* dims, int32_t T, void* ws, void** act_sh, float** sgate) {
+  if (!dims || !ws || !act_sh || !sgate) return host_fail(YN_E_INVALID, "null argument");
+  if (T < 1 || T > ROUTE_MAX_ROWS) return host_fail(YN_E_UNSUPPORTED, "rows must be in [1, 4096]");
+  const RouteWs L = route_ws(*dims, T);
+  *act_sh = reinterpret_cast<uint8_t*>(ws) + L.act_sh;
+  *sgate = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + L.sgate);
+  return YN_OK;
+}
+
 extern "C" int yn_to_f16_kperm(const void* x, int64_t rows, int32_t cols, void* out, void* stream) {
   if (!x || !out || rows < 1 || cols < 8 || cols % 8) return host_fail(YN_E_INVALID, "bad rows/cols or null");
   const long long n = rows * (long long)cols;
@@ -161,8 +208,11 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   if (mode == 0 && !act_out) return host_fail(YN_E_INVALID, "gate/up needs act_out");
   if (mode == 1 && !y_out) return host_fail(YN_E_INVALID, "down needs y_out");
   const yn_record& r = layer->record;
-  if (r.bits != 4 || r.group_size != 64)
-    return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: routed experts must be 4-bit g64");
+  const bool fmt_ok = (r.bits == 4 && r.group_size == 64) || (r.bits == 2 && (r.group_size == 64 || r.group_size == 32)) ||
+                      (mode == 1 && r.bits == 8 && r.group_size == 64);
+  if (!fmt_ok)
+    return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: records must be 4-bit g64 or 2-bit g64/g32 "
+                                       "(8-bit g64 for the down projection)");
   const int H = dims->hidden, I = dims->moe_inter;
   if (H % 512 || I % 512)  // whole 128-row down tiles, 64-unit gate/up tiles, scale rows in 8-group blocks
     return host_fail(YN_E_UNSUPPORTED, "tensor-core expert GEMM: hidden and moe_inter must be multiples of 512");
@@ -188,9 +238,16 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   a.act_out = reinterpret_cast<uint16_t*>(act_out);
   a.y_out = reinterpret_cast<uint16_t*>(y_out);
   a.err = err;
-  const size_t smem = tc_smem(mode == 0 ? H : I);
-  const void* kern = mode == 0 ? reinterpret_cast<const void*>(k_tc_experts<0>)
-                               : reinterpret_cast<const void*>(k_tc_experts<1>);
+  const size_t smem = tc_smem(mode == 0 ? H : I, r.bits);
+  const int fi = r.bits == 8 ? 3 : r.bits == 4 ? 0 : r.group_size == 64 ? 1 : 2;
+  const void* kern0[3] = {reinterpret_cast<const void*>(k_tc_experts<0, 4, 64>),
+                          reinterpret_cast<const void*>(k_tc_experts<0, 2, 64>),
+                          reinterpret_cast<const void*>(k_tc_experts<0, 2, 32>)};
+  const void* kern1[4] = {reinterpret_cast<const void*>(k_tc_experts<1, 4, 64>),
+                          reinterpret_cast<const void*>(k_tc_experts<1, 2, 64>),
+                          reinterpret_cast<const void*>(k_tc_experts<1, 2, 32>),
+                          reinterpret_cast<const void*>(k_tc_experts<1, 8, 64>)};
+  const void* kern = mode == 0 ? kern0[fi] : kern1[fi];
   int rc = host_set_smem(kern, smem);
   if (rc) return rc;
   int dev = 0, sms = 0;
@@ -199,8 +256,8 @@ extern "C" int yn_tc_experts(const yn_dims* dims, const yn_layer* layer, int32_t
   const int grid = std::max(1, std::min(n_tiles, sms));  // persistent: one CTA per SM walks the tiles
   TcMaps maps;
   if ((rc = make_row_maps(b_rows, n_rows, mode == 0 ? H : I, mode == 1, &maps))) return rc;
-  if (mode == 0) k_tc_experts<0><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a, maps);
-  else k_tc_experts<1><<<grid, TCW_THREADS, smem, as_st(stream)>>>(a, maps);
+  void* args[] = {&a, &maps};
+  YN_CUDA_T(cudaLaunchKernel(kern, dim3(grid), dim3(TCW_THREADS), args, smem, as_st(stream)));
   YN_CUDA_T(cudaGetLastError());
   return YN_OK;
 }

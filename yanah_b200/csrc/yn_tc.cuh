@@ -91,6 +91,15 @@ YN_DEV void tc_unpack4(uint32_t w, uint32_t (&pr)[4]) {
 
 YN_DEV int kperm(int k) { const int p = k & 7; return (k & ~7) | (p < 4 ? 2 * p : 2 * (p - 4) + 1); }
 
+// K order of the A tile for BITS-bit codes: inside every unit of 16 codes,
+// pair p of the unpack (MmaFmt<BITS>: codes lo(p), hi(p)) sits at positions
+// 2p, 2p+1. For 4-bit this is kperm above.
+template <int BITS>
+YN_DEV int kperm_fmt(int k) {
+  const int j = k & 15, p = MmaFmt<BITS>::pair_of(j);
+  return (k & ~15) | (2 * p + (j == MmaFmt<BITS>::hi(p) ? 1 : 0));
+}
+
 YN_DEV uint64_t tc_desc(uint32_t smem_addr) {
   // K-major, 128-byte swizzle: start address (>>4), leading offset 1 (unused
   // for swizzled K-major), stride offset 1024 bytes between 8-row atoms,
@@ -145,6 +154,9 @@ YN_DEV void tc_ld32(uint32_t taddr, float (&v)[32]) {
 
 YN_DEV void tc_cpa16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+YN_DEV void tc_cpa8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 YN_DEV void tc_cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -212,6 +224,51 @@ YN_DEV void tc_dequant_row(const uint8_t* codes, uint16_t sc_bits, uint16_t bi_b
   }
 }
 
+// Generic producer dequantisation (2- and 8-bit codes; 4-bit uses
+// tc_dequant_row): this thread's 32 codes of one 64-code stage of a weight row
+// (two units of 16 codes, MmaFmt<BITS>::WORDS words each) into 4 chunks of
+// the swizzled A tile from chunk i0. w = s * q + b as one fp32 FMA of the
+// unpacked (mult * q) and s / mult (exact: a power of two), rounded to fp16
+// (MODE 0) or bf16 (MODE 1).
+template <int MODE, int BITS>
+YN_DEV void tc_dequant_gen(const uint8_t* codes, uint16_t sc_bits, uint16_t bi_bits, uint8_t* Arow, int t, int i0) {
+  using F = MmaFmt<BITS>;
+  uint32_t words[2 * F::WORDS];
+#pragma unroll
+  for (int v = 0; v < 2 * F::WORDS; v += 2) {
+    const uint2 c = *reinterpret_cast<const uint2*>(codes + 4 * v);
+    words[v] = c.x;
+    words[v + 1] = c.y;
+  }
+  const float s = f16_to_f32(sc_bits), b = f16_to_f32(bi_bits);
+  const __half2 k1024 = __float2half2_rn(1024.0f);
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    uint32_t pr[8];
+    F::unpack_raw(words + u * F::WORDS, pr);
+    uint32_t o[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      __half2 h = *reinterpret_cast<__half2*>(&pr[p]);
+      h = __hsub2(h, k1024);  // mult * q, exact
+      const float2 q = __half22float2(h);
+      const float m = __fmul_rn(s, F::inv_mult(p));
+      const float w0 = __fmaf_rn(q.x, m, b), w1 = __fmaf_rn(q.y, m, b);
+      if (MODE == 0) {
+        __half2 hw = __floats2half2_rn(w0, w1);
+        o[p] = *reinterpret_cast<uint32_t*>(&hw);
+      } else {
+        __nv_bfloat162 bw = __floats2bfloat162_rn(w0, w1);
+        o[p] = *reinterpret_cast<uint32_t*>(&bw);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+      *reinterpret_cast<uint4*>(Arow + (((i0 + 2 * u + c) ^ (t & 7)) << 4)) =
+          make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+  }
+}
+
 // SwiGLU with the same bf16 rounding points as swiglu_bf16, but the sigmoid
 // from the hardware exponential and an approximate divide: these outputs are
 // held to the bf16 output tolerance, not to bit equality, and the epilogue
@@ -258,21 +315,35 @@ constexpr int TC_NW = 8 / TC_NH;             // code words per producer thread a
 #define TC_EPW 8
 #endif
 static_assert(TC_EPW == 4 || TC_EPW == 8, "epilogue warps: 4 or 8");
+// Code staging per format: bytes of one row per 64-code stage, bytes per
+// producer thread, ring slots (fewer for 8-bit, whose slots are twice as
+// large) and stages in flight ahead of the dequantiser.
+template <int BITS>
+struct TcFmt {
+  static constexpr int ROWB = 8 * BITS;
+  static constexpr int TB = ROWB / TC_NH;
+  static constexpr int CR = BITS == 8 ? 4 : TC_CR;
+  static constexpr int PC = CR - 2;
+  static constexpr int SLOT = TC_M * ROWB;
+};
 constexpr int TC_EW = TC_PW;                 // first epilogue warp (a multiple of 4: warp % 4 = TMEM lane quadrant)
 constexpr int TC_MW = TC_PW + TC_EPW;        // the MMA warp
 constexpr int TC_LW = TC_MW + 1;             // the B-row loader warp
 constexpr int TCW_THREADS = 32 * (TC_MW + 2);
 
-template <int MODE>
+template <int MODE, int BITS, int GS>
 __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, const __grid_constant__ TcMaps maps) {
+  using FT = TcFmt<BITS>;
+  constexpr int GPS = 64 / GS;   // quantisation groups per 64-code stage
+  constexpr int SPB = 8 / GPS;   // stages per 8-group block of scales
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + (((smem_u32(smem_raw) + 1023u) & ~1023u) - smem_u32(smem_raw));
   uint8_t* Abuf = smem;
   uint8_t* Bbuf = Abuf + TC_S * TC_A_BYTES;
   uint8_t* Cbuf = Bbuf + TC_S * TC_B_BYTES;
   const int Kd = MODE == 0 ? a.H : a.I;
-  const int NG = Kd / 64, NK = Kd / 64;
-  uint64_t* full = reinterpret_cast<uint64_t*>(Cbuf + TC_CR * TC_C_BYTES);
+  const int NG = Kd / GS, NK = Kd / 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(Cbuf + FT::CR * FT::SLOT);
   uint64_t* empty = full + TC_S;
   uint64_t* acc_full = empty + TC_S;
   uint64_t* acc_empty = acc_full + 2;
@@ -316,7 +387,7 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
       const bool up = (MODE == 0) && (t & 1);
       const int wrow = MODE == 0 ? tl.u0 + (t >> 1) : tl.u0 + t;
       const int pw = MODE == 0 ? (up ? 3 : 0) : 6;
-      return {rec + a.rg.off[pw] + (size_t)wrow * (Kd / 2),
+      return {rec + a.rg.off[pw] + (size_t)wrow * (Kd * BITS / 8),
               reinterpret_cast<const uint4*>(rec + a.rg.off[pw + 1] + (size_t)wrow * NG * 2),
               reinterpret_cast<const uint4*>(rec + a.rg.off[pw + 2] + (size_t)wrow * NG * 2), good};
     };
@@ -341,13 +412,18 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
     // ring (TC_CR slots, read back only by this thread); one group per stage
     auto issue_codes = [&](const RowSrc& r, int ring, int kc) {
       if (r.good) {
-        uint8_t* cd = Cbuf + (ring % TC_CR) * TC_C_BYTES + t * 32 + h * 4 * TC_NW;
+        uint8_t* cd = Cbuf + (ring % FT::CR) * FT::SLOT + t * FT::ROWB + h * FT::TB;
+        const uint8_t* sw = r.w + FT::ROWB * kc + h * FT::TB;
+        if (FT::TB == 8) {
+          tc_cpa8(cd, sw);
+        } else {
 #pragma unroll
-        for (int v = 0; v < TC_NW / 4; ++v) tc_cpa16(cd + 16 * v, r.w + 32 * kc + h * 4 * TC_NW + 16 * v);
+          for (int v = 0; v < FT::TB / 16; ++v) tc_cpa16(cd + 16 * v, sw + 16 * v);
+        }
       }
       tc_cpa_commit();
     };
-    for (int kc = 0; kc < TC_PC; ++kc) issue_codes(nsrc, kc, kc);  // NK >= 8 > TC_PC
+    for (int kc = 0; kc < FT::PC; ++kc) issue_codes(nsrc, kc, kc);  // NK >= 8 > PC
     for (int ti = blockIdx.x; ti < n_tiles && ok; ti += gridDim.x) {
       const RowSrc src = nsrc;
       const bool good = src.good;
@@ -357,15 +433,18 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
       if (more) ntl = a.tiles[tn];
       // scales and biases of this row in blocks of 8 groups (16-byte loads, one block ahead)
       uint4 s8 = make_uint4(0, 0, 0, 0), b8 = s8, s8n = ns8, b8n = nb8;
-      for (int kc0 = 0; kc0 < NK && ok; kc0 += 8) {
+      for (int kc0 = 0; kc0 < NK && ok; kc0 += SPB) {
         s8 = s8n;
         b8 = b8n;
-        if (good && kc0 + 8 < NK) {
-          s8n = src.s[(kc0 + 8) / 8];
-          b8n = src.b[(kc0 + 8) / 8];
+        if (good && kc0 + SPB < NK) {
+          s8n = src.s[(kc0 + SPB) / SPB];
+          b8n = src.b[(kc0 + SPB) / SPB];
         }
-        if (more && kc0 == (NK > 8 ? 8 : 0)) nslot = a.slot_of ? a.slot_of[ntl.e] : ntl.e;
-        if (more && kc0 + 8 >= NK) {  // last block: the next tile's sources and first scale block
+        // the next tile's code words are issued from stage NK - PC on: its sources are known from the
+        // block holding that stage (its slot one block earlier when there is one)
+        const int ns_blk = ((NK - FT::PC) / SPB) * SPB, slot_blk = ns_blk >= SPB ? SPB : 0;
+        if (more && kc0 == slot_blk) nslot = a.slot_of ? a.slot_of[ntl.e] : ntl.e;
+        if (more && kc0 == ns_blk) {  // the next tile's sources and first scale block
           nsrc = row_src(ntl, nslot);
           if (nsrc.good) {
             ns8 = nsrc.s[0];
@@ -373,22 +452,25 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
           }
         }
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < SPB; ++jj) {
           const int kc = kc0 + jj;
           const int s = (g + kc) % TC_S;
-          if (kc + TC_PC < NK) issue_codes(src, g + kc + TC_PC, kc + TC_PC);
-          else if (more) issue_codes(nsrc, g + kc + TC_PC, kc + TC_PC - NK);
+          if (kc + FT::PC < NK) issue_codes(src, g + kc + FT::PC, kc + FT::PC);
+          else if (more) issue_codes(nsrc, g + kc + FT::PC, kc + FT::PC - NK);
           else tc_cpa_commit();  // keep one group per stage
           // the stage's A buffer is free once the MMA of TC_S stages back has committed
           if (g + kc >= TC_S) ok = mbar_wait_bounded(&empty[s], (((g + kc) / TC_S) - 1) & 1, a.err);
-          tc_cpa_wait<TC_PC>();  // this stage's code words have landed
+          tc_cpa_wait<FT::PC>();  // this stage's code words have landed
           if (!ok) break;
           if (good) {
-            const uint32_t sw = jj < 2 ? s8.x : jj < 4 ? s8.y : jj < 6 ? s8.z : s8.w;
-            const uint32_t bw = jj < 2 ? b8.x : jj < 4 ? b8.y : jj < 6 ? b8.z : b8.w;
-            tc_dequant_row<MODE, TC_NW>(Cbuf + ((g + kc) % TC_CR) * TC_C_BYTES + t * 32 + h * 4 * TC_NW,
-                                        (uint16_t)(sw >> (16 * (jj & 1))), (uint16_t)(bw >> (16 * (jj & 1))),
-                                        Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128, t, h * TC_NW);
+            const int gi = jj * GPS + (GPS == 2 ? h : 0);   // this thread's group inside the 8-group block
+            const uint32_t sw = gi < 2 ? s8.x : gi < 4 ? s8.y : gi < 6 ? s8.z : s8.w;
+            const uint32_t bw = gi < 2 ? b8.x : gi < 4 ? b8.y : gi < 6 ? b8.z : b8.w;
+            const uint8_t* cd = Cbuf + ((g + kc) % FT::CR) * FT::SLOT + t * FT::ROWB + h * FT::TB;
+            uint8_t* arow = Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+            const uint16_t sb16 = (uint16_t)(sw >> (16 * (gi & 1))), bb16 = (uint16_t)(bw >> (16 * (gi & 1)));
+            if (BITS == 4) tc_dequant_row<MODE, TC_NW>(cd, sb16, bb16, arow, t, h * TC_NW);
+            else tc_dequant_gen<MODE, BITS>(cd, sb16, bb16, arow, t, 4 * h);
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           mbar_arrive1(&full[s]);
@@ -419,7 +501,7 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
           // lanes 2i (gate of unit u) and 2i+1 (up of unit u) share the columns:
           // of each column pair the gate lane takes the even column, the up lane
           // the odd one, after one exchange
-          const int ku = kperm(tl.u0 + (m >> 1));
+          const int ku = kperm_fmt<BITS>(tl.u0 + (m >> 1));
           const bool is_up = m & 1;
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
@@ -539,6 +621,45 @@ __global__ void k_gather_f16_kperm(const uint16_t* x, const int32_t* row_of, lon
     }
     reinterpret_cast<uint4*>(out + (size_t)p * cols)[blk] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+}
+
+// out[p] = row (row_of ? row_of[p] : p) of x (bf16) in the K order of
+// BITS-bit codes (kperm_fmt), as fp16 (F16) or bf16: one unit of 16 elements
+// (two 16-byte loads and stores) per thread step.
+template <int BITS, bool F16>
+__global__ void k_perm_rows(const uint16_t* x, const int32_t* row_of, long long rows, int cols, uint16_t* out) {
+  using F = MmaFmt<BITS>;
+  const long long nu = rows * (cols / 16);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nu; i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i / (cols / 16);
+    const int u = (int)(i - p * (cols / 16));
+    const uint16_t* src = x + (size_t)(row_of ? row_of[p] : p) * cols + 16 * u;
+    const uint4 v0 = reinterpret_cast<const uint4*>(src)[0], v1 = reinterpret_cast<const uint4*>(src)[1];
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // output positions 2q, 2q+1: the codes of pair q
+      const int lo = F::lo(q), hi = F::hi(q);
+      const uint16_t a = (uint16_t)(w[lo >> 1] >> (16 * (lo & 1))), b = (uint16_t)(w[hi >> 1] >> (16 * (hi & 1)));
+      if (F16) {
+        __half2 h = __floats2half2_rn(bf16_to_f32(a), bf16_to_f32(b));
+        o[q] = *reinterpret_cast<uint32_t*>(&h);
+      } else {
+        o[q] = (uint32_t)a | ((uint32_t)b << 16);
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)p * cols + 16 * u);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// out[t][c] = bf16(scale[t] * y[t][c]) (y bf16): the gated shared-expert term
+// sigmoid(g) * y_shared of every row, rounded as the single-row path rounds it.
+__global__ void k_scale_rows(const uint16_t* y, const float* scale, long long rows, int cols, uint16_t* out) {
+  const long long n = rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = f32_to_bf16(__fmul_rn(scale[i / cols], bf16_to_f32(y[i])));
 }
 
 // out[t] = h_res[t] + (sum_j bf16(y[pair_of[t][j]] * w[t][j]) in column order [+ ysh[t]]),
