@@ -82,6 +82,7 @@ def test_backend_moe_equals_ready_rest_split():
     split = be.moe_rest(0, x, ids, w, mem, rows, handle)
     be.fence()
     assert np.array_equal(bf16_np(whole), bf16_np(split))
-    with pytest.raises(NotImplementedError):
-        be.moe(0, x, ids, w, mem, {}, sync=True)
+    # no expert of this row in `rows` (a staging group that holds none of them): no contribution
+    none = be.moe(0, x, ids, w, mem, {}, sync=True)
+    assert not none.float().abs().any()
     assert be.check_error() == 0

@@ -84,3 +84,46 @@ def test_batch_lfm2_verify_rows():
     # a speculative-verify batch (1 + 4 rows) on the LFM2-shaped layer: 64 experts, top-4, I 1536, no shared expert
     from yanah_b200.synthetic import lfm2_stack
     _check_layer(lfm2_stack(n_layers=40), 3, batch=5)
+
+
+def test_peer_wait_gives_up_with_an_error_and_the_gpu_stays_usable():
+    """Rank 0 of a two-rank layer whose peer never raises its flags (the peer
+    buffer is one of this process's own, which no kernel ever flags): the
+    layer's waits give up after their limit (2 s), the rank's error word holds
+    YN_ERR_PEER_TIMEOUT, the call returns, and a normal one-rank layer on the
+    same GPU afterwards still matches the oracle."""
+    import ctypes as C
+    import time
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    cfg = qwen3_next_stack(n_layers=48)
+    B = 16
+    one = ExpertParallelStack(cfg, batch=B, layers=[4])  # every expert local, slot = expert id
+    lib, D = _lib.lib(), C.byref(one.dims)
+    cfg2 = _lib.EpConfig(0, 2, B // 2, 0, cfg.n_experts // 2, 1)
+    sym_b, loc_b = int(lib.yn_ep_sym_bytes(D, C.byref(cfg2))), int(lib.yn_ep_local_bytes(D, C.byref(cfg2)))
+    sym = torch.zeros(sym_b, dtype=torch.uint8, device="cuda")
+    silent_peer = torch.zeros(sym_b, dtype=torch.uint8, device="cuda")
+    local = torch.zeros(loc_b, dtype=torch.uint8, device="cuda")
+    _lib.check(lib.yn_ep_init(sym.data_ptr(), local.data_ptr(), D, C.byref(cfg2), stream_ptr()))
+    peers = (C.c_void_p * 2)(sym.data_ptr(), silent_peer.data_ptr())
+    h = bf16_dev(hidden_rows(cfg, B // 2, stream=5))
+    out = torch.empty_like(h)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    _lib.check(lib.yn_ep_layer(D, C.byref(one.structs[0]), 0, C.byref(cfg2), h.data_ptr(), out.data_ptr(), peers,
+                               local.data_ptr(), stream_ptr()))
+    code = C.c_int32(0)
+    _lib.check(lib.yn_ep_error(local.data_ptr(), D, C.byref(cfg2), stream_ptr(), C.byref(code)))
+    waited = time.time() - t0
+    assert code.value == 6, code.value          # YN_ERR_PEER_TIMEOUT
+    assert 1.5 < waited < 30.0, waited
+    # the context is intact: the one-rank layer is still right
+    hb = hidden_rows(cfg, B, stream=6)
+    got = bf16_np(one.step(bf16_dev(hb)))
+    torch.cuda.synchronize()
+    assert one.check_error() == 0
+    ref = cpu.OracleStack(cfg, threads=8).layer(4, hb[[0, 9]])["out"]
+    assert rel_l2(got[[0, 9]], ref) < REL_L2_TOL
+    one.close()
