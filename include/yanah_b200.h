@@ -306,6 +306,9 @@ int yn_ipc_close(void* dev_ptr);
 /* Copy between any host/device addresses (cudaMemcpyDefault), then wait for
  * `stream`: readback for callers that hold raw device pointers. */
 int yn_memcpy(void* dst, const void* src, size_t bytes, void* stream);
+/* The same copy, ordered on `stream` and not waited for (pinned host memory
+ * for an asynchronous host<->device transfer). */
+int yn_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);
 
 /* -------------------------------------------- prefill: tensor-core GEMM */
 

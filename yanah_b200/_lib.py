@@ -117,6 +117,7 @@ _SIGS = {
     "yn_ipc_import": (C.c_int, [_P, C.POINTER(C.c_void_p)]),
     "yn_ipc_close": (C.c_int, [_P]),
     "yn_memcpy": (C.c_int, [_P, _P, C.c_size_t, _P]),
+    "yn_memcpy_async": (C.c_int, [_P, _P, C.c_size_t, _P]),
     "yn_rows_route_bytes": (C.c_size_t, [C.POINTER(Dims), _I]),
     "yn_rows_route": (C.c_int, [C.POINTER(Dims), C.POINTER(Layer), _P, _I, _P, _P, _P, _P, C.c_size_t, _P]),
     "yn_route_error": (C.c_int, [_P, C.POINTER(Dims), _P, C.POINTER(C.c_int32)]),

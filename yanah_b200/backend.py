@@ -108,11 +108,25 @@ class CudaMoEBackend:
         self.layers = [DeviceLayer(cfg, l, dense_layer(cfg, l), self._dummy, 0, None, self.device)
                        for l in range(cfg.n_layers)]
         self.ws = Workspace(self.dims, self.device, self.stream)
-        self._lut = torch.zeros(cfg.n_experts, dtype=torch.int32, device=self.device)
-        # expert -> slot tables go up through a ring of pinned buffers (no host sync)
-        self._lut_host = [torch.empty(cfg.n_experts, dtype=torch.int32, pin_memory=True) for _ in range(8)]
-        self._lut_ev: List[Optional[torch.cuda.Event]] = [None] * len(self._lut_host)
+        # constant per layer: the dense pointers and record layout of each layer's descriptor
+        self._structs = [L.struct() for L in self.layers]
+        self._records = [record_struct(cfg.record_spec(l)) for l in range(cfg.n_layers)]
+        self._tg: Dict[int, tuple] = {}
+        # expert -> slot tables go up through a ring of pinned host rows into a ring of device rows,
+        # one row per kernel launch that reads a table; a row is rewritten only after the event
+        # recorded behind its last copy has completed (no host sync on the common path)
+        n_lut = 8
+        E = cfg.n_experts
+        self._lut_host = torch.zeros((n_lut, E), dtype=torch.int32, pin_memory=True)
+        self._lut_np = self._lut_host.numpy()
+        self._lut_dev = torch.zeros((n_lut, E), dtype=torch.int32, device=self.device)
+        self._lut_ev = [torch.cuda.Event() for _ in range(n_lut)]
+        self._lut_used = [False] * n_lut
         self._lut_i = 0
+        self._lut_last = None        # (memory, rows, ring row) of the last table written
+        # pinned landing rows for the routing readback (ids, then lookahead probabilities)
+        self._ids_host = torch.empty(_lib.YN_MAX_ROWS * cfg.top_k, dtype=torch.int32, pin_memory=True)
+        self._fp_host = torch.empty(max(lookahead, 1) * E, dtype=torch.float32, pin_memory=True)
         self._pre: Dict[int, dict] = {}
         self._unfenced: Optional[torch.cuda.Event] = None
         self._route_ws: Optional[torch.Tensor] = None     # yn_rows_route workspace (prompt passes)
@@ -127,28 +141,35 @@ class CudaMoEBackend:
         return [t for t in range(layer + 1, layer + 1 + self.lookahead) if t < self.cfg.n_layers]
 
     def _layer_struct(self, layer: int, memory: CudaExpertMemory, rows: Dict[int, int]) -> _lib.Layer:
-        """Layer descriptor whose routed experts live in `memory` at `rows`."""
-        i = self._lut_i
-        self._lut_i = (i + 1) % len(self._lut_host)
-        if self._lut_ev[i] is not None:
-            self._lut_ev[i].synchronize()        # the copy out of this buffer has run
-        lut = self._lut_host[i].numpy()
-        lut[:] = 0
-        if rows:
-            lut[np.fromiter(rows.keys(), dtype=np.int64)] = np.fromiter(rows.values(), dtype=np.int64)
-        with torch.cuda.stream(self.stream):
-            dev = torch.empty(self.cfg.n_experts, dtype=torch.int32, device=self.device)
-            dev.copy_(self._lut_host[i], non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record(self.stream)
-        self._lut_ev[i] = ev
-        self._lut = dev   # freed tensors are reused in stream order by the caching allocator
-        L = self.layers[layer].struct()
+        """Layer descriptor whose routed experts live in `memory` at `rows`.
+        A table equal to the previous one (moe_rest after a moe_ready that
+        had every expert) reuses that device row."""
+        last = self._lut_last
+        if last is not None and last[0] is memory and last[1] == rows:
+            i = last[2]
+        else:
+            i = self._lut_i
+            self._lut_i = (i + 1) % len(self._lut_ev)
+            if self._lut_used[i]:
+                self._lut_ev[i].synchronize()        # the copy out of this row has run
+            lut = self._lut_np[i]
+            lut[:] = 0
+            if rows:
+                n = len(rows)
+                lut[np.fromiter(rows.keys(), dtype=np.int64, count=n)] = np.fromiter(rows.values(), dtype=np.int64,
+                                                                                     count=n)
+            _lib.check(_lib.lib().yn_memcpy_async(self._lut_dev[i].data_ptr(), self._lut_host[i].data_ptr(),
+                                                  lut.nbytes, self._st()))
+            self._lut_ev[i].record(self.stream)
+            self._lut_used[i] = True
+            self._lut_last = (memory, dict(rows), i)
+        dev = self._lut_dev[i]
+        L = _lib.Layer.from_buffer_copy(self._structs[layer])
         L.expert_base = memory.arena.base
         L.slot_stride = memory.arena.slot_bytes
         L.n_slots = memory.n
-        L.expert_slot = self._lut.data_ptr()
-        L.record = record_struct(self.cfg.record_spec(layer))
+        L.expert_slot = dev.data_ptr()
+        L.record = self._records[layer]
         return L
 
     def layout(self) -> ExpertLayout:
@@ -166,9 +187,11 @@ class CudaMoEBackend:
         T = h1.shape[0]
         if T > _lib.YN_MAX_ROWS:
             return self._pre_rows(layer, h1)
-        targets = self._targets(layer)
-        tg = (_lib.Layer * max(len(targets), 1))(*[self.layers[t].struct() for t in targets]) if targets else None
-        _lib.check(_lib.lib().yn_post_attention(C.byref(self.dims), C.byref(self.layers[layer].struct()),
+        if layer not in self._tg:
+            t = self._targets(layer)
+            self._tg[layer] = (t, (_lib.Layer * len(t))(*[self._structs[j] for j in t]) if t else None)
+        targets, tg = self._tg[layer]
+        _lib.check(_lib.lib().yn_post_attention(C.byref(self.dims), C.byref(self._structs[layer]),
                                                 h1.data_ptr(), T, tg, len(targets), self.ws.ptr, self._st()))
         x = self.ws.tensor("x", (T, self.cfg.hidden), torch.bfloat16)
         logits = self.ws.tensor("logits", (T, self.cfg.n_experts), torch.float32)
@@ -202,36 +225,41 @@ class CudaMoEBackend:
             x = torch.empty((T, H), dtype=torch.bfloat16, device=self.device)
             ids = torch.empty((T, K), dtype=torch.int32, device=self.device)
             w = torch.empty((T, K), dtype=torch.float32, device=self.device)
-        _lib.check(lib.yn_rows_route(C.byref(self.dims), C.byref(self.layers[layer].struct()), h1.data_ptr(), T,
+        _lib.check(lib.yn_rows_route(C.byref(self.dims), C.byref(self._structs[layer]), h1.data_ptr(), T,
                                      x.data_ptr(), ids.data_ptr(), w.data_ptr(), self._route_ws.data_ptr(),
                                      self._route_ws.numel(), self._st()))
         self._pre = {"layer": layer, "T": T, "targets": [], "rows": (ids, w)}
         return h1, x, None
 
-    def _ids_w(self):
+    def _ids_w(self, fprobs: bool = False):
         T, K = self._pre["T"], self.cfg.top_k
         if "rows" in self._pre:
             ids, w = self._pre["rows"]
             with torch.cuda.stream(self.stream):
                 ids_np = ids.cpu().numpy().astype(np.int64)      # the routing sync
-            return ids_np, w
+            return ids_np, w, None
+        lib, st = _lib.lib(), self._st()
         ids = self.ws.tensor("ids", (T, K), torch.int32)
-        with torch.cuda.stream(self.stream):
-            ids_np = ids.cpu().numpy().astype(np.int64)          # the routing sync
-        return ids_np, self.ws.tensor("weights", (T, K), torch.float32)
+        _lib.check(lib.yn_memcpy_async(self._ids_host.data_ptr(), ids.data_ptr(), T * K * 4, st))
+        n_fp = len(self._pre["targets"]) if fprobs else 0
+        if n_fp:
+            fp = self.ws.tensor("fprobs", (n_fp, self.cfg.n_experts), torch.float32)
+            _lib.check(lib.yn_memcpy_async(self._fp_host.data_ptr(), fp.data_ptr(), fp.numel() * 4, st))
+        self.stream.synchronize()                                 # the routing sync
+        ids_np = self._ids_host.numpy()[:T * K].reshape(T, K).astype(np.int64)
+        fp_np = self._fp_host.numpy()[:n_fp * self.cfg.n_experts].reshape(n_fp, -1) if n_fp else None
+        return ids_np, self.ws.tensor("weights", (T, K), torch.float32), fp_np
 
     def route(self, logits):
         """Routing of the last `pre_moe` (computed there on the device)."""
-        return self._ids_w()
+        ids, w, _ = self._ids_w()
+        return ids, w
 
     def route_and_forecast(self, logits, h_res, targets: Sequence[int]):
-        ids, w = self._ids_w()
         have = self._pre["targets"]
-        if not have:
+        ids, w, fp_np = self._ids_w(fprobs=True)
+        if fp_np is None:
             return ids, w, {}
-        fp = self.ws.tensor("fprobs", (max(len(have), 1), self.cfg.n_experts), torch.float32)
-        with torch.cuda.stream(self.stream):
-            fp_np = fp.cpu().numpy()
         return ids, w, {t: fp_np[have.index(t)].copy() for t in targets if t in have}
 
     # ---------------------------------------------------------------- experts
@@ -357,7 +385,7 @@ class CudaMoEBackend:
     def _shared_layer(self, layer: int) -> _lib.Layer:
         """The shared expert's down matrix as a one-slot 'expert' of 8-bit
         records for the grouped down GEMM (pieces at their own addresses)."""
-        L = self.layers[layer].struct()
+        L = _lib.Layer.from_buffer_copy(self._structs[layer])
         m = self.layers[layer].shared[2]
         L.expert_base = m.w.data_ptr()
         L.slot_stride = 16

@@ -566,3 +566,10 @@ extern "C" int yn_memcpy(void* dst, const void* src, size_t bytes, void* stream)
   YN_CUDA_B(cudaStreamSynchronize(as_st(stream)));
   return YN_OK;
 }
+
+extern "C" int yn_memcpy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!bytes) return YN_OK;
+  if (!dst || !src) return host_fail(YN_E_INVALID, "null argument");
+  YN_CUDA_B(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, as_st(stream)));
+  return YN_OK;
+}

@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass
-from typing import List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 import torch
@@ -168,6 +168,7 @@ class Workspace:
         _lib.check(lib.yn_workspace_init(self.buf.data_ptr(), self.nbytes, C.byref(dims), stream_ptr(stream)))
         self.view = _lib.WsView()
         _lib.check(lib.yn_workspace_view(self.buf.data_ptr(), C.byref(dims), C.byref(self.view)))
+        self._views: Dict[tuple, torch.Tensor] = {}
 
     @property
     def ptr(self) -> int:
@@ -175,11 +176,14 @@ class Workspace:
 
     def tensor(self, name: str, shape, dtype) -> torch.Tensor:
         """A torch view of a named workspace region (see _lib.WsView)."""
-        addr = getattr(self.view, name)
-        off = addr - self.ptr
-        elem = torch.empty((), dtype=dtype).element_size()
-        n = int(np.prod(shape))
-        return self.buf[off:off + n * elem].view(dtype).view(*shape)
+        key = (name, tuple(shape), dtype)
+        t = self._views.get(key)
+        if t is None:
+            off = getattr(self.view, name) - self.ptr
+            elem = torch.empty((), dtype=dtype).element_size()
+            n = int(np.prod(shape))
+            t = self._views[key] = self.buf[off:off + n * elem].view(dtype).view(*shape)
+        return t
 
     def check_error(self, stream=None) -> int:
         code = C.c_int32(0)

@@ -273,8 +273,9 @@ class StreamingDecoder:
             h_next = h_res + be.moe_finalize(l, routed)
         if ev_ready is not None:
             self.stats._pending.append(("stall", ev_ready, ev_demand))
-        self.ev_compute = torch.cuda.Event()
-        self.ev_compute.record(self.compute)
+        if self.ev_compute is None:
+            self.ev_compute = torch.cuda.Event()
+        self.ev_compute.record(self.compute)     # copies queued from here on wait for this layer's kernels
         pol.release(out)
         self.stats.layers += 1
         return h_next
