@@ -260,6 +260,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_flow(const FlowArgs a)
     for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1 + 32);
     fence_mbar_init();
   }
+  if (tid < 8) reinterpret_cast<uint32_t*>(smem + DEC_ZERO_OFF)[tid] = 0u;
   load_layer(&lay[0], a.layers, 0);
   load_layer(&lay[1], a.layers, a.n_layers > 1 ? 1 : 0);
   __syncthreads();
