@@ -170,13 +170,13 @@ YN_DEV bool tc_wait(uint64_t* bar, uint32_t parity, int* err) {
 // Producer-side dequantisation of NW code words (8 codes each) of one 64-code
 // stage of a weight row, words i0 .. i0+NW-1 of the stage, into the swizzled
 // A tile (fp16 for MODE 0, bf16 for MODE 1). t: the tile row (swizzle phase).
-template <int MODE, int NW>
+// `codes`: the thread's first 16-byte piece of code words; piece v at codes + v * PS.
+template <int MODE, int NW, int PS>
 YN_DEV void tc_dequant_row(const uint8_t* codes, uint16_t sc_bits, uint16_t bi_bits, uint8_t* Arow, int t, int i0) {
-  const uint4* cw = reinterpret_cast<const uint4*>(codes);
   uint32_t words[NW];
 #pragma unroll
   for (int v = 0; v < NW / 4; ++v) {
-    const uint4 c = cw[v];
+    const uint4 c = *reinterpret_cast<const uint4*>(codes + v * PS);
     words[4 * v] = c.x;
     words[4 * v + 1] = c.y;
     words[4 * v + 2] = c.z;
@@ -229,14 +229,16 @@ YN_DEV void tc_dequant_row(const uint8_t* codes, uint16_t sc_bits, uint16_t bi_b
 // (two units of 16 codes, MmaFmt<BITS>::WORDS words each) into 4 chunks of
 // the swizzled A tile from chunk i0. w = s * q + b as one fp32 FMA of the
 // unpacked (mult * q) and s / mult (exact: a power of two), rounded to fp16
-// (MODE 0) or bf16 (MODE 1).
-template <int MODE, int BITS>
+// (MODE 0) or bf16 (MODE 1). The thread's code words come in pieces of at
+// most 16 bytes, piece v at codes + v * PS.
+template <int MODE, int BITS, int PS>
 YN_DEV void tc_dequant_gen(const uint8_t* codes, uint16_t sc_bits, uint16_t bi_bits, uint8_t* Arow, int t, int i0) {
   using F = MmaFmt<BITS>;
+  constexpr int PB = 2 * F::WORDS * 4 < 16 ? 2 * F::WORDS * 4 : 16;   // piece bytes (the thread's bytes, at most 16)
   uint32_t words[2 * F::WORDS];
 #pragma unroll
   for (int v = 0; v < 2 * F::WORDS; v += 2) {
-    const uint2 c = *reinterpret_cast<const uint2*>(codes + 4 * v);
+    const uint2 c = *reinterpret_cast<const uint2*>(codes + (4 * v / PB) * PS + (4 * v) % PB);
     words[v] = c.x;
     words[v + 1] = c.y;
   }
@@ -325,6 +327,14 @@ struct TcFmt {
   static constexpr int CR = BITS == 8 ? 4 : TC_CR;
   static constexpr int PC = CR - 2;
   static constexpr int SLOT = TC_M * ROWB;
+  // A slot holds each producer thread's TB bytes as pieces of min(TB, 16) bytes laid out
+  // [part h][piece][tile row t]: the 32 threads of a warp (consecutive rows, one part) touch
+  // consecutive pieces, so their copies and reads are free of bank conflicts.
+  static constexpr int PB = TB < 16 ? TB : 16;   // piece bytes
+  static constexpr int PS = TC_M * PB;            // bytes between a thread's pieces
+  YN_DEV static uint8_t* at(uint8_t* ring, int slot, int t, int h) {
+    return ring + slot * SLOT + h * (TC_M * TB) + t * PB;
+  }
 };
 constexpr int TC_EW = TC_PW;                 // first epilogue warp (a multiple of 4: warp % 4 = TMEM lane quadrant)
 constexpr int TC_MW = TC_PW + TC_EPW;        // the MMA warp
@@ -412,13 +422,13 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
     // ring (TC_CR slots, read back only by this thread); one group per stage
     auto issue_codes = [&](const RowSrc& r, int ring, int kc) {
       if (r.good) {
-        uint8_t* cd = Cbuf + (ring % FT::CR) * FT::SLOT + t * FT::ROWB + h * FT::TB;
+        uint8_t* cd = FT::at(Cbuf, ring % FT::CR, t, h);
         const uint8_t* sw = r.w + FT::ROWB * kc + h * FT::TB;
         if (FT::TB == 8) {
           tc_cpa8(cd, sw);
         } else {
 #pragma unroll
-          for (int v = 0; v < FT::TB / 16; ++v) tc_cpa16(cd + 16 * v, sw + 16 * v);
+          for (int v = 0; v < FT::TB / 16; ++v) tc_cpa16(cd + FT::PS * v, sw + 16 * v);
         }
       }
       tc_cpa_commit();
@@ -466,11 +476,11 @@ __global__ void __launch_bounds__(TCW_THREADS, 1) k_tc_experts(const TcArgs a, c
             const int gi = jj * GPS + (GPS == 2 ? h : 0);   // this thread's group inside the 8-group block
             const uint32_t sw = gi < 2 ? s8.x : gi < 4 ? s8.y : gi < 6 ? s8.z : s8.w;
             const uint32_t bw = gi < 2 ? b8.x : gi < 4 ? b8.y : gi < 6 ? b8.z : b8.w;
-            const uint8_t* cd = Cbuf + ((g + kc) % FT::CR) * FT::SLOT + t * FT::ROWB + h * FT::TB;
+            const uint8_t* cd = FT::at(Cbuf, (g + kc) % FT::CR, t, h);
             uint8_t* arow = Abuf + s * TC_A_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
             const uint16_t sb16 = (uint16_t)(sw >> (16 * (gi & 1))), bb16 = (uint16_t)(bw >> (16 * (gi & 1)));
-            if (BITS == 4) tc_dequant_row<MODE, TC_NW>(cd, sb16, bb16, arow, t, h * TC_NW);
-            else tc_dequant_gen<MODE, BITS>(cd, sb16, bb16, arow, t, 4 * h);
+            if (BITS == 4) tc_dequant_row<MODE, TC_NW, FT::PS>(cd, sb16, bb16, arow, t, h * TC_NW);
+            else tc_dequant_gen<MODE, BITS, FT::PS>(cd, sb16, bb16, arow, t, 4 * h);
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           mbar_arrive1(&full[s]);
