@@ -843,13 +843,14 @@ def run_verify(args, rank: int, world: int):
     stack.close()
 
 
-def hooks_sample(cfg, dev, inputs, n_tok: int) -> dict:
+def hooks_sample(cfg, dev, inputs, n_tok: int, layers=None, warm: int = 1) -> dict:
     """The same decode through the per-layer hook sequence the reference's
     orchestrator calls on a backend (orchestrator.py:226-300, every routed
     expert a pool hit): pre_moe -> route (the routed ids come to the host: the
     reference's routing sync) -> moe_ready -> moe_rest -> h_res +
-    moe_finalize, on CudaMoEBackend with every expert of every layer resident
-    in one CudaExpertMemory (slot = layer * E + expert)."""
+    moe_finalize, on CudaMoEBackend with every expert of every layer in
+    `layers` (default: all) resident in one CudaExpertMemory (slot = i * E +
+    expert for the i-th of those layers)."""
     import numpy as np
     import torch
 
@@ -857,35 +858,74 @@ def hooks_sample(cfg, dev, inputs, n_tok: int) -> dict:
     from yanah_b200.device import fill_synthetic_experts
 
     E = cfg.n_experts
+    layer_ids = list(range(cfg.n_layers)) if layers is None else list(layers)
     be = CudaMoEBackend(cfg, dev, lookahead=0)
-    mem = be.make_expert_memory(cfg.n_layers * E)
-    for l in range(cfg.n_layers):
-        fill_synthetic_experts(mem.arena, cfg, l, first_slot=l * E)
+    mem = be.make_expert_memory(len(layer_ids) * E)
+    for i, l in enumerate(layer_ids):
+        fill_synthetic_experts(mem.arena, cfg, l, first_slot=i * E)
     torch.cuda.synchronize(dev)
 
     def token(h):
-        for l in range(cfg.n_layers):
+        for i, l in enumerate(layer_ids):
             h_res, x, logits = be.pre_moe(l, h)
             ids, w = be.route(logits)
-            rows = {int(e): l * E + int(e) for e in np.unique(ids)}
+            rows = {int(e): i * E + int(e) for e in np.unique(ids)}
             handle = be.moe_ready(l, x, ids, mem, rows)
             out = be.moe_rest(l, x, ids, w, mem, rows, handle)
             h = h_res + be.moe_finalize(l, out)
         return h
 
-    token(inputs[0:1])
+    for t in range(warm):
+        token(inputs[t % inputs.shape[0]:t % inputs.shape[0] + 1])
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     for t in range(n_tok):
-        token(inputs[t:t + 1])
+        token(inputs[t % inputs.shape[0]:t % inputs.shape[0] + 1])
     torch.cuda.synchronize(dev)
     secs = time.perf_counter() - t0
     if be.check_error():
         raise RuntimeError("device error in the hook-sequence decode")
     del mem
-    return {"value": round(n_tok / secs, 2), "unit": "tok/s", "tokens": n_tok,
+    return {"value": round(n_tok / secs, 2), "unit": "tok/s", "tokens": n_tok, "layers": len(layer_ids),
+            "us_per_layer": round(secs / n_tok / len(layer_ids) * 1e6, 2),
             "path": "CudaMoEBackend hooks per layer: pre_moe, route (host routing sync), moe_ready, moe_rest, "
                     "moe_finalize; every expert resident"}
+
+
+HOOKS_METRIC = "decode tok/s through the per-layer backend hooks, bs1 (Qwen3-Next-80B-A3B-shaped)"
+
+
+def run_hooks(args, rank: int, world: int):
+    """bs1 decode through the per-layer hook sequence (pre_moe, route,
+    moe_ready, moe_rest, moe_finalize on CudaMoEBackend; the per-layer
+    kernels k_post_attention, k_expert_up, k_expert_down) over the stack or a
+    sub-stack (--layers): one step = --hook-tokens tokens, host loop and
+    routing syncs included, wall clock around the steps."""
+    import torch
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.synthetic import hidden_stream_id, qwen3_next_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = qwen3_next_stack(seed=0)
+    layer_ids = list(range(args.first_layer, args.first_layer + (args.layers or cfg.n_layers)))
+    N = args.hook_tokens
+    inputs = torch.empty((N, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(inputs.data_ptr(), N * cfg.hidden, cfg.seed, hidden_stream_id(rank), 1.0, 0.0,
+                                        stream_ptr()))
+    r = hooks_sample(cfg, dev, inputs, N * args.steps, layers=layer_ids, warm=N * args.warmup)
+    secs = N * args.steps / r["value"]
+    line = {
+        "metric": HOOKS_METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": sub_label("qwen3_next_80b_a3b_moe_stack48_bs1_hooks", args, cfg.n_layers),
+                   "layers": len(layer_ids), "tokens_per_step": N},
+        "hooks": {"us_per_layer": r["us_per_layer"], "path": r["path"]},
+    }
+    print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------ our arm
@@ -1034,11 +1074,12 @@ def main():
     ap.add_argument("--no-hooks", action="store_true", help="skip the per-layer hook-sequence (e2e_hooks) sample")
     ap.add_argument("--layers", type=int, default=0, help="profile a sub-stack of this many layers (0: all 48)")
     ap.add_argument("--first-layer", type=int, default=0)
-    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill", "verify", "sweep"],
+    ap.add_argument("--workload", choices=["resident", "streaming", "ep", "prefill", "verify", "sweep", "hooks"],
                     default="resident",
                     help="resident: the 48-layer all-in-HBM decode (default); streaming: 20%% slot pool + host tier; "
                          "ep: batch of 64 rows, experts sharded over the GPUs; prefill: tensor-core prefill; "
-                         "verify: 1+4-row speculative-verify batches; sweep: prefill through the prefill sweep")
+                         "verify: 1+4-row speculative-verify batches; sweep: prefill through the prefill sweep; "
+                         "hooks: bs1 decode through the per-layer backend hooks")
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
     ap.add_argument("--decode-kernel", choices=["flow", "barrier"], default="flow",
                     help="resident workload: the data-flow persistent decode (default) or the grid-barrier form")
@@ -1046,6 +1087,7 @@ def main():
                     help="verify workload: tcgen05 grouped GEMM (default) or the union-of-experts batch path")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
+    ap.add_argument("--hook-tokens", type=int, default=16, help="tokens per step of the hooks workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1074,6 +1116,9 @@ def main():
         elif args.workload == "sweep":
             if rank == 0:
                 run_sweep(args, rank, world)
+        elif args.workload == "hooks":
+            if rank == 0:
+                run_hooks(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

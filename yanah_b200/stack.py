@@ -28,8 +28,8 @@ DECODE_STAMPS = 16
 DECODE_PHASES = ["loads", "wait_p1_tile", "norm_frags", "p1_rows", "bar1", "route", "issue_c", "p2_tiles",
                  "swiglu_issue_d", "bar2", "p3_frags", "wait_d", "p3_tiles", "combine", "end"]
 # Data-flow form (yn_stack_flow_decode): the same 16 stamps per layer; phases 12-14 are empty.
-FLOW_PHASES = ["h_in", "wait_p1_tile", "norm", "p1_rows_frags", "route", "issue", "gate_up_act_out", "act_in",
-               "frags_down", "y_out", "y_in", "combine_h_out", "-", "-", "-"]
+FLOW_PHASES = ["h_in", "wait_p1_tile", "norm", "p1_rows_frags", "route", "issue", "gate_up_act_out",
+               "act_in_frags_down", "y_out_next_issue", "y_in", "combine_h_out", "-", "-", "-", "-"]
 
 
 def flow_phase_report(timing: np.ndarray) -> dict:
