@@ -89,6 +89,16 @@ YN_DEV float warp_max(float v) {
   for (int m = 16; m > 0; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
   return v;
 }
+// Integer key of a finite float whose signed order is the float order (-0 below +0), and back.
+YN_DEV int f32_order_key(float f) {
+  const int b = __float_as_int(f);
+  return b ^ ((b >> 31) & 0x7FFFFFFF);
+}
+YN_DEV float f32_from_order_key(int k) { return __int_as_float(k ^ ((k >> 31) & 0x7FFFFFFF)); }
+// Warp maximum of finite floats as one redux instruction (the value warp_max returns; of +0 and -0, +0).
+YN_DEV float warp_max_redux(float v) {
+  return f32_from_order_key(__reduce_max_sync(0xffffffffu, f32_order_key(v)));
+}
 
 // ----------------------------------------------------------- time & flags
 YN_DEV uint64_t globaltimer_ns() {

@@ -286,7 +286,9 @@ YN_DEV float rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uin
   }
   __syncthreads();
   const float tot = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
-  const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)DEC_H), eps));
+  // DEC_H is a power of two, so tot * (1 / H) is tot / H exactly
+  static_assert((DEC_H & (DEC_H - 1)) == 0, "hidden size: a power of two");
+  const float r = __frsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)DEC_H), eps));
   float mx = 0.0f;
 #pragma unroll
   for (int i = tid; i < DEC_H; i += DEC_THREADS) {
@@ -294,10 +296,11 @@ YN_DEV float rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uin
     out[i] = o;
     mx = fmaxf(mx, fabsf(bf16_to_f32(o)));
   }
-  mx = warp_max(mx);
+  // mx >= 0: the unsigned order of the bits is the float order
+  mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
   if ((tid & 31) == 0) red[8 + (tid >> 5)] = mx;
   __syncthreads();
-  return warp_max(red[8 + (tid & 15)]);
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(red[8 + (tid & 15)])));
 }
 
 // P1 compute: router rows, shared pairs, shared_expert_gate (canonical fp32
@@ -353,11 +356,10 @@ YN_DEV bool route_block(const u64* f_logits, uint32_t ep, int* err, int K, int n
   bool fail = false;
   const float x = __uint_as_float(wait_flag(f_logits + tid, ep, err, fail));
   if (__syncthreads_or(fail)) return false;
-  float m = warp_max(x);
+  float m = warp_max_redux(x);
   if (lane == 0) red[warp] = m;
   __syncthreads();
-  m = red[lane & 15];
-  m = warp_max(m);
+  m = warp_max_redux(red[lane & 15]);
   v[tid] = yn_expf(__fsub_rn(x, m));
   __syncthreads();
   if (warp == 0) {
