@@ -596,16 +596,16 @@ YN_DEV const uint8_t* expert_record(const DecLayer& L, int e) {
 }
 
 // Copies of this CTA's C tile, issued by one warp tile by tile; tile t
-// completes on its own mbarrier (count 1 + 32), so P2 starts on tile 0 while
-// later tiles are in flight. Per tile: the gate and up codes of its 8 rows
-// (two contiguous 8-row pieces) go as two bulk copies (lane 0 posts their
-// byte count); the four small scale/bias pieces go as 16-byte cp.async over
-// the 32 lanes, which then arrive on the barrier when their copies land. A
-// tile (8 units) never crosses an expert boundary.
+// completes on its own mbarrier (count 1: lane 0 posts the tile's bytes), so
+// P2 starts on tile 0 while later tiles are in flight. Per tile, six bulk
+// copies from six lanes: the gate and up codes of its 8 rows and the four
+// 8-row scale/bias pieces (each a contiguous run of whole 16-byte units).
+// A tile (8 units) never crosses an expert boundary.
 template <int BITS, int GS, class Args>
 YN_DEV void copy_c(const Args& a, const DecLayer& L, const int32_t* ids, const CSeg& sg, int ntile, uint8_t* C,
                    uint64_t* barT, int t0, int tstep) {
-  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2, CS = SBH / 16;
+  constexpr int RB = DEC_H * BITS / 8, SBH = DEC_H / GS * 2;
+  static_assert(SBH % 16 == 0 && RB % 16 == 0, "bulk copies move whole 16-byte units");
   const int lane = threadIdx.x & 31;
   if (!ntile) return;
   const uint8_t* rec0 = expert_record(L, ids[sg.j[0]]);
@@ -616,17 +616,16 @@ YN_DEV void copy_c(const Args& a, const DecLayer& L, const int32_t* ids, const C
     const int row = 8 * t, seg = row >= sg.rows[0] ? 1 : 0;
     const int n = sg.n0[seg] + (seg ? row - sg.rows[0] : row);
     const uint8_t* rec = seg ? rec1 : rec0;
-    if (lane == 0) mbar_arrive_expect_tx(&barT[t], 16u * RB);
+    if (lane == 0) mbar_arrive_expect_tx(&barT[t], 16u * RB + 32u * SBH);
     __syncwarp();
-    if (lane < 2)
+    if (lane < 2) {   // gate and up codes: 8 rows each
       bulk_g2s(C + (size_t)lane * a.c_rows * a.c_rb + (size_t)row * RB, rec + L.rg.off[3 * lane] + (size_t)n * RB,
                8u * RB, &barT[t]);
-    for (int c = lane; c < 4 * 8 * CS; c += 32) {   // gate s, gate b, up s, up b: 8 rows x SBH bytes each
-      const int q = c / (8 * CS), o = (c % (8 * CS)) * 16;
-      cp16(C + sbase + (size_t)q * a.c_rows * a.c_sb + (size_t)row * SBH + o,
-           rec + L.rg.off[3 * (q >> 1) + 1 + (q & 1)] + (size_t)n * SBH + o);
+    } else if (lane < 6) {   // gate s, gate b, up s, up b: 8 rows x SBH bytes each
+      const int q = lane - 2;
+      bulk_g2s(C + sbase + (size_t)q * a.c_rows * a.c_sb + (size_t)row * SBH,
+               rec + L.rg.off[3 * (q >> 1) + 1 + (q & 1)] + (size_t)n * SBH, 8u * SBH, &barT[t]);
     }
-    cp_arrive(&barT[t]);
   }
 }
 
@@ -920,7 +919,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
 
   if (tid == 0) {
     mbar_init(barA, DEC_THREADS);
-    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1 + 32);  // one issuing warp per tile
+    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1);  // the issuing lane's expect_tx
     mbar_init(barD, DEC_THREADS);
     fence_mbar_init();
   }

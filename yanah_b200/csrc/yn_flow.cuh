@@ -200,7 +200,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_flow(const FlowArgs a)
   uint64_t* barD = barA + 1;                                  // routed down rows
   uint64_t* barS = barA + 2;                                  // shared down rows
   float* red = reinterpret_cast<float*>(smem + 32);           // 24 floats
-  int* eflag = reinterpret_cast<int*>(smem + 128);
   int* ids_ok_s = reinterpret_cast<int*>(smem + 132);
   uint64_t* barT = reinterpret_cast<uint64_t*>(smem + 136);  // DEC_MAX_OCT gate/up tile barriers
   uint16_t* hs = reinterpret_cast<uint16_t*>(smem + a.off_hs);
@@ -257,7 +256,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_flow(const FlowArgs a)
     mbar_init(barA, DEC_THREADS);
     mbar_init(barD, 1);
     mbar_init(barS, 1);
-    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1 + 32);
+    for (int t = 0; t < DEC_MAX_OCT; ++t) mbar_init(&barT[t], 1);
     fence_mbar_init();
   }
   if (tid < 8) reinterpret_cast<uint32_t*>(smem + DEC_ZERO_OFF)[tid] = 0u;
