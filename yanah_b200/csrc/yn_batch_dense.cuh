@@ -90,7 +90,9 @@ YN_DEV void dense_rows2(const uint8_t* ca, const uint16_t* sa, const uint16_t* b
   float acca[BD_TOK], accb[BD_TOK];
 #pragma unroll
   for (int t = 0; t < BD_TOK; ++t) acca[t] = accb[t] = 0.0f;
-#pragma unroll
+  // the chunk loop stays rolled: a batch launch is short and starts with a cold instruction cache, and the
+  // unrolled body (tokens x rows x 16 FMAs per chunk) is large
+#pragma unroll 1
   for (int c = 0; c < CPL; ++c) {
     const int ci = l + 32 * c;
     const uint4 wa = *reinterpret_cast<const uint4*>(ca + 16 * ci);
