@@ -753,6 +753,113 @@ def run_verify_tc(args, rank: int, world: int):
     del g
 
 
+def run_verify_flow(args, rank: int, world: int):
+    """Speculative verify: 1 + 4 draft rows per step through the 40
+    LFM2-shaped layers in ONE persistent launch per step
+    (yn_rows_flow_decode): per layer each distinct routed expert of the 5 rows
+    is read from HBM once by a group of CTAs, with the rows as the GEMV's MMA
+    columns, and every exchange between CTAs is a flagged word. HBM-bound:
+    the roofline counts each distinct expert record a layer routes to once,
+    plus the router and norm."""
+    import numpy as np
+    import torch
+
+    from yanah_b200 import _lib
+    from yanah_b200.device import stream_ptr
+    from yanah_b200.stack import ResidentStack
+    from yanah_b200.synthetic import hidden_stream_id, lfm2_stack
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = lfm2_stack(seed=0)
+    B = 5
+    layer_ids = list(range(args.first_layer, args.first_layer + (args.layers or cfg.n_layers)))
+    stack = ResidentStack(cfg, device=dev, layers=layer_ids)
+    H, K, L = cfg.hidden, cfg.top_k, len(layer_ids)
+    rows = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().yn_synth_bf16(rows.data_ptr(), B * H, cfg.seed, hidden_stream_id(700), 1.0, 0.0,
+                                        stream_ptr()))
+    out = torch.empty_like(rows)
+    # untimed traced pass: distinct experts per layer (the algorithmic bytes)
+    trace = torch.full((L, B, K), -1, dtype=torch.int32, device=dev)
+    stack.rows_decode(rows, out, trace=trace)
+    torch.cuda.synchronize(dev)
+    if stack.rows_error():
+        raise RuntimeError("device error in the first verify step")
+    tr = trace.cpu().numpy()
+    n_distinct = [len(np.unique(tr[l])) for l in range(L)]
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            stack.rows_decode(rows, out, stream=s)
+    s.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid(dev.index)) as clk:
+        with torch.cuda.stream(s):
+            start.record(s)
+            for _ in range(args.steps):
+                stack.rows_decode(rows, out, stream=s)
+            end.record(s)
+        s.synchronize()
+    ms = start.elapsed_time(end)
+    if stack.rows_error():
+        raise RuntimeError("device error during the timed verify steps")
+    value = B * args.steps / (ms / 1e3)
+    h_in = torch.empty((B, H), dtype=torch.bfloat16, pin_memory=True)
+    h_in.copy_(rows)
+    h_out = torch.empty_like(h_in, pin_memory=True)
+    with torch.cuda.stream(s):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            rows.copy_(h_in, non_blocking=True)
+            stack.rows_decode(rows, out, stream=s)
+            h_out.copy_(out, non_blocking=True)
+        e1.record(s)
+    s.synchronize()
+    e2e = B * args.steps / (e0.elapsed_time(e1) / 1e3)
+    timing = None
+    if args.phases:
+        G = torch.cuda.get_device_properties(dev).multi_processor_count
+        tm = torch.zeros((L, 16, G), dtype=torch.int64, device=dev)
+        with torch.cuda.stream(s):
+            stack.rows_decode(rows, out, timing=tm, stream=s)
+        s.synchronize()
+        t = tm.cpu().numpy().astype(np.float64)
+        names = ["h_in", "norm", "router_rows", "route_plan_issue", "gate_up_frags", "gate_up_tiles", "act_in",
+                 "down_frags", "down_tiles", "combine_h_out"]
+        d = np.diff(t[:, :11, :], axis=1) / 1e3          # (L, 10, G) us
+        timing = {"phases_mean_us": {n: round(float(d[:, i].mean()), 3) for i, n in enumerate(names)},
+                  "phases_max_us": {n: round(float(d[:, i].max(axis=1).mean()), 3) for i, n in enumerate(names)},
+                  "layer_us": round(float((t[-1, 10] - t[0, 0]).max() / 1e3 / L), 3)}
+    rec = [cfg.record_spec(l).record_bytes for l in layer_ids]
+    hbm_bytes = sum(n * r for n, r in zip(n_distinct, rec)) + L * cfg.dense_bytes_per_layer()
+    hbm, src = peaks()
+    step_s = ms / args.steps / 1e3
+    achieved = hbm_bytes / step_s / 1e9
+    line = {
+        "metric": VERIFY_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": sub_label("lfm2_24b_a2b_moe_stack40_verify_1p4", args, cfg.n_layers), "layers": L,
+                   "rows_per_step": B, "hidden": H, "experts": cfg.n_experts, "top_k": K, "moe_inter": cfg.moe_inter,
+                   "expert_bits": "4-bit g64",
+                   "path": "persistent multi-row data-flow decode (yn_rows_flow_decode), one launch per step",
+                   "l2": "no flush: a step reads the routed records of 40 layers (~1.7 GB > 126 MB L2)"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2, "d2h_bytes_per_step": B * H * 2},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "roofline": {"bound": "hbm", "kernel": "k_rows_flow", "achieved": round(achieved, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
+                     "bytes_per_step": hbm_bytes, "distinct_experts_per_layer_mean": round(float(np.mean(n_distinct)), 2),
+                     "traffic": None},
+    }
+    if timing:
+        line["phases"] = timing
+    print(json.dumps(line), flush=True)
+
+
 def run_verify(args, rank: int, world: int):
     """Speculative verify: 1 + 4 draft rows per step through the 40
     LFM2-shaped layers on the batch path (each routed expert record read
@@ -1083,8 +1190,11 @@ def main():
     ap.add_argument("--batch", type=int, default=64, help="rows per step of the ep workload")
     ap.add_argument("--decode-kernel", choices=["flow", "barrier"], default="flow",
                     help="resident workload: the data-flow persistent decode (default) or the grid-barrier form")
-    ap.add_argument("--verify-path", choices=["tc", "batch"], default="tc",
-                    help="verify workload: tcgen05 grouped GEMM (default) or the union-of-experts batch path")
+    ap.add_argument("--verify-path", choices=["flow", "tc", "batch"], default="flow",
+                    help="verify workload: the persistent multi-row decode (default), the tcgen05 grouped GEMM "
+                         "(the prefill sequence) or the union-of-experts batch path")
+    ap.add_argument("--phases", action="store_true",
+                    help="verify workload (flow path): also report per-phase times from one stamped launch")
     ap.add_argument("--stream-tokens", type=int, default=32, help="tokens per step of the streaming workload")
     ap.add_argument("--rho", type=float, default=0.0, help="AR(1) correlation of consecutive streaming inputs")
     ap.add_argument("--hook-tokens", type=int, default=16, help="tokens per step of the hooks workload")
@@ -1112,7 +1222,7 @@ def main():
                 run_prefill(args, rank, world)
         elif args.workload == "verify":
             if rank == 0:
-                (run_verify if args.verify_path == "batch" else run_verify_tc)(args, rank, world)
+                {"flow": run_verify_flow, "batch": run_verify, "tc": run_verify_tc}[args.verify_path](args, rank, world)
         elif args.workload == "sweep":
             if rank == 0:
                 run_sweep(args, rank, world)

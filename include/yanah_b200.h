@@ -226,6 +226,29 @@ int yn_stack_flow_decode(const yn_dims* dims, const void* table, const yn_layer*
 /* Read and clear the stack decode error word (synchronises the stream);
  * either form's scratch. */
 int yn_stack_error(void* scratch, const yn_dims* dims, void* stream, int32_t* code_out);
+/* A batch of n_rows <= 8 token rows through every layer in one persistent
+ * cooperative launch, in data-flow form: the forward of a speculative-verify
+ * pass (moe_prefetch/speculative.py:121-193 runs the 1 + depth rows of a
+ * draft through the model and compares; here its MoE part) and small decode
+ * batches, every expert resident. Per layer each routed expert of the
+ * batch (the union over its rows, ascending id) is read from HBM once by a
+ * group of CTAs, its rows being the columns of the GEMV
+ * (mlx_backend.py:411-436 moe over a batch's experts, :442-459 the expert
+ * MLP); routing of every row is bit-identical to yn_post_attention
+ * (mlx_backend.py:308-316). Compiled for hidden 2048, 64 experts, intermediate
+ * 1536, top_k <= 8, 4-bit g64 routed experts, 8-bit g64 router, no shared
+ * expert (the LFM2-24B-A2B shape); other shapes return YN_E_UNSUPPORTED.
+ * table: yn_stack_prepare. inputs / outputs: (n_rows, hidden) bf16.
+ * scratch: yn_rows_flow_scratch_bytes(dims, max_rows) for n_rows <= max_rows
+ * (error word first: yn_stack_error reads it). trace_ids / trace_weights:
+ * (n_layers, n_rows, k); trace_hidden: (n_layers, n_rows, hidden) each
+ * layer's input rows; timing: (n_layers, 16, n_SMs) global-timer stamps;
+ * each may be NULL. */
+size_t yn_rows_flow_scratch_bytes(const yn_dims* dims, int32_t max_rows);
+int yn_rows_flow_decode(const yn_dims* dims, const void* table, const yn_layer* layers, int32_t n_layers,
+                        const void* inputs, int32_t n_rows, void* outputs, void* scratch, size_t scratch_bytes,
+                        int32_t* trace_ids, void* trace_hidden, float* trace_weights, int64_t* timing,
+                        void* stream);
 
 /* ------------------------------------- batch decode, expert parallelism */
 

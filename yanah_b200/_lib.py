@@ -94,6 +94,9 @@ _SIGS = {
     "yn_stack_flow_decode": (C.c_int, [C.POINTER(Dims), _P, C.POINTER(Layer), _I, _P, _I, _P, _P, C.c_size_t, _P,
                                        _P, _P, _P, _P]),
     "yn_stack_error": (C.c_int, [_P, C.POINTER(Dims), _P, C.POINTER(C.c_int32)]),
+    "yn_rows_flow_scratch_bytes": (C.c_size_t, [C.POINTER(Dims), _I]),
+    "yn_rows_flow_decode": (C.c_int, [C.POINTER(Dims), _P, C.POINTER(Layer), _I, _P, _I, _P, _P, C.c_size_t, _P,
+                                      _P, _P, _P, _P]),
     "yn_slot_copy": (C.c_int, [_P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_void_p), _I, C.c_int64, _P]),
     "yn_record_event": (C.c_int, [_P, _P]),
     "yn_event_create": (C.c_int, [C.POINTER(C.c_void_p)]),

@@ -48,6 +48,9 @@
 #define YN_HOST_DEV __host__ __device__
 #endif
 
+// Translation units that use only the device building blocks define
+// YN_NO_BATCH_EP_KERNELS: the non-template kernels below (external linkage)
+// are then left to yn_batch.cu.
 namespace ynb {
 
 constexpr int BT_MAX_TOK = 64;                       // rows of one batch (all ranks)
@@ -359,6 +362,7 @@ struct CombineArgs {
 // rows (and CTA 0 the ids) into rank d's gather buffer; each CTA then raises
 // its own flag there, flag[rank][cta] (a release at system scope, after the
 // block barrier, so it covers every store of the CTA).
+#ifndef YN_NO_BATCH_EP_KERNELS
 __global__ void __launch_bounds__(BT_THREADS) k_ep_dispatch(const DispatchArgs a) {
   const int d = blockIdx.x, nb = gridDim.y;
   const EpStep& s = a.st;
@@ -383,6 +387,7 @@ __global__ void __launch_bounds__(BT_THREADS) k_ep_dispatch(const DispatchArgs a
   __syncthreads();  // the CTA's stores, then its flag (a release covers them)
   if (threadIdx.x == 0) st_release_sys_u64(a.peers.flag[d] + s.rank * BT_MAX_DISPATCH + blockIdx.y, ep_stamp(s));
 }
+#endif  // YN_NO_BATCH_EP_KERNELS
 
 // ------------------------------------------------------------ fragments
 // One row per block: stage the row in shared memory, power-of-two scale from
@@ -874,6 +879,7 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_down(const BatchDownArgs a
 // out = sum_j bf16(y_j * w_j) in column order (+ shared, + residual), as the
 // single-row combine; starts once the rank's counter shows every (pair,
 // row tile) unit of this layer.
+#ifndef YN_NO_BATCH_EP_KERNELS
 __global__ void __launch_bounds__(BT_THREADS) k_batch_combine(const CombineArgs a) {
   const unsigned long long target = ep_stamp(a.st) * a.per_layer;
   if (!wait_geq_block(a.cnt, target, a.st.err)) return;
@@ -891,9 +897,12 @@ __global__ void __launch_bounds__(BT_THREADS) k_batch_combine(const CombineArgs 
   if (a.mode == 2) o = bf16r(__fadd_rn(bf16_to_f32(a.h_res[(size_t)t * a.H + r]), o));
   a.out[(size_t)t * a.H + r] = f32_to_bf16(o);
 }
+#endif  // YN_NO_BATCH_EP_KERNELS
 
+#ifndef YN_NO_BATCH_EP_KERNELS
 __global__ void k_ep_step_end(unsigned long long* epoch) {
   if (threadIdx.x == 0 && blockIdx.x == 0) *epoch += 1ull;
 }
+#endif  // YN_NO_BATCH_EP_KERNELS
 
 }  // namespace ynb

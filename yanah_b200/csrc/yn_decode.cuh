@@ -285,10 +285,13 @@ YN_DEV float rmsnorm_smem(const uint16_t* h, const uint16_t* w_g, float eps, uin
     if ((tid & 31) == 0) red[tid >> 5] = ss;
   }
   __syncthreads();
-  const float tot = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+  // warp partials in warp order and r = 1 / sqrt(.) with two roundings, as the
+  // canonical RMSNorm defines them (a fused rsqrt rounds once and can differ
+  // in the last bit)
+  const float tot = __fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), red[2]), red[3]);
   // DEC_H is a power of two, so tot * (1 / H) is tot / H exactly
   static_assert((DEC_H & (DEC_H - 1)) == 0, "hidden size: a power of two");
-  const float r = __frsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)DEC_H), eps));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)DEC_H), eps)));
   float mx = 0.0f;
 #pragma unroll
   for (int i = tid; i < DEC_H; i += DEC_THREADS) {
@@ -816,7 +819,7 @@ YN_DEV void p3_frags(const DecodeArgs& a, uint16_t* stage, uint32_t* xf3, float*
 // one decoded), DEC_STAMPS per layer, at timing[(layer * DEC_STAMPS + slot) *
 // gridDim.x + blockIdx.x]; a block-wide sync before each stamp attributes the
 // time of the slowest warp of the CTA. Out of line: off the hot code path.
-__device__ __noinline__ void stamp_at(long long* timing, int layer, int slot) {
+static __device__ __noinline__ void stamp_at(long long* timing, int layer, int slot) {
   __syncthreads();
   if (threadIdx.x == 0)
     timing[((size_t)layer * DEC_STAMPS + slot) * gridDim.x + blockIdx.x] = (long long)globaltimer_ns();
@@ -877,6 +880,9 @@ YN_DEV void p2_swiglu(const DecodeArgs& a, const CSeg& sg, int ntile, const floa
   reinterpret_cast<uint32_t*>(a.act)[((size_t)sg.j[s] * DEC_I + n) / 2] = pk;
 }
 
+// Translation units that only need the building blocks above define
+// YN_NO_STACK_DECODE_KERNEL (the kernel has external linkage: one definition).
+#ifndef YN_NO_STACK_DECODE_KERNEL
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* barA = reinterpret_cast<uint64_t*>(smem);
@@ -1113,5 +1119,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_stack_decode(const DecodeArg
     if (grid_wait(a, gen * (unsigned)G, eflag)) { drain(); return; }
   }
 }
+#endif  // YN_NO_STACK_DECODE_KERNEL
 
 }  // namespace ynb

@@ -99,6 +99,7 @@ class ResidentStack:
         sb = max(int(lib.yn_stack_scratch_bytes(C.byref(self.dims))),
                  int(lib.yn_stack_flow_scratch_bytes(C.byref(self.dims))))
         self.scratch = torch.zeros(sb, dtype=torch.uint8, device=self.device)
+        self._rows_scratch: Optional[torch.Tensor] = None
         self.layer_array = arr
         torch.cuda.synchronize(self.device)
 
@@ -155,6 +156,39 @@ class ResidentStack:
                                        inputs.data_ptr(), inputs.shape[0], outputs.data_ptr(), self.scratch.data_ptr(),
                                        self.scratch.numel(), ptr(trace), ptr(trace_hidden), ptr(trace_weights),
                                        ptr(timing), stream_ptr(stream)))
+
+    ROWS_MAX = 8
+
+    def rows_decode(self, inputs: torch.Tensor, outputs: torch.Tensor, trace: Optional[torch.Tensor] = None,
+                    trace_hidden: Optional[torch.Tensor] = None, trace_weights: Optional[torch.Tensor] = None,
+                    timing: Optional[torch.Tensor] = None, stream=None) -> None:
+        """A batch of T <= 8 rows (inputs (T,H) -> outputs (T,H)) through every
+        layer in ONE persistent launch (yn_rows_flow_decode): the MoE forward
+        of a speculative-verify pass. trace: (L, T, k) int32 routed ids;
+        trace_hidden: (L, T, H) bf16 input rows of every layer;
+        trace_weights: (L, T, k) fp32; timing: (L, 16, n_SM) int64 stamps.
+        Errors land in the stack scratch's error word (decode_error)."""
+        lib = _lib.lib()
+        if self._rows_scratch is None:
+            nb = int(lib.yn_rows_flow_scratch_bytes(C.byref(self.dims), self.ROWS_MAX))
+            self._rows_scratch = torch.zeros(nb, dtype=torch.uint8, device=self.device)
+        n = len(self.structs)
+        ptr = lambda t: t.data_ptr() if t is not None else None
+        _lib.check(lib.yn_rows_flow_decode(C.byref(self.dims), self.table.data_ptr(), self.layer_array, n,
+                                           inputs.data_ptr(), inputs.shape[0], outputs.data_ptr(),
+                                           self._rows_scratch.data_ptr(), self._rows_scratch.numel(), ptr(trace),
+                                           ptr(trace_hidden), ptr(trace_weights), ptr(timing), stream_ptr(stream)))
+
+    def rows_error(self, stream=None) -> int:
+        """Read and clear the error word of the batch decode (synchronises)."""
+        if self._rows_scratch is None:
+            return 0
+        code = C.c_int32(0)
+        rc = _lib.lib().yn_stack_error(self._rows_scratch.data_ptr(), C.byref(self.dims), stream_ptr(stream),
+                                       C.byref(code))
+        if rc != _lib.YN_OK and code.value == 0:
+            _lib.check(rc)
+        return code.value
 
     def decode_error(self, stream=None) -> int:
         code = C.c_int32(0)
