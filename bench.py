@@ -827,12 +827,16 @@ def run_verify_flow(args, rank: int, world: int):
             stack.rows_decode(rows, out, timing=tm, stream=s)
         s.synchronize()
         t = tm.cpu().numpy().astype(np.float64)
-        names = ["h_in", "norm", "router_rows", "route_plan_issue", "gate_up_frags", "gate_up_tiles", "act_in",
-                 "down_frags", "down_tiles", "combine_h_out"]
-        d = np.diff(t[:, :11, :], axis=1) / 1e3          # (L, 10, G) us
+        names = ["h_in", "norm", "router_rows", "logits_in_route", "plan_issue", "gate_up_frags", "gate_up_groups",
+                 "act_in", "down_frags", "down_groups", "combine_h_out"]
+        d = np.diff(t[:, :12, :], axis=1) / 1e3          # (L, 11, G) us
         timing = {"phases_mean_us": {n: round(float(d[:, i].mean()), 3) for i, n in enumerate(names)},
                   "phases_max_us": {n: round(float(d[:, i].max(axis=1).mean()), 3) for i, n in enumerate(names)},
-                  "layer_us": round(float((t[-1, 10] - t[0, 0]).max() / 1e3 / L), 3)}
+                  "layer_us": round(float((t[-1, 11] - t[0, 0]).max() / 1e3 / L), 3),
+                  "warp0_stage_wait_gate_up_us": round(float(t[:, 12].mean() / 1e3), 3),
+                  "warp0_stage_wait_down_us": round(float(t[:, 13].mean() / 1e3), 3),
+                  "groups_per_cta_mean": {"gate_up_8_units": round(float((t[:, 14] // 1000).mean()), 2),
+                                          "down_16_rows": round(float((t[:, 14] % 1000).mean()), 2)}}
     rec = [cfg.record_spec(l).record_bytes for l in layer_ids]
     hbm_bytes = sum(n * r for n, r in zip(n_distinct, rec)) + L * cfg.dense_bytes_per_layer()
     hbm, src = peaks()

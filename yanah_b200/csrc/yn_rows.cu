@@ -42,6 +42,7 @@ RowsScratch rows_scratch(const yn_dims& d, int T) {
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 size_t r128(size_t v) { return (v + 127) / 128 * 128; }
 
 }  // namespace
@@ -58,6 +59,7 @@ extern "C" int yn_rows_flow_decode(const yn_dims* dims, const void* table, const
   if (!dims || !table || !layers || !inputs || !outputs || !scratch) return host_fail(YN_E_INVALID, "null argument");
   const yn_dims& d = *dims;
   if (n_layers < 1) return host_fail(YN_E_INVALID, "n_layers must be >= 1");
+
   if (n_rows < 1 || n_rows > RF_TMAX)
     return host_fail(YN_E_UNSUPPORTED, "rows decode: n_rows must be in [1, " + std::to_string(RF_TMAX) + "]");
   if (d.hidden != RF_H || d.n_experts != RF_E || d.moe_inter != RF_I || d.shared_inter != 0 || d.top_k < 1 ||
@@ -74,7 +76,7 @@ extern "C" int yn_rows_flow_decode(const yn_dims* dims, const void* table, const
       return host_fail(YN_E_UNSUPPORTED, "rows decode: the router must be 8-bit (64 x 2048) with groups of 64");
     for (int i = 0; i < 9; ++i)
       if (L.record.piece_offset[i] % 16) return host_fail(YN_E_UNSUPPORTED, "rows decode: record pieces must be 16-byte aligned");
-    if (!al16(L.expert_base) || L.slot_stride % 16)
+    if (!al16(L.expert_base) || L.slot_stride % 16 || L.n_slots < 1)
       return host_fail(YN_E_UNSUPPORTED, "rows decode: slot arena and stride must be 16-byte aligned");
     if (!al16(L.router.weight) || !al16(L.router.scales) || !al16(L.router.biases) || !al16(L.post_norm))
       return host_fail(YN_E_UNSUPPORTED, "rows decode: router pieces and norm must be 16-byte aligned");
@@ -98,15 +100,14 @@ extern "C" int yn_rows_flow_decode(const yn_dims* dims, const void* table, const
   o = r128(o + (size_t)n_rows * RF_XSU * 4);
   a.off_xg = (int)o;
   o = r128(o + (size_t)8 * RF_GSU * 8);   // eight rows always: the MMA reads the group data of all 8 columns
-  a.off_red = (int)o;
-  o = r128(o + (size_t)2048 * 4);
-  a.off_slots = (int)o;
-  const long long room = (long long)optin - (long long)o;
-  const int nslot = (int)std::min<long long>(RF_MAX_SLOTS, room / RF_SLOT);
-  if (nslot < 2)
-    return host_fail(YN_E_UNSUPPORTED, "rows decode: shared memory holds fewer than two ring slots (" +
-                                           std::to_string(optin) + " B per block)");
-  const size_t smem = o + (size_t)nslot * RF_SLOT;
+  a.off_ring = (int)o;
+  o += (size_t)RF_WARPS * RF_NST * RF_CSLOT;
+  a.off_rsc = (int)o;
+  o = r128(o + (size_t)RF_WARPS * RF_NST * RF_SSLOT);
+  if (o > (size_t)optin)
+    return host_fail(YN_E_UNSUPPORTED, "rows decode needs " + std::to_string(o) + " B of shared memory (" +
+                                           std::to_string(optin) + " available)");
+  const size_t smem = o;
   uint8_t* sc = reinterpret_cast<uint8_t*>(scratch);
   a.T = n_rows;
   a.K = d.top_k;
@@ -126,7 +127,6 @@ extern "C" int yn_rows_flow_decode(const yn_dims* dims, const void* table, const
   a.trace_w = trace_weights;
   a.err = reinterpret_cast<int*>(sc + S.err);
   a.timing = reinterpret_cast<long long*>(timing);
-  a.nslot = nslot;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   // stale epochs of an earlier launch must not match this launch's layers
   YN_CUDA_R(cudaMemsetAsync(sc + S.f_logits, 0, S.total - S.f_logits, st));

@@ -22,18 +22,20 @@
 //       each in ascending order; pair slot of (row t, expert e) = the rows
 //       of the experts below e + the rows of e before t. CTAs
 //       [G d / D, G (d+1) / D) take expert d.
-//   GU  the CTA's share of its expert's 96 gate/up tiles (16 units: 16 gate
-//       and 16 up rows) streams through a ring of shared-memory slots
-//       (16-byte cp.async, 16-byte chunks of a row swizzled by row & 7);
-//       per tile the 16 warps split gate/up x 8 K slices of the tensor-core
-//       GEMV whose n = 8 MMA columns are the expert's rows (warp_tile of the
-//       batch path), the slices are summed in slice order, SwiGLU, and the
+//   GU  the CTA's share of its expert's 8-unit groups (8 gate + 8 up rows:
+//       16 MMA rows) is split over its warps; each warp streams its rows
+//       over the whole K through a private ring of 4 stage slots (16-byte
+//       cp.async of 128 code bytes per row, chunks swizzled by row & 7, plus
+//       the stage's scales and biases; cp.async groups, no block sync) and
+//       keeps the GEMV accumulators in registers: tensor-core MMAs whose
+//       n = 8 columns are the expert's rows, in the batch path's arithmetic.
+//       Gate and up of a unit end in the same lane: SwiGLU there, and the
 //       activations go out as flagged words, two units per word.
-//   Dn  the CTA's down tiles (32 output rows) follow in the same ring, so
-//       their copies start while gate/up tiles are computed; once all of
-//       its expert's activations have arrived (published by the expert's
-//       CTAs), fragments, GEMV, and the expert outputs y go out as flagged
-//       words, two rows per word.
+//   Dn  the warp's 16-row groups of the expert's down rows follow in the
+//       same ring (their first stages are fetched during the gate/up tail);
+//       once all of the expert's activations have arrived (published by its
+//       CTAs), fragments, the same GEMV, and the expert outputs y go out as
+//       flagged words, two rows per word.
 //   C   CTA b owns a slice of the T x H/2 output words: the k routed y in
 //       column order times the routing weights, then the residual; the
 //       words are the next layer's input (or the outputs after the last
@@ -58,33 +60,34 @@ constexpr int RF_WARPS = RF_THREADS / 32;
 constexpr int RF_H = 2048, RF_E = 64, RF_I = 1536;
 constexpr int RF_TMAX = 8, RF_KMAX = 8;
 constexpr int RF_BITS = 4, RF_GS = 64;
-constexpr int RF_UR = 16;                     // gate/up units per tile
-constexpr int RF_DR = 32;                     // down output rows per tile
-constexpr int RF_NUT = RF_I / RF_UR;          // 96 gate/up tiles per expert
-constexpr int RF_NDT = RF_H / RF_DR;          // 64 down tiles per expert
+constexpr int RF_GU_UNITS = 8;                // gate/up work group: 8 units = 8 gate + 8 up rows (16 MMA rows)
+constexpr int RF_DN_ROWS = 16;                // down work group: 16 output rows
+constexpr int RF_NGU = RF_I / RF_GU_UNITS;    // 192 gate/up groups per expert
+constexpr int RF_NGD_R = RF_H / RF_DN_ROWS;   // 128 down groups per expert
 constexpr int RF_RB = RF_H * RF_BITS / 8;     // 1024 code bytes per gate/up row
 constexpr int RF_RBD = RF_I * RF_BITS / 8;    // 768 per down row
 constexpr int RF_NG = RF_H / RF_GS;           // 32 groups per gate/up row
 constexpr int RF_NGD = RF_I / RF_GS;          // 24 per down row
 constexpr int RF_RNG = RF_H / DEC_DGS;        // 32 groups per router row
-constexpr int RF_SRB = 80;    // shared-memory bytes per gate/up scale row (64 + 16: consecutive rows change bank)
-constexpr int RF_SRBD = 64;   // per down scale row (48 + 16)
+constexpr int RF_KSTAGE = 128;                // code bytes of a row per K stage (256 codes, 4 groups)
+constexpr int RF_NKU = RF_RB / RF_KSTAGE;     // 8 stages per gate/up row
+constexpr int RF_NKD = RF_RBD / RF_KSTAGE;    // 6 stages per down row
+constexpr int RF_GPS = RF_KSTAGE * 8 / RF_BITS / RF_GS;   // 4 groups per stage
+constexpr int RF_CSLOT = 16 * RF_KSTAGE;      // 2,048 B: a stage's 16 code rows (two 1 KB swizzle atoms)
+constexpr int RF_SSLOT = 2 * 16 * RF_GPS * 2; // 256 B: their scales and biases
+constexpr int RF_NST = 4;                     // ring stages per warp (3 in flight while one is computed)
 constexpr int RF_XSU = RF_H / 2 + 16;   // fragment words per row (frag_stride_words), gate/up
 constexpr int RF_XSD = RF_I / 2 + 16;   // down
 constexpr int RF_GSU = RF_NG + 2;       // group-data entries per row (gdata_stride), gate/up
 constexpr int RF_GSD = RF_NGD + 2;      // down
-constexpr int RF_SLOT = 2 * RF_UR * RF_RB + 4 * RF_UR * RF_SRB;   // 37,888 B: one gate/up tile
-constexpr int RF_MAX_SLOTS = 6;
 constexpr int RF_MAX_CW = 64;           // output words per CTA
-constexpr int RF_STAMPS = 16;
-static_assert(RF_DR * RF_RBD + 2 * RF_DR * RF_SRBD <= RF_SLOT, "a down tile fits a slot");
-static_assert(RF_SLOT % 128 == 0, "slots stay 128-byte aligned");
+static_assert(RF_GPS == 4 && RF_NKU * RF_KSTAGE == RF_RB && RF_NKD * RF_KSTAGE == RF_RBD, "whole stages");
+static_assert(RF_CSLOT % 1024 == 0, "code slots stay on 1 KB swizzle atoms");
 static_assert(RF_E == 64, "every router row has a CTA of its own");
 static_assert(RF_XSU == RF_H / 2 + 16 && RF_XSD == RF_I / 2 + 16, "batch-path fragment strides (4-bit)");
 
 // Fixed shared-memory header (byte offsets).
 constexpr int RF_OFF_BARR = 0;       // router / norm tile barrier
-constexpr int RF_OFF_BARS = 64;      // ring slot barriers (<= 8)
 constexpr int RF_OFF_RED = 128;      // 32 floats
 constexpr int RF_OFF_IDS = 256;      // (T, K) routed ids
 constexpr int RF_OFF_W = 512;        // (T, K) routing weights
@@ -121,8 +124,7 @@ struct RowsArgs {
   float* trace_w;           // (L, T, K) or null
   int* err;
   long long* timing;        // (L, RF_STAMPS, G) global-timer stamps, or null
-  int nslot;
-  int off_x, off_xf, off_xg, off_red, off_slots;
+  int off_x, off_xf, off_xg, off_ring, off_rsc;
 };
 
 YN_DEV void rf_stamp(const RowsArgs& a, int layer, int slot) {
@@ -161,32 +163,60 @@ YN_DEV void rf_issue_rtile(const DecLayer& L, int b, bool router, uint8_t* smem,
   }
 }
 
-// RMSNorm of T rows in place, each in the canonical 128-thread order (four
-// rows per pass): x = bf16(w * bf16(h * r)), r = 1 / sqrt(sum(h^2) / H + eps)
-// with the warp partials summed in warp order. Ends with a block sync.
+// RMSNorm of T rows in place, each in the canonical 128-thread order:
+// x = bf16(w * bf16(h * r)), r = 1 / sqrt(sum(h^2) / H + eps), thread i of a
+// row summing h[i + 128 m] in ascending m, a butterfly inside each warp and
+// the four warp partials summed in warp order. Thread (q, i) takes rows q and
+// q + 4 as two independent chains. Ends with a block sync.
 YN_DEV void rf_rmsnorm_rows(uint16_t* x, const uint16_t* w, int T, float eps, float* red, float* rinv) {
+  static_assert(RF_TMAX <= 8 && RF_THREADS == 512, "four rows of 128 threads per pass, two passes per thread");
   const int tid = threadIdx.x, q = tid >> 7, i = tid & 127;
-  for (int t0 = 0; t0 < T; t0 += 4) {
-    const int t = t0 + q;
-    float ss = 0.0f;
-    if (t < T)
-      for (int j = i; j < RF_H; j += 128) {
-        const float v = bf16_to_f32(x[(size_t)t * RF_H + j]);
-        ss = __fmaf_rn(v, v, ss);
-      }
-    ss = group_sum_bfly(ss, 32);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;   // red[4 q + warp of the row]
-    __syncthreads();
-    if (tid < 4 && t0 + tid < T) {
-      const float* r4 = red + 4 * tid;
-      const float tot = __fadd_rn(__fadd_rn(__fadd_rn(r4[0], r4[1]), r4[2]), r4[3]);
-      rinv[t0 + tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)RF_H), eps)));
+  const int t0 = q, t1 = q + 4;
+  float s0 = 0.0f, s1 = 0.0f;
+  const uint16_t* x0 = x + (size_t)t0 * RF_H;
+  const uint16_t* x1 = x + (size_t)t1 * RF_H;
+  const bool h0 = t0 < T, h1 = t1 < T;
+#pragma unroll
+  for (int m = 0; m < RF_H / 128; ++m) {
+    const int j = i + 128 * m;
+    if (h0) {
+      const float v = bf16_to_f32(x0[j]);
+      s0 = __fmaf_rn(v, v, s0);
     }
-    __syncthreads();
+    if (h1) {
+      const float v = bf16_to_f32(x1[j]);
+      s1 = __fmaf_rn(v, v, s1);
+    }
   }
-  for (int k = tid; k < T * RF_H; k += RF_THREADS) {
-    const int t = k / RF_H, j = k % RF_H;
-    x[k] = f32_to_bf16(__fmul_rn(bf16_to_f32(w[j]), bf16r(__fmul_rn(bf16_to_f32(x[k]), rinv[t]))));
+  s0 = group_sum_bfly(s0, 32);
+  s1 = group_sum_bfly(s1, 32);
+  if ((tid & 31) == 0) {
+    red[tid >> 5] = s0;          // row q: red[4 q + warp of the row]
+    red[16 + (tid >> 5)] = s1;   // row q + 4
+  }
+  __syncthreads();
+  if (tid < T) {
+    const float* r4 = red + 4 * tid;
+    const float tot = __fadd_rn(__fadd_rn(__fadd_rn(r4[0], r4[1]), r4[2]), r4[3]);
+    rinv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)RF_H), eps)));
+  }
+  __syncthreads();
+  for (int k = tid; k < T * RF_H / 8; k += RF_THREADS) {   // 8 elements per step
+    const int t = k / (RF_H / 8), j8 = k % (RF_H / 8);
+    const float r = rinv[t];
+    uint4 hv = reinterpret_cast<const uint4*>(x)[k];
+    const uint4 wv = reinterpret_cast<const uint4*>(w)[j8];
+    uint32_t* hp = reinterpret_cast<uint32_t*>(&hv);
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = __fmul_rn(bf16_to_f32((uint16_t)(wp[e] & 0xFFFFu)),
+                                 bf16r(__fmul_rn(bf16_to_f32((uint16_t)(hp[e] & 0xFFFFu)), r)));
+      const float hi = __fmul_rn(bf16_to_f32((uint16_t)(wp[e] >> 16)),
+                                 bf16r(__fmul_rn(bf16_to_f32((uint16_t)(hp[e] >> 16)), r)));
+      hp[e] = (uint32_t)f32_to_bf16(lo) | ((uint32_t)f32_to_bf16(hi) << 16);
+    }
+    reinterpret_cast<uint4*>(x)[k] = hv;
   }
   __syncthreads();
 }
@@ -194,22 +224,30 @@ YN_DEV void rf_rmsnorm_rows(uint16_t* x, const uint16_t* w, int T, float eps, fl
 // Batch-path fragments (the layout k_batch_frags writes) of n rows of Kd bf16
 // values, rows[i] the source row of fragment row i: per row a power-of-two
 // scale from max|x|, the fp16 pair words, and per group {-1024 * sum of the
-// fragment values, scale * sum(x)}, then {1 / scale, 0}. Ends with a block
-// sync.
-template <int BITS, int GS>
-YN_DEV void rf_frags(const uint16_t* src, int Kd, const int* rows, int n, uint32_t* XF, int xs_w, float2* XG,
-                     int gsd, float* rsc) {
+// fragment values, scale * sum(x)}, then {1 / scale, 0}. Group sums: eight
+// threads per group, 8 consecutive values each, then a butterfly. Ends with a
+// block sync.
+template <int BITS, int GS, int Kd>
+YN_DEV void rf_frags(const uint16_t* src, const int* rows, int n, uint32_t* XF, int xs_w, float2* XG, int gsd,
+                     float* rsc) {
   using F = BFmt<BITS, GS>;
+  static_assert(GS == 64 && F::WPL == 8, "eight threads of 8 codes (one code word) per group");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (warp < n) {
-    const uint16_t* x = src + (size_t)rows[warp] * Kd;
+    const uint4* x = reinterpret_cast<const uint4*>(src + (size_t)rows[warp] * Kd);
     float mx = 0.0f;
-    for (int k = lane; k < Kd; k += 32) mx = fmaxf(mx, fabsf(bf16_to_f32(x[k])));
+    for (int k = lane; k < Kd / 8; k += 32) {
+      const uint4 v = x[k];
+      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)   // |x| as the magnitude bits of bf16: the order of the floats
+        mx = fmaxf(mx, fmaxf(bf16_to_f32((uint16_t)(vv[e] & 0x7FFFu)), bf16_to_f32((uint16_t)((vv[e] >> 16) & 0x7FFFu))));
+    }
     mx = warp_max(mx);
     if (lane == 0) rsc[warp] = fp16_input_scale(mx);
   }
   __syncthreads();
-  const int hw = Kd / 2;
+  constexpr int hw = Kd / 2;
   for (int i = tid; i < n * hw; i += RF_THREADS) {
     const int r = i / hw, w = i - r * hw;
     const uint16_t* x = src + (size_t)rows[r] * Kd;
@@ -220,21 +258,26 @@ YN_DEV void rf_frags(const uint16_t* src, int Kd, const int* rows, int n, uint32
                                   __fmul_rn(bf16_to_f32(x[base + BW<BITS>::hi(p)]), m));
     XF[(size_t)r * xs_w + w] = *reinterpret_cast<uint32_t*>(&h);
   }
-  const int NG = Kd / GS;
-  for (int q = warp; q < n * NG; q += RF_WARPS) {
-    const int r = q / NG, g = q - r * NG;
-    const uint16_t* x = src + (size_t)rows[r] * Kd;
-    const float scale = rsc[r];
+  constexpr int NG = Kd / GS;
+  for (int i = tid; i < n * NG * 8; i += RF_THREADS) {   // every lane of a warp takes part (butterflies)
+    const int sub = i & 7, gq = i >> 3, r = gq / NG, g = gq - r * NG;
+    const bool ok = r < n;
     float sx = 0.0f, o = 0.0f;
-    for (int k = g * GS + lane; k < (g + 1) * GS; k += 32) {
-      const float v = bf16_to_f32(x[k]);
-      sx = __fadd_rn(sx, v);
-      const float m = __fmul_rn(scale, BW<BITS>::inv_mult(BW<BITS>::pair_of(k % F::WPL)));
-      o = __fadd_rn(o, __half2float(__float2half_rn(__fmul_rn(v, m))));
+    if (ok) {
+      const float scale = rsc[r];
+      const uint4 v = *reinterpret_cast<const uint4*>(src + (size_t)rows[r] * Kd + g * GS + 8 * sub);
+      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = bf16_to_f32((uint16_t)((e & 1) ? vv[e >> 1] >> 16 : vv[e >> 1] & 0xFFFFu));
+        sx = __fadd_rn(sx, f);
+        const float m = __fmul_rn(scale, BW<BITS>::inv_mult(BW<BITS>::pair_of(e)));
+        o = __fadd_rn(o, __half2float(__float2half_rn(__fmul_rn(f, m))));
+      }
     }
-    sx = group_sum_bfly(sx, 32);
-    o = group_sum_bfly(o, 32);
-    if (lane == 0) XG[(size_t)r * gsd + g] = make_float2(__fmul_rn(-1024.0f, o), __fmul_rn(scale, sx));
+    sx = group_sum_bfly(sx, 8);
+    o = group_sum_bfly(o, 8);
+    if (ok && sub == 0) XG[(size_t)r * gsd + g] = make_float2(__fmul_rn(-1024.0f, o), __fmul_rn(rsc[r], sx));
   }
   if (tid < n) {
     XG[(size_t)tid * gsd + NG] = make_float2(__fdiv_rn(1.0f, rsc[tid]), 0.0f);
@@ -243,51 +286,151 @@ YN_DEV void rf_frags(const uint16_t* src, int Kd, const int* rows, int n, uint32
   __syncthreads();
 }
 
-// Copies of ring item i of this CTA (gate/up tile u_t0 + i for i < n_up, else
-// down tile d_t0 + i - n_up of the expert record `rec`) into slot S: every
-// thread issues its 16-byte pieces and arrives (no-increment) on `bar`,
-// which therefore completes when every piece has landed (count = threads).
-YN_DEV void rf_issue(const uint8_t* rec, const RecGeom& rg, int i, int n_up, int u_t0, int d_t0, uint8_t* S,
-                     uint64_t* bar) {
-  const int tid = threadIdx.x;
-  if (i < n_up) {
-    const int u0 = (u_t0 + i) * RF_UR;
-    constexpr int CPR = RF_RB / 16;   // 64 chunks per row
-    for (int q = tid; q < 2 * RF_UR * CPR; q += RF_THREADS) {
-      const int row = q / CPR, ch = q % CPR, mat = row / RF_UR, rr = row % RF_UR;
-      cp16(S + (size_t)row * RF_RB + ((ch ^ (row & 7)) << 4),
-           rec + rg.off[mat ? 3 : 0] + (size_t)(u0 + rr) * RF_RB + 16 * ch);
+// The MMAs of this kernel as plain (non-volatile) asm: pure register
+// functions, so the compiler may interleave the independent group chains of
+// a stage (volatile asm keeps every MMA in program order). The shared-memory
+// reads (ldmatrix) stay volatile, ordered after the stage waits.
+YN_DEV void rf_mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+YN_DEV void rf_mmac(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const float (&c)[4]) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+        "f"(c[3]));
+}
+
+YN_DEV void cp8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+YN_DEV void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+YN_DEV void cp_wait_prefetched() { asm volatile("cp.async.wait_group %0;" ::"n"(RF_NST - 2) : "memory"); }
+
+// One K stage of a warp's 16 weight rows into its ring slots: the rows' 128
+// code bytes of stage k (16-byte chunks swizzled by row & 7, so the ldmatrix
+// rows of a chunk fall in different banks) and the 4 groups' scales and
+// biases (8 bytes a row each), issued by the warp's lanes (4 + 1 copies
+// each), not committed. Gate/up group (gu): rows 0..7 are the gate rows of
+// units row0..row0+7, rows 8..15 their up rows; down group: output rows
+// row0..row0+15.
+YN_DEV void rf_issue_stage(uint8_t* cslot, uint8_t* sslot, const uint8_t* rec, const RecGeom& rg, bool gu, int row0,
+                           int k, int lane) {
+  const int ch = lane & 7, rq = lane >> 3;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const int row = rq + 4 * m;
+    const uint8_t* src = gu ? rec + rg.off[m < 2 ? 0 : 3] + (size_t)(row0 + (row & 7)) * RF_RB
+                            : rec + rg.off[6] + (size_t)(row0 + row) * RF_RBD;
+    cp16(cslot + row * RF_KSTAGE + ((ch ^ (row & 7)) << 4), src + k * RF_KSTAGE + 16 * ch);
+  }
+  const int row = lane & 15, which = lane >> 4;   // scales (0) or biases (1) of row
+  const int sb = gu ? RF_NG * 2 : RF_NGD * 2;
+  const int piece = gu ? (row < 8 ? (which ? 2 : 1) : (which ? 5 : 4)) : (which ? 8 : 7);
+  const int srow = gu ? row0 + (row & 7) : row0 + row;
+  cp8(sslot + which * (16 * RF_GPS * 2) + row * (RF_GPS * 2), rec + rg.off[piece] + (size_t)srow * sb + k * (RF_GPS * 2));
+}
+
+// The MMAs of one stage (4 groups of 2 chunks) for the warp's 16 rows and up
+// to 8 batch rows (the n = 8 columns), accumulated into acc (lane (g, c):
+// weight rows g and g+8, batch rows 2c and 2c+1), in the batch path's
+// arithmetic (warp_tile): each group's tile starts at the group's unpack
+// offset, and its scale and bias are applied in fp32.
+YN_DEV void rf_stage_mma(const uint8_t* slot, const uint8_t* sslot, int k, const uint32_t* XF, int xs, const float2* XG,
+                         int gsd, int ntok, float (&acc)[4]) {
+  using F = BFmt<RF_BITS, RF_GS>;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7), mch = lane >> 4;
+  const uint16_t* Ss = reinterpret_cast<const uint16_t*>(sslot);
+  const uint16_t* Bs = Ss + 16 * RF_GPS;
+  const int t0 = 2 * c;
+#pragma unroll
+  for (int gi = 0; gi < RF_GPS; ++gi) {
+    uint32_t wr[4];
+    ldsm_x4(wr, slot + mrow * RF_KSTAGE + (((2 * gi + mch) ^ (mrow & 7)) << 4));
+    const int grp = RF_GPS * k + gi;
+    float d[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int ch = 8 * k + 2 * gi + h;
+      uint32_t pa[F::PPW], pb[F::PPW], xb[F::PPW];
+      BW<RF_BITS>::unpack(wr[2 * h], pa);
+      BW<RF_BITS>::unpack(wr[2 * h + 1], pb);
+      if (g < ntok) {
+        const uint4 v = *reinterpret_cast<const uint4*>(XF + (size_t)g * xs + (size_t)(ch * 4 + c) * F::PPW);
+        xb[0] = v.x; xb[1] = v.y; xb[2] = v.z; xb[3] = v.w;
+      } else {
+        xb[0] = xb[1] = xb[2] = xb[3] = 0u;
+      }
+      const uint32_t A0[4] = {pa[0], pb[0], pa[1], pb[1]}, B0[2] = {xb[0], xb[1]};
+      if (h == 0) {
+        const float n0 = XG[(size_t)t0 * gsd + grp].x, n1 = XG[(size_t)(t0 + 1) * gsd + grp].x;
+        const float ci[4] = {n0, n1, n0, n1};
+        rf_mmac(d, A0, B0, ci);
+      } else {
+        rf_mma(d, A0, B0);
+      }
+      const uint32_t A1[4] = {pa[2], pb[2], pa[3], pb[3]}, B1[2] = {xb[2], xb[3]};
+      rf_mma(d, A1, B1);
     }
-    uint8_t* Sc = S + 2 * RF_UR * RF_RB;
-    constexpr int SPR = RF_NG * 2 / 16;   // 4 chunks per scale row
-    for (int q = tid; q < 4 * RF_UR * SPR; q += RF_THREADS) {
-      const int pc = q / (RF_UR * SPR), rem = q % (RF_UR * SPR), rr = rem / SPR, ch = rem % SPR;
-      const int piece = pc == 0 ? 1 : pc == 1 ? 2 : pc == 2 ? 4 : 5;   // gate s, gate b, up s, up b
-      cp16(Sc + (size_t)(pc * RF_UR + rr) * RF_SRB + 16 * ch,
-           rec + rg.off[piece] + (size_t)(u0 + rr) * (RF_NG * 2) + 16 * ch);
-    }
-  } else {
-    const int r0 = (d_t0 + i - n_up) * RF_DR;
-    constexpr int CPR = RF_RBD / 16;   // 48 chunks per row (a multiple of 8: the XOR stays in the row)
-    for (int q = tid; q < RF_DR * CPR; q += RF_THREADS) {
-      const int row = q / CPR, ch = q % CPR;
-      cp16(S + (size_t)row * RF_RBD + ((ch ^ (row & 7)) << 4), rec + rg.off[6] + (size_t)(r0 + row) * RF_RBD + 16 * ch);
-    }
-    uint8_t* Sc = S + RF_DR * RF_RBD;
-    constexpr int SPR = RF_NGD * 2 / 16;   // 3 chunks per scale row
-    for (int q = tid; q < 2 * RF_DR * SPR; q += RF_THREADS) {
-      const int pc = q / (RF_DR * SPR), rem = q % (RF_DR * SPR), rr = rem / SPR, ch = rem % SPR;
-      cp16(Sc + (size_t)(pc * RF_DR + rr) * RF_SRBD + 16 * ch,
-           rec + rg.off[pc ? 8 : 7] + (size_t)(r0 + rr) * (RF_NGD * 2) + 16 * ch);
+    const float x0 = XG[(size_t)t0 * gsd + grp].y, x1 = XG[(size_t)(t0 + 1) * gsd + grp].y;
+    const float s0 = f16_to_f32(Ss[g * RF_GPS + gi]), s1 = f16_to_f32(Ss[(g + 8) * RF_GPS + gi]);
+    const float b0 = f16_to_f32(Bs[g * RF_GPS + gi]), b1 = f16_to_f32(Bs[(g + 8) * RF_GPS + gi]);
+    acc[0] = __fmaf_rn(s0, d[0], __fmaf_rn(b0, x0, acc[0]));
+    acc[1] = __fmaf_rn(s0, d[1], __fmaf_rn(b0, x1, acc[1]));
+    acc[2] = __fmaf_rn(s1, d[2], __fmaf_rn(b1, x0, acc[2]));
+    acc[3] = __fmaf_rn(s1, d[3], __fmaf_rn(b1, x1, acc[3]));
+  }
+}
+
+// A finished gate/up group: lane (g, c) holds gate (acc 0, 1) and up (acc 2, 3)
+// of unit u0 + g for batch rows 2c, 2c+1; SwiGLU, and units g, g+1 go out as
+// one flagged word per row.
+YN_DEV void rf_gu_out(const float (&acc)[4], const float2* XG, int Td, u64* f_act_rows, int u0, uint32_t ep) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3, t0 = 2 * c;
+  uint32_t v[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float inv = XG[(size_t)(t0 + h) * RF_GSU + RF_NG].x;
+    v[h] = (uint32_t)f32_to_bf16(swiglu_bf16(bf16r(__fmul_rn(acc[h], inv)), bf16r(__fmul_rn(acc[2 + h], inv))));
+  }
+  const uint32_t n0 = __shfl_down_sync(0xffffffffu, v[0], 4), n1 = __shfl_down_sync(0xffffffffu, v[1], 4);
+  if (!(g & 1)) {
+    if (t0 < Td) put_flag(f_act_rows + (size_t)t0 * (RF_I / 2) + (u0 + g) / 2, v[0] | (n0 << 16), ep);
+    if (t0 + 1 < Td) put_flag(f_act_rows + (size_t)(t0 + 1) * (RF_I / 2) + (u0 + g) / 2, v[1] | (n1 << 16), ep);
+  }
+}
+
+// A finished down group: lane (g, c) holds output rows r0 + g (acc 0, 1) and
+// r0 + g + 8 (acc 2, 3) for batch rows 2c, 2c+1; rows g, g+1 go out as one
+// flagged word.
+YN_DEV void rf_dn_out(const float (&acc)[4], const float2* XG, int Td, u64* f_y_rows, int r0, uint32_t ep) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3, t0 = 2 * c;
+  uint32_t v[4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float inv = XG[(size_t)(t0 + h) * RF_GSD + RF_NGD].x;
+    v[h] = (uint32_t)f32_to_bf16(__fmul_rn(acc[h], inv));
+    v[2 + h] = (uint32_t)f32_to_bf16(__fmul_rn(acc[2 + h], inv));
+  }
+  uint32_t n[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) n[q] = __shfl_down_sync(0xffffffffu, v[q], 4);
+  if (!(g & 1)) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (t0 + h >= Td) continue;
+      u64* fr = f_y_rows + (size_t)(t0 + h) * (RF_H / 2);
+      put_flag(fr + (r0 + g) / 2, v[h] | (n[h] << 16), ep);
+      put_flag(fr + (r0 + g + 8) / 2, v[2 + h] | (n[2 + h] << 16), ep);
     }
   }
-  cp_arrive(bar);
 }
 
 __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* barR = reinterpret_cast<uint64_t*>(smem + RF_OFF_BARR);
-  uint64_t* barS = reinterpret_cast<uint64_t*>(smem + RF_OFF_BARS);
   float* red = reinterpret_cast<float*>(smem + RF_OFF_RED);
   int32_t* ids_s = reinterpret_cast<int32_t*>(smem + RF_OFF_IDS);
   float* w_s = reinterpret_cast<float*>(smem + RF_OFF_W);
@@ -305,27 +448,31 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
   uint16_t* xb = reinterpret_cast<uint16_t*>(smem + a.off_x);
   uint32_t* XF = reinterpret_cast<uint32_t*>(smem + a.off_xf);
   float2* XG = reinterpret_cast<float2*>(smem + a.off_xg);
-  float* RED = reinterpret_cast<float*>(smem + a.off_red);
-  uint8_t* slots = smem + a.off_slots;
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, c = lane & 3;
-  const int G = gridDim.x, b = blockIdx.x, T = a.T, K = a.K, NS = a.nslot;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // this warp's stage slots (code rows, scales)
+  uint8_t* cring = smem + a.off_ring + (size_t)warp * RF_NST * RF_CSLOT;
+  uint8_t* sring = smem + a.off_rsc + (size_t)warp * RF_NST * RF_SSLOT;
+  const int G = gridDim.x, b = blockIdx.x, T = a.T, K = a.K;
   const int W = T * (RF_H / 2);
   const int cw0 = (int)((long long)W * b / G), ncw = (int)((long long)W * (b + 1) / G) - cw0;
   const bool router_cta = b < RF_E;
 
   if (tid == 0) {
     mbar_init(barR, 1);
-    for (int s = 0; s < NS; ++s) mbar_init(&barS[s], RF_THREADS);
     fence_mbar_init();
   }
   if (tid < 8) misc[16 + tid] = tid;
   load_layer(&lay[0], a.layers, 0);
   __syncthreads();
   if (tid == 0) rf_issue_rtile(lay[0], b, router_cta, smem, barR);
-  uint32_t phR = 0, seq = 0;
+  uint32_t phR = 0;
   bool pendR = true;
-  auto drain = [&]() {
+  // diagnostics (timing only, thread 0): ns waiting on its warp's ring stages (gate/up, down)
+  unsigned long long dg_wait_gu = 0, dg_wait_dn = 0, dg_t = 0;
+  const bool diag = a.timing != nullptr && tid == 0;
+  auto dg_now = [&]() { return diag ? globaltimer_ns() : 0ull; };
+  auto drain = [&]() {   // block-uniform: every copy in flight lands before the CTA returns
     asm volatile("cp.async.wait_all;" ::: "memory");
     if (pendR) mbar_wait_block(barR, phR, nullptr);
   };
@@ -408,6 +555,7 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       }
     }
     if (__syncthreads_or(fail)) { drain(); return; }
+    rf_stamp(a, layer, 4);
     if (tid < T * K) atomicOr(&rowmask[ids_s[tid]], 1u << (tid / K));
     if (b == 0 && tid < T * K) {
       if (a.trace_ids) a.trace_ids[(size_t)layer * T * K + tid] = ids_s[tid];
@@ -446,16 +594,18 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       drain();
       return;
     }
-    // this CTA's expert, its rows and its tiles
+    // this CTA's expert, its rows, and this warp's work groups
     const int d = (int)(((long long)(b + 1) * D - 1) / G);
     const int lo = (int)((long long)d * G / D), hi = (int)((long long)(d + 1) * G / D);
     const int r = b - lo, nd = hi - lo;
     const int e = elist[d];
     const uint32_t rm = rowmask[e];
     const int Td = __popc(rm), ps0 = pbase[e];
-    const int u_t0 = RF_NUT * r / nd, n_up = RF_NUT * (r + 1) / nd - u_t0;
-    const int d_t0 = RF_NDT * r / nd, n_dn = RF_NDT * (r + 1) / nd - d_t0;
-    const int n_items = n_up + n_dn;
+    const int gu0 = RF_NGU * r / nd, ngu = RF_NGU * (r + 1) / nd - gu0;        // 8-unit groups of the CTA
+    const int dn0 = RF_NGD_R * r / nd, ndn = RF_NGD_R * (r + 1) / nd - dn0;    // 16-row groups
+    const int my_gu = warp < ngu ? (ngu - warp + RF_WARPS - 1) / RF_WARPS : 0;    // groups w, w + 16, ...
+    const int my_dn = warp < ndn ? (ndn - warp + RF_WARPS - 1) / RF_WARPS : 0;
+    const int n_gu_items = my_gu * RF_NKU, n_items = n_gu_items + my_dn * RF_NKD;
     const uint8_t* rec = expert_record(L, e);
     if (tid < RF_TMAX) {   // local row tid -> its row: the position of set bit number tid of rm
       int pos = 0, cnt = 0;
@@ -466,97 +616,70 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
         }
       misc[8 + tid] = pos;
     }
-    const uint32_t base = seq;
-    for (int i = 0; i < n_items && i < NS; ++i)
-      rf_issue(rec, L.rg, i, n_up, u_t0, d_t0, slots + (size_t)((base + i) % NS) * RF_SLOT, &barS[(base + i) % NS]);
+    // the warp's ring: item j = stage j % NK of its group j / NK (gate/up items first, then down) in slot
+    // j % RF_NST; RF_NST - 1 items in flight; one cp.async commit group per item and lane, empty past the end
+    auto issue_item = [&](int j) {
+      if (j < n_items) {
+        const int sl = j % RF_NST;
+        const bool gu = j < n_gu_items;
+        const int row0 = gu ? (gu0 + warp + RF_WARPS * (j / RF_NKU)) * RF_GU_UNITS
+                            : (dn0 + warp + RF_WARPS * ((j - n_gu_items) / RF_NKD)) * RF_DN_ROWS;
+        const int k = gu ? j % RF_NKU : (j - n_gu_items) % RF_NKD;
+        rf_issue_stage(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, rec, L.rg, gu, row0, k, lane);
+      }
+      cp_commit();
+    };
+    // item j's stage in shared memory: this lane's copies landed, then every lane's (and every lane is done
+    // with item j - 1, whose slot the next issue refills)
+    auto wait_item = [&]() {
+      cp_wait_prefetched();
+      __syncwarp();
+    };
+#pragma unroll
+    for (int j = 0; j < RF_NST - 1; ++j) issue_item(j);
     __syncthreads();   // misc[8..16)
-    rf_stamp(a, layer, 4);
-    rf_frags<RF_BITS, RF_GS>(xb, RF_H, misc + 8, Td, XF, RF_XSU, XG, RF_GSU, rowf + 8);
     rf_stamp(a, layer, 5);
-    // -------- GU: gate/up tiles, SwiGLU, activations out
-    for (int i = 0; i < n_up; ++i) {
-      const uint32_t q = base + i;
-      uint8_t* S = slots + (size_t)(q % NS) * RF_SLOT;
-      if (!mbar_wait_block(&barS[q % NS], (q / NS) & 1u, a.err)) { drain(); return; }
-      const int mat = warp >> 3, ks = warp & 7;
-      const uint16_t* Sc = reinterpret_cast<const uint16_t*>(S + 2 * RF_UR * RF_RB);
-      constexpr int SH = RF_SRB / 2;
-      // warp_tile reads the scale row of weight row r0 + g at S[(r0 + g) * SH]: gate rows are 0..15, up rows 16..31
-      const uint16_t* Sm = Sc + (size_t)(mat ? 2 * RF_UR - RF_UR : 0) * SH;
-      const uint16_t* Bm = Sc + (size_t)(mat ? 3 * RF_UR - RF_UR : RF_UR) * SH;
-      float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-      warp_tile<RF_BITS, RF_GS, 1>(S, RF_RB, RF_UR * mat, Sm, Bm, SH, ks * 8, 8, XF, RF_XSU, XG, RF_GSU, Td, acc);
-      float* rd = RED + (size_t)(mat * 8 + ks) * RF_UR * 8;
-      rd[g * 8 + 2 * c] = acc[0][0];
-      rd[g * 8 + 2 * c + 1] = acc[0][1];
-      rd[(g + 8) * 8 + 2 * c] = acc[0][2];
-      rd[(g + 8) * 8 + 2 * c + 1] = acc[0][3];
-      __syncthreads();   // the slot is read: refill it
-      if (i + NS < n_items) rf_issue(rec, L.rg, i + NS, n_up, u_t0, d_t0, S, &barS[q % NS]);
-      if (tid < 8 * Td) {
-        const int tl = tid >> 3, up = tid & 7;
-        const float inv = XG[(size_t)tl * RF_GSU + RF_NG].x;
-        uint32_t pk = 0;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int u = 2 * up + h;
-          float gs = 0.0f, us = 0.0f;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            gs = __fadd_rn(gs, RED[((size_t)k * RF_UR + u) * 8 + tl]);
-            us = __fadd_rn(us, RED[((size_t)(8 + k) * RF_UR + u) * 8 + tl]);
-          }
-          const float gv = bf16r(__fmul_rn(gs, inv)), uv = bf16r(__fmul_rn(us, inv));
-          pk |= (uint32_t)f32_to_bf16(swiglu_bf16(gv, uv)) << (16 * h);
-        }
-        put_flag(a.f_act + ((size_t)par * a.P + ps0 + tl) * (RF_I / 2) + ((u_t0 + i) * RF_UR) / 2 + up, pk, ep);
-      }
-      // the next wait's block sync orders these RED reads before the next tile's writes
-    }
+    rf_frags<RF_BITS, RF_GS, RF_H>(xb, misc + 8, Td, XF, RF_XSU, XG, RF_GSU, rowf + 8);
     rf_stamp(a, layer, 6);
-    // -------- Dn: the expert's activations of all its rows, fragments, down tiles
-    rf_wait_words(a.f_act + ((size_t)par * a.P + ps0) * (RF_I / 2), reinterpret_cast<uint32_t*>(xb), Td * (RF_I / 2),
-                  ep, a.err, fail);
-    if (__syncthreads_or(fail)) { drain(); return; }
-    rf_stamp(a, layer, 7);
-    rf_frags<RF_BITS, RF_GS>(xb, RF_I, misc + 16, Td, XF, RF_XSD, XG, RF_GSD, rowf + 8);
-    rf_stamp(a, layer, 8);
-    for (int i = n_up; i < n_items; ++i) {
-      const uint32_t q = base + i;
-      uint8_t* S = slots + (size_t)(q % NS) * RF_SLOT;
-      if (!mbar_wait_block(&barS[q % NS], (q / NS) & 1u, a.err)) { drain(); return; }
-      const int rs = warp & 1, ks = warp >> 1;
-      const uint16_t* Sd = reinterpret_cast<const uint16_t*>(S + RF_DR * RF_RBD);
-      constexpr int SH = RF_SRBD / 2;
-      float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-      warp_tile<RF_BITS, RF_GS, 1>(S, RF_RBD, 16 * rs, Sd, Sd + (size_t)RF_DR * SH, SH, ks * 6, 6, XF, RF_XSD, XG,
-                                   RF_GSD, Td, acc);
-      float* rd = RED + (size_t)ks * RF_DR * 8;
-      const int ra = 16 * rs + g;
-      rd[ra * 8 + 2 * c] = acc[0][0];
-      rd[ra * 8 + 2 * c + 1] = acc[0][1];
-      rd[(ra + 8) * 8 + 2 * c] = acc[0][2];
-      rd[(ra + 8) * 8 + 2 * c + 1] = acc[0][3];
-      __syncthreads();
-      if (i + NS < n_items) rf_issue(rec, L.rg, i + NS, n_up, u_t0, d_t0, S, &barS[q % NS]);
-      if (tid < 16 * Td) {
-        const int tl = tid >> 4, rp = tid & 15;
-        const float inv = XG[(size_t)tl * RF_GSD + RF_NGD].x;
-        uint32_t pk = 0;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = 2 * rp + h;
-          float y = 0.0f;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) y = __fadd_rn(y, RED[((size_t)k * RF_DR + row) * 8 + tl]);
-          pk |= (uint32_t)f32_to_bf16(__fmul_rn(y, inv)) << (16 * h);
-        }
-        const int r0 = (d_t0 + i - n_up) * RF_DR;
-        put_flag(a.f_y + ((size_t)par * a.P + ps0 + tl) * (RF_H / 2) + r0 / 2 + rp, pk, ep);
+    // -------- GU: the warp's gate/up groups, SwiGLU, activations out
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    u64* fa = a.f_act + ((size_t)par * a.P + ps0) * (RF_I / 2);
+    for (int j = 0; j < n_gu_items; ++j) {
+      dg_t = dg_now();
+      wait_item();
+      if (diag) dg_wait_gu += dg_now() - dg_t;
+      issue_item(j + RF_NST - 1);   // into the slot of item j - 1
+      const int sl = j % RF_NST;
+      rf_stage_mma(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, j % RF_NKU, XF, RF_XSU, XG, RF_GSU,
+                   Td, acc);
+      if (j % RF_NKU == RF_NKU - 1) {
+        rf_gu_out(acc, XG, Td, fa, (gu0 + warp + RF_WARPS * (j / RF_NKU)) * RF_GU_UNITS, ep);
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
       }
     }
-    seq = base + (uint32_t)n_items;
+    rf_stamp(a, layer, 7);
+    // -------- Dn: the expert's activations of all its rows, fragments, the warp's down groups
+    rf_wait_words(fa, reinterpret_cast<uint32_t*>(xb), Td * (RF_I / 2), ep, a.err, fail);
+    if (__syncthreads_or(fail)) { drain(); return; }
+    rf_stamp(a, layer, 8);
+    rf_frags<RF_BITS, RF_GS, RF_I>(xb, misc + 16, Td, XF, RF_XSD, XG, RF_GSD, rowf + 8);
     rf_stamp(a, layer, 9);
+    u64* fy = a.f_y + ((size_t)par * a.P + ps0) * (RF_H / 2);
+    for (int j = n_gu_items; j < n_items; ++j) {
+      dg_t = dg_now();
+      wait_item();
+      if (diag) dg_wait_dn += dg_now() - dg_t;
+      issue_item(j + RF_NST - 1);
+      const int jd = j - n_gu_items;
+      const int sl = j % RF_NST;
+      rf_stage_mma(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, jd % RF_NKD, XF, RF_XSD, XG, RF_GSD,
+                   Td, acc);
+      if (jd % RF_NKD == RF_NKD - 1) {
+        rf_dn_out(acc, XG, Td, fy, (dn0 + warp + RF_WARPS * (jd / RF_NKD)) * RF_DN_ROWS, ep);
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      }
+    }
+    rf_stamp(a, layer, 10);
     // -------- C: this CTA's output words (column order, then the residual)
     if (tid < ncw) {
       const int w = cw0 + tid, t = w / (RF_H / 2), p = w % (RF_H / 2);
@@ -590,7 +713,14 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       else reinterpret_cast<uint32_t*>(a.outputs)[w] = pk;
     }
     if (__syncthreads_or(fail)) { drain(); return; }
-    rf_stamp(a, layer, 10);
+    rf_stamp(a, layer, 11);
+    if (diag) {   // per-layer durations (ns) in stamp slots 12..14
+      long long* tm = a.timing + ((size_t)layer * DEC_STAMPS) * gridDim.x + blockIdx.x;
+      tm[12 * (size_t)gridDim.x] = (long long)dg_wait_gu;
+      tm[13 * (size_t)gridDim.x] = (long long)dg_wait_dn;
+      tm[14 * (size_t)gridDim.x] = (long long)(ngu * 1000 + ndn);
+      dg_wait_gu = dg_wait_dn = 0;
+    }
   }
   drain();
 }
