@@ -88,6 +88,7 @@ static_assert(RF_XSU == RF_H / 2 + 16 && RF_XSD == RF_I / 2 + 16, "batch-path fr
 
 // Fixed shared-memory header (byte offsets).
 constexpr int RF_OFF_BARR = 0;       // router / norm tile barrier
+constexpr int RF_OFF_ZERO = 64;      // 16 zero bytes: the B fragment of batch columns past the rows
 constexpr int RF_OFF_RED = 128;      // 32 floats
 constexpr int RF_OFF_IDS = 256;      // (T, K) routed ids
 constexpr int RF_OFF_W = 512;        // (T, K) routing weights
@@ -315,8 +316,9 @@ YN_DEV void cp_wait_prefetched() { asm volatile("cp.async.wait_group %0;" ::"n"(
 // each), not committed. Gate/up group (gu): rows 0..7 are the gate rows of
 // units row0..row0+7, rows 8..15 their up rows; down group: output rows
 // row0..row0+15.
-YN_DEV void rf_issue_stage(uint8_t* cslot, uint8_t* sslot, const uint8_t* rec, const RecGeom& rg, bool gu, int row0,
-                           int k, int lane) {
+template <bool gu>
+YN_DEV void rf_issue_stage(uint8_t* cslot, uint8_t* sslot, const uint8_t* rec, const RecGeom& rg, int row0, int k,
+                           int lane) {
   const int ch = lane & 7, rq = lane >> 3;
 #pragma unroll
   for (int m = 0; m < 4; ++m) {
@@ -337,8 +339,9 @@ YN_DEV void rf_issue_stage(uint8_t* cslot, uint8_t* sslot, const uint8_t* rec, c
 // weight rows g and g+8, batch rows 2c and 2c+1), in the batch path's
 // arithmetic (warp_tile): each group's tile starts at the group's unpack
 // offset, and its scale and bias are applied in fp32.
-YN_DEV void rf_stage_mma(const uint8_t* slot, const uint8_t* sslot, int k, const uint32_t* XF, int xs, const float2* XG,
-                         int gsd, int ntok, float (&acc)[4]) {
+template <int xs, int gsd>
+YN_DEV void rf_stage_mma(const uint8_t* slot, const uint8_t* sslot, int k, const uint32_t* XF, const float2* XG, int ntok,
+                         float (&acc)[4]) {
   using F = BFmt<RF_BITS, RF_GS>;
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const int mrow = ((lane >> 3) & 1) * 8 + (lane & 7), mch = lane >> 4;
@@ -357,11 +360,12 @@ YN_DEV void rf_stage_mma(const uint8_t* slot, const uint8_t* sslot, int k, const
       uint32_t pa[F::PPW], pb[F::PPW], xb[F::PPW];
       BW<RF_BITS>::unpack(wr[2 * h], pa);
       BW<RF_BITS>::unpack(wr[2 * h + 1], pb);
-      if (g < ntok) {
-        const uint4 v = *reinterpret_cast<const uint4*>(XF + (size_t)g * xs + (size_t)(ch * 4 + c) * F::PPW);
+      {   // batch columns past the expert's rows read the zero block (an address choice, no branch)
+        extern __shared__ __align__(128) uint8_t smem_z[];
+        const uint4* src = g < ntok ? reinterpret_cast<const uint4*>(XF + (size_t)g * xs + (size_t)(ch * 4 + c) * F::PPW)
+                                    : reinterpret_cast<const uint4*>(smem_z + RF_OFF_ZERO);
+        const uint4 v = *src;
         xb[0] = v.x; xb[1] = v.y; xb[2] = v.z; xb[3] = v.w;
-      } else {
-        xb[0] = xb[1] = xb[2] = xb[3] = 0u;
       }
       const uint32_t A0[4] = {pa[0], pb[0], pa[1], pb[1]}, B0[2] = {xb[0], xb[1]};
       if (h == 0) {
@@ -463,6 +467,7 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
     fence_mbar_init();
   }
   if (tid < 8) misc[16 + tid] = tid;
+  if (tid < 4) reinterpret_cast<uint32_t*>(smem + RF_OFF_ZERO)[tid] = 0u;
   load_layer(&lay[0], a.layers, 0);
   __syncthreads();
   if (tid == 0) rf_issue_rtile(lay[0], b, router_cta, smem, barR);
@@ -625,7 +630,8 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
         const int row0 = gu ? (gu0 + warp + RF_WARPS * (j / RF_NKU)) * RF_GU_UNITS
                             : (dn0 + warp + RF_WARPS * ((j - n_gu_items) / RF_NKD)) * RF_DN_ROWS;
         const int k = gu ? j % RF_NKU : (j - n_gu_items) % RF_NKD;
-        rf_issue_stage(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, rec, L.rg, gu, row0, k, lane);
+        if (gu) rf_issue_stage<true>(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, rec, L.rg, row0, k, lane);
+        else rf_issue_stage<false>(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, rec, L.rg, row0, k, lane);
       }
       cp_commit();
     };
@@ -650,8 +656,8 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       if (diag) dg_wait_gu += dg_now() - dg_t;
       issue_item(j + RF_NST - 1);   // into the slot of item j - 1
       const int sl = j % RF_NST;
-      rf_stage_mma(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, j % RF_NKU, XF, RF_XSU, XG, RF_GSU,
-                   Td, acc);
+      rf_stage_mma<RF_XSU, RF_GSU>(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, j % RF_NKU, XF, XG, Td,
+                                   acc);
       if (j % RF_NKU == RF_NKU - 1) {
         rf_gu_out(acc, XG, Td, fa, (gu0 + warp + RF_WARPS * (j / RF_NKU)) * RF_GU_UNITS, ep);
         acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
@@ -659,6 +665,7 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
     }
     rf_stamp(a, layer, 7);
     // -------- Dn: the expert's activations of all its rows, fragments, the warp's down groups
+    __syncthreads();   // warps without gate/up groups wait here in the barrier, not in polls beside the working warps
     rf_wait_words(fa, reinterpret_cast<uint32_t*>(xb), Td * (RF_I / 2), ep, a.err, fail);
     if (__syncthreads_or(fail)) { drain(); return; }
     rf_stamp(a, layer, 8);
@@ -672,13 +679,14 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       issue_item(j + RF_NST - 1);
       const int jd = j - n_gu_items;
       const int sl = j % RF_NST;
-      rf_stage_mma(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, jd % RF_NKD, XF, RF_XSD, XG, RF_GSD,
-                   Td, acc);
+      rf_stage_mma<RF_XSD, RF_GSD>(cring + (size_t)sl * RF_CSLOT, sring + (size_t)sl * RF_SSLOT, jd % RF_NKD, XF, XG, Td,
+                                   acc);
       if (jd % RF_NKD == RF_NKD - 1) {
         rf_dn_out(acc, XG, Td, fy, (dn0 + warp + RF_WARPS * (jd / RF_NKD)) * RF_DN_ROWS, ep);
         acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
       }
     }
+    __syncthreads();   // likewise for warps without down groups
     rf_stamp(a, layer, 10);
     // -------- C: this CTA's output words (column order, then the residual)
     if (tid < ncw) {
