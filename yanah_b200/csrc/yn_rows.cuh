@@ -600,8 +600,8 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       return;
     }
     // this CTA's expert, its rows, and this warp's work groups
-    const int d = (int)(((long long)(b + 1) * D - 1) / G);
-    const int lo = (int)((long long)d * G / D), hi = (int)((long long)(d + 1) * G / D);
+    const int d = ((b + 1) * D - 1) / G;   // (b + 1) * D <= 148 * 64: 32-bit
+    const int lo = d * G / D, hi = (d + 1) * G / D;
     const int r = b - lo, nd = hi - lo;
     const int e = elist[d];
     const uint32_t rm = rowmask[e];
@@ -641,11 +641,14 @@ __global__ void __launch_bounds__(RF_THREADS, 1) k_rows_flow(const RowsArgs a) {
       cp_wait_prefetched();
       __syncwarp();
     };
-#pragma unroll
-    for (int j = 0; j < RF_NST - 1; ++j) issue_item(j);
+    // the first stage before the fragments, the next two after them: a warp's copy issue stalls once the
+    // SM's outstanding copies fill up, and the fragment build needs no copy
+    issue_item(0);
     __syncthreads();   // misc[8..16)
     rf_stamp(a, layer, 5);
     rf_frags<RF_BITS, RF_GS, RF_H>(xb, misc + 8, Td, XF, RF_XSU, XG, RF_GSU, rowf + 8);
+#pragma unroll
+    for (int j = 1; j < RF_NST - 1; ++j) issue_item(j);
     rf_stamp(a, layer, 6);
     // -------- GU: the warp's gate/up groups, SwiGLU, activations out
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
