@@ -73,7 +73,7 @@ constexpr int RF_KSTAGE = 128;                // code bytes of a row per K stage
 constexpr int RF_NKU = RF_RB / RF_KSTAGE;     // 8 stages per gate/up row
 constexpr int RF_NKD = RF_RBD / RF_KSTAGE;    // 6 stages per down row
 constexpr int RF_GPS = RF_KSTAGE * 8 / RF_BITS / RF_GS;   // 4 groups per stage
-constexpr int RF_CSLOT = 16 * RF_KSTAGE;      // 2,048 B: a stage's 16 code rows (two 1 KB swizzle atoms)
+constexpr int RF_CSLOT = 16 * RF_KSTAGE;      // 2,048 B: a stage's 16 code rows
 constexpr int RF_SSLOT = 2 * 16 * RF_GPS * 2; // 256 B: their scales and biases
 constexpr int RF_NST = 4;                     // ring stages per warp (3 in flight while one is computed)
 constexpr int RF_XSU = RF_H / 2 + 16;   // fragment words per row (frag_stride_words), gate/up
@@ -82,7 +82,7 @@ constexpr int RF_GSU = RF_NG + 2;       // group-data entries per row (gdata_str
 constexpr int RF_GSD = RF_NGD + 2;      // down
 constexpr int RF_MAX_CW = 64;           // output words per CTA
 static_assert(RF_GPS == 4 && RF_NKU * RF_KSTAGE == RF_RB && RF_NKD * RF_KSTAGE == RF_RBD, "whole stages");
-static_assert(RF_CSLOT % 1024 == 0, "code slots stay on 1 KB swizzle atoms");
+static_assert(RF_CSLOT % 128 == 0, "code slots stay 128-byte aligned");
 static_assert(RF_E == 64, "every router row has a CTA of its own");
 static_assert(RF_XSU == RF_H / 2 + 16 && RF_XSD == RF_I / 2 + 16, "batch-path fragment strides (4-bit)");
 
