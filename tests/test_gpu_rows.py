@@ -67,3 +67,57 @@ def test_rows_flow_rejects_other_shapes():
     with pytest.raises(_lib.YanahError) as e:
         st.rows_decode(x, torch.empty_like(x))
     assert e.value.code == _lib.YN_E_UNSUPPORTED
+
+
+def test_rows_flow_slot_table_and_identical_rows():
+    """Two layouts and two batch shapes that the random-row test does not
+    reach. (1) Experts behind an expert -> slot table in a permuted arena
+    with spare slots: the same outputs, bit for bit, as the identity layout
+    (only the record addresses change). (2) Five identical rows: every row
+    routes to the same k experts, so each expert has all five rows and ~37
+    CTAs; every output row equals the single-row decode of that row, bit for
+    bit (the GEMV columns are independent and the work split is the same)."""
+    from yanah_b200 import _lib
+    from yanah_b200.device import DeviceLayer, ExpertArena
+    from yanah_b200.stack import ResidentStack
+    from yanah_b200.synthetic import dense_layer, lfm2_stack
+    import ctypes as C
+    cfg = lfm2_stack(seed=0, n_layers=2)
+    st = ResidentStack(cfg, "cuda")
+    row = hidden_rows(cfg, 1, stream=33)
+    x = bf16_dev(np.repeat(row, 5, axis=0))
+    base = torch.empty_like(x)
+    st.rows_decode(x, base)
+    one_in = x[:1].clone()
+    one = torch.empty_like(one_in)
+    st.rows_decode(one_in, one)
+    torch.cuda.synchronize()
+    assert st.rows_error() == 0
+    b = bf16_np(base)
+    for t in range(1, 5):
+        assert np.array_equal(b[t], b[0]), t
+    assert np.array_equal(b[0], bf16_np(one)[0])
+    # the same stack behind slot tables: expert e in slot (5 e + 2) mod (E + 3) of a larger arena
+    E = cfg.n_experts
+    slot_of = np.array([(5 * e + 2) % (E + 3) for e in range(E)], np.int32)
+    assert len(set(slot_of.tolist())) == E
+    keep = []
+    for i, l in enumerate(st.layer_ids):
+        old = st.arenas[i]
+        arena = ExpertArena(E + 3, old.slot_bytes, st.device)
+        arena.buf.fill_(0xA5)
+        for e in range(E):
+            arena.slot_view(int(slot_of[e])).copy_(old.slot_view(e))
+        smap = torch.from_numpy(slot_of).to(st.device)
+        layer = DeviceLayer(cfg, l, dense_layer(cfg, l), arena, 0, smap, st.device)
+        keep.append((arena, smap, layer))
+    structs = [k[2].struct() for k in keep]
+    arr = (_lib.Layer * len(structs))(*structs)
+    tb = st.table.numel()
+    _lib.check(_lib.lib().yn_stack_prepare(C.byref(st.dims), arr, len(structs), st.table.data_ptr(), tb))
+    st.structs, st.layer_array = structs, arr
+    moved = torch.empty_like(x)
+    st.rows_decode(x, moved)
+    torch.cuda.synchronize()
+    assert st.rows_error() == 0
+    assert np.array_equal(bf16_np(moved), b)
