@@ -124,6 +124,9 @@ class CudaMoEBackend:
         self._lut_used = [False] * n_lut
         self._lut_i = 0
         self._lut_last = None        # (memory, rows, ring row) of the last table written
+        # layer descriptors over (layer, table row, memory), built once: the launches only read them
+        self._desc: Dict[tuple, _lib.Layer] = {}
+        self._desc_mem: Dict[tuple, object] = {}
         # pinned landing rows for the routing readback (ids, then lookahead probabilities)
         self._ids_host = torch.empty(_lib.YN_MAX_ROWS * cfg.top_k, dtype=torch.int32, pin_memory=True)
         self._fp_host = torch.empty(max(lookahead, 1) * E, dtype=torch.float32, pin_memory=True)
@@ -163,13 +166,16 @@ class CudaMoEBackend:
             self._lut_ev[i].record(self.stream)
             self._lut_used[i] = True
             self._lut_last = (memory, dict(rows), i)
-        dev = self._lut_dev[i]
-        L = _lib.Layer.from_buffer_copy(self._structs[layer])
-        L.expert_base = memory.arena.base
-        L.slot_stride = memory.arena.slot_bytes
-        L.n_slots = memory.n
-        L.expert_slot = dev.data_ptr()
-        L.record = self._records[layer]
+        key = (layer, i, id(memory))
+        L = self._desc.get(key)
+        if L is None or self._desc_mem.get(key) is not memory:
+            L = _lib.Layer.from_buffer_copy(self._structs[layer])
+            L.expert_base = memory.arena.base
+            L.slot_stride = memory.arena.slot_bytes
+            L.n_slots = memory.n
+            L.expert_slot = self._lut_dev[i].data_ptr()
+            L.record = self._records[layer]
+            self._desc[key], self._desc_mem[key] = L, memory
         return L
 
     def layout(self) -> ExpertLayout:
@@ -265,7 +271,7 @@ class CudaMoEBackend:
     # ---------------------------------------------------------------- experts
     def moe_ready(self, layer: int, x, ids: np.ndarray, memory: CudaExpertMemory, ready: Dict[int, int]):
         """Start the routed columns whose experts are already in memory."""
-        cols = [j for j in range(ids.shape[1]) if int(ids[0, j]) in ready]
+        cols = [j for j, e in enumerate(ids[0].tolist()) if e in ready]
         if cols:
             L = self._layer_struct(layer, memory, ready)
             cc = (C.c_int32 * len(cols))(*cols)
@@ -274,9 +280,12 @@ class CudaMoEBackend:
         return cols
 
     def moe_rest(self, layer: int, x, ids: np.ndarray, w, memory: CudaExpertMemory, rows: Dict[int, int],
-                 handle) -> torch.Tensor:
+                 handle, h_res: Optional[torch.Tensor] = None) -> torch.Tensor:
         """The remaining columns, then the weighted sum over all k columns in
-        column order plus the gated shared expert."""
+        column order plus the gated shared expert. With `h_res` (a caller of
+        its own, not the reference's orchestrator, whose `moe_finalize` result
+        it adds itself) the residual is added in the same kernel, with the
+        same rounding as bf16(h_res + moe_finalize(...))."""
         cols = set(handle or [])
         rest = [j for j in range(ids.shape[1]) if j not in cols]
         L = self._layer_struct(layer, memory, rows)
@@ -284,7 +293,7 @@ class CudaMoEBackend:
             cc = (C.c_int32 * len(rest))(*rest)
             _lib.check(_lib.lib().yn_moe_up(C.byref(self.dims), C.byref(L), None, None, ids.shape[0], cc, len(rest),
                                             self.ws.ptr, self._st()))
-        return self._down(L, ids.shape[0])
+        return self._down(L, ids.shape[0], h_res)
 
     def moe(self, layer: int, x, ids: np.ndarray, w, memory: CudaExpertMemory, rows: Dict[int, int],
             sync: bool = True) -> torch.Tensor:
@@ -367,10 +376,11 @@ class CudaMoEBackend:
         _lib.check(lib.yn_pairs_combine(D, y.data_ptr(), p_of, w.data_ptr(), None, None, T, out.data_ptr(), st))
         return out
 
-    def _down(self, L, T: int) -> torch.Tensor:
+    def _down(self, L, T: int, h_res: Optional[torch.Tensor] = None) -> torch.Tensor:
         out = torch.empty((T, self.cfg.hidden), dtype=torch.bfloat16, device=self.device)
-        mode = 1 if self.cfg.shared_inter else 0
-        _lib.check(_lib.lib().yn_moe_down(C.byref(self.dims), C.byref(L), None, None, T, None, mode, out.data_ptr(),
+        mode = 2 if h_res is not None else (1 if self.cfg.shared_inter else 0)
+        _lib.check(_lib.lib().yn_moe_down(C.byref(self.dims), C.byref(L), None, None, T,
+                                          h_res.data_ptr() if h_res is not None else None, mode, out.data_ptr(),
                                           self.ws.ptr, self._st()))
         return out
 

@@ -51,15 +51,16 @@ class RouterForecast:
         neg = -score
         part = np.argpartition(neg, k - 1)[:k]          # the k most probable, in no particular order
         order = part[np.argsort(neg[part])]             # most probable first; ties as numpy's sort leaves them
-        out = [(int(e), float(score[e])) for e in order]
-        self._pending.setdefault(target_layer, set()).update(e for e, _ in out)
+        ids = order.tolist()
+        out = list(zip(ids, score[order].astype(np.float64).tolist()))
+        self._pending.setdefault(target_layer, set()).update(ids)
         self.stats.forecasts += 1
         self.stats.candidates += len(out)
         return out
 
     def observe(self, layer: int, routed: np.ndarray) -> None:
         """Score the pending forecast of `layer` against the experts it routed."""
-        actual = {int(e) for e in np.unique(np.asarray(routed))}
+        actual = set(np.asarray(routed).ravel().tolist())
         pred = self._pending.pop(layer, None)
         if pred is None:
             return

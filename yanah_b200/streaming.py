@@ -117,7 +117,7 @@ class PoolPolicy:
         ready: Dict[int, int] = {}
         misses: List[int] = []
         adopted: List[int] = []
-        for e in sorted({int(v) for v in np.asarray(ids).reshape(-1)}):
+        for e in sorted(set(np.asarray(ids).ravel().tolist())):
             key = (l, e)
             s = pool.hit(key)
             if s is None:
@@ -268,9 +268,8 @@ class StreamingDecoder:
                 self.compute.wait_event(ev_demand)
             for ev in waits:
                 self.compute.wait_event(ev)
-        routed = be.moe_rest(l, x, ids, w, pool.memory, out, handle)
-        with torch.cuda.stream(self.compute):
-            h_next = h_res + be.moe_finalize(l, routed)
+        # routed + shared + residual in the down kernel: bf16(h_res + moe_finalize(...)) of orchestrator.py:287
+        h_next = be.moe_rest(l, x, ids, w, pool.memory, out, handle, h_res=h_res)
         if ev_ready is not None:
             self.stats._pending.append(("stall", ev_ready, ev_demand))
         if self.ev_compute is None:
