@@ -127,9 +127,9 @@ def test_streaming_decoder_matches_reference_engine(fx, world):
     reads = {"demand": [], "spec": []}
     copy = dec._copy
 
-    def logged(stream, pairs, layer):
+    def logged(stream, pairs, layer, after):
         reads["demand" if stream is dec.copy else "spec"].extend([layer, e, sl] for e, sl in pairs)
-        return copy(stream, pairs, layer)
+        return copy(stream, pairs, layer, after)
     dec._copy = logged
     dec.trace = []
     L = cfg.n_layers

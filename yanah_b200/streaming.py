@@ -199,7 +199,9 @@ class StreamingDecoder:
         self.policy = PoolPolicy(self.pool, self.fc, threshold, issue_cap, top)
         self.host = host if host is not None else HostTier(cfg, self.device)
         self.events: Dict[Tuple[int, int], torch.cuda.Event] = {}   # forecast copies in flight
-        self.ev_compute: Optional[torch.cuda.Event] = None
+        self.ev_compute: Optional[torch.cuda.Event] = None          # the last layer's kernels
+        self._ev_layer = [torch.cuda.Event(), torch.cuda.Event()]   # alternate: the previous layer's stays valid
+        self._ev_i = 0
         self.stats = StreamStats()
         self.measure = measure
         self.generation = 0
@@ -208,12 +210,13 @@ class StreamingDecoder:
         self.trace: Optional[list] = None
 
     # ------------------------------------------------------------- copies
-    def _copy(self, stream, pairs: List[Tuple[int, int]], layer: int) -> Optional[torch.cuda.Event]:
-        """Host records of `layer` -> slots, on `stream` after the last compute."""
+    def _copy(self, stream, pairs: List[Tuple[int, int]], layer: int,
+              after: Optional[torch.cuda.Event]) -> Optional[torch.cuda.Event]:
+        """Host records of `layer` -> slots, on `stream` after the compute event `after`."""
         if not pairs:
             return None
-        if self.ev_compute is not None:
-            stream.wait_event(self.ev_compute)
+        if after is not None:
+            stream.wait_event(after)
         ev0 = torch.cuda.Event(enable_timing=True) if self.measure else None
         ev1 = torch.cuda.Event(enable_timing=True)
         if ev0 is not None:
@@ -232,6 +235,10 @@ class StreamingDecoder:
 
     # -------------------------------------------------------------- layers
     def layer(self, l: int, h: torch.Tensor) -> torch.Tensor:
+        """One pool-path layer. The pool's steps run in the reference engine's
+        order (classify, issue, publish, expire, release); the expert kernels are
+        launched before the forecast bookkeeping, so the device computes while
+        the host selects and reserves the next layers' candidates."""
         be, pool, pol = self.be, self.pool, self.policy
         h_res, x, logits = be.pre_moe(l, h)
         targets = [t for t in (l + 1, l + 2) if t < self.cfg.n_layers]
@@ -244,21 +251,11 @@ class StreamingDecoder:
             if ev is not None and not ev.query():
                 waits.append(ev)
                 del ready[e]
-        ev_demand = self._copy(self.copy, [(e, out[e]) for e in misses], l)
+        # copies into slots the last layer's kernels may have read wait for those kernels
+        ev_prev = self.ev_compute
+        ev_demand = self._copy(self.copy, [(e, out[e]) for e in misses], l, ev_prev)
         self.stats.demand_records += len(misses)
         handle = be.moe_ready(l, x, ids, pool.memory, ready)
-        # forecasts for the next layers, copied while this layer computes
-        reserved, cands = pol.issue(targets, probs)
-        for t, pairs in reserved.items():
-            ev = self._copy(self.spec, pairs, t)
-            for e, _ in pairs:
-                self.events[(t, e)] = ev
-            self.stats.spec_records += len(pairs)
-        if self.trace is not None and ids.shape[0] == 1:
-            self.trace.append((self.generation, l, [int(e) for e in ids[0]], cands))
-        pol.publish(l, misses, out)
-        for k in pol.expire(l):
-            self.events.pop(k, None)
         ev_ready = None
         if ev_demand is not None or waits:
             if self.measure and ev_demand is not None:
@@ -272,9 +269,22 @@ class StreamingDecoder:
         h_next = be.moe_rest(l, x, ids, w, pool.memory, out, handle, h_res=h_res)
         if ev_ready is not None:
             self.stats._pending.append(("stall", ev_ready, ev_demand))
-        if self.ev_compute is None:
-            self.ev_compute = torch.cuda.Event()
-        self.ev_compute.record(self.compute)     # copies queued from here on wait for this layer's kernels
+        self._ev_i ^= 1
+        self.ev_compute = self._ev_layer[self._ev_i]
+        self.ev_compute.record(self.compute)     # copies queued from the next layer on wait for this layer's kernels
+        # forecasts for the next layers, copied while this layer computes (into partition slots, which this
+        # layer's kernels do not read: its slots are pinned)
+        reserved, cands = pol.issue(targets, probs)
+        for t, pairs in reserved.items():
+            ev = self._copy(self.spec, pairs, t, ev_prev)
+            for e, _ in pairs:
+                self.events[(t, e)] = ev
+            self.stats.spec_records += len(pairs)
+        if self.trace is not None and ids.shape[0] == 1:
+            self.trace.append((self.generation, l, [int(e) for e in ids[0]], cands))
+        pol.publish(l, misses, out)
+        for k in pol.expire(l):
+            self.events.pop(k, None)
         pol.release(out)
         self.stats.layers += 1
         return h_next
