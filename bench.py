@@ -980,7 +980,7 @@ def hooks_sample(cfg, dev, inputs, n_tok: int, layers=None, warm: int = 1) -> di
         for i, l in enumerate(layer_ids):
             h_res, x, logits = be.pre_moe(l, h)
             ids, w = be.route(logits)
-            rows = {int(e): i * E + int(e) for e in np.unique(ids)}
+            rows = {e: i * E + e for e in set(ids.ravel().tolist())}
             handle = be.moe_ready(l, x, ids, mem, rows)
             out = be.moe_rest(l, x, ids, w, mem, rows, handle)
             h = h_res + be.moe_finalize(l, out)

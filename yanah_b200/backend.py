@@ -130,6 +130,7 @@ class CudaMoEBackend:
         # pinned landing rows for the routing readback (ids, then lookahead probabilities)
         self._ids_host = torch.empty(_lib.YN_MAX_ROWS * cfg.top_k, dtype=torch.int32, pin_memory=True)
         self._fp_host = torch.empty(max(lookahead, 1) * E, dtype=torch.float32, pin_memory=True)
+        self._ids_np, self._fp_np = self._ids_host.numpy(), self._fp_host.numpy()
         self._pre: Dict[int, dict] = {}
         self._unfenced: Optional[torch.cuda.Event] = None
         self._route_ws: Optional[torch.Tensor] = None     # yn_rows_route workspace (prompt passes)
@@ -156,11 +157,8 @@ class CudaMoEBackend:
             if self._lut_used[i]:
                 self._lut_ev[i].synchronize()        # the copy out of this row has run
             lut = self._lut_np[i]
-            lut[:] = 0
-            if rows:
-                n = len(rows)
-                lut[np.fromiter(rows.keys(), dtype=np.int64, count=n)] = np.fromiter(rows.values(), dtype=np.int64,
-                                                                                     count=n)
+            if rows:   # only the entries of `rows`: a launch reads the table at its routed experts, all in `rows`
+                lut[list(rows.keys())] = list(rows.values())
             _lib.check(_lib.lib().yn_memcpy_async(self._lut_dev[i].data_ptr(), self._lut_host[i].data_ptr(),
                                                   lut.nbytes, self._st()))
             self._lut_ev[i].record(self.stream)
@@ -252,8 +250,8 @@ class CudaMoEBackend:
             fp = self.ws.tensor("fprobs", (n_fp, self.cfg.n_experts), torch.float32)
             _lib.check(lib.yn_memcpy_async(self._fp_host.data_ptr(), fp.data_ptr(), fp.numel() * 4, st))
         self.stream.synchronize()                                 # the routing sync
-        ids_np = self._ids_host.numpy()[:T * K].reshape(T, K).astype(np.int64)
-        fp_np = self._fp_host.numpy()[:n_fp * self.cfg.n_experts].reshape(n_fp, -1) if n_fp else None
+        ids_np = self._ids_np[:T * K].reshape(T, K).astype(np.int64)
+        fp_np = self._fp_np[:n_fp * self.cfg.n_experts].reshape(n_fp, -1) if n_fp else None
         return ids_np, self.ws.tensor("weights", (T, K), torch.float32), fp_np
 
     def route(self, logits):
