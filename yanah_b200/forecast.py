@@ -49,8 +49,9 @@ class RouterForecast:
         if k <= 0:
             return []
         neg = -score
-        part = np.argpartition(neg, k - 1)[:k]          # the k most probable, in no particular order
-        order = part[np.argsort(neg[part])]             # most probable first; ties as numpy's sort leaves them
+        # numpy's argpartition (introselect) and default argsort, as the array methods the module functions call
+        part = neg.argpartition(k - 1)[:k]              # the k most probable, in no particular order
+        order = part[neg[part].argsort()]               # most probable first; ties as numpy's sort leaves them
         ids = order.tolist()
         out = list(zip(ids, score[order].astype(np.float64).tolist()))
         self._pending.setdefault(target_layer, set()).update(ids)
