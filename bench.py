@@ -842,6 +842,14 @@ def run_verify_flow(args, rank: int, world: int):
     hbm, src = peaks()
     step_s = ms / args.steps / 1e3
     achieved = hbm_bytes / step_s / 1e9
+    traffic = None   # DRAM bytes per step: the ratio of a small ncu capture, applied to this step's bytes
+    tf = ROOT / "profiles" / "kernel_traffic.json"
+    if tf.exists() and not args.layers:
+        try:
+            ratio = json.loads(tf.read_text()).get("k_rows_flow_ratio_dram_to_algorithmic")
+            traffic = int(ratio * hbm_bytes) if ratio else None
+        except (ValueError, AttributeError, TypeError):
+            traffic = None
     line = {
         "metric": VERIFY_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
@@ -857,7 +865,7 @@ def run_verify_flow(args, rank: int, world: int):
         "roofline": {"bound": "hbm", "kernel": "k_rows_flow", "achieved": round(achieved, 1), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": src,
                      "bytes_per_step": hbm_bytes, "distinct_experts_per_layer_mean": round(float(np.mean(n_distinct)), 2),
-                     "traffic": None},
+                     "traffic": traffic},
     }
     if timing:
         line["phases"] = timing
